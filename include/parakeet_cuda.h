@@ -1,0 +1,258 @@
+/*
+ * parakeet_cuda.h -- C ABI of libparakeet_cuda, the B200 (sm_100a) greedy
+ * transducer decoder for parakeet.cpp's TDT and RNN-T/EOU token loops.
+ *
+ * The library replaces the decoder dispatch of parakeet.cpp (the reference):
+ *   - tdt_prepare_runtime   src/parakeet_tdt.cpp:585-718  -> pk_create
+ *   - tdt_init_state        src/parakeet_tdt.cpp:813-863  -> pk_stream_reset
+ *   - tdt_decode_window     src/parakeet_tdt.cpp:865-981  -> pk_stream_window
+ *   - tdt_greedy_decode     src/parakeet_tdt.cpp:983-1005 -> pk_decode_batch (B >= 1)
+ *   - eou_prepare_runtime   src/parakeet_eou.cpp:172-204  -> pk_create (PK_MODEL_EOU)
+ *   - eou_init_state        src/parakeet_eou.cpp:206-230  -> pk_stream_reset
+ *   - eou_decode_window     src/parakeet_eou.cpp:232-336  -> pk_stream_window
+ *   - eou_greedy_decode     src/parakeet_eou.cpp:338-387  -> pk_decode_batch
+ *
+ * Conventions (mirroring the reference's int return codes, parakeet_tdt.h:185-205):
+ *   - every entry point returns a pk_status; 0 is success, nothing aborts;
+ *   - pk_last_error() returns a thread-local message for the last failure;
+ *   - weights are passed as raw GGUF tensor blocks (ggml type F32 / F16 / Q8_0,
+ *     row-major [ne1][ne0] with ne0 = input features contiguous, the layout the
+ *     converter writes in scripts/convert-nemo-to-gguf.py:405-413); the library
+ *     copies and repacks them once; the caller keeps ownership of its buffers;
+ *   - encoder output is f32 [T][d_enc] row-major, on the host or on the device;
+ *   - one context per device; calls on one context are not concurrent
+ *     (same rule as parakeet::Engine, include/parakeet/engine.h:35-55).
+ *
+ * No C++ or torch types cross this boundary.
+ */
+#ifndef PARAKEET_CUDA_H
+#define PARAKEET_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PK_ABI_VERSION 1
+
+typedef enum pk_status {
+    PK_OK             = 0,
+    PK_ERR_DMODEL     = 1,  /* encoder d_model mismatch (tdt_decode_window rc 1, parakeet_tdt.cpp:874-878) */
+    PK_ERR_INVALID    = 2,  /* null pointer, negative size, bad option */
+    PK_ERR_MODEL      = 3,  /* missing tensor, wrong shape, unsupported ggml type */
+    PK_ERR_CUDA       = 4,  /* CUDA runtime error (message in pk_last_error) */
+    PK_ERR_OOM        = 5,  /* device allocation failed */
+    PK_ERR_TIMEOUT    = 6,  /* a bounded device-side wait (grid barrier) ran out */
+    PK_ERR_CAPACITY   = 7,  /* caller's output buffer too small; *_needed fields hold the size */
+    PK_ERR_NO_DEVICE  = 8,  /* no CUDA device / not sm_100 */
+    PK_ERR_DEVICE     = 9   /* a device-side index check failed (bad token / frame index) */
+} pk_status;
+
+/* ggml tensor type ids accepted in pk_tensor.type (values of enum ggml_type). */
+enum { PK_GGML_F32 = 0, PK_GGML_F16 = 1, PK_GGML_Q8_0 = 8 };
+
+/* Decoder families (ParakeetModelType, src/parakeet_ctc.h:225-230). */
+enum { PK_MODEL_TDT = 1, PK_MODEL_EOU = 2 };
+
+/* One GGUF tensor: raw blocks exactly as stored in the file / ggml tensor.
+ * 2-D weights: ne0 = in_features (contiguous), ne1 = out_features.
+ * 1-D biases: ne0 = length, ne1 = 1. */
+typedef struct pk_tensor {
+    const void * data;
+    int32_t      type;     /* PK_GGML_* */
+    int32_t      reserved;
+    int64_t      ne0;
+    int64_t      ne1;
+    uint64_t     nbytes;
+} pk_tensor;
+
+/* One prediction-net LSTM layer (TdtLstmLayer, src/parakeet_ctc.h:180-185);
+ * GGUF names {tdt,eou}.predict.lstm.<l>.{w_ih,w_hh,b_ih,b_hh}. */
+typedef struct pk_lstm_layer {
+    pk_tensor w_ih;   /* [4H][in]  gate order i, f, g, o (PyTorch) */
+    pk_tensor w_hh;   /* [4H][H]   */
+    pk_tensor b_ih;   /* [4H] f32  */
+    pk_tensor b_hh;   /* [4H] f32  */
+} pk_lstm_layer;
+
+/* Decoder hyper-parameters and weights. Field meaning follows the GGUF metadata
+ * parakeet.tdt.* / parakeet.eou.* read at src/parakeet_ctc.cpp:424-460. */
+typedef struct pk_model_desc {
+    int32_t model_type;            /* PK_MODEL_TDT or PK_MODEL_EOU */
+    int32_t d_enc;                 /* encoder d_model (1024 TDT, 512 EOU) */
+    int32_t pred_hidden;           /* H: LSTM hidden = embedding dim (640) */
+    int32_t joint_hidden;          /* J: joint hidden (640) */
+    int32_t n_layers;              /* L: LSTM layers (2 TDT, 1 EOU) */
+    int32_t vocab_size;            /* V: joint emits V+1 token logits (blank included) */
+    int32_t blank_id;              /* normally V (parakeet_ctc.cpp:430, :454) */
+    int32_t num_durations;         /* TDT duration head size (0 for EOU) */
+    const int32_t * durations;     /* TDT duration values, num_durations entries */
+    int32_t eou_id;                /* EOU <EOU> id (-1: vocab_size-2, parakeet_eou.cpp:182) */
+    int32_t eob_id;                /* EOU <EOB> id (-1: vocab_size-1, parakeet_eou.cpp:183) */
+    int32_t max_symbols_per_step;  /* default per-frame symbol cap (TDT 10, EOU 5) */
+    int32_t n_vocab_pieces;        /* number of tokenizer pieces (EOU special-piece rule) */
+    const uint8_t * special_piece; /* EOU: 1 where piece is "<...>" (parakeet_eou.cpp:315-319); may be NULL */
+    pk_tensor embed;               /* [V+1][H] predict.embed.weight */
+    const pk_lstm_layer * lstm;    /* n_layers entries */
+    pk_tensor joint_enc_w;         /* [J][d_enc] */
+    pk_tensor joint_enc_b;         /* [J] */
+    pk_tensor joint_pred_w;        /* [J][H] */
+    pk_tensor joint_pred_b;        /* [J] */
+    pk_tensor joint_out_w;         /* [V+1+num_durations][J] */
+    pk_tensor joint_out_b;         /* [V+1+num_durations] */
+} pk_model_desc;
+
+typedef struct pk_ctx pk_ctx;
+
+/* Math modes for the step loop (pk_set_option(PK_OPT_MATH, ...)). */
+enum {
+    PK_MATH_F32 = 0   /* exact dequantized weights, f32 activations, f32 FMA (reference-faithful) */
+};
+
+/* Options. */
+enum {
+    PK_OPT_TIMEOUT_US  = 1,  /* bound (microseconds) on every device-side grid-barrier wait */
+    PK_OPT_MATH        = 2,  /* PK_MATH_* */
+    PK_OPT_MAX_SYMBOLS = 3   /* default max_symbols_per_step override (> 0) */
+};
+
+/* Static information about a context. */
+typedef struct pk_info {
+    int32_t model_type, d_enc, pred_hidden, joint_hidden, n_layers;
+    int32_t vocab_size, blank_id, num_durations, v_plus_1, v_out;
+    int32_t eou_id, eob_id, max_symbols_per_step;
+    int32_t device, sm_count, grid_ctas;
+    uint64_t weight_bytes_device;   /* bytes of repacked weights held on the device */
+} pk_info;
+
+/* --- context ------------------------------------------------------------ */
+
+/* Validates the descriptor, dequantizes/repacks every decoder tensor onto
+ * `device` and sizes the persistent step-loop kernel. Replaces
+ * tdt_prepare_runtime (src/parakeet_tdt.cpp:585) / eou_prepare_runtime
+ * (src/parakeet_eou.cpp:172). */
+pk_status pk_create(const pk_model_desc * desc, int device, pk_ctx ** out);
+void      pk_destroy(pk_ctx * ctx);
+pk_status pk_get_info(const pk_ctx * ctx, pk_info * info);
+pk_status pk_set_option(pk_ctx * ctx, int32_t option, int64_t value);
+/* Thread-local message describing the last non-OK status of this thread. */
+const char * pk_last_error(void);
+int32_t   pk_abi_version(void);
+
+/* --- batched greedy decode ----------------------------------------------- */
+
+/* A batch of independent utterances (the reference decodes one at a time,
+ * src/parakeet_tdt.h:185-205; batching is new here). */
+typedef struct pk_batch {
+    const float *   enc;               /* f32 [frames][d_enc]; utterance b starts at frame frame_offsets[b] */
+    int32_t         enc_on_device;     /* 1: `enc` is a device pointer on the context's device */
+    int32_t         B;                 /* number of utterances (>= 0) */
+    int32_t         d_enc;             /* must equal the model's d_enc (else PK_ERR_DMODEL) */
+    int32_t         max_symbols_per_step; /* <= 0: model default */
+    const int64_t * frame_offsets;     /* host, B entries */
+    const int32_t * n_frames;          /* host, B entries (>= 0) */
+} pk_batch;
+
+/* Results. Pointers are host memory unless results_on_device = 1. Token ids of
+ * utterance b are tokens[token_offsets[b] .. token_offsets[b+1]), in emission
+ * order (TdtDecodeResult::token_ids, src/parakeet_tdt.h:168-173). */
+typedef struct pk_result {
+    int32_t   results_on_device;  /* 1: tokens/token_offsets/steps/eou_* are device pointers */
+    int32_t * tokens;             /* capacity tokens_cap */
+    int64_t   tokens_cap;
+    int64_t * token_offsets;      /* B+1 entries */
+    int32_t * steps;              /* B entries: joint evaluations (out_steps); may be NULL */
+    int32_t * eou_bounds;         /* EOU: segment ends (token index within the utterance); may be NULL */
+    int64_t   eou_bounds_cap;
+    int64_t * eou_offsets;        /* EOU: B+1 entries into eou_bounds; may be NULL */
+    float *   finish_ms;          /* host, B entries: device time from loop start to the utterance's last step; may be NULL */
+    /* outputs */
+    int64_t   tokens_needed;      /* total tokens emitted (set also on PK_ERR_CAPACITY) */
+    int64_t   eou_bounds_needed;
+    int64_t   total_steps;        /* sum of steps over the batch */
+    int64_t   loop_iterations;    /* batched step-loop iterations */
+    double    encproj_ms;         /* device time of the enc-proj GEMM (CUDA events) */
+    double    loop_ms;            /* device time of the persistent step loop */
+    double    total_ms;           /* device time of the whole call incl. copies */
+} pk_result;
+
+/* Greedy decode of B fresh utterances (each starts from tdt_init_state /
+ * eou_init_state). One persistent kernel runs every step of every utterance
+ * on the device; there is no host round trip per token. */
+pk_status pk_decode_batch(pk_ctx * ctx, const pk_batch * batch, pk_result * result);
+
+/* Upper bound on tokens a batch can emit: sum_b n_frames[b] * max(1, max_symbols). */
+int64_t   pk_tokens_capacity(const int32_t * n_frames, int32_t B, int32_t max_symbols_per_step);
+
+/* --- teacher-forced trace (parity harness) -------------------------------- */
+
+/* Runs the same kernel as pk_decode_batch but, when forced_token is given,
+ * replaces the device argmax of step s of utterance b with the caller's
+ * decision (forced_token / forced_dur_idx, [B][max_steps]; a negative token
+ * means "use the device argmax") so the device follows the oracle's
+ * trajectory. Records per step: logits [B][max_steps][v_out], the device's own
+ * argmax, and the LSTM state after the step [B][max_steps][L][H]. */
+typedef struct pk_trace {
+    int32_t         max_steps;
+    const int32_t * forced_token;     /* host [B][max_steps] or NULL (free running) */
+    const int32_t * forced_dur_idx;   /* host [B][max_steps] or NULL */
+    float *         logits;           /* host [B][max_steps][v_out] or NULL */
+    float *         h;                /* host [B][max_steps][L][H] or NULL */
+    float *         c;                /* host [B][max_steps][L][H] or NULL */
+    int32_t *       argmax_token;     /* host [B][max_steps] or NULL */
+    int32_t *       argmax_dur_idx;   /* host [B][max_steps] or NULL */
+} pk_trace;
+
+pk_status pk_decode_trace(pk_ctx * ctx, const pk_batch * batch, pk_trace * trace, pk_result * result);
+
+/* --- streaming (tdt_decode_window / eou_decode_window) -------------------- */
+
+/* Per-utterance decoder state (TdtDecodeState, src/parakeet_tdt.h:175-183;
+ * EouDecodeState, src/parakeet_eou.h:53-66), kept on the device. */
+typedef struct pk_stream pk_stream;
+
+/* Host view of a stream's state, for export / import (resume). */
+typedef struct pk_stream_state {
+    float * h;                    /* [L][H] */
+    float * c;                    /* [L][H] */
+    float * pred_out;             /* [H] last-layer h (the prediction-net output) */
+    int32_t symbols_this_step;
+    int32_t carry_frames;         /* TDT: frames the last duration jumped past the window */
+    int32_t initialized;
+    int32_t last_token;           /* EOU */
+    int32_t segment_start_token;  /* EOU */
+} pk_stream_state;
+
+pk_status pk_stream_create(pk_ctx * ctx, pk_stream ** out);
+void      pk_stream_destroy(pk_stream * s);
+/* tdt_init_state / eou_init_state: h = c = 0, one LSTM step on embed[blank]. */
+pk_status pk_stream_reset(pk_stream * s);
+/* Decode one window of n_frames encoder frames, continuing the stream's state.
+ * `n_tokens_before` is the caller's running token count on entry (the size of
+ * out_tokens in the reference); EOU boundaries are expressed in that count.
+ * tokens receives only this window's tokens. Mirrors tdt_decode_window's
+ * semantics: n_frames <= 0 returns 0 without initialising (TDT); an
+ * uninitialised state is initialised first; carry_frames crosses windows. */
+pk_status pk_stream_window(pk_stream * s, const float * enc, int32_t enc_on_device,
+                           int32_t n_frames, int32_t d_enc, int32_t max_symbols_per_step,
+                           int32_t n_tokens_before,
+                           int32_t * tokens, int32_t tokens_cap, int32_t * n_tokens,
+                           int32_t * steps,
+                           int32_t * eou_bounds, int32_t bounds_cap, int32_t * n_bounds);
+pk_status pk_stream_get_state(const pk_stream * s, pk_stream_state * st);
+pk_status pk_stream_set_state(pk_stream * s, const pk_stream_state * st);
+
+/* --- multi-GPU host helper ------------------------------------------------ */
+
+/* Longest-processing-time partition of utterances over n_shards devices by
+ * frame count (descending T, each to the shard with the least total T; ties
+ * to the lowest shard id). shard_of[b] receives the shard of utterance b. */
+pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_shards, int32_t * shard_of);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PARAKEET_CUDA_H */
