@@ -37,6 +37,12 @@ extern "C" {
 
 #define PK_ABI_VERSION 1
 
+#if defined(__GNUC__) || defined(__clang__)
+#define PK_API __attribute__((visibility("default")))
+#else
+#define PK_API
+#endif
+
 typedef enum pk_status {
     PK_OK             = 0,
     PK_ERR_DMODEL     = 1,  /* encoder d_model mismatch (tdt_decode_window rc 1, parakeet_tdt.cpp:874-878) */
@@ -133,13 +139,13 @@ typedef struct pk_info {
  * `device` and sizes the persistent step-loop kernel. Replaces
  * tdt_prepare_runtime (src/parakeet_tdt.cpp:585) / eou_prepare_runtime
  * (src/parakeet_eou.cpp:172). */
-pk_status pk_create(const pk_model_desc * desc, int device, pk_ctx ** out);
-void      pk_destroy(pk_ctx * ctx);
-pk_status pk_get_info(const pk_ctx * ctx, pk_info * info);
-pk_status pk_set_option(pk_ctx * ctx, int32_t option, int64_t value);
+PK_API pk_status pk_create(const pk_model_desc * desc, int device, pk_ctx ** out);
+PK_API void      pk_destroy(pk_ctx * ctx);
+PK_API pk_status pk_get_info(const pk_ctx * ctx, pk_info * info);
+PK_API pk_status pk_set_option(pk_ctx * ctx, int32_t option, int64_t value);
 /* Thread-local message describing the last non-OK status of this thread. */
-const char * pk_last_error(void);
-int32_t   pk_abi_version(void);
+PK_API const char * pk_last_error(void);
+PK_API int32_t   pk_abi_version(void);
 
 /* --- batched greedy decode ----------------------------------------------- */
 
@@ -181,10 +187,10 @@ typedef struct pk_result {
 /* Greedy decode of B fresh utterances (each starts from tdt_init_state /
  * eou_init_state). One persistent kernel runs every step of every utterance
  * on the device; there is no host round trip per token. */
-pk_status pk_decode_batch(pk_ctx * ctx, const pk_batch * batch, pk_result * result);
+PK_API pk_status pk_decode_batch(pk_ctx * ctx, const pk_batch * batch, pk_result * result);
 
 /* Upper bound on tokens a batch can emit: sum_b n_frames[b] * max(1, max_symbols). */
-int64_t   pk_tokens_capacity(const int32_t * n_frames, int32_t B, int32_t max_symbols_per_step);
+PK_API int64_t   pk_tokens_capacity(const int32_t * n_frames, int32_t B, int32_t max_symbols_per_step);
 
 /* --- teacher-forced trace (parity harness) -------------------------------- */
 
@@ -205,7 +211,7 @@ typedef struct pk_trace {
     int32_t *       argmax_dur_idx;   /* host [B][max_steps] or NULL */
 } pk_trace;
 
-pk_status pk_decode_trace(pk_ctx * ctx, const pk_batch * batch, pk_trace * trace, pk_result * result);
+PK_API pk_status pk_decode_trace(pk_ctx * ctx, const pk_batch * batch, pk_trace * trace, pk_result * result);
 
 /* --- streaming (tdt_decode_window / eou_decode_window) -------------------- */
 
@@ -225,31 +231,31 @@ typedef struct pk_stream_state {
     int32_t segment_start_token;  /* EOU */
 } pk_stream_state;
 
-pk_status pk_stream_create(pk_ctx * ctx, pk_stream ** out);
-void      pk_stream_destroy(pk_stream * s);
+PK_API pk_status pk_stream_create(pk_ctx * ctx, pk_stream ** out);
+PK_API void      pk_stream_destroy(pk_stream * s);
 /* tdt_init_state / eou_init_state: h = c = 0, one LSTM step on embed[blank]. */
-pk_status pk_stream_reset(pk_stream * s);
+PK_API pk_status pk_stream_reset(pk_stream * s);
 /* Decode one window of n_frames encoder frames, continuing the stream's state.
  * `n_tokens_before` is the caller's running token count on entry (the size of
  * out_tokens in the reference); EOU boundaries are expressed in that count.
  * tokens receives only this window's tokens. Mirrors tdt_decode_window's
  * semantics: n_frames <= 0 returns 0 without initialising (TDT); an
  * uninitialised state is initialised first; carry_frames crosses windows. */
-pk_status pk_stream_window(pk_stream * s, const float * enc, int32_t enc_on_device,
+PK_API pk_status pk_stream_window(pk_stream * s, const float * enc, int32_t enc_on_device,
                            int32_t n_frames, int32_t d_enc, int32_t max_symbols_per_step,
                            int32_t n_tokens_before,
                            int32_t * tokens, int32_t tokens_cap, int32_t * n_tokens,
                            int32_t * steps,
                            int32_t * eou_bounds, int32_t bounds_cap, int32_t * n_bounds);
-pk_status pk_stream_get_state(const pk_stream * s, pk_stream_state * st);
-pk_status pk_stream_set_state(pk_stream * s, const pk_stream_state * st);
+PK_API pk_status pk_stream_get_state(const pk_stream * s, pk_stream_state * st);
+PK_API pk_status pk_stream_set_state(pk_stream * s, const pk_stream_state * st);
 
 /* --- multi-GPU host helper ------------------------------------------------ */
 
 /* Longest-processing-time partition of utterances over n_shards devices by
  * frame count (descending T, each to the shard with the least total T; ties
  * to the lowest shard id). shard_of[b] receives the shard of utterance b. */
-pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_shards, int32_t * shard_of);
+PK_API pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_shards, int32_t * shard_of);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,781 @@
+// pk_api.cu -- the extern "C" surface of libparakeet_cuda (include/parakeet_cuda.h):
+// context creation and weight repack, the per-call workspace, and the batch,
+// trace and streaming entry points built on the persistent step loop.
+
+#include "pk_internal.h"
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <numeric>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_err;
+
+pk_status fail(pk_status s, const char * fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return s;
+}
+
+#define PK_CK(call)                                                                         \
+    do {                                                                                    \
+        cudaError_t e_ = (call);                                                            \
+        if (e_ != cudaSuccess)                                                              \
+            return fail(e_ == cudaErrorMemoryAllocation ? PK_ERR_OOM : PK_ERR_CUDA,         \
+                        "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+
+#define PK_TRY(expr)                      \
+    do {                                  \
+        pk_status s_ = (expr);            \
+        if (s_ != PK_OK) return s_;       \
+    } while (0)
+
+struct DevBuf {
+    void * p = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap && (p != nullptr || bytes == 0)) return cudaSuccess;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        const size_t want = bytes + bytes / 8 + 256;
+        cudaError_t e = cudaMalloc(&p, want);
+        if (e == cudaSuccess) cap = want;
+        return e;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+    template <class T> T * as() const { return static_cast<T *>(p); }
+};
+
+}  // namespace
+
+struct pk_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int sm_count = 0, grid = 0, chunk = 32, ldx = 0;
+    size_t smem = 0;
+    int type = PK_MODEL_TDT, H = 0, J = 0, De = 0, L = 0, V = 0, V1 = 0, Vo = 0, Nd = 0;
+    int blank = 0, eou = -1, eob = -1, max_sym = 10, n_special = 0;
+    long long timeout_ns = 5000000000ll;
+    int math = PK_MATH_F32;
+    uint64_t weight_bytes = 0;
+    // weights (f32 on the device)
+    DevBuf embed, w_ih[pk::kMaxLayers], w_hh[pk::kMaxLayers], b_ih[pk::kMaxLayers],
+        b_hh[pk::kMaxLayers], enc_w, enc_b, pred_w, pred_b, out_w, out_b, durations, special;
+    // per-call workspace
+    DevBuf enc, encp, h, c, predp, hid, ust, keys, live, emit, ctl, bar, tstart, finish, tok,
+        tokregion, bnd, bndregion, frameoff, offsets, boffsets, compact, bcompact;
+    DevBuf tr_logits, tr_h, tr_c, tr_tok, tr_dur, tr_ftok, tr_fdur;
+    cudaEvent_t ev[6] = {};
+    std::vector<DevBuf *> all_bufs() {
+        std::vector<DevBuf *> v = {&embed, &enc_w, &enc_b, &pred_w, &pred_b, &out_w, &out_b,
+                                   &durations, &special, &enc, &encp, &h, &c, &predp, &hid, &ust,
+                                   &keys, &live, &emit, &ctl, &bar, &tstart, &finish, &tok,
+                                   &tokregion, &bnd, &bndregion, &frameoff, &offsets, &boffsets,
+                                   &compact, &bcompact, &tr_logits, &tr_h, &tr_c, &tr_tok, &tr_dur,
+                                   &tr_ftok, &tr_fdur};
+        for (int l = 0; l < pk::kMaxLayers; ++l) {
+            v.push_back(&w_ih[l]); v.push_back(&w_hh[l]); v.push_back(&b_ih[l]); v.push_back(&b_hh[l]);
+        }
+        return v;
+    }
+};
+
+struct pk_stream {
+    pk_ctx * ctx = nullptr;
+    DevBuf h, c;     // [L][H]
+    int sym = 0, carry = 0, initialized = 0, last = -1, segstart = 0, symx = 0;
+};
+
+namespace {
+
+using namespace pk;
+
+bool shape_ok(const pk_tensor & t, int64_t ne0, int64_t ne1) {
+    return t.data && t.ne0 == ne0 && (ne1 <= 1 ? (t.ne1 <= 1) : t.ne1 == ne1);
+}
+
+size_t raw_bytes(int type, int64_t ne0, int64_t rows) {
+    if (type == PK_GGML_F32) return (size_t) (ne0 * rows) * 4;
+    if (type == PK_GGML_F16) return (size_t) (ne0 * rows) * 2;
+    return (size_t) (rows * (ne0 / 32)) * 34;
+}
+
+// Upload one GGUF tensor (first `keep_rows` rows) and dequantize it to f32.
+pk_status upload(pk_ctx * x, const pk_tensor & t, int64_t keep_rows, DevBuf & dst, DevBuf & scratch,
+                 const char * name) {
+    if (!t.data) return fail(PK_ERR_MODEL, "tensor %s missing", name);
+    if (t.type != PK_GGML_F32 && t.type != PK_GGML_F16 && t.type != PK_GGML_Q8_0)
+        return fail(PK_ERR_MODEL, "tensor %s: unsupported ggml type %d", name, t.type);
+    if (t.type == PK_GGML_Q8_0 && t.ne0 % 32 != 0)
+        return fail(PK_ERR_MODEL, "tensor %s: q8_0 row of %lld not a multiple of 32", name, (long long) t.ne0);
+    const int64_t rows_all = t.ne1 > 0 ? t.ne1 : 1;
+    const int64_t rows = std::min(rows_all, keep_rows);
+    const size_t nb = raw_bytes(t.type, t.ne0, rows);
+    if (t.nbytes < nb) return fail(PK_ERR_MODEL, "tensor %s: %llu bytes < %zu needed", name,
+                                   (unsigned long long) t.nbytes, nb);
+    PK_CK(scratch.ensure(nb));
+    PK_CK(cudaMemcpy(scratch.p, t.data, nb, cudaMemcpyHostToDevice));
+    const size_t fb = (size_t) (t.ne0 * rows) * sizeof(float);
+    PK_CK(dst.ensure(fb));
+    PK_CK(launch_dequant(scratch.p, t.type, t.ne0, rows, dst.as<float>(), x->stream));
+    PK_CK(cudaStreamSynchronize(x->stream));
+    x->weight_bytes += fb;
+    return PK_OK;
+}
+
+pk_status validate_desc(const pk_model_desc * d) {
+    if (!d) return fail(PK_ERR_INVALID, "null descriptor");
+    if (d->model_type != PK_MODEL_TDT && d->model_type != PK_MODEL_EOU)
+        return fail(PK_ERR_MODEL, "bad model_type %d", d->model_type);
+    const int H = d->pred_hidden, J = d->joint_hidden, De = d->d_enc, L = d->n_layers;
+    const int V1 = d->vocab_size + 1;
+    if (H <= 0 || J <= 0 || De <= 0 || L <= 0 || d->vocab_size <= 0)
+        return fail(PK_ERR_MODEL, "bad dims H=%d J=%d De=%d L=%d V=%d", H, J, De, L, d->vocab_size);
+    if (L > kMaxLayers) return fail(PK_ERR_MODEL, "%d LSTM layers > %d supported", L, kMaxLayers);
+    if (H % 4 != 0 || J % 4 != 0)
+        return fail(PK_ERR_MODEL, "pred_hidden and joint_hidden must be multiples of 4");
+    if (d->blank_id < 0 || d->blank_id >= V1) return fail(PK_ERR_MODEL, "blank_id out of range");
+    const int Nd = d->model_type == PK_MODEL_TDT ? d->num_durations : 0;
+    if (d->model_type == PK_MODEL_TDT) {
+        if (Nd <= 0 || !d->durations) return fail(PK_ERR_MODEL, "TDT model needs durations");
+        for (int i = 0; i < Nd; ++i)
+            if (d->durations[i] < 0) return fail(PK_ERR_MODEL, "negative duration");
+    }
+    const int Vo = V1 + Nd;
+    if (!d->lstm) return fail(PK_ERR_MODEL, "missing LSTM layers");
+    if (d->embed.ne0 != H || d->embed.ne1 < V1) return fail(PK_ERR_MODEL, "embed shape");
+    if (!shape_ok(d->joint_enc_w, De, J) || !shape_ok(d->joint_enc_b, J, 1))
+        return fail(PK_ERR_MODEL, "joint.enc shape");
+    if (!shape_ok(d->joint_pred_w, H, J) || !shape_ok(d->joint_pred_b, J, 1))
+        return fail(PK_ERR_MODEL, "joint.pred shape");
+    if (d->joint_out_w.ne0 != J || d->joint_out_w.ne1 < Vo || d->joint_out_b.ne0 < Vo)
+        return fail(PK_ERR_MODEL, "joint.out shape");
+    for (int l = 0; l < L; ++l) {
+        const pk_lstm_layer & y = d->lstm[l];
+        if (!shape_ok(y.w_ih, H, 4 * H) || !shape_ok(y.w_hh, H, 4 * H) ||
+            !shape_ok(y.b_ih, 4 * H, 1) || !shape_ok(y.b_hh, 4 * H, 1))
+            return fail(PK_ERR_MODEL, "lstm layer %d shape", l);
+    }
+    return PK_OK;
+}
+
+// Arguments of one run of the step loop.
+struct Run {
+    const float * enc = nullptr;
+    bool enc_dev = false;
+    int B = 0;
+    const int64_t * frame_off = nullptr;
+    const int32_t * n_frames = nullptr;
+    int msym = 1;
+    std::vector<int32_t> t0, sym0, nbefore, segstart, last, symx, fresh;
+    const float * h_in = nullptr;    // device [L][H] state to resume (B == 1)
+    const float * c_in = nullptr;
+    const pk_trace * trace = nullptr;
+    // outputs
+    std::vector<int32_t> ust;
+    std::vector<int32_t> ctl;
+    float ms_encproj = 0.f, ms_loop = 0.f;
+};
+
+pk_status run_loop(pk_ctx * x, Run & r) {
+    const int B = r.B, H = x->H, J = x->J, L = x->L;
+    cudaStream_t s = x->stream;
+    int64_t frames = 0;
+    for (int b = 0; b < B; ++b) {
+        if (r.n_frames[b] < 0) return fail(PK_ERR_INVALID, "n_frames[%d] < 0", b);
+        if (r.n_frames[b] > 0) {
+            if (r.frame_off[b] < 0) return fail(PK_ERR_INVALID, "frame_offsets[%d] < 0", b);
+            frames = std::max<int64_t>(frames, r.frame_off[b] + r.n_frames[b]);
+        }
+    }
+    if (frames > 0 && !r.enc) return fail(PK_ERR_INVALID, "null encoder output");
+    const int msym1 = std::max(1, r.msym);
+    std::vector<int64_t> tokregion(B), bndregion(B);
+    int64_t tok_total = 0, bnd_total = 0;
+    for (int b = 0; b < B; ++b) {
+        tokregion[b] = tok_total;
+        bndregion[b] = bnd_total;
+        tok_total += (int64_t) r.n_frames[b] * msym1;
+        bnd_total += r.n_frames[b];
+    }
+    const size_t Bs = (size_t) std::max(B, 1);
+    PK_CK(x->encp.ensure((size_t) frames * J * 4));
+    PK_CK(x->h.ensure(2 * (size_t) L * Bs * H * 4));
+    PK_CK(x->c.ensure((size_t) L * Bs * H * 4));
+    PK_CK(x->predp.ensure(Bs * J * 4));
+    PK_CK(x->hid.ensure(Bs * J * 4));
+    PK_CK(x->ust.ensure(Bs * kUst * 4));
+    PK_CK(x->keys.ensure(Bs * 2 * 8));
+    PK_CK(x->live.ensure(2 * Bs * 4));
+    PK_CK(x->emit.ensure(2 * Bs * 4));
+    PK_CK(x->ctl.ensure(kCtl * 4));
+    PK_CK(x->bar.ensure(2 * 4));
+    PK_CK(x->tstart.ensure(8));
+    PK_CK(x->finish.ensure(Bs * 8));
+    PK_CK(x->tok.ensure((size_t) std::max<int64_t>(tok_total, 1) * 4));
+    PK_CK(x->tokregion.ensure(Bs * 8));
+    PK_CK(x->bnd.ensure((size_t) std::max<int64_t>(bnd_total, 1) * 4));
+    PK_CK(x->bndregion.ensure(Bs * 8));
+    PK_CK(x->frameoff.ensure(Bs * 8));
+
+    PK_CK(cudaEventRecord(x->ev[0], s));
+    const float * encsrc = r.enc;
+    if (frames > 0 && !r.enc_dev) {
+        PK_CK(x->enc.ensure((size_t) frames * x->De * 4));
+        PK_CK(cudaMemcpyAsync(x->enc.p, r.enc, (size_t) frames * x->De * 4, cudaMemcpyHostToDevice, s));
+        encsrc = x->enc.as<float>();
+    }
+    PK_CK(cudaEventRecord(x->ev[1], s));
+    if (frames > 0)
+        PK_CK(launch_encproj_f32(encsrc, frames, x->De, x->enc_w.as<float>(), x->enc_b.as<float>(), J,
+                                 x->encp.as<float>(), s));
+    PK_CK(cudaEventRecord(x->ev[2], s));
+
+    // Host-built initial per-utterance state and lists.
+    std::vector<int32_t> ust((size_t) B * kUst, 0), live, emit;
+    for (int b = 0; b < B; ++b) {
+        int32_t * u = &ust[(size_t) b * kUst];
+        u[U_T] = r.t0[b];
+        u[U_SYM] = r.sym0[b];
+        u[U_HBUF] = 0;
+        u[U_LAST] = r.last[b];
+        u[U_SEGSTART] = r.segstart[b];
+        u[U_NBEFORE] = r.nbefore[b];
+        u[U_NFRAMES] = r.n_frames[b];
+        u[U_SYMX] = r.symx[b];
+        if (r.n_frames[b] > 0 && r.t0[b] < r.n_frames[b]) live.push_back(b);
+        if (r.fresh[b]) { emit.push_back(b); emit.push_back(x->blank | (1 << 31)); }
+    }
+    std::vector<int32_t> ctl(kCtl, 0);
+    ctl[C_SEL] = 0;
+    ctl[C_NLIVE0] = (int32_t) live.size();
+    ctl[C_NEMIT] = (int32_t) (emit.size() / 2);
+    if (B > 0) {
+        PK_CK(cudaMemcpyAsync(x->ust.p, ust.data(), ust.size() * 4, cudaMemcpyHostToDevice, s));
+        PK_CK(cudaMemcpyAsync(x->frameoff.p, r.frame_off, (size_t) B * 8, cudaMemcpyHostToDevice, s));
+        PK_CK(cudaMemcpyAsync(x->tokregion.p, tokregion.data(), (size_t) B * 8, cudaMemcpyHostToDevice, s));
+        PK_CK(cudaMemcpyAsync(x->bndregion.p, bndregion.data(), (size_t) B * 8, cudaMemcpyHostToDevice, s));
+        if (!live.empty())
+            PK_CK(cudaMemcpyAsync(x->live.p, live.data(), live.size() * 4, cudaMemcpyHostToDevice, s));
+        if (!emit.empty())
+            PK_CK(cudaMemcpyAsync(x->emit.p, emit.data(), emit.size() * 4, cudaMemcpyHostToDevice, s));
+        PK_CK(cudaMemsetAsync(x->keys.p, 0, (size_t) B * 16, s));
+        PK_CK(cudaMemsetAsync(x->finish.p, 0, (size_t) B * 8, s));
+    }
+    PK_CK(cudaMemcpyAsync(x->ctl.p, ctl.data(), kCtl * 4, cudaMemcpyHostToDevice, s));
+    PK_CK(cudaMemsetAsync(x->bar.p, 0, 8, s));
+    if (r.h_in) {
+        PK_CK(cudaMemcpyAsync(x->h.p, r.h_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
+        PK_CK(cudaMemcpyAsync(x->c.p, r.c_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
+    }
+
+    LoopParams P{};
+    P.H = H; P.J = J; P.L = L; P.V1 = x->V1; P.Vo = x->Vo; P.Nd = x->Nd; P.blank = x->blank;
+    P.eou = x->eou; P.eob = x->eob; P.is_tdt = x->type == PK_MODEL_TDT ? 1 : 0;
+    P.max_sym = r.msym; P.B = B; P.n_special = x->n_special;
+    P.chunk = x->chunk; P.ldx = x->ldx; P.timeout_ns = x->timeout_ns;
+    P.embed = x->embed.as<float>();
+    for (int l = 0; l < L; ++l) {
+        P.w_ih[l] = x->w_ih[l].as<float>(); P.w_hh[l] = x->w_hh[l].as<float>();
+        P.b_ih[l] = x->b_ih[l].as<float>(); P.b_hh[l] = x->b_hh[l].as<float>();
+    }
+    P.pred_w = x->pred_w.as<float>(); P.pred_b = x->pred_b.as<float>();
+    P.out_w = x->out_w.as<float>(); P.out_b = x->out_b.as<float>();
+    P.durations = x->durations.as<int32_t>(); P.special = x->special.as<uint8_t>();
+    P.encp = x->encp.as<float>(); P.frame_off = x->frameoff.as<int64_t>();
+    P.h = x->h.as<float>(); P.c = x->c.as<float>(); P.predp = x->predp.as<float>();
+    P.hid = x->hid.as<float>(); P.ust = x->ust.as<int32_t>();
+    P.keys = x->keys.as<unsigned long long>(); P.live = x->live.as<int32_t>();
+    P.emit = x->emit.as<int32_t>(); P.ctl = x->ctl.as<int32_t>(); P.bar = x->bar.as<unsigned>();
+    P.t_start = x->tstart.as<unsigned long long>(); P.finish_ns = x->finish.as<unsigned long long>();
+    P.tok_out = x->tok.as<int32_t>(); P.tok_region = x->tokregion.as<int64_t>();
+    P.bnd_out = x->bnd.as<int32_t>(); P.bnd_region = x->bndregion.as<int64_t>();
+    if (r.trace && r.trace->max_steps > 0 && B > 0) {
+        const pk_trace & t = *r.trace;
+        const size_t S = (size_t) t.max_steps;
+        P.trace_steps = t.max_steps;
+        PK_CK(x->tr_logits.ensure((size_t) B * S * x->Vo * 4));
+        PK_CK(x->tr_h.ensure((size_t) B * S * L * H * 4));
+        PK_CK(x->tr_c.ensure((size_t) B * S * L * H * 4));
+        PK_CK(x->tr_tok.ensure((size_t) B * S * 4));
+        PK_CK(x->tr_dur.ensure((size_t) B * S * 4));
+        PK_CK(cudaMemsetAsync(x->tr_logits.p, 0, (size_t) B * S * x->Vo * 4, s));
+        PK_CK(cudaMemsetAsync(x->tr_h.p, 0, (size_t) B * S * L * H * 4, s));
+        PK_CK(cudaMemsetAsync(x->tr_c.p, 0, (size_t) B * S * L * H * 4, s));
+        PK_CK(cudaMemsetAsync(x->tr_tok.p, 0xFF, (size_t) B * S * 4, s));
+        PK_CK(cudaMemsetAsync(x->tr_dur.p, 0xFF, (size_t) B * S * 4, s));
+        P.tr_logits = x->tr_logits.as<float>(); P.tr_h = x->tr_h.as<float>();
+        P.tr_c = x->tr_c.as<float>(); P.tr_tok = x->tr_tok.as<int32_t>();
+        P.tr_dur = x->tr_dur.as<int32_t>();
+        if (t.forced_token) {
+            PK_CK(x->tr_ftok.ensure((size_t) B * S * 4));
+            PK_CK(x->tr_fdur.ensure((size_t) B * S * 4));
+            PK_CK(cudaMemcpyAsync(x->tr_ftok.p, t.forced_token, (size_t) B * S * 4, cudaMemcpyHostToDevice, s));
+            if (t.forced_dur_idx)
+                PK_CK(cudaMemcpyAsync(x->tr_fdur.p, t.forced_dur_idx, (size_t) B * S * 4, cudaMemcpyHostToDevice, s));
+            else
+                PK_CK(cudaMemsetAsync(x->tr_fdur.p, 0, (size_t) B * S * 4, s));
+            P.forced_tok = x->tr_ftok.as<int32_t>();
+            P.forced_dur = x->tr_fdur.as<int32_t>();
+        }
+    }
+    PK_CK(cudaEventRecord(x->ev[3], s));
+    if (B > 0) PK_CK(launch_step_loop(P, x->grid, x->smem, s));
+    PK_CK(cudaEventRecord(x->ev[4], s));
+    r.ust.assign((size_t) B * kUst, 0);
+    r.ctl.assign(kCtl, 0);
+    if (B > 0) PK_CK(cudaMemcpyAsync(r.ust.data(), x->ust.p, (size_t) B * kUst * 4, cudaMemcpyDeviceToHost, s));
+    PK_CK(cudaMemcpyAsync(r.ctl.data(), x->ctl.p, kCtl * 4, cudaMemcpyDeviceToHost, s));
+    PK_CK(cudaStreamSynchronize(s));
+    PK_CK(cudaEventElapsedTime(&r.ms_encproj, x->ev[1], x->ev[2]));
+    PK_CK(cudaEventElapsedTime(&r.ms_loop, x->ev[3], x->ev[4]));
+    if (r.ctl[C_ERR] != 0) {
+        const int code = r.ctl[C_ERR];
+        if (code == PK_ERR_TIMEOUT)
+            return fail(PK_ERR_TIMEOUT, "step loop: a grid-barrier wait exceeded %lld us",
+                        x->timeout_ns / 1000);
+        return fail((pk_status) code, "step loop: device index check failed (utterance %d)",
+                    r.ctl[C_ERRINFO]);
+    }
+    if (r.trace && r.trace->max_steps > 0 && B > 0) {
+        const pk_trace & t = *r.trace;
+        const size_t S = (size_t) t.max_steps;
+        if (t.logits) PK_CK(cudaMemcpy(t.logits, x->tr_logits.p, (size_t) B * S * x->Vo * 4, cudaMemcpyDeviceToHost));
+        if (t.h) PK_CK(cudaMemcpy(t.h, x->tr_h.p, (size_t) B * S * L * H * 4, cudaMemcpyDeviceToHost));
+        if (t.c) PK_CK(cudaMemcpy(t.c, x->tr_c.p, (size_t) B * S * L * H * 4, cudaMemcpyDeviceToHost));
+        if (t.argmax_token) PK_CK(cudaMemcpy(t.argmax_token, x->tr_tok.p, (size_t) B * S * 4, cudaMemcpyDeviceToHost));
+        if (t.argmax_dur_idx) PK_CK(cudaMemcpy(t.argmax_dur_idx, x->tr_dur.p, (size_t) B * S * 4, cudaMemcpyDeviceToHost));
+    }
+    return PK_OK;
+}
+
+// Compaction of per-utterance regions into the caller's result buffers.
+pk_status emit_results(pk_ctx * x, const Run & r, pk_result * res) {
+    const int B = r.B;
+    cudaStream_t s = x->stream;
+    PK_CK(x->offsets.ensure((size_t) (B + 1) * 8));
+    PK_CK(x->boffsets.ensure((size_t) (B + 1) * 8));
+    int64_t ntok = 0, nbnd = 0, nsteps = 0;
+    for (int b = 0; b < B; ++b) {
+        ntok += r.ust[(size_t) b * kUst + U_NTOK];
+        nbnd += r.ust[(size_t) b * kUst + U_NBND];
+        nsteps += r.ust[(size_t) b * kUst + U_STEPS];
+    }
+    res->tokens_needed = ntok;
+    res->eou_bounds_needed = nbnd;
+    res->total_steps = nsteps;
+    res->loop_iterations = r.ctl[C_ITERS];
+    res->encproj_ms = r.ms_encproj;
+    res->loop_ms = r.ms_loop;
+    if (ntok > res->tokens_cap || (ntok > 0 && !res->tokens))
+        return fail(PK_ERR_CAPACITY, "token buffer holds %lld, %lld needed", (long long) res->tokens_cap,
+                    (long long) ntok);
+    if (res->eou_bounds && nbnd > res->eou_bounds_cap)
+        return fail(PK_ERR_CAPACITY, "boundary buffer holds %lld, %lld needed",
+                    (long long) res->eou_bounds_cap, (long long) nbnd);
+    const bool dev = res->results_on_device != 0;
+    PK_CK(launch_scan(x->ust.as<int32_t>(), B, U_NTOK, x->offsets.as<int64_t>(), s));
+    if (dev) {
+        if (res->tokens)
+            PK_CK(launch_gather(x->ust.as<int32_t>(), B, U_NTOK, x->tok.as<int32_t>(),
+                                x->tokregion.as<int64_t>(), x->offsets.as<int64_t>(), res->tokens, s));
+        if (res->token_offsets)
+            PK_CK(cudaMemcpyAsync(res->token_offsets, x->offsets.p, (size_t) (B + 1) * 8, cudaMemcpyDeviceToDevice, s));
+        if (res->steps) PK_CK(launch_extract_field(x->ust.as<int32_t>(), B, U_STEPS, res->steps, s));
+    } else {
+        PK_CK(x->compact.ensure((size_t) std::max<int64_t>(ntok, 1) * 4));
+        PK_CK(launch_gather(x->ust.as<int32_t>(), B, U_NTOK, x->tok.as<int32_t>(),
+                            x->tokregion.as<int64_t>(), x->offsets.as<int64_t>(), x->compact.as<int32_t>(), s));
+        if (ntok > 0) PK_CK(cudaMemcpyAsync(res->tokens, x->compact.p, (size_t) ntok * 4, cudaMemcpyDeviceToHost, s));
+        if (res->token_offsets)
+            PK_CK(cudaMemcpyAsync(res->token_offsets, x->offsets.p, (size_t) (B + 1) * 8, cudaMemcpyDeviceToHost, s));
+        if (res->steps)
+            for (int b = 0; b < B; ++b) res->steps[b] = r.ust[(size_t) b * kUst + U_STEPS];
+    }
+    if (res->eou_bounds && x->type == PK_MODEL_EOU) {
+        PK_CK(launch_scan(x->ust.as<int32_t>(), B, U_NBND, x->boffsets.as<int64_t>(), s));
+        int32_t * dst = res->eou_bounds;
+        if (!dev) {
+            PK_CK(x->bcompact.ensure((size_t) std::max<int64_t>(nbnd, 1) * 4));
+            dst = x->bcompact.as<int32_t>();
+        }
+        PK_CK(launch_gather(x->ust.as<int32_t>(), B, U_NBND, x->bnd.as<int32_t>(),
+                            x->bndregion.as<int64_t>(), x->boffsets.as<int64_t>(), dst, s));
+        if (!dev && nbnd > 0)
+            PK_CK(cudaMemcpyAsync(res->eou_bounds, dst, (size_t) nbnd * 4, cudaMemcpyDeviceToHost, s));
+        if (res->eou_offsets)
+            PK_CK(cudaMemcpyAsync(res->eou_offsets, x->boffsets.p, (size_t) (B + 1) * 8,
+                                  dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, s));
+    }
+    if (res->finish_ms && B > 0) {
+        std::vector<unsigned long long> fin((size_t) B);
+        unsigned long long t0 = 0;
+        PK_CK(cudaMemcpyAsync(fin.data(), x->finish.p, (size_t) B * 8, cudaMemcpyDeviceToHost, s));
+        PK_CK(cudaMemcpyAsync(&t0, x->tstart.p, 8, cudaMemcpyDeviceToHost, s));
+        PK_CK(cudaStreamSynchronize(s));
+        for (int b = 0; b < B; ++b)
+            res->finish_ms[b] = fin[(size_t) b] > t0 ? (float) ((double) (fin[(size_t) b] - t0) * 1e-6) : 0.0f;
+    }
+    PK_CK(cudaEventRecord(x->ev[5], s));
+    PK_CK(cudaStreamSynchronize(s));
+    float tot = 0.f;
+    PK_CK(cudaEventElapsedTime(&tot, x->ev[0], x->ev[5]));
+    res->total_ms = tot;
+    return PK_OK;
+}
+
+pk_status batch_run(pk_ctx * x, const pk_batch * b, const pk_trace * trace, pk_result * res) {
+    if (!x || !b || !res) return fail(PK_ERR_INVALID, "null argument");
+    if (b->d_enc != x->De)
+        return fail(PK_ERR_DMODEL, "encoder d_model mismatch (%d vs %d)", b->d_enc, x->De);
+    if (b->B < 0) return fail(PK_ERR_INVALID, "B < 0");
+    if (b->B > 0 && (!b->frame_offsets || !b->n_frames)) return fail(PK_ERR_INVALID, "null offsets");
+    PK_CK(cudaSetDevice(x->device));
+    Run r;
+    r.enc = b->enc;
+    r.enc_dev = b->enc_on_device != 0;
+    r.B = b->B;
+    r.frame_off = b->frame_offsets;
+    r.n_frames = b->n_frames;
+    r.msym = b->max_symbols_per_step > 0 ? b->max_symbols_per_step : x->max_sym;
+    r.trace = trace;
+    const size_t n = (size_t) std::max(b->B, 0);
+    r.t0.assign(n, 0); r.sym0.assign(n, 0); r.nbefore.assign(n, 0); r.segstart.assign(n, 0);
+    r.last.assign(n, -1); r.symx.assign(n, 0); r.fresh.assign(n, 0);
+    for (int i = 0; i < b->B; ++i)   // tdt_decode_window initialises only when n_frames > 0 (:879-883)
+        r.fresh[(size_t) i] = (x->type == PK_MODEL_EOU || b->n_frames[i] > 0) ? 1 : 0;
+    PK_TRY(run_loop(x, r));
+    return emit_results(x, r, res);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char * pk_last_error(void) { return g_err.c_str(); }
+int32_t pk_abi_version(void) { return PK_ABI_VERSION; }
+
+pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
+    if (!out) return fail(PK_ERR_INVALID, "null output pointer");
+    *out = nullptr;
+    PK_TRY(validate_desc(d));
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0)
+        return fail(PK_ERR_NO_DEVICE, "no CUDA device");
+    if (device < 0 || device >= ndev) return fail(PK_ERR_NO_DEVICE, "device %d of %d", device, ndev);
+    cudaDeviceProp prop;
+    PK_CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(PK_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only",
+                    device, prop.major, prop.minor);
+    if (!prop.cooperativeLaunch) return fail(PK_ERR_NO_DEVICE, "device lacks cooperative launch");
+    PK_CK(cudaSetDevice(device));
+    pk_ctx * x = new pk_ctx();
+    x->device = device;
+    x->sm_count = prop.multiProcessorCount;
+    x->type = d->model_type;
+    x->H = d->pred_hidden; x->J = d->joint_hidden; x->De = d->d_enc; x->L = d->n_layers;
+    x->V = d->vocab_size; x->V1 = d->vocab_size + 1;
+    x->Nd = x->type == PK_MODEL_TDT ? d->num_durations : 0;
+    x->Vo = x->V1 + x->Nd;
+    x->blank = d->blank_id;
+    x->max_sym = d->max_symbols_per_step > 0 ? d->max_symbols_per_step : (x->type == PK_MODEL_TDT ? 10 : 5);
+    if (x->type == PK_MODEL_EOU) {
+        x->eou = d->eou_id >= 0 ? d->eou_id : d->vocab_size - 2;
+        x->eob = d->eob_id >= 0 ? d->eob_id : d->vocab_size - 1;
+    }
+    auto cleanup = [&](pk_status s) { pk_destroy(x); return s; };
+    if (cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return cleanup(fail(PK_ERR_CUDA, "stream creation failed"));
+    for (auto & e : x->ev)
+        if (cudaEventCreate(&e) != cudaSuccess) return cleanup(fail(PK_ERR_CUDA, "event creation failed"));
+    DevBuf scratch;
+    pk_status st = PK_OK;
+    auto up = [&](const pk_tensor & t, int64_t keep, DevBuf & dst, const char * name) {
+        if (st == PK_OK) st = upload(x, t, keep, dst, scratch, name);
+    };
+    up(d->embed, x->V1, x->embed, "predict.embed.weight");
+    for (int l = 0; l < x->L; ++l) {
+        up(d->lstm[l].w_ih, 1 << 30, x->w_ih[l], "lstm.w_ih");
+        up(d->lstm[l].w_hh, 1 << 30, x->w_hh[l], "lstm.w_hh");
+        up(d->lstm[l].b_ih, 1, x->b_ih[l], "lstm.b_ih");
+        up(d->lstm[l].b_hh, 1, x->b_hh[l], "lstm.b_hh");
+    }
+    up(d->joint_enc_w, 1 << 30, x->enc_w, "joint.enc.weight");
+    up(d->joint_enc_b, 1, x->enc_b, "joint.enc.bias");
+    up(d->joint_pred_w, 1 << 30, x->pred_w, "joint.pred.weight");
+    up(d->joint_pred_b, 1, x->pred_b, "joint.pred.bias");
+    up(d->joint_out_w, x->Vo, x->out_w, "joint.out.weight");
+    scratch.release();
+    if (st != PK_OK) return cleanup(st);
+    {   // joint.out.bias: keep the first Vo entries
+        pk_tensor ob = d->joint_out_b;
+        if (ob.type != PK_GGML_F32 && ob.type != PK_GGML_F16)
+            return cleanup(fail(PK_ERR_MODEL, "joint.out.bias must be f32/f16"));
+        ob.ne0 = x->Vo;
+        ob.ne1 = 1;
+        DevBuf sc;
+        st = upload(x, ob, 1, x->out_b, sc, "joint.out.bias");
+        sc.release();
+        if (st != PK_OK) return cleanup(st);
+    }
+    std::vector<int32_t> durs(d->durations ? d->durations : nullptr,
+                              d->durations ? d->durations + x->Nd : nullptr);
+    if (durs.empty()) durs.push_back(0);
+    if (x->durations.ensure(durs.size() * 4) != cudaSuccess ||
+        cudaMemcpy(x->durations.p, durs.data(), durs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return cleanup(fail(PK_ERR_CUDA, "durations upload failed"));
+    std::vector<uint8_t> special;
+    if (x->type == PK_MODEL_EOU && d->special_piece && d->n_vocab_pieces > 0)
+        special.assign(d->special_piece, d->special_piece + d->n_vocab_pieces);
+    x->n_special = (int) special.size();
+    if (special.empty()) special.push_back(0);
+    if (x->special.ensure(special.size()) != cudaSuccess ||
+        cudaMemcpy(x->special.p, special.data(), special.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return cleanup(fail(PK_ERR_CUDA, "special-piece table upload failed"));
+
+    // Step-loop launch shape: one CTA per SM, activation chunks sized to shared memory.
+    x->grid = x->sm_count;
+    x->ldx = ((std::max(2 * x->H, x->J) + 3) / 4) * 4;
+    x->chunk = 32;
+    const size_t smem_cap = std::min<size_t>(prop.sharedMemPerBlockOptin, 200 * 1024);
+    while (x->chunk > 1 && step_loop_smem_bytes(x->chunk, x->ldx, x->H, x->grid) > smem_cap) x->chunk >>= 1;
+    x->smem = step_loop_smem_bytes(x->chunk, x->ldx, x->H, x->grid);
+    if (x->smem > smem_cap) return cleanup(fail(PK_ERR_MODEL, "hidden sizes too large for shared memory"));
+    if (step_loop_configure(x->smem) != cudaSuccess)
+        return cleanup(fail(PK_ERR_CUDA, "cannot configure %zu B of shared memory", x->smem));
+    int per_sm = 0;
+    if (step_loop_occupancy(x->smem, &per_sm) != cudaSuccess || per_sm < 1)
+        return cleanup(fail(PK_ERR_CUDA, "step loop does not fit one CTA per SM"));
+    *out = x;
+    return PK_OK;
+}
+
+void pk_destroy(pk_ctx * x) {
+    if (!x) return;
+    cudaSetDevice(x->device);
+    if (x->stream) cudaStreamSynchronize(x->stream);
+    for (DevBuf * b : x->all_bufs()) b->release();
+    for (auto & e : x->ev)
+        if (e) cudaEventDestroy(e);
+    if (x->stream) cudaStreamDestroy(x->stream);
+    delete x;
+}
+
+pk_status pk_get_info(const pk_ctx * x, pk_info * i) {
+    if (!x || !i) return fail(PK_ERR_INVALID, "null argument");
+    i->model_type = x->type; i->d_enc = x->De; i->pred_hidden = x->H; i->joint_hidden = x->J;
+    i->n_layers = x->L; i->vocab_size = x->V; i->blank_id = x->blank; i->num_durations = x->Nd;
+    i->v_plus_1 = x->V1; i->v_out = x->Vo; i->eou_id = x->eou; i->eob_id = x->eob;
+    i->max_symbols_per_step = x->max_sym; i->device = x->device; i->sm_count = x->sm_count;
+    i->grid_ctas = x->grid; i->weight_bytes_device = x->weight_bytes;
+    return PK_OK;
+}
+
+pk_status pk_set_option(pk_ctx * x, int32_t opt, int64_t v) {
+    if (!x) return fail(PK_ERR_INVALID, "null context");
+    switch (opt) {
+        case PK_OPT_TIMEOUT_US:
+            if (v <= 0) return fail(PK_ERR_INVALID, "timeout must be > 0");
+            x->timeout_ns = v * 1000;
+            return PK_OK;
+        case PK_OPT_MATH:
+            if (v != PK_MATH_F32) return fail(PK_ERR_INVALID, "unsupported math mode %lld", (long long) v);
+            x->math = (int) v;
+            return PK_OK;
+        case PK_OPT_MAX_SYMBOLS:
+            if (v <= 0) return fail(PK_ERR_INVALID, "max_symbols must be > 0");
+            x->max_sym = (int) v;
+            return PK_OK;
+        default:
+            return fail(PK_ERR_INVALID, "unknown option %d", opt);
+    }
+}
+
+int64_t pk_tokens_capacity(const int32_t * n_frames, int32_t B, int32_t msym) {
+    int64_t s = 0;
+    const int m = msym > 0 ? msym : 1;
+    for (int b = 0; n_frames && b < B; ++b) s += (int64_t) std::max(n_frames[b], 0) * m;
+    return s;
+}
+
+pk_status pk_decode_batch(pk_ctx * x, const pk_batch * b, pk_result * res) {
+    return batch_run(x, b, nullptr, res);
+}
+
+pk_status pk_decode_trace(pk_ctx * x, const pk_batch * b, pk_trace * t, pk_result * res) {
+    if (!t || t->max_steps < 0) return fail(PK_ERR_INVALID, "bad trace");
+    return batch_run(x, b, t, res);
+}
+
+pk_status pk_stream_create(pk_ctx * x, pk_stream ** out) {
+    if (!x || !out) return fail(PK_ERR_INVALID, "null argument");
+    *out = nullptr;
+    PK_CK(cudaSetDevice(x->device));
+    pk_stream * s = new pk_stream();
+    s->ctx = x;
+    const size_t n = (size_t) x->L * x->H * 4;
+    if (s->h.ensure(n) != cudaSuccess || s->c.ensure(n) != cudaSuccess ||
+        cudaMemset(s->h.p, 0, n) != cudaSuccess || cudaMemset(s->c.p, 0, n) != cudaSuccess) {
+        pk_stream_destroy(s);
+        return fail(PK_ERR_OOM, "stream state allocation failed");
+    }
+    *out = s;
+    return PK_OK;
+}
+
+void pk_stream_destroy(pk_stream * s) {
+    if (!s) return;
+    if (s->ctx) cudaSetDevice(s->ctx->device);
+    s->h.release();
+    s->c.release();
+    delete s;
+}
+
+namespace {
+pk_status stream_run(pk_stream * s, const float * enc, bool enc_dev, int n_frames, int msym,
+                     int n_before, bool force_init, Run & r) {
+    pk_ctx * x = s->ctx;
+    const bool fresh = force_init || !s->initialized;
+    if (fresh) { s->sym = 0; s->carry = 0; s->last = -1; s->segstart = 0; s->symx = 0; }
+    int t0 = 0;
+    if (x->type == PK_MODEL_TDT && s->carry > 0 && n_frames > 0) {   // :907-910
+        t0 = std::min(s->carry, n_frames);
+        s->carry -= t0;
+    }
+    static const int64_t zero_off = 0;
+    r.enc = enc; r.enc_dev = enc_dev; r.B = 1; r.frame_off = &zero_off;
+    r.n_frames = &n_frames;
+    r.msym = msym;
+    r.t0 = {t0}; r.sym0 = {x->type == PK_MODEL_TDT ? s->sym : 0}; r.nbefore = {n_before};
+    r.segstart = {s->segstart}; r.last = {s->last}; r.symx = {s->symx}; r.fresh = {fresh ? 1 : 0};
+    if (!fresh) { r.h_in = s->h.as<float>(); r.c_in = s->c.as<float>(); }
+    PK_TRY(run_loop(x, r));
+    const int32_t * u = r.ust.data();
+    const size_t LH = (size_t) x->L * x->H;
+    PK_CK(cudaMemcpyAsync(s->h.p, x->h.as<float>() + (size_t) u[U_HBUF] * LH, LH * 4,
+                          cudaMemcpyDeviceToDevice, x->stream));
+    PK_CK(cudaMemcpyAsync(s->c.p, x->c.p, LH * 4, cudaMemcpyDeviceToDevice, x->stream));
+    PK_CK(cudaStreamSynchronize(x->stream));
+    if (x->type == PK_MODEL_TDT) {
+        s->sym = u[U_SYM];
+        if (n_frames > 0) s->carry = std::max(0, u[U_T] - n_frames);   // :979
+    } else {
+        s->symx = u[U_SYMX];
+        s->sym = u[U_SYMX];
+        s->last = u[U_LAST];
+        s->segstart = u[U_SEGSTART];
+    }
+    s->initialized = 1;
+    return PK_OK;
+}
+}  // namespace
+
+pk_status pk_stream_reset(pk_stream * s) {
+    if (!s || !s->ctx) return fail(PK_ERR_INVALID, "null stream");
+    PK_CK(cudaSetDevice(s->ctx->device));
+    Run r;
+    return stream_run(s, nullptr, false, 0, s->ctx->max_sym, 0, true, r);
+}
+
+pk_status pk_stream_window(pk_stream * s, const float * enc, int32_t enc_on_device, int32_t n_frames,
+                           int32_t d_enc, int32_t msym_in, int32_t n_before, int32_t * tokens,
+                           int32_t tokens_cap, int32_t * n_tokens, int32_t * steps,
+                           int32_t * bounds, int32_t bounds_cap, int32_t * n_bounds) {
+    if (!s || !s->ctx) return fail(PK_ERR_INVALID, "null stream");
+    pk_ctx * x = s->ctx;
+    if (n_tokens) *n_tokens = 0;
+    if (steps) *steps = 0;
+    if (n_bounds) *n_bounds = 0;
+    if (d_enc != x->De)
+        return fail(PK_ERR_DMODEL, "encoder d_model mismatch (%d vs %d)", d_enc, x->De);
+    if (x->type == PK_MODEL_TDT && n_frames <= 0) return PK_OK;      // :879
+    if (n_frames < 0) n_frames = 0;
+    if (n_frames > 0 && !enc) return fail(PK_ERR_INVALID, "null encoder output");
+    PK_CK(cudaSetDevice(x->device));
+    const int msym = msym_in > 0 ? msym_in : x->max_sym;
+    Run r;
+    PK_TRY(stream_run(s, enc, enc_on_device != 0, n_frames, msym, n_before, false, r));
+    const int32_t * u = r.ust.data();
+    const int nt = u[U_NTOK], nb = u[U_NBND];
+    if (nt > tokens_cap || (nt > 0 && !tokens))
+        return fail(PK_ERR_CAPACITY, "token buffer holds %d, %d needed", tokens_cap, nt);
+    if (nt > 0) PK_CK(cudaMemcpy(tokens, x->tok.p, (size_t) nt * 4, cudaMemcpyDeviceToHost));
+    if (bounds && nb > 0) {
+        if (nb > bounds_cap) return fail(PK_ERR_CAPACITY, "boundary buffer holds %d, %d needed", bounds_cap, nb);
+        PK_CK(cudaMemcpy(bounds, x->bnd.p, (size_t) nb * 4, cudaMemcpyDeviceToHost));
+    }
+    if (n_tokens) *n_tokens = nt;
+    if (steps) *steps = u[U_STEPS];
+    if (n_bounds) *n_bounds = nb;
+    return PK_OK;
+}
+
+pk_status pk_stream_get_state(const pk_stream * s, pk_stream_state * st) {
+    if (!s || !s->ctx || !st) return fail(PK_ERR_INVALID, "null argument");
+    pk_ctx * x = s->ctx;
+    PK_CK(cudaSetDevice(x->device));
+    const size_t LH = (size_t) x->L * x->H;
+    std::vector<float> h(LH), c(LH);
+    PK_CK(cudaMemcpy(h.data(), s->h.p, LH * 4, cudaMemcpyDeviceToHost));
+    PK_CK(cudaMemcpy(c.data(), s->c.p, LH * 4, cudaMemcpyDeviceToHost));
+    if (st->h) std::memcpy(st->h, h.data(), LH * 4);
+    if (st->c) std::memcpy(st->c, c.data(), LH * 4);
+    if (st->pred_out) std::memcpy(st->pred_out, h.data() + (size_t) (x->L - 1) * x->H, (size_t) x->H * 4);
+    st->symbols_this_step = s->sym;
+    st->carry_frames = s->carry;
+    st->initialized = s->initialized;
+    st->last_token = s->last;
+    st->segment_start_token = s->segstart;
+    return PK_OK;
+}
+
+pk_status pk_stream_set_state(pk_stream * s, const pk_stream_state * st) {
+    if (!s || !s->ctx || !st || !st->h || !st->c) return fail(PK_ERR_INVALID, "null argument");
+    pk_ctx * x = s->ctx;
+    PK_CK(cudaSetDevice(x->device));
+    const size_t LH = (size_t) x->L * x->H;
+    PK_CK(cudaMemcpy(s->h.p, st->h, LH * 4, cudaMemcpyHostToDevice));
+    PK_CK(cudaMemcpy(s->c.p, st->c, LH * 4, cudaMemcpyHostToDevice));
+    s->sym = st->symbols_this_step;
+    s->symx = st->symbols_this_step;
+    s->carry = st->carry_frames;
+    s->initialized = st->initialized;
+    s->last = st->last_token;
+    s->segstart = st->segment_start_token;
+    return PK_OK;
+}
+
+pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_shards, int32_t * shard_of) {
+    if (B < 0 || n_shards <= 0 || (B > 0 && (!n_frames || !shard_of)))
+        return fail(PK_ERR_INVALID, "bad sharding arguments");
+    std::vector<int> idx((size_t) B);
+    std::iota(idx.begin(), idx.end(), 0);
+    std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return n_frames[a] > n_frames[b]; });
+    std::vector<int64_t> load((size_t) n_shards, 0);
+    for (int i : idx) {
+        int best = 0;
+        for (int k = 1; k < n_shards; ++k)
+            if (load[(size_t) k] < load[(size_t) best]) best = k;
+        shard_of[i] = best;
+        load[(size_t) best] += std::max(n_frames[i], 0);
+    }
+    return PK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,117 @@
+// pk_internal.h -- host/device declarations shared by libparakeet_cuda's
+// translation units (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "parakeet_cuda.h"
+
+namespace pk {
+
+constexpr int kMaxLayers = 4;
+constexpr int kThreads = 256;      // step-loop CTA size (8 warps)
+constexpr int kWarps = kThreads / 32;
+
+// Per-utterance integer state, [B][kUst] in device memory.
+enum UstField : int {
+    U_T = 0,          // current frame index t (frame pointer)
+    U_SYM,            // symbols_this_step (working value)
+    U_NTOK,           // tokens emitted in this call
+    U_STEPS,          // joint evaluations in this call (out_steps)
+    U_HBUF,           // which of the two h buffers holds the current state
+    U_LAST,           // EOU last_token
+    U_SEGSTART,       // EOU segment_start_token (in the caller's running count)
+    U_NBND,           // EOU boundaries recorded in this call
+    U_NBEFORE,        // caller's running token count on entry (EOU boundary base)
+    U_NFRAMES,        // window length T
+    U_SYMX,           // EOU symbols_this_step as left by the last finished frame
+    kUst = 16
+};
+
+// Control words, int32 [kCtl] in device memory.
+enum CtlField : int {
+    C_ERR = 0,        // pk_status set by the device (timeout / index check)
+    C_SEL,            // which live list is current
+    C_NLIVE0,         // live count of list 0
+    C_NLIVE1,         // live count of list 1
+    C_NEMIT,          // entries in the emit list
+    C_NDECIDED,       // utterances decided by the last leader (trace bookkeeping)
+    C_ITERS,          // batched loop iterations completed
+    C_ERRINFO,        // first failing utterance / index (diagnostics)
+    kCtl = 16
+};
+
+// Everything the persistent step-loop kernel needs (passed by value).
+struct LoopParams {
+    // geometry
+    int H, J, L, V1, Vo, Nd, blank, eou, eob, is_tdt, max_sym, B, n_special;
+    int chunk;                 // max utterances per shared-memory chunk (power of two, <= 32)
+    int ldx;                   // floats per chunk row in shared memory (>= max(2H, J))
+    long long timeout_ns;      // bound on every grid-barrier wait
+    // weights (f32, row-major [out][in])
+    const float * embed;
+    const float * w_ih[kMaxLayers];
+    const float * w_hh[kMaxLayers];
+    const float * b_ih[kMaxLayers];
+    const float * b_hh[kMaxLayers];
+    const float * pred_w;
+    const float * pred_b;
+    const float * out_w;
+    const float * out_b;
+    const int32_t * durations;
+    const uint8_t * special;
+    // inputs
+    const float * encp;        // [frames][J] enc-proj incl. bias
+    const int64_t * frame_off; // [B]
+    // state
+    float * h;                 // [2][L][B][H]
+    float * c;                 // [L][B][H]
+    float * predp;             // [B][J]
+    float * hid;               // [B][J]
+    int32_t * ust;             // [B][kUst]
+    unsigned long long * keys; // [B][2] packed argmax keys (token, duration)
+    int32_t * live;            // [2][B]
+    int32_t * emit;            // [B][2]: utterance, token | reset << 31
+    int32_t * ctl;             // [kCtl]
+    unsigned int * bar;        // [2]: arrival count, generation
+    unsigned long long * t_start;   // [1] globaltimer at loop start
+    unsigned long long * finish_ns; // [B]
+    // outputs
+    int32_t * tok_out;         // per-utterance regions
+    const int64_t * tok_region;// [B] region start
+    int32_t * bnd_out;         // EOU boundaries, per-utterance regions (cap T)
+    const int64_t * bnd_region;
+    // teacher-forced trace (trace_steps == 0: off)
+    int trace_steps;
+    const int32_t * forced_tok;
+    const int32_t * forced_dur;
+    float * tr_logits;         // [B][S][Vo]
+    float * tr_h;              // [B][S][L][H]
+    float * tr_c;
+    int32_t * tr_tok;
+    int32_t * tr_dur;
+};
+
+// Launch wrappers (defined in the .cu files).
+cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s);
+size_t      step_loop_smem_bytes(int chunk, int ldx, int H, int grid);
+cudaError_t step_loop_configure(size_t smem);
+cudaError_t step_loop_occupancy(size_t smem, int * blocks_per_sm);
+
+cudaError_t launch_encproj_f32(const float * enc, int64_t frames, int De, const float * w,
+                               const float * b, int J, float * out, cudaStream_t s);
+
+cudaError_t launch_dequant(const void * src, int type, int64_t ne0, int64_t rows,
+                           float * dst, cudaStream_t s);
+
+// offsets[b+1] = offsets[b] + ust[b][field].
+cudaError_t launch_scan(const int32_t * ust, int B, int field, int64_t * offsets, cudaStream_t s);
+// Copy each utterance's region src[region[b] ...] to dst[offsets[b] ...].
+cudaError_t launch_gather(const int32_t * ust, int B, int field, const int32_t * src,
+                          const int64_t * region, const int64_t * offsets, int32_t * dst,
+                          cudaStream_t s);
+cudaError_t launch_extract_field(const int32_t * ust, int B, int field, int32_t * dst,
+                                 cudaStream_t s);
+
+}  // namespace pk

@@ -1,0 +1,705 @@
+// pk_loop.cu -- the persistent greedy-decode step loop (sm_100a).
+//
+// One cooperative launch (one CTA per SM) runs every step of every utterance
+// of a batch. Per batched step:
+//
+//   [L0 .. L_{L-1}]  LSTM layers for the utterances that emitted (emit list);
+//                    CTA k owns hidden units [k*upc, (k+1)*upc) and their four
+//                    gate rows (host_lstm_step, src/parakeet_tdt.cpp:106-142)
+//   [P]              pred-proj for those utterances, then the joint hidden
+//                    hid = relu(enc_proj[t] + pred_proj) for every live one
+//                    (host_joint_step, src/parakeet_tdt.cpp:154-177, first half)
+//   [J]              joint output rows split over CTAs; per-CTA argmax merged
+//                    with 64-bit atomicMax keys (argmax_f32 :25-32: first index
+//                    of the maximum wins)
+//   leader           the last CTA to reach the barrier applies the greedy
+//                    control of tdt_decode_window (:919-969) / eou_decode_window
+//                    (parakeet_eou.cpp:267-334) to every live utterance, writes
+//                    tokens, and compacts the live and emit lists
+//
+// Phases are separated by grid barriers whose waits are bounded by a
+// globaltimer deadline; a wait that runs out records PK_ERR_TIMEOUT and the
+// kernel returns. Cross-CTA data is read with ld.global.cg (L2) after the
+// barrier's acquire.
+//
+// Math here is f32 on CUDA cores with exactly dequantized weights (the
+// reference-faithful mode): only the summation order differs from the CPU.
+
+#include "pk_internal.h"
+
+#include <math.h>
+
+namespace pk {
+namespace {
+
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned * p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release(unsigned * p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned * p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Order-preserving 64-bit argmax key: larger value wins, then the smaller index
+// (the reference's strict '>' keeps the first maximum). -0 is folded onto +0
+// because the reference compares them equal.
+__device__ __forceinline__ unsigned long long make_key(float v, int idx) {
+    unsigned u = __float_as_uint(v);
+    if (u == 0x80000000u) u = 0u;
+    const unsigned ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long) ord << 32) | (unsigned long long) (0xFFFFFFFFu - (unsigned) idx);
+}
+__device__ __forceinline__ int key_index(unsigned long long k) {
+    return (int) (0xFFFFFFFFu - (unsigned) (k & 0xFFFFFFFFull));
+}
+
+__device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// Shared-memory carve-up of the dynamic buffer.
+struct Smem {
+    float * xs;                     // [chunk][ldx] activations of one utterance chunk
+    float * gates;                  // [chunk][upc][4]
+    unsigned long long * wbest;     // [kWarps][32][2]
+    int * s_utt;                    // [32]
+    int * s_aux;                    // [32] token / step
+    int * s_aux2;                   // [32] reset / h-buffer
+    int * s_scan;                   // [kWarps + 2]
+    int * s_flag;                   // [4]
+};
+
+__device__ __forceinline__ Smem carve(unsigned char * raw, const LoopParams & P, int upc) {
+    Smem s;
+    size_t off = 0;
+    s.xs = reinterpret_cast<float *>(raw + off);
+    off += (size_t) P.chunk * P.ldx * sizeof(float);
+    s.gates = reinterpret_cast<float *>(raw + off);
+    off += (size_t) P.chunk * upc * 4 * sizeof(float);
+    off = (off + 15) & ~(size_t) 15;
+    s.wbest = reinterpret_cast<unsigned long long *>(raw + off);
+    off += (size_t) kWarps * 32 * 2 * sizeof(unsigned long long);
+    s.s_utt = reinterpret_cast<int *>(raw + off); off += 32 * sizeof(int);
+    s.s_aux = reinterpret_cast<int *>(raw + off); off += 32 * sizeof(int);
+    s.s_aux2 = reinterpret_cast<int *>(raw + off); off += 32 * sizeof(int);
+    s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * sizeof(int);
+    s.s_flag = reinterpret_cast<int *>(raw + off);
+    return s;
+}
+
+// ---- warp dot products over a chunk of CP utterances -----------------------
+//
+// Lanes split K in float4 slices (k = 4*lane + 128*i); each lane keeps CP
+// partial sums, then a butterfly exchange leaves the full sum for utterance
+// c = lane >> (5 - log2 CP) in that lane (31 shuffles for CP = 32).
+template <int CP>
+__device__ __forceinline__ float transpose_reduce(float (&acc)[CP], int lane) {
+#pragma unroll
+    for (int lev = 0; lev < 5; ++lev) {
+        const int o = 16 >> lev;
+        const int n = (CP >> lev) > 0 ? (CP >> lev) : 1;
+        if (n > 1) {
+            const int half = n >> 1;
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < half; ++i) {
+                const float send = up ? acc[i] : acc[i + half];
+                const float keep = up ? acc[i + half] : acc[i];
+                acc[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+            }
+        } else {
+            acc[0] += __shfl_xor_sync(0xFFFFFFFFu, acc[0], o);
+        }
+    }
+    return acc[0];
+}
+
+template <int CP> struct Lg2 {
+    static constexpr int v = CP >= 32 ? 5 : CP >= 16 ? 4 : CP >= 8 ? 3 : CP >= 4 ? 2 : CP >= 2 ? 1 : 0;
+};
+
+template <int CP>
+__device__ __forceinline__ float warp_dot(const float * __restrict__ w, const float * xs, int ldx,
+                                          int K, int lane) {
+    float acc[CP];
+#pragma unroll
+    for (int c = 0; c < CP; ++c) acc[c] = 0.0f;
+    for (int k = 4 * lane; k < K; k += 128) {
+        const float4 wv = __ldg(reinterpret_cast<const float4 *>(w + k));
+#pragma unroll
+        for (int c = 0; c < CP; ++c) {
+            const float4 xv = *reinterpret_cast<const float4 *>(xs + c * ldx + k);
+            float a = acc[c];
+            a = fmaf(wv.x, xv.x, a);
+            a = fmaf(wv.y, xv.y, a);
+            a = fmaf(wv.z, xv.z, a);
+            a = fmaf(wv.w, xv.w, a);
+            acc[c] = a;
+        }
+    }
+    return transpose_reduce<CP>(acc, lane);
+}
+
+template <int CP> __device__ __forceinline__ int owner_shift() { return 5 - Lg2<CP>::v; }
+
+__device__ __forceinline__ int pow2ceil(int n) {
+    int p = 1;
+    while (p < n) p <<= 1;
+    return p;
+}
+
+__device__ __forceinline__ int lg2_pow2(int p) { return 31 - __clz(p); }
+
+// ---- grid barrier -------------------------------------------------------------
+
+__device__ __forceinline__ bool grid_arrive(const LoopParams & P, const Smem & S) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned old = atom_add_acq_rel(&P.bar[0], 1u);
+        S.s_flag[0] = (old == gridDim.x - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    return S.s_flag[0] != 0;
+}
+
+__device__ __forceinline__ void grid_release(const LoopParams & P, unsigned gen) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        atomicExch(&P.bar[0], 0u);
+        __threadfence();
+        st_release(&P.bar[1], gen + 1u);
+    }
+    __syncthreads();
+}
+
+// Returns false if the wait ran out or an error was flagged.
+__device__ __forceinline__ bool grid_wait(const LoopParams & P, unsigned gen, const Smem & S) {
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const unsigned long long t0 = gtimer();
+        unsigned it = 0;
+        while (ld_acquire(&P.bar[1]) == gen) {
+            if ((++it & 63u) == 0u) {
+                if (__ldcg(&P.ctl[C_ERR]) != 0) { ok = 0; break; }
+                if ((long long) (gtimer() - t0) > P.timeout_ns) {
+                    atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        S.s_flag[1] = ok;
+    }
+    __syncthreads();
+    return S.s_flag[1] != 0;
+}
+
+__device__ __forceinline__ bool grid_barrier(const LoopParams & P, unsigned & gen, const Smem & S) {
+    if (grid_arrive(P, S)) {
+        grid_release(P, gen);
+    } else if (!grid_wait(P, gen, S)) {
+        return false;
+    }
+    ++gen;
+    return __ldcg(&P.ctl[C_ERR]) == 0;
+}
+
+// Block-wide exclusive scan of one int per thread.
+__device__ __forceinline__ int block_excl_scan(int v, const Smem & S, int & total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) S.s_scan[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = lane < kWarps ? S.s_scan[lane] : 0;
+        int y = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int z = __shfl_up_sync(0xFFFFFFFFu, y, o);
+            if (lane >= o) y += z;
+        }
+        if (lane < kWarps) S.s_scan[lane] = y - w;
+        if (lane == kWarps - 1) S.s_scan[kWarps] = y;
+    }
+    __syncthreads();
+    total = S.s_scan[kWarps];
+    const int r = x - v + S.s_scan[warp];
+    __syncthreads();
+    return r;
+}
+
+// ---- LSTM layer phase ----------------------------------------------------------
+
+template <int CP>
+__device__ void lstm_rows(const LoopParams & P, int l, int u0, int nu, int upc, int nc,
+                          const Smem & S) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int H = P.H;
+    const int sh = owner_shift<CP>();
+    const int c = lane >> sh;
+    const bool owner = (lane & ((1 << sh) - 1)) == 0;
+    for (int r = warp; r < 4 * nu; r += kWarps) {
+        const int jj = r >> 2, q = r & 3;
+        const int gr = q * H + u0 + jj;
+        const float dih = warp_dot<CP>(P.w_ih[l] + (size_t) gr * H, S.xs, P.ldx, H, lane);
+        const float dhh = warp_dot<CP>(P.w_hh[l] + (size_t) gr * H, S.xs + H, P.ldx, H, lane);
+        if (owner && c < nc) {
+            // g = W_ih x + b_ih; g += b_hh; g += W_hh h  (parakeet_tdt.cpp:123-125)
+            const float g = ((__ldg(P.b_ih[l] + gr) + dih) + __ldg(P.b_hh[l] + gr)) + dhh;
+            S.gates[(c * upc + jj) * 4 + q] = g;
+        }
+    }
+}
+
+__device__ void phase_lstm(const LoopParams & P, int l, int n_emit, const Smem & S) {
+    const int H = P.H, L = P.L, B = P.B;
+    const int upc = (H + (int) gridDim.x - 1) / (int) gridDim.x;
+    const int u0 = (int) blockIdx.x * upc;
+    const int nu = max(0, min(H, u0 + upc) - u0);
+    if (nu == 0) return;
+    const int K2 = 2 * H;
+    for (int cs = 0; cs < n_emit; cs += P.chunk) {
+        const int nc = min(P.chunk, n_emit - cs);
+        const int cp = pow2ceil(nc);
+        if (threadIdx.x < nc) {
+            const int utt = __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
+            const int tr = __ldcg(&P.emit[2 * (cs + threadIdx.x) + 1]);
+            S.s_utt[threadIdx.x] = utt;
+            S.s_aux[threadIdx.x] = tr & 0x7FFFFFFF;                              // token
+            S.s_aux2[threadIdx.x] = ((tr >> 31) & 1) | (__ldcg(&P.ust[utt * kUst + U_HBUF]) << 1);
+        }
+        __syncthreads();
+        const int k4n = K2 / 4;
+        for (int idx = threadIdx.x; idx < cp * k4n; idx += blockDim.x) {
+            const int cc = idx / k4n;
+            const int k = 4 * (idx - cc * k4n);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (cc < nc) {
+                const int utt = S.s_utt[cc];
+                const int reset = S.s_aux2[cc] & 1, hb = S.s_aux2[cc] >> 1;
+                if (k < H) {
+                    if (l == 0)
+                        v = __ldg(reinterpret_cast<const float4 *>(P.embed + (size_t) S.s_aux[cc] * H + k));
+                    else
+                        v = __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) hb * L + (l - 1)) * B + utt) * H + k));
+                } else if (!reset) {
+                    v = __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) (hb ^ 1) * L + l) * B + utt) * H + (k - H)));
+                }
+            }
+            *reinterpret_cast<float4 *>(S.xs + cc * P.ldx + k) = v;
+        }
+        __syncthreads();
+        switch (cp) {
+            case 1: lstm_rows<1>(P, l, u0, nu, upc, nc, S); break;
+            case 2: lstm_rows<2>(P, l, u0, nu, upc, nc, S); break;
+            case 4: lstm_rows<4>(P, l, u0, nu, upc, nc, S); break;
+            case 8: lstm_rows<8>(P, l, u0, nu, upc, nc, S); break;
+            case 16: lstm_rows<16>(P, l, u0, nu, upc, nc, S); break;
+            default: lstm_rows<32>(P, l, u0, nu, upc, nc, S); break;
+        }
+        __syncthreads();
+        // cell update, parakeet_tdt.cpp:128-136
+        for (int idx = threadIdx.x; idx < nc * nu; idx += blockDim.x) {
+            const int cc = idx / nu, jj = idx - (idx / nu) * nu;
+            const int j = u0 + jj;
+            const int utt = S.s_utt[cc];
+            const int reset = S.s_aux2[cc] & 1, hb = S.s_aux2[cc] >> 1;
+            const float * g = S.gates + (cc * upc + jj) * 4;
+            const float i_g = sigmoid_ref(g[0]);
+            const float f_g = sigmoid_ref(g[1]);
+            const float g_g = tanhf(g[2]);
+            const float o_g = sigmoid_ref(g[3]);
+            float * cptr = P.c + ((size_t) l * B + utt) * H + j;
+            const float c_old = reset ? 0.0f : __ldcg(cptr);
+            const float c_new = f_g * c_old + i_g * g_g;
+            *cptr = c_new;
+            P.h[(((size_t) hb * L + l) * B + utt) * H + j] = o_g * tanhf(c_new);
+        }
+        __syncthreads();
+    }
+}
+
+// ---- pred-proj + joint hidden phase --------------------------------------------
+
+template <int CP>
+__device__ void pred_rows(const LoopParams & P, int j0, int nr, int nc, const Smem & S) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int sh = owner_shift<CP>();
+    const int c = lane >> sh;
+    const bool owner = (lane & ((1 << sh) - 1)) == 0;
+    for (int r = warp; r < nr; r += kWarps) {
+        const int j = j0 + r;
+        const float d = warp_dot<CP>(P.pred_w + (size_t) j * P.H, S.xs, P.ldx, P.H, lane);
+        if (owner && c < nc) P.predp[(size_t) S.s_utt[c] * P.J + j] = __ldg(P.pred_b + j) + d;
+    }
+}
+
+__device__ void phase_pred(const LoopParams & P, bool first, int n_emit, int sel, int n_live,
+                           const Smem & S) {
+    const int H = P.H, J = P.J, L = P.L, B = P.B;
+    const int rpc = (J + (int) gridDim.x - 1) / (int) gridDim.x;
+    const int j0 = (int) blockIdx.x * rpc;
+    const int nr = max(0, min(J, j0 + rpc) - j0);
+    const int * live = P.live + (size_t) sel * B;
+    const int n_list = first ? n_live : n_emit;
+    if (nr > 0) {
+        for (int cs = 0; cs < n_list; cs += P.chunk) {
+            const int nc = min(P.chunk, n_list - cs);
+            const int cp = pow2ceil(nc);
+            if (threadIdx.x < nc) {
+                const int utt = first ? __ldcg(&live[cs + threadIdx.x])
+                                      : __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
+                S.s_utt[threadIdx.x] = utt;
+                S.s_aux2[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+            }
+            __syncthreads();
+            const int k4n = H / 4;
+            for (int idx = threadIdx.x; idx < cp * k4n; idx += blockDim.x) {
+                const int cc = idx / k4n;
+                const int k = 4 * (idx - cc * k4n);
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (cc < nc)
+                    v = __ldcg(reinterpret_cast<const float4 *>(
+                        P.h + (((size_t) S.s_aux2[cc] * L + (L - 1)) * B + S.s_utt[cc]) * H + k));
+                *reinterpret_cast<float4 *>(S.xs + cc * P.ldx + k) = v;
+            }
+            __syncthreads();
+            switch (cp) {
+                case 1: pred_rows<1>(P, j0, nr, nc, S); break;
+                case 2: pred_rows<2>(P, j0, nr, nc, S); break;
+                case 4: pred_rows<4>(P, j0, nr, nc, S); break;
+                case 8: pred_rows<8>(P, j0, nr, nc, S); break;
+                case 16: pred_rows<16>(P, j0, nr, nc, S); break;
+                default: pred_rows<32>(P, j0, nr, nc, S); break;
+            }
+            __syncthreads();
+        }
+        // hidden = relu((b_enc + W_enc enc_t) + (b_pred + W_pred pred)), :168-171
+        for (int idx = threadIdx.x; idx < n_live * nr; idx += blockDim.x) {
+            const int i = idx / nr, jj = idx - (idx / nr) * nr;
+            const int utt = __ldcg(&live[i]);
+            const int j = j0 + jj;
+            const int t = __ldcg(&P.ust[utt * kUst + U_T]);
+            const float v = __ldcg(P.encp + ((size_t) __ldg(P.frame_off + utt) + t) * J + j)
+                          + __ldcg(P.predp + (size_t) utt * J + j);
+            P.hid[(size_t) utt * J + j] = (0.0f < v) ? v : 0.0f;
+        }
+    }
+    // Trace: state after the step just decided, for every utterance decided by
+    // the last leader (the previous live list).
+    if (P.trace_steps > 0 && !first && blockIdx.x == 0) {
+        const int n_dec = __ldcg(&P.ctl[C_NDECIDED]);
+        const int * prev = P.live + (size_t) (sel ^ 1) * B;
+        const int LH = L * H;
+        for (int i = 0; i < n_dec; ++i) {
+            const int utt = __ldcg(&prev[i]);
+            const int step = __ldcg(&P.ust[utt * kUst + U_STEPS]) - 1;
+            if (step < 0 || step >= P.trace_steps) continue;
+            const int hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+            for (int k = threadIdx.x; k < LH; k += blockDim.x) {
+                const int l = k / H, j = k - (k / H) * H;
+                const size_t dst = ((size_t) utt * P.trace_steps + step) * LH + k;
+                if (P.tr_h) P.tr_h[dst] = __ldcg(P.h + (((size_t) hb * L + l) * B + utt) * H + j);
+                if (P.tr_c) P.tr_c[dst] = __ldcg(P.c + ((size_t) l * B + utt) * H + j);
+            }
+        }
+    }
+}
+
+// ---- joint output + partial argmax phase ---------------------------------------
+
+template <int CP>
+__device__ void joint_rows(const LoopParams & P, int r0, int nr, int nc, const Smem & S,
+                           unsigned long long & bt, unsigned long long & bd) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int sh = owner_shift<CP>();
+    const int c = lane >> sh;
+    const bool owner = (lane & ((1 << sh) - 1)) == 0;
+    for (int rr = warp; rr < nr; rr += kWarps) {
+        const int r = r0 + rr;
+        const float d = warp_dot<CP>(P.out_w + (size_t) r * P.J, S.xs, P.ldx, P.J, lane);
+        if (owner && c < nc) {
+            const float logit = __ldg(P.out_b + r) + d;
+            if (P.trace_steps > 0) {
+                const int step = S.s_aux[c];
+                if (step < P.trace_steps)
+                    P.tr_logits[((size_t) S.s_utt[c] * P.trace_steps + step) * P.Vo + r] = logit;
+            }
+            if (r < P.V1) {
+                const unsigned long long k = make_key(logit, r);
+                bt = k > bt ? k : bt;
+            } else {
+                const unsigned long long k = make_key(logit, r - P.V1);
+                bd = k > bd ? k : bd;
+            }
+        }
+    }
+}
+
+__device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Smem & S) {
+    const int J = P.J, B = P.B;
+    const int rpc = (P.Vo + (int) gridDim.x - 1) / (int) gridDim.x;
+    const int r0 = (int) blockIdx.x * rpc;
+    const int nr = max(0, min(P.Vo, r0 + rpc) - r0);
+    if (nr == 0) return;
+    const int * live = P.live + (size_t) sel * B;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int cs = 0; cs < n_live; cs += P.chunk) {
+        const int nc = min(P.chunk, n_live - cs);
+        const int cp = pow2ceil(nc);
+        if (threadIdx.x < nc) {
+            const int utt = __ldcg(&live[cs + threadIdx.x]);
+            S.s_utt[threadIdx.x] = utt;
+            S.s_aux[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
+        }
+        __syncthreads();
+        const int k4n = J / 4;
+        for (int idx = threadIdx.x; idx < cp * k4n; idx += blockDim.x) {
+            const int cc = idx / k4n;
+            const int k = 4 * (idx - cc * k4n);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (cc < nc)
+                v = __ldcg(reinterpret_cast<const float4 *>(P.hid + (size_t) S.s_utt[cc] * J + k));
+            *reinterpret_cast<float4 *>(S.xs + cc * P.ldx + k) = v;
+        }
+        __syncthreads();
+        unsigned long long bt = 0ull, bd = 0ull;
+        switch (cp) {
+            case 1: joint_rows<1>(P, r0, nr, nc, S, bt, bd); break;
+            case 2: joint_rows<2>(P, r0, nr, nc, S, bt, bd); break;
+            case 4: joint_rows<4>(P, r0, nr, nc, S, bt, bd); break;
+            case 8: joint_rows<8>(P, r0, nr, nc, S, bt, bd); break;
+            case 16: joint_rows<16>(P, r0, nr, nc, S, bt, bd); break;
+            default: joint_rows<32>(P, r0, nr, nc, S, bt, bd); break;
+        }
+        // lanes that own utterance c hold the warp's best keys; gather per warp
+        const int sh = 5 - lg2_pow2(cp);
+        if ((lane & ((1 << sh) - 1)) == 0) {
+            const int c = lane >> sh;
+            S.wbest[(warp * 32 + c) * 2 + 0] = bt;
+            S.wbest[(warp * 32 + c) * 2 + 1] = bd;
+        }
+        __syncthreads();
+        if (threadIdx.x < nc) {
+            unsigned long long kt = 0ull, kd = 0ull;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const unsigned long long a = S.wbest[(w * 32 + threadIdx.x) * 2 + 0];
+                const unsigned long long b = S.wbest[(w * 32 + threadIdx.x) * 2 + 1];
+                kt = a > kt ? a : kt;
+                kd = b > kd ? b : kd;
+            }
+            const int utt = S.s_utt[threadIdx.x];
+            if (kt) atomicMax(&P.keys[2 * utt + 0], kt);
+            if (kd) atomicMax(&P.keys[2 * utt + 1], kd);
+        }
+        __syncthreads();
+    }
+}
+
+// ---- leader: greedy control for every live utterance -------------------------
+
+__device__ void leader_decide(const LoopParams & P, const Smem & S) {
+    const int B = P.B;
+    const int sel = __ldcg(&P.ctl[C_SEL]);
+    const int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
+    const int * live_in = P.live + (size_t) sel * B;
+    int * live_out = P.live + (size_t) (sel ^ 1) * B;
+    int base_emit = 0, base_live = 0;
+    const int msym = P.max_sym;
+    for (int r0 = 0; r0 < n_live; r0 += blockDim.x) {
+        const int i = r0 + threadIdx.x;
+        int e = 0, lv = 0, utt = -1, etok = 0, ereset = 0;
+        if (i < n_live) {
+            utt = __ldcg(&live_in[i]);
+            int * u = P.ust + utt * kUst;
+            const unsigned long long kt = atomicExch(&P.keys[2 * utt + 0], 0ull);
+            const unsigned long long kd = P.is_tdt ? atomicExch(&P.keys[2 * utt + 1], 0ull) : 0ull;
+            int tok = key_index(kt);
+            int di = P.is_tdt ? key_index(kd) : 0;
+            if (kt == 0ull || tok < 0 || tok >= P.V1 || (P.is_tdt && (kd == 0ull || di < 0 || di >= P.Nd))) {
+                atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+                P.ctl[C_ERRINFO] = utt;
+                tok = P.blank;
+                di = 0;
+            }
+            const int step = __ldcg(&u[U_STEPS]);
+            if (P.trace_steps > 0 && step < P.trace_steps) {
+                const size_t ti = (size_t) utt * P.trace_steps + step;
+                if (P.tr_tok) P.tr_tok[ti] = tok;
+                if (P.tr_dur) P.tr_dur[ti] = di;
+                if (P.forced_tok) {
+                    const int ft = __ldg(P.forced_tok + ti);
+                    if (ft >= 0 && ft < P.V1) {
+                        tok = ft;
+                        const int fd = P.forced_dur ? __ldg(P.forced_dur + ti) : 0;
+                        di = (P.is_tdt && fd >= 0 && fd < P.Nd) ? fd : 0;
+                    }
+                }
+            }
+            u[U_STEPS] = step + 1;
+            int t = __ldcg(&u[U_T]);
+            int sym = __ldcg(&u[U_SYM]);
+            int ntok = __ldcg(&u[U_NTOK]);
+            const int T = __ldcg(&u[U_NFRAMES]);
+            bool emit_tok = false;
+            if (P.is_tdt) {
+                // parakeet_tdt.cpp:938-968
+                const int dur = P.Nd > 0 ? __ldg(P.durations + di) : di;
+                const int adv = dur > 1 ? dur : 1;
+                if (tok == P.blank) {
+                    t += adv;
+                    sym = 0;
+                } else {
+                    emit_tok = true;
+                    e = 1; etok = tok;
+                    ++sym;
+                    if (dur > 0 || sym >= msym) { t += adv; sym = 0; }
+                }
+            } else {
+                // parakeet_eou.cpp:271-333. The frame loop resets symbols_this_step
+                // at each frame start; U_SYMX keeps the value a frame ended with
+                // (what the reference's state holds after the window).
+                if (tok == P.blank || tok == P.eob) {
+                    u[U_SYMX] = sym;
+                    t += 1; sym = 0;
+                } else if (tok == P.eou) {
+                    u[U_SYMX] = sym;
+                    const int total = __ldcg(&u[U_NBEFORE]) + ntok;
+                    if (total > __ldcg(&u[U_SEGSTART])) {
+                        const int nb = __ldcg(&u[U_NBND]);
+                        if (P.bnd_out != nullptr && nb < T) P.bnd_out[P.bnd_region[utt] + nb] = total;
+                        u[U_NBND] = nb + 1;
+                        u[U_SEGSTART] = total;
+                    }
+                    e = 1; etok = P.blank; ereset = 1;
+                    u[U_LAST] = P.blank;
+                    t += 1; sym = 0;
+                } else if (tok < P.n_special && __ldg(P.special + tok)) {
+                    u[U_SYMX] = sym;
+                    t += 1; sym = 0;
+                } else {
+                    emit_tok = true;
+                    e = 1; etok = tok;
+                    u[U_LAST] = tok;
+                    ++sym;
+                    if (sym >= msym) { u[U_SYMX] = sym; t += 1; sym = 0; }
+                }
+            }
+            if (emit_tok) {
+                const int cap = T * (msym > 0 ? msym : 1);
+                if (ntok < cap) {
+                    P.tok_out[P.tok_region[utt] + ntok] = tok;
+                    ++ntok;
+                } else {
+                    atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+                    P.ctl[C_ERRINFO] = utt;
+                }
+            }
+            if (e) u[U_HBUF] = __ldcg(&u[U_HBUF]) ^ 1;
+            u[U_T] = t;
+            u[U_SYM] = sym;
+            u[U_NTOK] = ntok;
+            lv = t < T ? 1 : 0;
+            if (!lv) P.finish_ns[utt] = gtimer();
+        }
+        int tot_e = 0, tot_l = 0;
+        const int pe = block_excl_scan(e, S, tot_e);
+        const int pl = block_excl_scan(lv, S, tot_l);
+        if (e) {
+            P.emit[2 * (base_emit + pe)] = utt;
+            P.emit[2 * (base_emit + pe) + 1] = etok | (ereset << 31);
+        }
+        if (lv) live_out[base_live + pl] = utt;
+        base_emit += tot_e;
+        base_live += tot_l;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        P.ctl[C_NEMIT] = base_emit;
+        P.ctl[C_NLIVE0 + (sel ^ 1)] = base_live;
+        P.ctl[C_NDECIDED] = n_live;
+        P.ctl[C_SEL] = sel ^ 1;
+        P.ctl[C_ITERS] = __ldcg(&P.ctl[C_ITERS]) + 1;
+    }
+    __threadfence();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams P) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int upc = (P.H + (int) gridDim.x - 1) / (int) gridDim.x;
+    const Smem S = carve(smem_raw, P, upc);
+    unsigned gen = 0u;   // the host zeroes the barrier words before every launch
+    if (blockIdx.x == 0 && threadIdx.x == 0) *P.t_start = gtimer();
+    bool first = true;
+    for (;;) {
+        const int n_emit = __ldcg(&P.ctl[C_NEMIT]);
+        if (n_emit > 0) {
+            for (int l = 0; l < P.L; ++l) {
+                phase_lstm(P, l, n_emit, S);
+                if (!grid_barrier(P, gen, S)) return;
+            }
+        }
+        const int sel = __ldcg(&P.ctl[C_SEL]);
+        const int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
+        phase_pred(P, first, n_emit, sel, n_live, S);
+        if (!grid_barrier(P, gen, S)) return;
+        first = false;
+        if (n_live == 0) break;
+        phase_joint(P, sel, n_live, S);
+        if (grid_arrive(P, S)) {
+            leader_decide(P, S);
+            grid_release(P, gen);
+        } else if (!grid_wait(P, gen, S)) {
+            return;
+        }
+        ++gen;
+        if (__ldcg(&P.ctl[C_ERR]) != 0) return;
+    }
+}
+
+}  // namespace
+
+size_t step_loop_smem_bytes(int chunk, int ldx, int H, int grid) {
+    const int upc = (H + grid - 1) / grid;
+    size_t off = (size_t) chunk * ldx * sizeof(float);
+    off += (size_t) chunk * upc * 4 * sizeof(float);
+    off = (off + 15) & ~(size_t) 15;
+    off += (size_t) kWarps * 32 * 2 * sizeof(unsigned long long);
+    off += 3 * 32 * sizeof(int) + (kWarps + 2) * sizeof(int) + 4 * sizeof(int);
+    return off;
+}
+
+cudaError_t step_loop_configure(size_t smem) {
+    return cudaFuncSetAttribute(step_loop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int) smem);
+}
+
+cudaError_t step_loop_occupancy(size_t smem, int * blocks_per_sm) {
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, step_loop_kernel, kThreads, smem);
+}
+
+cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s) {
+    void * args[] = {const_cast<LoopParams *>(&p)};
+    return cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(step_loop_kernel),
+                                       dim3(grid), dim3(kThreads), args, smem, s);
+}
+
+}  // namespace pk
