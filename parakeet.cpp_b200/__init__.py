@@ -273,3 +273,6 @@ class Stream:
                                  int(s["carry_frames"]), int(s["initialized"]),
                                  int(s["last_token"]), int(s["segment_start_token"]))
         _check(lib().pk_stream_set_state(self.h, C.byref(st)), "pk_stream_set_state")
+
+
+from . import multi  # noqa: E402,F401  (needs shard_lpt defined above)

@@ -235,3 +235,50 @@ def write_gguf(model: DecoderModel, path: str) -> None:
     wr.write_kv_data_to_file()
     wr.write_tensors_to_file()
     wr.close()
+
+
+def read_gguf(path: str) -> DecoderModel:
+    """Load the decoder part of a parakeet GGUF (converter output or write_gguf).
+
+    Metadata defaults follow the reference loader (src/parakeet_ctc.cpp:424-460):
+    TDT pred_hidden/joint_hidden 640, 2 layers, 5 durations {0,1,2,3,4}, vocab 8192,
+    blank = vocab; EOU 1 layer, vocab 1026, max_symbols_per_step 5, eou/eob ids
+    -1 (resolved later to vocab-2 / vocab-1)."""
+    from gguf import GGUFReader
+    r = GGUFReader(path)
+
+    def val(key, default):
+        f = r.fields.get(key)
+        return default if f is None else f.contents()
+
+    mtype = val("parakeet.model.type", "ctc")
+    if mtype not in ("tdt", "eou"):
+        raise ValueError(f"{path}: model type {mtype!r} has no transducer decoder")
+    p = mtype
+    if p == "tdt":
+        H = int(val("parakeet.tdt.pred_hidden", 640)); L = int(val("parakeet.tdt.pred_rnn_layers", 2))
+        J = int(val("parakeet.tdt.joint_hidden", 640)); V = int(val("parakeet.tdt.vocab_size", 8192))
+        durs = [int(x) for x in val("parakeet.tdt.durations", [0, 1, 2, 3, 4])]
+        eou_id = eob_id = -1
+        msym = 10
+    else:
+        H = int(val("parakeet.eou.pred_hidden", 640)); L = int(val("parakeet.eou.pred_rnn_layers", 1))
+        J = int(val("parakeet.eou.joint_hidden", 640)); V = int(val("parakeet.eou.vocab_size", 1026))
+        durs = []
+        eou_id = int(val("parakeet.eou.eou_id", -1)); eob_id = int(val("parakeet.eou.eob_id", -1))
+        msym = int(val("parakeet.eou.max_symbols_per_step", 5))
+    blank = int(val(f"parakeet.{p}.blank_id", V))
+    De = int(val("parakeet.encoder.d_model", 1024))
+    pieces = [str(x) for x in val("tokenizer.ggml.tokens", [])]
+    tensors: Dict[str, Tensor] = {}
+    for t in r.tensors:
+        if not t.name.startswith(p + "."):
+            continue
+        shape = [int(x) for x in t.shape]
+        ne0, ne1 = shape[0], (shape[1] if len(shape) > 1 else 1)
+        raw = np.ascontiguousarray(t.data).view(np.uint8).reshape(-1).copy()
+        tensors[t.name] = Tensor(raw, int(t.tensor_type), ne0, ne1)
+    wtype = {GGML_Q8_0: "q8_0", GGML_F16: "f16", GGML_F32: "f32"}.get(
+        tensors[f"{p}.joint.out.weight"].type, "?")
+    return DecoderModel(mtype, De, H, J, L, V, blank, durs, eou_id, eob_id, msym, pieces,
+                        tensors, -1, wtype)

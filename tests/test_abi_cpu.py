@@ -1,0 +1,95 @@
+"""CPU tests of the C-ABI library: it loads, exports every declared symbol, and
+its host-only logic (sharding, capacity, error paths without a device) works.
+No compute is called here."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "parakeet_cuda.h")
+
+
+def declared_symbols():
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"^PK_API[^;(]*?\b(pk_\w+)\s*\(", txt, flags=re.M)))
+
+
+def test_header_and_binding_agree(pk):
+    assert declared_symbols() == sorted(pk.abi.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(pk):
+    L = C.CDLL(pk.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(L, name), name
+    assert pk.lib().pk_abi_version() == 1
+
+
+def test_struct_sizes_match_header(pk):
+    # pk_tensor: ptr + 2 x i32 + 2 x i64 + u64 = 40 bytes on LP64
+    assert C.sizeof(pk.abi.pk_tensor) == 40
+    assert C.sizeof(pk.abi.pk_lstm_layer) == 160
+
+
+def test_shard_lpt_balances(pk):
+    T = pk.synth.lengths_lognormal(4096, seed=5)
+    for world in (1, 2, 4, 8):
+        owner = pk.shard_lpt(T, world)
+        loads = np.bincount(owner, weights=T, minlength=world)
+        assert owner.min() >= 0 and owner.max() < world
+        assert loads.max() - loads.min() <= T.max()
+        # deterministic
+        assert np.array_equal(owner, pk.shard_lpt(T, world))
+
+
+def test_shard_lpt_matches_python_lpt(pk):
+    T = np.array([5, 9, 9, 1, 0, 7, 3], np.int32)
+    order = sorted(range(len(T)), key=lambda i: (-T[i], i))
+    load = [0, 0, 0]
+    exp = np.zeros(len(T), np.int32)
+    for i in order:
+        k = int(np.argmin(load))
+        exp[i] = k
+        load[k] += T[i]
+    assert np.array_equal(pk.shard_lpt(T, 3), exp)
+
+
+def test_tokens_capacity(pk):
+    T = np.array([3, 0, 10], np.int32)
+    f = pk.lib().pk_tokens_capacity
+    assert f(T.ctypes.data, 3, 10) == 130
+    assert f(T.ctypes.data, 3, 0) == 13
+
+
+def test_invalid_arguments_report_status(pk):
+    L = pk.lib()
+    assert L.pk_shard_lpt(None, 3, 0, None) == pk.abi.PK_ERR_INVALID
+    assert "sharding" in pk.last_error()
+    assert L.pk_create(None, 0, None) == pk.abi.PK_ERR_INVALID
+
+
+def test_create_without_device_fails_cleanly(pk):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    m = pk.synth.make_decoder("tdt", vocab_size=32, d_enc=32, pred_hidden=32, joint_hidden=32)
+    with pytest.raises(pk.PkError) as e:
+        pk.Decoder(m)
+    assert e.value.status in (pk.abi.PK_ERR_NO_DEVICE, pk.abi.PK_ERR_CUDA)
+
+
+def test_gguf_round_trip(pk, tmp_path):
+    m = pk.synth.make_decoder("eou", vocab_size=40, d_enc=32, pred_hidden=32, joint_hidden=64,
+                              n_layers=1, wtype="f16", eou_id=36, eob_id=37)
+    p = str(tmp_path / "m.gguf")
+    pk.synth.write_gguf(m, p)
+    m2 = pk.synth.read_gguf(p)
+    assert (m2.model_type, m2.vocab_size, m2.blank_id, m2.eou_id, m2.eob_id) == ("eou", 40, 40, 36, 37)
+    assert m2.pieces == m.pieces
+    for k, t in m.tensors.items():
+        t2 = m2.tensors[k]
+        assert (t.type, t.ne0, t.ne1) == (t2.type, t2.ne0, t2.ne1)
+        assert np.array_equal(t.data, t2.data)
