@@ -1,0 +1,447 @@
+#!/usr/bin/env python
+"""Throughput of the TDT/RNN-T greedy token loop on B200 (libparakeet_cuda).
+
+One "step" is one pk_decode_batch call over the configuration's batch of
+synthetic encoder outputs (random-init decoder weights of the named geometry):
+enc-proj GEMM, the persistent step-loop kernel, token compaction.
+
+  value : emitted tokens/s with encoder outputs resident in HBM and results left
+          on the device; time = sum over the K timed calls of the library's
+          CUDA-event time on its launching stream (max over ranks).
+  e2e   : the same metric through the same public call with pinned HOST encoder
+          outputs and HOST results (host<->device copies inside the timed call).
+
+Default workload (N=1): BASELINE config 2, TDT-0.6b-v3 q8_0, B=64,
+T ~ U[60, 1875]. For N>1 (torchrun, one rank per GPU) each rank decodes its LPT
+shard of a global batch of B*N utterances (weak scaling, no collective on the
+decode path).
+
+--impl reference times the reference's CPU decoder (the oracle port of
+src/parakeet_tdt.cpp / src/parakeet_eou.cpp; the reference itself cannot be
+built here: it needs the un-vendored ggml) on all host cores.
+"""
+import argparse
+import importlib.util
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "parakeet.cpp_b200")
+
+CONFIGS = {
+    "1": dict(model="tdt_0_6b", wtype="q8_0", B=1, lengths=("const", 125), blank_bias=2.0,
+              desc="TDT-0.6b-v3 q8_0, B=1, T=125"),
+    "2": dict(model="tdt_0_6b", wtype="q8_0", B=64, lengths=("uniform", 60, 1875), blank_bias=2.0,
+              desc="TDT-0.6b-v3 q8_0, B=64, T~U[60,1875]"),
+    "3": dict(model="eou_120m", wtype="f16", B=256, lengths=("const", 50), blank_bias=2.0,
+              desc="EOU-120m f16, B=256, T=50"),
+    "4": dict(model="tdt_1_1b", wtype="q8_0", B=1024, lengths=("const", 750), blank_bias=2.0,
+              desc="TDT-1.1b, B=1024, T=750"),
+    "5": dict(model="tdt_0_6b", wtype="q8_0", B=512, lengths=("lognormal",), blank_bias=2.0,
+              desc="TDT-0.6b-v3 q8_0, 512 per GPU (4096 over 8), T lognormal(250, 0.8) in [25, 3750]"),
+}
+METRIC = "tdt_greedy_decode_tokens_per_sec"
+
+
+def load(name, path, pkg_dir=None):
+    if name in sys.modules:
+        return sys.modules[name]
+    kw = {"submodule_search_locations": [pkg_dir]} if pkg_dir else {}
+    spec = importlib.util.spec_from_file_location(name, path, **kw)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def pkg():
+    return load("parakeet_b200", os.path.join(PKG_DIR, "__init__.py"), PKG_DIR)
+
+
+def oracle_mod():
+    pkg()
+    return load("pk_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
+
+
+def make_model(pk, cfg, wtype, blank_bias):
+    fn = getattr(pk.synth, cfg["model"])
+    return fn(seed=1234, wtype=wtype, blank_bias=blank_bias)
+
+
+def global_lengths(pk, cfg, B_total):
+    kind = cfg["lengths"]
+    if kind[0] == "const":
+        return np.full(B_total, kind[1], np.int32)
+    if kind[0] == "uniform":
+        return pk.synth.lengths_uniform(B_total, kind[1], kind[2], seed=7)
+    return pk.synth.lengths_lognormal(B_total, 250.0, 0.8, 25, 3750, seed=7)
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------- clocks ----
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU legs ----
+
+def cpu_sample_run(orc_o, enc, offs, T, threads, budget_s, msym=None):
+    """Oracle decode of a bounded sample: the first utterances of the batch,
+    each truncated to a frame cap chosen so the run takes about budget_s."""
+    # calibrate: one utterance of up to 40 frames
+    t40 = int(min(40, max(1, T[0])))
+    t0 = time.perf_counter()
+    orc_o.decode_window(enc[int(offs[0]):int(offs[0]) + t40], max_symbols=msym)
+    per_frame = max((time.perf_counter() - t0) / t40, 1e-5)
+    n_utt = int(min(len(T), max(1, threads)))
+    cap = int(max(10, min(int(np.max(T)), budget_s * threads / (n_utt * per_frame))))
+    Ts = np.minimum(T[:n_utt], cap).astype(np.int32)
+    Ts = np.maximum(Ts, 1)
+    t0 = time.perf_counter()
+    r = orc_o.decode_batch(enc, offs[:n_utt], Ts, n_threads=threads, max_symbols=msym)
+    wall = time.perf_counter() - t0
+    ntok = int(sum(len(x) for x in r["tokens"]))
+    nsteps = int(np.sum(r["steps"]))
+    return {"tokens": ntok, "steps": nsteps, "wall_s": wall, "n_utt": n_utt, "cap": cap,
+            "frames": int(Ts.sum()), "p50_ms": float(np.median(r["ms"]))}
+
+
+# ------------------------------------------------------------ helpers ----
+
+def per_iter_bytes(model):
+    """Algorithmic weight bytes of one batched loop iteration, as stored (q8_0 34 B
+    per 32 weights, f16 2 B, f32 4 B): the joint output layer every iteration;
+    LSTM + pred-proj (+ biases) in iterations with an emission."""
+    p = model.prefix
+    T = model.tensors
+    joint = T[f"{p}.joint.out.weight"].nbytes + T[f"{p}.joint.out.bias"].nbytes
+    lstm = sum(T[f"{p}.predict.lstm.{l}.{k}"].nbytes for l in range(model.n_layers)
+               for k in ("w_ih", "w_hh", "b_ih", "b_hh"))
+    pred = T[f"{p}.joint.pred.weight"].nbytes + T[f"{p}.joint.pred.bias"].nbytes
+    return joint, lstm + pred
+
+
+def profiled_traffic(config_key):
+    """dram bytes per loop iteration of the step-loop kernel from the committed ncu
+    summary (profiles/step_loop_kernel_config<k>.md), or None."""
+    path = os.path.join(ROOT, "profiles", f"step_loop_kernel_config{config_key}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"dram_bytes_per_iteration:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+def read_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ main ----
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--wtype", default=None)
+    ap.add_argument("--blank-bias", type=float, default=None)
+    ap.add_argument("--batch", type=int, default=None, help="override utterances per GPU")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 0)
+
+    cfg = dict(CONFIGS[args.config])
+    wtype = args.wtype or cfg["wtype"]
+    blank_bias = cfg["blank_bias"] if args.blank_bias is None else args.blank_bias
+    B = args.batch or cfg["B"]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    pk = pkg()
+    model = make_model(pk, cfg, wtype, blank_bias)
+    B_total = B * world
+    T_all = global_lengths(pk, cfg, B_total)
+    idx = pk.multi.shard_indices(T_all, world)[rank] if world > 1 else np.arange(B_total)
+    T = T_all[idx].astype(np.int32)
+    enc, offs = pk.synth.encoder_batch(T, model.d_enc, seed=99 + rank)
+    config = {"workload": cfg["desc"] + (f" (wtype {wtype})" if wtype != cfg["wtype"] else ""),
+              "config": args.config, "utterances_per_gpu": int(len(T)), "global_batch": int(B_total),
+              "frames_per_gpu": int(T.sum()), "blank_bias": blank_bias,
+              "l2": f"inputs {enc.nbytes / 1e6:.0f} MB of encoder output per step (L2 is 126 MB)",
+              "parallelism": f"utterance shards x{world}" if world > 1 else "single GPU"}
+
+    if args.impl == "reference":
+        return run_reference(args, model, enc, offs, T, config, rank)
+    return run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wtype)
+
+
+def run_reference(args, model, enc, offs, T, config, rank):
+    if rank != 0:
+        return 0
+    orc = oracle_mod()
+    o = orc.Oracle(model)
+    threads = host_cores()
+    budget = max(1.0, 150.0 / max(1, args.steps + min(args.warmup, 1)))
+    for _ in range(min(args.warmup, 1)):
+        cpu_sample_run(o, enc, offs, T, threads, min(budget, 2.0))
+    toks = steps = 0
+    wall = 0.0
+    last = None
+    for _ in range(args.steps):
+        last = cpu_sample_run(o, enc, offs, T, threads, budget)
+        toks += last["tokens"]
+        steps += last["steps"]
+        wall += last["wall_s"]
+    v = toks / wall if wall > 0 else 0.0
+    sample = (f"first {last['n_utt']} utterances of the batch, each truncated to {last['cap']} "
+              f"frames ({last['frames']} frames), one utterance per thread")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / max(1, args.steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init weights, N(0,1) encoder outputs)", "config": config,
+        "steps_per_sec": steps / wall if wall > 0 else 0.0,
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+    return 0
+
+
+def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wtype):
+    import ctypes as C
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    torch.cuda.set_device(local_rank)
+    dec = pk.Decoder(model, device=local_rank)
+    msym = dec.info.max_symbols_per_step
+    Bn = len(T)
+    cap = int(pk.lib().pk_tokens_capacity(T.ctypes.data, Bn, msym))
+    # device-resident inputs / outputs for the value path
+    enc_pin = torch.from_numpy(enc).pin_memory()
+    enc_dev = enc_pin.to(f"cuda:{local_rank}")
+    tok_dev = torch.empty(max(cap, 1), dtype=torch.int32, device=enc_dev.device)
+    off_dev = torch.empty(Bn + 1, dtype=torch.int64, device=enc_dev.device)
+    steps_dev = torch.empty(max(Bn, 1), dtype=torch.int32, device=enc_dev.device)
+    fin = np.zeros(max(Bn, 1), np.float32)
+    torch.cuda.synchronize()
+    batch_dev, keep_dev = dec.make_batch(enc_dev.data_ptr(), offs, T, enc_on_device=True)
+    batch_host, keep_host = dec.make_batch(enc_pin.numpy(), offs, T)
+
+    def res_dev():
+        r = pk.abi.pk_result()
+        r.results_on_device = 1
+        r.tokens, r.tokens_cap = C.c_void_p(tok_dev.data_ptr()), cap
+        r.token_offsets, r.steps = C.c_void_p(off_dev.data_ptr()), C.c_void_p(steps_dev.data_ptr())
+        r.finish_ms = C.c_void_p(fin.ctypes.data)
+        return r
+
+    tok_host = np.zeros(max(cap, 1), np.int32)
+    off_host = np.zeros(Bn + 1, np.int64)
+    steps_host = np.zeros(max(Bn, 1), np.int32)
+    tok_host_t = torch.from_numpy(tok_host)
+
+    def res_host():
+        r = pk.abi.pk_result()
+        r.tokens, r.tokens_cap = C.c_void_p(tok_host.ctypes.data), cap
+        r.token_offsets, r.steps = C.c_void_p(off_host.ctypes.data), C.c_void_p(steps_host.ctypes.data)
+        return r
+
+    def call(batch, res):
+        rc = dec.decode_batch_raw(batch, res)
+        if rc != 0:
+            raise pk.PkError(rc, "pk_decode_batch", pk.last_error())
+        return res
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        call(batch_dev, res_dev())
+    # ---- value: device-resident inputs ----
+    clocks = ClockSampler(local_rank)
+    barrier()
+    clocks.start()
+    t_wall = time.perf_counter()
+    tot_ms = loop_ms = enc_ms = 0.0
+    tokens = steps = iters = emit_iters = launches = 0
+    lat = None
+    for _ in range(args.steps):
+        r = call(batch_dev, res_dev())
+        tot_ms += r.total_ms
+        loop_ms += r.loop_ms
+        enc_ms += r.encproj_ms
+        tokens += r.tokens_needed
+        steps += r.total_steps
+        iters += r.loop_iterations
+        emit_iters += r.emit_iterations
+        launches += r.kernel_launches
+        lat = r.encproj_ms + fin[:Bn].astype(np.float64)
+    barrier()
+    wall_s = time.perf_counter() - t_wall
+    clk = clocks.stop()
+    # ---- e2e: host buffers through the same public call ----
+    barrier()
+    e2e_ms = 0.0
+    e2e_tokens = 0
+    for _ in range(args.steps):
+        r = call(batch_host, res_host())
+        e2e_ms += r.total_ms
+        e2e_tokens += r.tokens_needed
+    barrier()
+    same = bool(np.array_equal(tok_host[:int(off_host[-1])], tok_dev[:int(off_host[-1])].cpu().numpy()))
+
+    stats = torch.tensor([tot_ms, loop_ms, e2e_ms, float(tokens), float(steps), float(e2e_tokens)],
+                         dtype=torch.float64, device=enc_dev.device)
+    if dist is not None:
+        mx = stats.clone()
+        dist.all_reduce(mx[:3], op=dist.ReduceOp.MAX)
+        sm = stats.clone()
+        dist.all_reduce(sm[3:], op=dist.ReduceOp.SUM)
+        stats = torch.cat([mx[:3], sm[3:]])
+    tot_ms, loop_ms_max, e2e_ms, tokens_all, steps_all, e2e_tokens_all = [float(x) for x in stats.cpu()]
+
+    result = None
+    if rank == 0:
+        value = tokens_all / (tot_ms / 1e3) if tot_ms > 0 else 0.0
+        joint_b, lstm_b = per_iter_bytes(model)
+        alg_bytes = joint_b * iters + lstm_b * emit_iters
+        achieved = alg_bytes / (loop_ms / 1e3) / 1e9 if loop_ms > 0 else 0.0
+        peak, peak_kind = read_peaks()
+        tr = profiled_traffic(args.config)
+        h2d = int(enc.nbytes)
+        d2h = int(tokens / max(1, args.steps)) * 4 + (Bn + 1) * 8 + Bn * 4
+        result = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init weights of the named geometry, N(0,1) encoder outputs)",
+            "config": config,
+            "steps_per_sec": steps_all / (tot_ms / 1e3) if tot_ms > 0 else 0.0,
+            "p50_utterance_latency_ms": float(np.median(lat)) if lat is not None and len(lat) else None,
+            "decode_split_ms_per_step": {"encproj": enc_ms / args.steps, "loop": loop_ms / args.steps,
+                                         "total": tot_ms / args.steps},
+            "loop_iterations_per_step": iters / args.steps,
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "wall_s_timed": wall_s,
+            "e2e": {"value": e2e_tokens_all / (e2e_ms / 1e3) if e2e_ms > 0 else 0.0, "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "tokens_match_device_run": same},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak if peak else None,
+                         "traffic": (tr * iters / args.steps) if tr else None,
+                         "kernel": "step_loop_kernel",
+                         "note": f"algorithmic bytes = joint.out weights ({joint_b} B) per loop "
+                                 f"iteration + LSTM/pred-proj weights ({lstm_b} B) per iteration with "
+                                 f"an emission, as stored ({wtype}); time = step-loop kernel CUDA events; "
+                                 f"peak {peak_kind}"},
+        }
+    if world == 1 and not args.no_cpu_baseline and rank == 0:
+        orc = oracle_mod()
+        o = orc.Oracle(model)
+        threads = host_cores()
+        cs = cpu_sample_run(o, enc, offs, T, threads, args.cpu_budget_s)
+        result["cpu_baseline"] = {
+            "value": cs["tokens"] / cs["wall_s"], "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"first {cs['n_utt']} utterances of the batch truncated to {cs['cap']} frames "
+                      f"({cs['frames']} frames, {cs['tokens']} tokens, {cs['wall_s']:.1f} s wall), "
+                      f"one utterance per thread, -O3 -ffast-math -funroll-loops",
+            "steps_per_sec": cs["steps"] / cs["wall_s"], "p50_utterance_ms": cs["p50_ms"]}
+    if rank == 0:
+        print(json.dumps(result))
+    dec.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

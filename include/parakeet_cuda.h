@@ -179,6 +179,8 @@ typedef struct pk_result {
     int64_t   eou_bounds_needed;
     int64_t   total_steps;        /* sum of steps over the batch */
     int64_t   loop_iterations;    /* batched step-loop iterations */
+    int64_t   emit_iterations;    /* iterations in which at least one utterance emitted (LSTM ran) */
+    int64_t   kernel_launches;    /* device kernels this call launched */
     double    encproj_ms;         /* device time of the enc-proj GEMM (CUDA events) */
     double    loop_ms;            /* device time of the persistent step loop */
     double    total_ms;           /* device time of the whole call incl. copies */

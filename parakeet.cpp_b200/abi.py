@@ -60,6 +60,7 @@ class pk_result(C.Structure):
                 ("eou_offsets", C.c_void_p), ("finish_ms", C.c_void_p),
                 ("tokens_needed", C.c_int64), ("eou_bounds_needed", C.c_int64),
                 ("total_steps", C.c_int64), ("loop_iterations", C.c_int64),
+                ("emit_iterations", C.c_int64), ("kernel_launches", C.c_int64),
                 ("encproj_ms", C.c_double), ("loop_ms", C.c_double), ("total_ms", C.c_double)]
 
 

@@ -190,6 +190,7 @@ struct Run {
     std::vector<int32_t> ust;
     std::vector<int32_t> ctl;
     float ms_encproj = 0.f, ms_loop = 0.f;
+    int launches = 0;          // kernels launched by this call
 };
 
 pk_status run_loop(pk_ctx * x, Run & r) {
@@ -241,9 +242,11 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         encsrc = x->enc.as<float>();
     }
     PK_CK(cudaEventRecord(x->ev[1], s));
-    if (frames > 0)
+    if (frames > 0) {
         PK_CK(launch_encproj_f32(encsrc, frames, x->De, x->enc_w.as<float>(), x->enc_b.as<float>(), J,
                                  x->encp.as<float>(), s));
+        ++r.launches;
+    }
     PK_CK(cudaEventRecord(x->ev[2], s));
 
     // Host-built initial per-utterance state and lists.
@@ -289,6 +292,11 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     P.eou = x->eou; P.eob = x->eob; P.is_tdt = x->type == PK_MODEL_TDT ? 1 : 0;
     P.max_sym = r.msym; P.B = B; P.n_special = x->n_special;
     P.chunk = x->chunk; P.ldx = x->ldx; P.timeout_ns = x->timeout_ns;
+    {
+        int64_t tmax = 0;
+        for (int b = 0; b < B; ++b) tmax = std::max<int64_t>(tmax, r.n_frames[b]);
+        P.max_iters = (int) std::min<int64_t>(tmax * (msym1 + 1) + 2, 1 << 30);
+    }
     P.embed = x->embed.as<float>();
     for (int l = 0; l < L; ++l) {
         P.w_ih[l] = x->w_ih[l].as<float>(); P.w_hh[l] = x->w_hh[l].as<float>();
@@ -335,7 +343,10 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         }
     }
     PK_CK(cudaEventRecord(x->ev[3], s));
-    if (B > 0) PK_CK(launch_step_loop(P, x->grid, x->smem, s));
+    if (B > 0) {
+        PK_CK(launch_step_loop(P, x->grid, x->smem, s));
+        ++r.launches;
+    }
     PK_CK(cudaEventRecord(x->ev[4], s));
     r.ust.assign((size_t) B * kUst, 0);
     r.ctl.assign(kCtl, 0);
@@ -365,7 +376,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
 }
 
 // Compaction of per-utterance regions into the caller's result buffers.
-pk_status emit_results(pk_ctx * x, const Run & r, pk_result * res) {
+pk_status emit_results(pk_ctx * x, Run & r, pk_result * res) {
     const int B = r.B;
     cudaStream_t s = x->stream;
     PK_CK(x->offsets.ensure((size_t) (B + 1) * 8));
@@ -380,6 +391,7 @@ pk_status emit_results(pk_ctx * x, const Run & r, pk_result * res) {
     res->eou_bounds_needed = nbnd;
     res->total_steps = nsteps;
     res->loop_iterations = r.ctl[C_ITERS];
+    res->emit_iterations = r.ctl[C_EMITITERS];
     res->encproj_ms = r.ms_encproj;
     res->loop_ms = r.ms_loop;
     if (ntok > res->tokens_cap || (ntok > 0 && !res->tokens))
@@ -390,17 +402,24 @@ pk_status emit_results(pk_ctx * x, const Run & r, pk_result * res) {
                     (long long) res->eou_bounds_cap, (long long) nbnd);
     const bool dev = res->results_on_device != 0;
     PK_CK(launch_scan(x->ust.as<int32_t>(), B, U_NTOK, x->offsets.as<int64_t>(), s));
+    ++r.launches;
     if (dev) {
-        if (res->tokens)
+        if (res->tokens && B > 0) {
             PK_CK(launch_gather(x->ust.as<int32_t>(), B, U_NTOK, x->tok.as<int32_t>(),
                                 x->tokregion.as<int64_t>(), x->offsets.as<int64_t>(), res->tokens, s));
+            ++r.launches;
+        }
         if (res->token_offsets)
             PK_CK(cudaMemcpyAsync(res->token_offsets, x->offsets.p, (size_t) (B + 1) * 8, cudaMemcpyDeviceToDevice, s));
-        if (res->steps) PK_CK(launch_extract_field(x->ust.as<int32_t>(), B, U_STEPS, res->steps, s));
+        if (res->steps && B > 0) {
+            PK_CK(launch_extract_field(x->ust.as<int32_t>(), B, U_STEPS, res->steps, s));
+            ++r.launches;
+        }
     } else {
         PK_CK(x->compact.ensure((size_t) std::max<int64_t>(ntok, 1) * 4));
         PK_CK(launch_gather(x->ust.as<int32_t>(), B, U_NTOK, x->tok.as<int32_t>(),
                             x->tokregion.as<int64_t>(), x->offsets.as<int64_t>(), x->compact.as<int32_t>(), s));
+        if (B > 0) ++r.launches;
         if (ntok > 0) PK_CK(cudaMemcpyAsync(res->tokens, x->compact.p, (size_t) ntok * 4, cudaMemcpyDeviceToHost, s));
         if (res->token_offsets)
             PK_CK(cudaMemcpyAsync(res->token_offsets, x->offsets.p, (size_t) (B + 1) * 8, cudaMemcpyDeviceToHost, s));
@@ -409,6 +428,7 @@ pk_status emit_results(pk_ctx * x, const Run & r, pk_result * res) {
     }
     if (res->eou_bounds && x->type == PK_MODEL_EOU) {
         PK_CK(launch_scan(x->ust.as<int32_t>(), B, U_NBND, x->boffsets.as<int64_t>(), s));
+        r.launches += B > 0 ? 2 : 1;
         int32_t * dst = res->eou_bounds;
         if (!dev) {
             PK_CK(x->bcompact.ensure((size_t) std::max<int64_t>(nbnd, 1) * 4));
@@ -436,6 +456,7 @@ pk_status emit_results(pk_ctx * x, const Run & r, pk_result * res) {
     float tot = 0.f;
     PK_CK(cudaEventElapsedTime(&tot, x->ev[0], x->ev[5]));
     res->total_ms = tot;
+    res->kernel_launches = r.launches;
     return PK_OK;
 }
 

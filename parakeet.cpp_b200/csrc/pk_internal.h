@@ -39,6 +39,7 @@ enum CtlField : int {
     C_NDECIDED,       // utterances decided by the last leader (trace bookkeeping)
     C_ITERS,          // batched loop iterations completed
     C_ERRINFO,        // first failing utterance / index (diagnostics)
+    C_EMITITERS,      // iterations whose leader produced a non-empty emit list
     kCtl = 16
 };
 
@@ -49,6 +50,7 @@ struct LoopParams {
     int chunk;                 // max utterances per shared-memory chunk (power of two, <= 32)
     int ldx;                   // floats per chunk row in shared memory (>= max(2H, J))
     long long timeout_ns;      // bound on every grid-barrier wait
+    int max_iters;             // bound on batched loop iterations (max_b T_b * (max_sym + 1) + 2)
     // weights (f32, row-major [out][in])
     const float * embed;
     const float * w_ih[kMaxLayers];

@@ -638,6 +638,7 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
         P.ctl[C_NDECIDED] = n_live;
         P.ctl[C_SEL] = sel ^ 1;
         P.ctl[C_ITERS] = __ldcg(&P.ctl[C_ITERS]) + 1;
+        if (base_emit > 0) P.ctl[C_EMITITERS] = __ldcg(&P.ctl[C_EMITITERS]) + 1;
     }
     __threadfence();
 }
@@ -649,7 +650,13 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
     unsigned gen = 0u;   // the host zeroes the barrier words before every launch
     if (blockIdx.x == 0 && threadIdx.x == 0) *P.t_start = gtimer();
     bool first = true;
-    for (;;) {
+    for (int iter = 0;; ++iter) {
+        // Every utterance advances its frame pointer at least once per
+        // (max_sym + 1) iterations, so this bound only trips on a bug.
+        if (iter > P.max_iters) {
+            if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+            return;
+        }
         const int n_emit = __ldcg(&P.ctl[C_NEMIT]);
         if (n_emit > 0) {
             for (int l = 0; l < P.L; ++l) {
