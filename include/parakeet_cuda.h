@@ -121,7 +121,10 @@ enum {
 enum {
     PK_OPT_TIMEOUT_US  = 1,  /* bound (microseconds) on every device-side grid-barrier wait */
     PK_OPT_MATH        = 2,  /* PK_MATH_* */
-    PK_OPT_MAX_SYMBOLS = 3   /* default max_symbols_per_step override (> 0) */
+    PK_OPT_MAX_SYMBOLS = 3,  /* default max_symbols_per_step override (> 0) */
+    PK_OPT_TEST_STALL  = 4   /* test hook: 1 = CTA 0 of the next step loop never arrives at its first
+                                grid barrier, so the other CTAs' bounded waits run out and the call
+                                returns PK_ERR_TIMEOUT (exercises failure detection without a fault) */
 };
 
 /* Static information about a context. */

@@ -72,6 +72,7 @@ struct pk_ctx {
     int blank = 0, eou = -1, eob = -1, max_sym = 10, n_special = 0;
     long long timeout_ns = 5000000000ll;
     int math = PK_MATH_F32;
+    int test_stall = 0;
     uint64_t weight_bytes = 0;
     // weights (f32 on the device)
     DevBuf embed, w_ih[pk::kMaxLayers], w_hh[pk::kMaxLayers], b_ih[pk::kMaxLayers],
@@ -292,6 +293,8 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     P.eou = x->eou; P.eob = x->eob; P.is_tdt = x->type == PK_MODEL_TDT ? 1 : 0;
     P.max_sym = r.msym; P.B = B; P.n_special = x->n_special;
     P.chunk = x->chunk; P.ldx = x->ldx; P.timeout_ns = x->timeout_ns;
+    P.test_stall = x->test_stall;
+    x->test_stall = 0;   // one-shot
     {
         int64_t tmax = 0;
         for (int b = 0; b < B; ++b) tmax = std::max<int64_t>(tmax, r.n_frames[b]);
@@ -622,6 +625,9 @@ pk_status pk_set_option(pk_ctx * x, int32_t opt, int64_t v) {
         case PK_OPT_MAX_SYMBOLS:
             if (v <= 0) return fail(PK_ERR_INVALID, "max_symbols must be > 0");
             x->max_sym = (int) v;
+            return PK_OK;
+        case PK_OPT_TEST_STALL:
+            x->test_stall = v != 0 ? 1 : 0;
             return PK_OK;
         default:
             return fail(PK_ERR_INVALID, "unknown option %d", opt);

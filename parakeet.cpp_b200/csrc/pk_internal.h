@@ -51,6 +51,7 @@ struct LoopParams {
     int ldx;                   // floats per chunk row in shared memory (>= max(2H, J))
     long long timeout_ns;      // bound on every grid-barrier wait
     int max_iters;             // bound on batched loop iterations (max_b T_b * (max_sym + 1) + 2)
+    int test_stall;            // test hook: CTA 0 returns before its first barrier
     // weights (f32, row-major [out][in])
     const float * embed;
     const float * w_ih[kMaxLayers];

@@ -649,6 +649,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
     const Smem S = carve(smem_raw, P, upc);
     unsigned gen = 0u;   // the host zeroes the barrier words before every launch
     if (blockIdx.x == 0 && threadIdx.x == 0) *P.t_start = gtimer();
+    // Test hook (PK_OPT_TEST_STALL): CTA 0 never arrives, every other CTA's
+    // first barrier wait runs out after timeout_ns and records PK_ERR_TIMEOUT.
+    if (P.test_stall && blockIdx.x == 0) return;
     bool first = true;
     for (int iter = 0;; ++iter) {
         // Every utterance advances its frame pointer at least once per
