@@ -110,6 +110,16 @@ bool shape_ok(const pk_tensor & t, int64_t ne0, int64_t ne1) {
     return t.data && t.ne0 == ne0 && (ne1 <= 1 ? (t.ne1 <= 1) : t.ne1 == ne1);
 }
 
+// Every copy goes through the context's stream (a non-blocking stream does not
+// order against the legacy default stream that plain cudaMemcpy/cudaMemset use:
+// a pageable host->device cudaMemcpy may return before its DMA lands).
+cudaError_t copy_sync(pk_ctx * x, void * dst, const void * src, size_t n, cudaMemcpyKind kind) {
+    if (n == 0) return cudaSuccess;
+    cudaError_t e = cudaMemcpyAsync(dst, src, n, kind, x->stream);
+    if (e != cudaSuccess) return e;
+    return cudaStreamSynchronize(x->stream);
+}
+
 size_t raw_bytes(int type, int64_t ne0, int64_t rows) {
     if (type == PK_GGML_F32) return (size_t) (ne0 * rows) * 4;
     if (type == PK_GGML_F16) return (size_t) (ne0 * rows) * 2;
@@ -130,7 +140,7 @@ pk_status upload(pk_ctx * x, const pk_tensor & t, int64_t keep_rows, DevBuf & ds
     if (t.nbytes < nb) return fail(PK_ERR_MODEL, "tensor %s: %llu bytes < %zu needed", name,
                                    (unsigned long long) t.nbytes, nb);
     PK_CK(scratch.ensure(nb));
-    PK_CK(cudaMemcpy(scratch.p, t.data, nb, cudaMemcpyHostToDevice));
+    PK_CK(cudaMemcpyAsync(scratch.p, t.data, nb, cudaMemcpyHostToDevice, x->stream));
     const size_t fb = (size_t) (t.ne0 * rows) * sizeof(float);
     PK_CK(dst.ensure(fb));
     PK_CK(launch_dequant(scratch.p, t.type, t.ne0, rows, dst.as<float>(), x->stream));
@@ -369,11 +379,11 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     if (r.trace && r.trace->max_steps > 0 && B > 0) {
         const pk_trace & t = *r.trace;
         const size_t S = (size_t) t.max_steps;
-        if (t.logits) PK_CK(cudaMemcpy(t.logits, x->tr_logits.p, (size_t) B * S * x->Vo * 4, cudaMemcpyDeviceToHost));
-        if (t.h) PK_CK(cudaMemcpy(t.h, x->tr_h.p, (size_t) B * S * L * H * 4, cudaMemcpyDeviceToHost));
-        if (t.c) PK_CK(cudaMemcpy(t.c, x->tr_c.p, (size_t) B * S * L * H * 4, cudaMemcpyDeviceToHost));
-        if (t.argmax_token) PK_CK(cudaMemcpy(t.argmax_token, x->tr_tok.p, (size_t) B * S * 4, cudaMemcpyDeviceToHost));
-        if (t.argmax_dur_idx) PK_CK(cudaMemcpy(t.argmax_dur_idx, x->tr_dur.p, (size_t) B * S * 4, cudaMemcpyDeviceToHost));
+        if (t.logits) PK_CK(copy_sync(x, t.logits, x->tr_logits.p, (size_t) B * S * x->Vo * 4, cudaMemcpyDeviceToHost));
+        if (t.h) PK_CK(copy_sync(x, t.h, x->tr_h.p, (size_t) B * S * L * H * 4, cudaMemcpyDeviceToHost));
+        if (t.c) PK_CK(copy_sync(x, t.c, x->tr_c.p, (size_t) B * S * L * H * 4, cudaMemcpyDeviceToHost));
+        if (t.argmax_token) PK_CK(copy_sync(x, t.argmax_token, x->tr_tok.p, (size_t) B * S * 4, cudaMemcpyDeviceToHost));
+        if (t.argmax_dur_idx) PK_CK(copy_sync(x, t.argmax_dur_idx, x->tr_dur.p, (size_t) B * S * 4, cudaMemcpyDeviceToHost));
     }
     return PK_OK;
 }
@@ -562,7 +572,7 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
                               d->durations ? d->durations + x->Nd : nullptr);
     if (durs.empty()) durs.push_back(0);
     if (x->durations.ensure(durs.size() * 4) != cudaSuccess ||
-        cudaMemcpy(x->durations.p, durs.data(), durs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        copy_sync(x, x->durations.p, durs.data(), durs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
         return cleanup(fail(PK_ERR_CUDA, "durations upload failed"));
     std::vector<uint8_t> special;
     if (x->type == PK_MODEL_EOU && d->special_piece && d->n_vocab_pieces > 0)
@@ -570,7 +580,7 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
     x->n_special = (int) special.size();
     if (special.empty()) special.push_back(0);
     if (x->special.ensure(special.size()) != cudaSuccess ||
-        cudaMemcpy(x->special.p, special.data(), special.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        copy_sync(x, x->special.p, special.data(), special.size(), cudaMemcpyHostToDevice) != cudaSuccess)
         return cleanup(fail(PK_ERR_CUDA, "special-piece table upload failed"));
 
     // Step-loop launch shape: one CTA per SM, activation chunks sized to shared memory.
@@ -658,7 +668,9 @@ pk_status pk_stream_create(pk_ctx * x, pk_stream ** out) {
     s->ctx = x;
     const size_t n = (size_t) x->L * x->H * 4;
     if (s->h.ensure(n) != cudaSuccess || s->c.ensure(n) != cudaSuccess ||
-        cudaMemset(s->h.p, 0, n) != cudaSuccess || cudaMemset(s->c.p, 0, n) != cudaSuccess) {
+        cudaMemsetAsync(s->h.p, 0, n, x->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->c.p, 0, n, x->stream) != cudaSuccess ||
+        cudaStreamSynchronize(x->stream) != cudaSuccess) {
         pk_stream_destroy(s);
         return fail(PK_ERR_OOM, "stream state allocation failed");
     }
@@ -742,10 +754,10 @@ pk_status pk_stream_window(pk_stream * s, const float * enc, int32_t enc_on_devi
     const int nt = u[U_NTOK], nb = u[U_NBND];
     if (nt > tokens_cap || (nt > 0 && !tokens))
         return fail(PK_ERR_CAPACITY, "token buffer holds %d, %d needed", tokens_cap, nt);
-    if (nt > 0) PK_CK(cudaMemcpy(tokens, x->tok.p, (size_t) nt * 4, cudaMemcpyDeviceToHost));
+    if (nt > 0) PK_CK(copy_sync(x, tokens, x->tok.p, (size_t) nt * 4, cudaMemcpyDeviceToHost));
     if (bounds && nb > 0) {
         if (nb > bounds_cap) return fail(PK_ERR_CAPACITY, "boundary buffer holds %d, %d needed", bounds_cap, nb);
-        PK_CK(cudaMemcpy(bounds, x->bnd.p, (size_t) nb * 4, cudaMemcpyDeviceToHost));
+        PK_CK(copy_sync(x, bounds, x->bnd.p, (size_t) nb * 4, cudaMemcpyDeviceToHost));
     }
     if (n_tokens) *n_tokens = nt;
     if (steps) *steps = u[U_STEPS];
@@ -759,8 +771,8 @@ pk_status pk_stream_get_state(const pk_stream * s, pk_stream_state * st) {
     PK_CK(cudaSetDevice(x->device));
     const size_t LH = (size_t) x->L * x->H;
     std::vector<float> h(LH), c(LH);
-    PK_CK(cudaMemcpy(h.data(), s->h.p, LH * 4, cudaMemcpyDeviceToHost));
-    PK_CK(cudaMemcpy(c.data(), s->c.p, LH * 4, cudaMemcpyDeviceToHost));
+    PK_CK(copy_sync(x, h.data(), s->h.p, LH * 4, cudaMemcpyDeviceToHost));
+    PK_CK(copy_sync(x, c.data(), s->c.p, LH * 4, cudaMemcpyDeviceToHost));
     if (st->h) std::memcpy(st->h, h.data(), LH * 4);
     if (st->c) std::memcpy(st->c, c.data(), LH * 4);
     if (st->pred_out) std::memcpy(st->pred_out, h.data() + (size_t) (x->L - 1) * x->H, (size_t) x->H * 4);
@@ -777,8 +789,8 @@ pk_status pk_stream_set_state(pk_stream * s, const pk_stream_state * st) {
     pk_ctx * x = s->ctx;
     PK_CK(cudaSetDevice(x->device));
     const size_t LH = (size_t) x->L * x->H;
-    PK_CK(cudaMemcpy(s->h.p, st->h, LH * 4, cudaMemcpyHostToDevice));
-    PK_CK(cudaMemcpy(s->c.p, st->c, LH * 4, cudaMemcpyHostToDevice));
+    PK_CK(copy_sync(x, s->h.p, st->h, LH * 4, cudaMemcpyHostToDevice));
+    PK_CK(copy_sync(x, s->c.p, st->c, LH * 4, cudaMemcpyHostToDevice));
     s->sym = st->symbols_this_step;
     s->symx = st->symbols_this_step;
     s->carry = st->carry_frames;

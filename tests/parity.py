@@ -34,13 +34,22 @@ def teacher_forced(dec, o, enc_utt, max_symbols=None):
     dur_mis = (ad != r["dur_idx"]) if o.is_tdt else np.zeros(S, bool)
     near = (r["margin_tok"] < TIE_MARGIN) | (o.is_tdt & (r["margin_dur"] < TIE_MARGIN))
     mis = tok_mis | dur_mis
+    per_step = np.max(np.abs(lg - r["logits"]), axis=1)
+    bad = np.nonzero(per_step > LOGIT_TOL)[0]
+    detail = ""
+    if len(bad):
+        s0 = int(bad[0])
+        detail = (f"first bad step {s0} of {S} ({len(bad)} bad): oracle frame {int(r['frame'][s0])}, "
+                  f"oracle token {int(r['token'][s0])}, device argmax {int(at[s0])}, "
+                  f"device row all-zero {bool(np.all(lg[s0] == 0))}, err {per_step[s0]:.3g}, "
+                  f"bad steps {bad[:12].tolist()}, frames {[int(r['frame'][k]) for k in bad[:12]]}")
     return {"steps": S, "logit_err": logit_err, "h_err": h_err, "c_err": c_err,
             "near_ties": int(np.sum(near)), "mismatch": int(np.sum(mis)),
-            "bad_mismatch": int(np.sum(mis & ~near)), "oracle": r}
+            "bad_mismatch": int(np.sum(mis & ~near)), "oracle": r, "detail": detail}
 
 
 def assert_tf_ok(st, what=""):
-    assert st["logit_err"] <= LOGIT_TOL, f"{what} logits max-abs {st['logit_err']:.3g}"
+    assert st["logit_err"] <= LOGIT_TOL, f"{what} logits max-abs {st['logit_err']:.3g}; {st.get('detail', '')}"
     assert st["h_err"] <= STATE_TOL, f"{what} h max-abs {st['h_err']:.3g}"
     assert st["c_err"] <= STATE_TOL, f"{what} c max-abs {st['c_err']:.3g}"
     assert st["bad_mismatch"] == 0, f"{what} {st['bad_mismatch']} argmax mismatches at margin >= 1e-3"
