@@ -262,6 +262,40 @@ PK_API pk_status pk_stream_set_state(pk_stream * s, const pk_stream_state * st);
  * to the lowest shard id). shard_of[b] receives the shard of utterance b. */
 PK_API pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_shards, int32_t * shard_of);
 
+/* --- decode without device allocation ------------------------------------- */
+
+/* No counterpart in the reference. Greedy decode of ONE fresh utterance that
+ * allocates no device memory during the call. For callers that cannot call
+ * cudaMalloc while decoding: a process running under a fixed device-memory
+ * budget whose allocator forbids new allocations after start-up, or a
+ * latency-critical audio thread where cudaMalloc's implicit device
+ * synchronisation and possible failure are not acceptable.
+ *
+ * Every buffer the decode needs beyond its inputs and outputs lives in one
+ * statically sized device array inside the library (PK_NOALLOC_SCRATCH_BYTES,
+ * held by every GPU that loads the library until the process exits). Limits:
+ * n_frames <= PK_NOALLOC_MAX_FRAMES, joint_hidden and pred_hidden <= 1024.
+ * Larger inputs are rejected with PK_ERR_INVALID. The context (weights) must
+ * already exist (pk_create allocates; this call does not).
+ *
+ * enc, tokens, n_tokens and steps are DEVICE pointers on the context's device;
+ * tokens_cap must be >= n_frames * max(1, max_symbols_per_step). On success
+ * *n_tokens and *steps (device int32) hold the token count and joint
+ * evaluations (tdt_greedy_decode / eou_greedy_decode semantics for one
+ * utterance).
+ *
+ * The first call on a device looks up the array's device address on that
+ * device (cudaGetSymbolAddress); make that first call before any stream
+ * capture. All calls share the one array, which keeps the last call's
+ * contents: calls that overlap on the GPU (from several threads or contexts
+ * on the same device) race with each other and must be serialised by the
+ * caller. The call blocks until its decode has finished. */
+#define PK_NOALLOC_MAX_FRAMES 4096
+#define PK_NOALLOC_SCRATCH_BYTES (17u * 1024u * 1024u)
+PK_API pk_status pk_decode_noalloc(pk_ctx * ctx, const float * enc, int32_t n_frames, int32_t d_enc,
+                                   int32_t max_symbols_per_step, int32_t * tokens, int32_t tokens_cap,
+                                   int32_t * n_tokens, int32_t * steps);
+
 #ifdef __cplusplus
 }
 #endif

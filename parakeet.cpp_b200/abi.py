@@ -82,7 +82,7 @@ EXPORTED_SYMBOLS = [
     "pk_create", "pk_destroy", "pk_get_info", "pk_set_option", "pk_last_error",
     "pk_abi_version", "pk_decode_batch", "pk_tokens_capacity", "pk_decode_trace",
     "pk_stream_create", "pk_stream_destroy", "pk_stream_reset", "pk_stream_window",
-    "pk_stream_get_state", "pk_stream_set_state", "pk_shard_lpt",
+    "pk_stream_get_state", "pk_stream_set_state", "pk_shard_lpt", "pk_decode_noalloc",
 ]
 
 

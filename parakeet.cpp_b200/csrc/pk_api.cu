@@ -818,3 +818,27 @@ pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_shards, in
 }
 
 }  // extern "C"
+
+namespace pk {
+
+pk_status set_error(pk_status s, const char * msg) { return fail(s, "%s", msg); }
+
+void ctx_view(const pk_ctx * x, CtxView * v) {
+    v->device = x->device; v->grid = x->grid; v->chunk = x->chunk; v->ldx = x->ldx;
+    v->smem = x->smem; v->stream = x->stream;
+    v->H = x->H; v->J = x->J; v->De = x->De; v->L = x->L; v->V1 = x->V1; v->Vo = x->Vo;
+    v->Nd = x->Nd; v->blank = x->blank; v->eou = x->eou; v->eob = x->eob;
+    v->is_tdt = x->type == PK_MODEL_TDT ? 1 : 0; v->max_sym = x->max_sym;
+    v->n_special = x->n_special; v->timeout_ns = x->timeout_ns;
+    v->embed = x->embed.as<float>();
+    for (int l = 0; l < kMaxLayers; ++l) {
+        v->w_ih[l] = x->w_ih[l].as<float>(); v->w_hh[l] = x->w_hh[l].as<float>();
+        v->b_ih[l] = x->b_ih[l].as<float>(); v->b_hh[l] = x->b_hh[l].as<float>();
+    }
+    v->enc_w = x->enc_w.as<float>(); v->enc_b = x->enc_b.as<float>();
+    v->pred_w = x->pred_w.as<float>(); v->pred_b = x->pred_b.as<float>();
+    v->out_w = x->out_w.as<float>(); v->out_b = x->out_b.as<float>();
+    v->durations = x->durations.as<int32_t>(); v->special = x->special.as<uint8_t>();
+}
+
+}  // namespace pk

@@ -117,4 +117,29 @@ cudaError_t launch_gather(const int32_t * ust, int B, int field, const int32_t *
 cudaError_t launch_extract_field(const int32_t * ust, int B, int field, int32_t * dst,
                                  cudaStream_t s);
 
+// Read-only view of a context for entry points defined outside pk_api.cu.
+struct CtxView {
+    int device, grid, chunk, ldx;
+    size_t smem;
+    cudaStream_t stream;
+    int H, J, De, L, V1, Vo, Nd, blank, eou, eob, is_tdt, max_sym, n_special;
+    long long timeout_ns;
+    const float * embed;
+    const float * w_ih[kMaxLayers];
+    const float * w_hh[kMaxLayers];
+    const float * b_ih[kMaxLayers];
+    const float * b_hh[kMaxLayers];
+    const float * enc_w;
+    const float * enc_b;
+    const float * pred_w;
+    const float * pred_b;
+    const float * out_w;
+    const float * out_b;
+    const int32_t * durations;
+    const uint8_t * special;
+};
+void ctx_view(const pk_ctx * ctx, CtxView * v);
+// Records `msg` as this thread's pk_last_error() text and returns s.
+pk_status set_error(pk_status s, const char * msg);
+
 }  // namespace pk
