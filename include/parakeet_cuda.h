@@ -114,7 +114,10 @@ typedef struct pk_ctx pk_ctx;
 
 /* Math modes for the step loop (pk_set_option(PK_OPT_MATH, ...)). */
 enum {
-    PK_MATH_F32 = 0   /* exact dequantized weights, f32 activations, f32 FMA (reference-faithful) */
+    PK_MATH_F32 = 0,  /* exact dequantized weights, f32 activations, f32 FMA on CUDA cores */
+    PK_MATH_TC  = 1   /* tensor cores (mma.sync f16, f32 accumulate): exact q8_0/f16 weights,
+                         activations as f16 hi+lo (22 significant bits); the default when every
+                         step-loop weight is q8_0 or f16 and H, J are multiples of 32 */
 };
 
 /* Options. */

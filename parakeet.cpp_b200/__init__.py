@@ -92,7 +92,9 @@ def shard_lpt(n_frames: Sequence[int], n_shards: int) -> np.ndarray:
 class Decoder:
     """A libparakeet_cuda context holding one repacked decoder on one device."""
 
-    def __init__(self, model, device: int = 0, desc: Optional[abi.ModelDesc] = None):
+    def __init__(self, model, device: int = 0, desc: Optional[abi.ModelDesc] = None,
+                 math: Optional[str] = None):
+        """math: None (library default: tensor cores when the weights allow), "tc" or "f32"."""
         self.model = model
         self._desc = desc if desc is not None else abi.ModelDesc(model)
         h = C.c_void_p()
@@ -101,6 +103,8 @@ class Decoder:
         info = abi.pk_info()
         _check(lib().pk_get_info(self.h, C.byref(info)), "pk_get_info")
         self.info = info
+        if math is not None:
+            self.set_option(abi.PK_OPT_MATH, {"tc": abi.PK_MATH_TC, "f32": abi.PK_MATH_F32}[math])
 
     def close(self):
         if getattr(self, "h", None) is not None and self.h.value:

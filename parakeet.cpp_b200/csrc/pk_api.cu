@@ -73,6 +73,12 @@ struct pk_ctx {
     long long timeout_ns = 5000000000ll;
     int math = PK_MATH_F32;
     int test_stall = 0;
+    // tensor-core step loop
+    int tc_ok = 0, tc_stationary = 0, tc_ldh = 0, rpc_j = 0, rpc_p = 0, upc = 0;
+    unsigned tc_sm_weights = 0;
+    size_t tc_smem = 0;
+    pk::TcBlock tcj{}, tcp{}, tcl[pk::kMaxLayers]{};
+    DevBuf tc_frag[2 + pk::kMaxLayers], tc_scale[2 + pk::kMaxLayers], g0;
     uint64_t weight_bytes = 0;
     // weights (f32 on the device)
     DevBuf embed, w_ih[pk::kMaxLayers], w_hh[pk::kMaxLayers], b_ih[pk::kMaxLayers],
@@ -88,7 +94,8 @@ struct pk_ctx {
                                    &keys, &live, &emit, &ctl, &bar, &tstart, &finish, &tok,
                                    &tokregion, &bnd, &bndregion, &frameoff, &offsets, &boffsets,
                                    &compact, &bcompact, &tr_logits, &tr_h, &tr_c, &tr_tok, &tr_dur,
-                                   &tr_ftok, &tr_fdur};
+                                   &tr_ftok, &tr_fdur, &g0};
+        for (int i = 0; i < 2 + pk::kMaxLayers; ++i) { v.push_back(&tc_frag[i]); v.push_back(&tc_scale[i]); }
         for (int l = 0; l < pk::kMaxLayers; ++l) {
             v.push_back(&w_ih[l]); v.push_back(&w_hh[l]); v.push_back(&b_ih[l]); v.push_back(&b_hh[l]);
         }
@@ -146,6 +153,193 @@ pk_status upload(pk_ctx * x, const pk_tensor & t, int64_t keep_rows, DevBuf & ds
     PK_CK(launch_dequant(scratch.p, t.type, t.ne0, rows, dst.as<float>(), x->stream));
     PK_CK(cudaStreamSynchronize(x->stream));
     x->weight_bytes += fb;
+    return PK_OK;
+}
+
+// ---- tensor-core weight repack (host side, once at pk_create) ----------------
+
+float half_bits_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t) (h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1Fu, m = h & 0x3FFu, bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else {
+            int sh = 0;
+            while ((m & 0x400u) == 0) { m <<= 1; ++sh; }
+            bits = sign | ((uint32_t) (113 - sh) << 23) | ((m & 0x3FFu) << 13);
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7F800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112) << 23) | (m << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+// A weight matrix as seen by one phase: rows of tensor `a`, optionally
+// continued along K by tensor `b` (the [W_ih | W_hh] concatenation).
+struct SrcMat {
+    const pk_tensor * a = nullptr;
+    const pk_tensor * b = nullptr;
+    int64_t ka = 0;
+    int type() const { return a->type; }
+    const pk_tensor & at(int64_t k, int64_t & kk) const {
+        if (b && k >= ka) { kk = k - ka; return *b; }
+        kk = k;
+        return *a;
+    }
+    uint8_t q_biased(int64_t row, int64_t k) const {
+        int64_t kk;
+        const pk_tensor & t = at(k, kk);
+        const uint8_t * blk = static_cast<const uint8_t *>(t.data) + (row * (t.ne0 / 32) + kk / 32) * 34;
+        return (uint8_t) ((int) (int8_t) blk[2 + kk % 32] + 128);
+    }
+    float scale(int64_t row, int64_t k) const {
+        int64_t kk;
+        const pk_tensor & t = at(k, kk);
+        const uint8_t * blk = static_cast<const uint8_t *>(t.data) + (row * (t.ne0 / 32) + kk / 32) * 34;
+        return half_bits_to_float((uint16_t) (blk[0] | (blk[1] << 8)));
+    }
+    uint16_t half(int64_t row, int64_t k) const {
+        int64_t kk;
+        const pk_tensor & t = at(k, kk);
+        return static_cast<const uint16_t *>(t.data)[row * t.ne0 + kk];
+    }
+};
+
+template <class RowMap>
+pk_status build_tc_block(pk_ctx * x, int G, int tiles, int K, const SrcMat & src, RowMap rowmap,
+                         DevBuf & dfrag, DevBuf & dscale, pk::TcBlock & out) {
+    const bool i8 = src.type() == PK_GGML_Q8_0;
+    const int nkb = K / 32;
+    const size_t per_lane = i8 ? 8 : 16;
+    const size_t cta_bytes = (size_t) tiles * nkb * 32 * per_lane;
+    const size_t cta_scales = i8 ? (size_t) tiles * nkb * 8 : 0;
+    std::vector<uint8_t> frag((size_t) G * cta_bytes);
+    std::vector<float> scale(std::max<size_t>((size_t) G * cta_scales, 1), 0.0f);
+    for (int cta = 0; cta < G; ++cta) {
+        for (int tile = 0; tile < tiles; ++tile) {
+            for (int kb = 0; kb < nkb; ++kb) {
+                for (int lane = 0; lane < 32; ++lane) {
+                    const int g = lane >> 2, t = lane & 3;
+                    const int64_t row = rowmap(cta, tile * 8 + g);
+                    uint8_t * dst = frag.data() + (size_t) cta * cta_bytes +
+                                    (((size_t) tile * nkb + kb) * 32 + lane) * per_lane;
+                    for (int ks = 0; ks < 2; ++ks) {
+                        const int64_t kk = (int64_t) kb * 32 + ks * 16;
+                        const int64_t ks4[4] = {kk + 2 * t, kk + 2 * t + 1, kk + 2 * t + 8, kk + 2 * t + 9};
+                        for (int e = 0; e < 4; ++e) {
+                            if (i8) {
+                                dst[ks * 4 + e] = row < 0 ? (uint8_t) 128 : src.q_biased(row, ks4[e]);
+                            } else {
+                                const uint16_t hv = row < 0 ? (uint16_t) 0 : src.half(row, ks4[e]);
+                                std::memcpy(dst + (ks * 4 + e) * 2, &hv, 2);
+                            }
+                        }
+                    }
+                }
+                if (i8) {
+                    for (int rr = 0; rr < 8; ++rr) {
+                        const int64_t row = rowmap(cta, tile * 8 + rr);
+                        scale[(size_t) cta * cta_scales + ((size_t) tile * nkb + kb) * 8 + rr] =
+                            row < 0 ? 0.0f : src.scale(row, (int64_t) kb * 32);
+                    }
+                }
+            }
+        }
+    }
+    PK_CK(dfrag.ensure(frag.size()));
+    PK_CK(copy_sync(x, dfrag.p, frag.data(), frag.size(), cudaMemcpyHostToDevice));
+    PK_CK(dscale.ensure(scale.size() * 4));
+    PK_CK(copy_sync(x, dscale.p, scale.data(), scale.size() * 4, cudaMemcpyHostToDevice));
+    out.frag = dfrag.as<uint8_t>();
+    out.scale = dscale.as<float>();
+    out.cta_bytes = (unsigned) cta_bytes;
+    out.cta_scales = (unsigned) cta_scales;
+    out.tiles = tiles;
+    out.K = K;
+    out.is_i8 = i8 ? 1 : 0;
+    return PK_OK;
+}
+
+bool tc_type_ok(const pk_tensor & t) { return t.type == PK_GGML_Q8_0 || t.type == PK_GGML_F16; }
+
+// Repack the step-loop weights for the tensor-core phases; leaves x->tc_ok = 0
+// (CUDA-core f32 phases only) when the model does not qualify.
+pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
+    const int H = x->H, J = x->J, L = x->L, G = x->grid;
+    x->tc_ok = 0;
+    if (H % 32 != 0 || J % 32 != 0) return PK_OK;
+    if (!tc_type_ok(d->joint_out_w) || !tc_type_ok(d->joint_pred_w) || !tc_type_ok(d->lstm[0].w_hh)) return PK_OK;
+    for (int l = 1; l < L; ++l)
+        if (!tc_type_ok(d->lstm[l].w_ih) || d->lstm[l].w_ih.type != d->lstm[l].w_hh.type) return PK_OK;
+    x->rpc_j = (x->Vo + G - 1) / G;
+    x->rpc_p = (J + G - 1) / G;
+    x->upc = (H + G - 1) / G;
+    const int rpc_j = x->rpc_j, rpc_p = x->rpc_p, upc = x->upc, Vo = x->Vo;
+    SrcMat sj; sj.a = &d->joint_out_w;
+    PK_TRY(build_tc_block(x, G, (rpc_j + 7) / 8, J, sj,
+                          [&](int cta, int r) -> int64_t {
+                              const int64_t row = (int64_t) cta * rpc_j + r;
+                              return (r < rpc_j && row < Vo) ? row : -1; },
+                          x->tc_frag[0], x->tc_scale[0], x->tcj));
+    SrcMat sp; sp.a = &d->joint_pred_w;
+    PK_TRY(build_tc_block(x, G, (rpc_p + 7) / 8, H, sp,
+                          [&](int cta, int r) -> int64_t {
+                              const int64_t row = (int64_t) cta * rpc_p + r;
+                              return (r < rpc_p && row < J) ? row : -1; },
+                          x->tc_frag[1], x->tc_scale[1], x->tcp));
+    auto unit_rows = [&](int cta, int r) -> int64_t {
+        const int jj = r / 4, q = r % 4;
+        const int64_t unit = (int64_t) cta * upc + jj;
+        return (jj < upc && unit < H) ? (int64_t) q * H + unit : -1;
+    };
+    const int tiles_l = (4 * upc + 7) / 8;
+    if (tiles_l > kTcRmax) return PK_OK;      // the LSTM phase runs one GEMM group per CTA
+    for (int l = 0; l < L; ++l) {
+        SrcMat sl;
+        if (l == 0) {
+            sl.a = &d->lstm[0].w_hh;                       // W_ih0 . embed comes from the g0 table
+        } else {
+            sl.a = &d->lstm[l].w_ih; sl.b = &d->lstm[l].w_hh; sl.ka = H;
+        }
+        PK_TRY(build_tc_block(x, G, tiles_l, l == 0 ? H : 2 * H, sl, unit_rows,
+                              x->tc_frag[2 + l], x->tc_scale[2 + l], x->tcl[l]));
+    }
+    // g0[v][4H] = b_ih0 + W_ih0 . embed[v] for every token v (f32 GEMM on the device)
+    PK_CK(x->g0.ensure((size_t) x->V1 * 4 * H * 4));
+    PK_CK(launch_encproj_f32(x->embed.as<float>(), x->V1, H, x->w_ih[0].as<float>(), x->b_ih[0].as<float>(),
+                             4 * H, x->g0.as<float>(), x->stream));
+    PK_CK(cudaStreamSynchronize(x->stream));
+    // stationary shared-memory layout
+    unsigned off = 0;
+    auto place = [&](pk::TcBlock & b) {
+        b.sm_frag = off; off += (b.cta_bytes + 15u) & ~15u;
+        b.sm_scale = off; off += ((b.cta_scales * 4u) + 15u) & ~15u;
+    };
+    place(x->tcj);
+    place(x->tcp);
+    for (int l = 0; l < L; ++l) place(x->tcl[l]);
+    const int kmax = std::max(std::max(J, H), L > 1 ? 2 * H : H);
+    x->tc_ldh = kmax + 8;
+    size_t need = step_loop_tc_smem_bytes(off, x->tc_ldh);
+    if (need <= smem_cap) {
+        x->tc_stationary = 1;
+        x->tc_sm_weights = off;
+    } else {
+        x->tc_stationary = 0;
+        x->tc_sm_weights = 0;
+        need = step_loop_tc_smem_bytes(0, x->tc_ldh);
+        if (need > smem_cap) return PK_OK;
+    }
+    x->tc_smem = need;
+    if (step_loop_configure(x->tc_smem, 1) != cudaSuccess) return PK_OK;
+    int per_sm = 0;
+    if (step_loop_occupancy(x->tc_smem, 1, &per_sm) != cudaSuccess || per_sm < 1) return PK_OK;
+    x->tc_ok = 1;
     return PK_OK;
 }
 
@@ -305,6 +499,17 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     P.chunk = x->chunk; P.ldx = x->ldx; P.timeout_ns = x->timeout_ns;
     P.test_stall = x->test_stall;
     x->test_stall = 0;   // one-shot
+    const bool use_tc = x->math == PK_MATH_TC && x->tc_ok;
+    if (use_tc) {
+        P.tc = 1;
+        P.stationary = x->tc_stationary;
+        P.sm_weights = x->tc_sm_weights;
+        P.ldh = x->tc_ldh;
+        P.rpc_j = x->rpc_j; P.rpc_p = x->rpc_p; P.upc = x->upc;
+        P.tcj = x->tcj; P.tcp = x->tcp;
+        for (int l = 0; l < L; ++l) P.tcl[l] = x->tcl[l];
+        P.g0 = x->g0.as<float>();
+    }
     {
         int64_t tmax = 0;
         for (int b = 0; b < B; ++b) tmax = std::max<int64_t>(tmax, r.n_frames[b]);
@@ -357,7 +562,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     }
     PK_CK(cudaEventRecord(x->ev[3], s));
     if (B > 0) {
-        PK_CK(launch_step_loop(P, x->grid, x->smem, s));
+        PK_CK(launch_step_loop(P, x->grid, use_tc ? x->tc_smem : x->smem, s));
         ++r.launches;
     }
     PK_CK(cudaEventRecord(x->ev[4], s));
@@ -591,11 +796,14 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
     while (x->chunk > 1 && step_loop_smem_bytes(x->chunk, x->ldx, x->H, x->grid) > smem_cap) x->chunk >>= 1;
     x->smem = step_loop_smem_bytes(x->chunk, x->ldx, x->H, x->grid);
     if (x->smem > smem_cap) return cleanup(fail(PK_ERR_MODEL, "hidden sizes too large for shared memory"));
-    if (step_loop_configure(x->smem) != cudaSuccess)
+    if (step_loop_configure(x->smem, 0) != cudaSuccess)
         return cleanup(fail(PK_ERR_CUDA, "cannot configure %zu B of shared memory", x->smem));
     int per_sm = 0;
-    if (step_loop_occupancy(x->smem, &per_sm) != cudaSuccess || per_sm < 1)
+    if (step_loop_occupancy(x->smem, 0, &per_sm) != cudaSuccess || per_sm < 1)
         return cleanup(fail(PK_ERR_CUDA, "step loop does not fit one CTA per SM"));
+    st = setup_tc(x, d, (size_t) prop.sharedMemPerBlockOptin);
+    if (st != PK_OK) return cleanup(st);
+    x->math = x->tc_ok ? PK_MATH_TC : PK_MATH_F32;
     *out = x;
     return PK_OK;
 }
@@ -629,7 +837,9 @@ pk_status pk_set_option(pk_ctx * x, int32_t opt, int64_t v) {
             x->timeout_ns = v * 1000;
             return PK_OK;
         case PK_OPT_MATH:
-            if (v != PK_MATH_F32) return fail(PK_ERR_INVALID, "unsupported math mode %lld", (long long) v);
+            if (v == PK_MATH_TC && !x->tc_ok)
+                return fail(PK_ERR_INVALID, "tensor-core math needs q8_0/f16 step-loop weights and H, J multiples of 32");
+            if (v != PK_MATH_F32 && v != PK_MATH_TC) return fail(PK_ERR_INVALID, "unsupported math mode %lld", (long long) v);
             x->math = (int) v;
             return PK_OK;
         case PK_OPT_MAX_SYMBOLS:

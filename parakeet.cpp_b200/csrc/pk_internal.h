@@ -43,6 +43,26 @@ enum CtlField : int {
     kCtl = 16
 };
 
+constexpr int kTcM = 16;         // utterances per tensor-core pass (mma M)
+constexpr int kTcRmax = 8;       // 8-row weight tiles per tensor-core GEMM group
+
+// One phase's weights in the tensor-core layout. Rows owned by CTA k are
+// padded to `tiles` tiles of 8 rows; per (tile, 32-wide K block, lane) the
+// lane's B fragments of mma.m16n8k16 for the block's two k-steps are stored
+// contiguously: q8_0 as biased bytes (q + 128, 8 B per lane) with an f32 scale
+// per (tile, block, row); f16 weights as halves (16 B per lane).
+struct TcBlock {
+    const uint8_t * frag;      // global [grid][cta_bytes]
+    const float * scale;       // global [grid][cta_scales] (q8_0 only)
+    unsigned cta_bytes;
+    unsigned cta_scales;       // floats per CTA
+    int tiles;
+    int K;                     // multiple of 32
+    int is_i8;
+    unsigned sm_frag;          // offsets inside the stationary shared-memory region
+    unsigned sm_scale;
+};
+
 // Everything the persistent step-loop kernel needs (passed by value).
 struct LoopParams {
     // geometry
@@ -52,6 +72,14 @@ struct LoopParams {
     long long timeout_ns;      // bound on every grid-barrier wait
     int max_iters;             // bound on batched loop iterations (max_b T_b * (max_sym + 1) + 2)
     int test_stall;            // test hook: CTA 0 returns before its first barrier
+    // tensor-core phases (tc = 1)
+    int tc;
+    int stationary;            // copy TC weights into shared memory at kernel start
+    unsigned sm_weights;       // bytes of the stationary region
+    int ldh;                   // halves per staged activation row (max K + 8)
+    int rpc_j, rpc_p, upc;     // joint rows, pred rows, LSTM units per CTA
+    TcBlock tcj, tcp, tcl[kMaxLayers];
+    const float * g0;          // [V+1][4H]: b_ih0 + W_ih0 . embed[v] (layer-0 input projection)
     // weights (f32, row-major [out][in])
     const float * embed;
     const float * w_ih[kMaxLayers];
@@ -99,8 +127,9 @@ struct LoopParams {
 // Launch wrappers (defined in the .cu files).
 cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s);
 size_t      step_loop_smem_bytes(int chunk, int ldx, int H, int grid);
-cudaError_t step_loop_configure(size_t smem);
-cudaError_t step_loop_occupancy(size_t smem, int * blocks_per_sm);
+size_t      step_loop_tc_smem_bytes(unsigned sm_weights, int ldh);
+cudaError_t step_loop_configure(size_t smem, int tc);
+cudaError_t step_loop_occupancy(size_t smem, int tc, int * blocks_per_sm);
 
 cudaError_t launch_encproj_f32(const float * enc, int64_t frames, int De, const float * w,
                                const float * b, int J, float * out, cudaStream_t s);

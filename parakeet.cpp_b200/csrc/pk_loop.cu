@@ -27,6 +27,7 @@
 
 #include "pk_internal.h"
 
+#include <cuda_fp16.h>
 #include <math.h>
 
 namespace pk {
@@ -336,6 +337,28 @@ __device__ void phase_lstm(const LoopParams & P, int l, int n_emit, const Smem &
     }
 }
 
+// Trace: LSTM state after the step just decided, for every utterance decided by
+// the last leader (the previous live list). Trace mode only (CTA 0).
+__device__ void trace_state_dump(const LoopParams & P, bool first, int sel) {
+    if (P.trace_steps <= 0 || first || blockIdx.x != 0) return;
+    const int H = P.H, L = P.L, B = P.B;
+    const int n_dec = __ldcg(&P.ctl[C_NDECIDED]);
+    const int * prev = P.live + (size_t) (sel ^ 1) * B;
+    const int LH = L * H;
+    for (int i = 0; i < n_dec; ++i) {
+        const int utt = __ldcg(&prev[i]);
+        const int step = __ldcg(&P.ust[utt * kUst + U_STEPS]) - 1;
+        if (step < 0 || step >= P.trace_steps) continue;
+        const int hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+        for (int k = threadIdx.x; k < LH; k += blockDim.x) {
+            const int l = k / H, j = k - (k / H) * H;
+            const size_t dst = ((size_t) utt * P.trace_steps + step) * LH + k;
+            if (P.tr_h) P.tr_h[dst] = __ldcg(P.h + (((size_t) hb * L + l) * B + utt) * H + j);
+            if (P.tr_c) P.tr_c[dst] = __ldcg(P.c + ((size_t) l * B + utt) * H + j);
+        }
+    }
+}
+
 // ---- pred-proj + joint hidden phase --------------------------------------------
 
 template <int CP>
@@ -402,25 +425,7 @@ __device__ void phase_pred(const LoopParams & P, bool first, int n_emit, int sel
             P.hid[(size_t) utt * J + j] = (0.0f < v) ? v : 0.0f;
         }
     }
-    // Trace: state after the step just decided, for every utterance decided by
-    // the last leader (the previous live list).
-    if (P.trace_steps > 0 && !first && blockIdx.x == 0) {
-        const int n_dec = __ldcg(&P.ctl[C_NDECIDED]);
-        const int * prev = P.live + (size_t) (sel ^ 1) * B;
-        const int LH = L * H;
-        for (int i = 0; i < n_dec; ++i) {
-            const int utt = __ldcg(&prev[i]);
-            const int step = __ldcg(&P.ust[utt * kUst + U_STEPS]) - 1;
-            if (step < 0 || step >= P.trace_steps) continue;
-            const int hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
-            for (int k = threadIdx.x; k < LH; k += blockDim.x) {
-                const int l = k / H, j = k - (k / H) * H;
-                const size_t dst = ((size_t) utt * P.trace_steps + step) * LH + k;
-                if (P.tr_h) P.tr_h[dst] = __ldcg(P.h + (((size_t) hb * L + l) * B + utt) * H + j);
-                if (P.tr_c) P.tr_c[dst] = __ldcg(P.c + ((size_t) l * B + utt) * H + j);
-            }
-        }
-    }
+    trace_state_dump(P, first, sel);
 }
 
 // ---- joint output + partial argmax phase ---------------------------------------
@@ -643,15 +648,401 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
     __threadfence();
 }
 
+// ---- tensor-core phases (PK_MATH_TC) -------------------------------------------
+//
+// Each phase is a small GEMM C[rows of this CTA][16 utterances] = W . X^T with
+// mma.sync.m16n8k16 (A = activations, 16 utterances x 16 k; B = 8 weight rows x
+// 16 k; f32 accumulation). Weights are exact: q8_0 quants enter as f16 (|q| <=
+// 127 is exact) and the per-32-block scale is applied in f32 after each block;
+// f16 weights enter as-is. Activations are split into f16 hi + lo (x = hi + lo
+// to 22 significant bits), two MMAs per k-step. The 8 warps split K in 32-wide
+// blocks and their partial tiles are summed through shared memory.
+
+struct TcSmem {
+    unsigned char * w;              // stationary weights (P.sm_weights bytes)
+    __half * xs_hi;                 // [16][ldh]
+    __half * xs_lo;                 // [16][ldh]
+    float * part;                   // [kWarps][kTcRmax][8][16]
+    float * C;                      // [kTcRmax][8][16]
+    int * s_utt;                    // [32]
+    int * s_aux;                    // [32]
+    int * s_aux2;                   // [32]
+    int * s_scan;                   // [kWarps + 2]
+    int * s_flag;                   // [4]
+};
+
+__device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams & P) {
+    TcSmem s;
+    size_t off = 0;
+    s.w = raw;
+    off += (P.sm_weights + 15) & ~15u;
+    s.xs_hi = reinterpret_cast<__half *>(raw + off); off += (size_t) kTcM * P.ldh * 2;
+    s.xs_lo = reinterpret_cast<__half *>(raw + off); off += (size_t) kTcM * P.ldh * 2;
+    s.part = reinterpret_cast<float *>(raw + off); off += (size_t) kWarps * kTcRmax * 128 * 4;
+    s.C = reinterpret_cast<float *>(raw + off); off += (size_t) kTcRmax * 128 * 4;
+    s.s_utt = reinterpret_cast<int *>(raw + off); off += 32 * 4;
+    s.s_aux = reinterpret_cast<int *>(raw + off); off += 32 * 4;
+    s.s_aux2 = reinterpret_cast<int *>(raw + off); off += 32 * 4;
+    s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * 4;
+    s.s_flag = reinterpret_cast<int *>(raw + off);
+    return s;
+}
+
+// The barrier / scan helpers only use s_scan and s_flag.
+__device__ __forceinline__ Smem as_smem(const TcSmem & T) {
+    Smem s{};
+    s.s_utt = T.s_utt; s.s_aux = T.s_aux; s.s_aux2 = T.s_aux2; s.s_scan = T.s_scan; s.s_flag = T.s_flag;
+    return s;
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const __half * p) {
+    const unsigned a = (unsigned) __cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Four biased bytes (q + 128) -> two f16x2 holding q exactly: byte b placed
+// under the f16 exponent of 1024 gives 1024 + b, minus 1152 gives q.
+__device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, uint32_t & hi) {
+    const uint32_t a = __byte_perm(v, 0x64646464u, 0x4140);
+    const uint32_t b = __byte_perm(v, 0x64646464u, 0x4342);
+    const __half2 bias = __half2half2(__ushort_as_half((unsigned short) 0x6480));  // 1152
+    __half2 ha = __hsub2(*reinterpret_cast<const __half2 *>(&a), bias);
+    __half2 hb = __hsub2(*reinterpret_cast<const __half2 *>(&b), bias);
+    lo = *reinterpret_cast<uint32_t *>(&ha);
+    hi = *reinterpret_cast<uint32_t *>(&hb);
+}
+
+// Stage up to 16 utterances' f32 activations [c][0..K) as f16 hi / lo.
+template <class F>
+__device__ __forceinline__ void tc_stage(const TcSmem & S, int ldh, int nc, int K, F src) {
+    const int k4n = K >> 2;
+    for (int idx = threadIdx.x; idx < kTcM * k4n; idx += blockDim.x) {
+        const int c = idx / k4n;
+        const int k = 4 * (idx - c * k4n);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < nc) v = src(c, k);
+        const __half2 h01 = __floats2half2_rn(v.x, v.y);
+        const __half2 h23 = __floats2half2_rn(v.z, v.w);
+        const float2 f01 = __half22float2(h01);
+        const float2 f23 = __half22float2(h23);
+        const __half2 l01 = __floats2half2_rn(v.x - f01.x, v.y - f01.y);
+        const __half2 l23 = __floats2half2_rn(v.z - f23.x, v.w - f23.y);
+        uint2 hv, lv;
+        hv.x = *reinterpret_cast<const uint32_t *>(&h01); hv.y = *reinterpret_cast<const uint32_t *>(&h23);
+        lv.x = *reinterpret_cast<const uint32_t *>(&l01); lv.y = *reinterpret_cast<const uint32_t *>(&l23);
+        *reinterpret_cast<uint2 *>(S.xs_hi + c * ldh + k) = hv;
+        *reinterpret_cast<uint2 *>(S.xs_lo + c * ldh + k) = lv;
+    }
+}
+
+__device__ __forceinline__ const uint8_t * tc_frag(const LoopParams & P, const TcSmem & S, const TcBlock & b) {
+    return P.stationary ? S.w + b.sm_frag : b.frag + (size_t) blockIdx.x * b.cta_bytes;
+}
+__device__ __forceinline__ const float * tc_scale(const LoopParams & P, const TcSmem & S, const TcBlock & b) {
+    return P.stationary ? reinterpret_cast<const float *>(S.w + b.sm_scale)
+                        : b.scale + (size_t) blockIdx.x * b.cta_scales;
+}
+
+// C[r][col][c] (r < nt tiles starting at tile t0, col = row within the tile,
+// c = utterance) for the staged activations.
+__device__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = lane & 3, g = lane >> 2;
+    const int nkb = b.K >> 5;
+    const int kb0 = (warp * nkb) / kWarps, kb1 = ((warp + 1) * nkb) / kWarps;
+    const uint8_t * frag = tc_frag(P, S, b);
+    const float * scale = tc_scale(P, S, b);
+    float acc[kTcRmax][4];
+#pragma unroll
+    for (int r = 0; r < kTcRmax; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+    const int mrow = ((lane >> 3) & 1) * 8 + (lane & 7);
+    const int mk = (lane >> 4) * 8;
+    const __half * ahp = S.xs_hi + mrow * P.ldh + mk;
+    const __half * alp = S.xs_lo + mrow * P.ldh + mk;
+    for (int kb = kb0; kb < kb1; ++kb) {
+        uint32_t ah0[4], al0[4], ah1[4], al1[4];
+        ldsm_x4(ah0, ahp + kb * 32);
+        ldsm_x4(al0, alp + kb * 32);
+        ldsm_x4(ah1, ahp + kb * 32 + 16);
+        ldsm_x4(al1, alp + kb * 32 + 16);
+#pragma unroll
+        for (int r = 0; r < kTcRmax; ++r) {
+            if (r < nt) {
+                const size_t fi = (size_t) ((t0 + r) * nkb + kb) * 32 + lane;
+                if (b.is_i8) {
+                    const uint2 w = *reinterpret_cast<const uint2 *>(frag + fi * 8);
+                    const float2 sc = *reinterpret_cast<const float2 *>(
+                        scale + (size_t) ((t0 + r) * nkb + kb) * 8 + 2 * t);
+                    float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+                    uint32_t b0, b1;
+                    biased_i8x4_to_h2x2(w.x, b0, b1);
+                    mma16816(tmp, ah0, b0, b1);
+                    mma16816(tmp, al0, b0, b1);
+                    biased_i8x4_to_h2x2(w.y, b0, b1);
+                    mma16816(tmp, ah1, b0, b1);
+                    mma16816(tmp, al1, b0, b1);
+                    acc[r][0] = fmaf(sc.x, tmp[0], acc[r][0]);
+                    acc[r][1] = fmaf(sc.y, tmp[1], acc[r][1]);
+                    acc[r][2] = fmaf(sc.x, tmp[2], acc[r][2]);
+                    acc[r][3] = fmaf(sc.y, tmp[3], acc[r][3]);
+                } else {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(frag + fi * 16);
+                    mma16816(acc[r], ah0, w.x, w.y);
+                    mma16816(acc[r], al0, w.x, w.y);
+                    mma16816(acc[r], ah1, w.z, w.w);
+                    mma16816(acc[r], al1, w.z, w.w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kTcRmax; ++r) {
+        if (r < nt) {
+            float * pp = S.part + ((warp * kTcRmax + r) * 8) * 16;
+            pp[(2 * t) * 16 + g] = acc[r][0];
+            pp[(2 * t + 1) * 16 + g] = acc[r][1];
+            pp[(2 * t) * 16 + g + 8] = acc[r][2];
+            pp[(2 * t + 1) * 16 + g + 8] = acc[r][3];
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nt * 128; idx += blockDim.x) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) s += S.part[w * kTcRmax * 128 + idx];
+        S.C[idx] = s;
+    }
+    __syncthreads();
+}
+
+__device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcSmem & S) {
+    const int H = P.H, L = P.L, B = P.B;
+    const int upc = P.upc;
+    const int u0 = (int) blockIdx.x * upc;
+    const int nu = max(0, min(H, u0 + upc) - u0);
+    if (nu == 0) return;
+    const TcBlock & bk = P.tcl[l];
+    for (int cs = 0; cs < n_emit; cs += kTcM) {
+        const int nc = min(kTcM, n_emit - cs);
+        if (threadIdx.x < nc) {
+            const int utt = __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
+            const int tr = __ldcg(&P.emit[2 * (cs + threadIdx.x) + 1]);
+            S.s_utt[threadIdx.x] = utt;
+            S.s_aux[threadIdx.x] = tr & 0x7FFFFFFF;
+            S.s_aux2[threadIdx.x] = ((tr >> 31) & 1) | (__ldcg(&P.ust[utt * kUst + U_HBUF]) << 1);
+        }
+        __syncthreads();
+        if (l == 0) {
+            // X = h_prev of layer 0 (zero on reset); W_ih0 . embed comes from the g0 table
+            tc_stage(S, P.ldh, nc, H, [&](int c, int k) {
+                const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
+                if (reset) return make_float4(0.f, 0.f, 0.f, 0.f);
+                return __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) (hb ^ 1) * L + 0) * B + utt) * H + k));
+            });
+        } else {
+            // X = [h_new of layer l-1 | h_prev of layer l]
+            tc_stage(S, P.ldh, nc, 2 * H, [&](int c, int k) {
+                const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
+                if (k < H)
+                    return __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) hb * L + (l - 1)) * B + utt) * H + k));
+                if (reset) return make_float4(0.f, 0.f, 0.f, 0.f);
+                return __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) (hb ^ 1) * L + l) * B + utt) * H + (k - H)));
+            });
+        }
+        __syncthreads();
+        tc_gemm(P, S, bk, 0, bk.tiles);
+        // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
+        for (int idx = threadIdx.x; idx < nc * nu; idx += blockDim.x) {
+            const int cc = idx / nu, jj = idx - (idx / nu) * nu;
+            const int j = u0 + jj;
+            const int utt = S.s_utt[cc];
+            const int reset = S.s_aux2[cc] & 1, hb = S.s_aux2[cc] >> 1;
+            float gate[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int row = jj * 4 + q;
+                const float mm = S.C[(row >> 3) * 128 + (row & 7) * 16 + cc];
+                const int gr = q * H + j;
+                if (l == 0) {
+                    // ((b_ih + W_ih x) + b_hh) + W_hh h, with b_ih + W_ih x from the table
+                    const float gx = __ldg(P.g0 + (size_t) S.s_aux[cc] * 4 * H + gr);
+                    gate[q] = (gx + __ldg(P.b_hh[0] + gr)) + mm;
+                } else {
+                    gate[q] = (__ldg(P.b_ih[l] + gr) + __ldg(P.b_hh[l] + gr)) + mm;
+                }
+            }
+            const float i_g = sigmoid_ref(gate[0]);
+            const float f_g = sigmoid_ref(gate[1]);
+            const float g_g = tanhf(gate[2]);
+            const float o_g = sigmoid_ref(gate[3]);
+            float * cptr = P.c + ((size_t) l * B + utt) * H + j;
+            const float c_old = reset ? 0.0f : __ldcg(cptr);
+            const float c_new = f_g * c_old + i_g * g_g;
+            *cptr = c_new;
+            P.h[(((size_t) hb * L + l) * B + utt) * H + j] = o_g * tanhf(c_new);
+        }
+        __syncthreads();
+    }
+}
+
+__device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int sel, int n_live,
+                              const TcSmem & S) {
+    const int H = P.H, J = P.J, L = P.L, B = P.B;
+    const int rpc = P.rpc_p;
+    const int j0 = (int) blockIdx.x * rpc;
+    const int nr = max(0, min(J, j0 + rpc) - j0);
+    const int * live = P.live + (size_t) sel * B;
+    const int n_list = first ? n_live : n_emit;
+    if (nr > 0) {
+        for (int cs = 0; cs < n_list; cs += kTcM) {
+            const int nc = min(kTcM, n_list - cs);
+            if (threadIdx.x < nc) {
+                const int utt = first ? __ldcg(&live[cs + threadIdx.x]) : __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
+                S.s_utt[threadIdx.x] = utt;
+                S.s_aux2[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+            }
+            __syncthreads();
+            tc_stage(S, P.ldh, nc, H, [&](int c, int k) {
+                return __ldcg(reinterpret_cast<const float4 *>(
+                    P.h + (((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H + k));
+            });
+            __syncthreads();
+            for (int t0 = 0; t0 < P.tcp.tiles; t0 += kTcRmax) {
+                const int nt = min(kTcRmax, P.tcp.tiles - t0);
+                tc_gemm(P, S, P.tcp, t0, nt);
+                for (int idx = threadIdx.x; idx < nc * nt * 8; idx += blockDim.x) {
+                    const int cc = idx / (nt * 8), row = t0 * 8 + (idx - cc * nt * 8);
+                    if (row < nr) {
+                        const int r = row - t0 * 8;
+                        const int j = j0 + row;
+                        P.predp[(size_t) S.s_utt[cc] * J + j] =
+                            __ldg(P.pred_b + j) + S.C[(r >> 3) * 128 + (r & 7) * 16 + cc];
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        // hidden = relu((b_enc + W_enc enc_t) + (b_pred + W_pred pred)), :168-171
+        for (int idx = threadIdx.x; idx < n_live * nr; idx += blockDim.x) {
+            const int i = idx / nr, jj = idx - (idx / nr) * nr;
+            const int utt = __ldcg(&live[i]);
+            const int j = j0 + jj;
+            const int t = __ldcg(&P.ust[utt * kUst + U_T]);
+            const float v = __ldcg(P.encp + ((size_t) __ldg(P.frame_off + utt) + t) * J + j)
+                          + __ldcg(P.predp + (size_t) utt * J + j);
+            P.hid[(size_t) utt * J + j] = (0.0f < v) ? v : 0.0f;
+        }
+    }
+    trace_state_dump(P, first, sel);
+}
+
+__device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & S) {
+    const int J = P.J, B = P.B;
+    const int rpc = P.rpc_j;
+    const int r0 = (int) blockIdx.x * rpc;
+    const int nr = max(0, min(P.Vo, r0 + rpc) - r0);
+    if (nr == 0) return;
+    const int * live = P.live + (size_t) sel * B;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int cs = 0; cs < n_live; cs += kTcM) {
+        const int nc = min(kTcM, n_live - cs);
+        if (threadIdx.x < nc) {
+            const int utt = __ldcg(&live[cs + threadIdx.x]);
+            S.s_utt[threadIdx.x] = utt;
+            S.s_aux[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
+        }
+        __syncthreads();
+        tc_stage(S, P.ldh, nc, J, [&](int c, int k) {
+            return __ldcg(reinterpret_cast<const float4 *>(P.hid + (size_t) S.s_utt[c] * J + k));
+        });
+        __syncthreads();
+        for (int t0 = 0; t0 < P.tcj.tiles; t0 += kTcRmax) {
+            const int nt = min(kTcRmax, P.tcj.tiles - t0);
+            tc_gemm(P, S, P.tcj, t0, nt);
+            // warp w handles utterances w and w + 8; lanes walk the group's rows
+            for (int cc = warp; cc < nc; cc += kWarps) {
+                unsigned long long bt = 0ull, bd = 0ull;
+                for (int rr = lane; rr < nt * 8; rr += 32) {
+                    const int row = t0 * 8 + rr;
+                    if (row >= nr) continue;
+                    const int r = r0 + row;
+                    const float logit = __ldg(P.out_b + r) + S.C[(rr >> 3) * 128 + (rr & 7) * 16 + cc];
+                    if (P.trace_steps > 0) {
+                        const int step = S.s_aux[cc];
+                        if (step < P.trace_steps)
+                            P.tr_logits[((size_t) S.s_utt[cc] * P.trace_steps + step) * P.Vo + r] = logit;
+                    }
+                    if (r < P.V1) {
+                        const unsigned long long k = make_key(logit, r);
+                        bt = k > bt ? k : bt;
+                    } else {
+                        const unsigned long long k = make_key(logit, r - P.V1);
+                        bd = k > bd ? k : bd;
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long ot = __shfl_xor_sync(0xFFFFFFFFu, bt, o);
+                    const unsigned long long od = __shfl_xor_sync(0xFFFFFFFFu, bd, o);
+                    bt = ot > bt ? ot : bt;
+                    bd = od > bd ? od : bd;
+                }
+                if (lane == 0) {
+                    const int utt = S.s_utt[cc];
+                    if (bt) atomicMax(&P.keys[2 * utt + 0], bt);
+                    if (bd) atomicMax(&P.keys[2 * utt + 1], bd);
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// Copy this CTA's slice of every tensor-core weight block into shared memory.
+__device__ void tc_load_stationary(const LoopParams & P, const TcSmem & T) {
+    auto copy = [&](unsigned dst_off, const void * src, unsigned bytes) {
+        const uint4 * s4 = reinterpret_cast<const uint4 *>(src);
+        uint4 * d4 = reinterpret_cast<uint4 *>(T.w + dst_off);
+        for (unsigned i = threadIdx.x; i < bytes / 16; i += blockDim.x) d4[i] = __ldg(s4 + i);
+    };
+    auto block = [&](const TcBlock & b) {
+        copy(b.sm_frag, b.frag + (size_t) blockIdx.x * b.cta_bytes, b.cta_bytes);
+        if (b.is_i8) copy(b.sm_scale, b.scale + (size_t) blockIdx.x * b.cta_scales, b.cta_scales * 4u);
+    };
+    block(P.tcj);
+    block(P.tcp);
+    for (int l = 0; l < P.L; ++l) block(P.tcl[l]);
+    __syncthreads();
+}
+
+template <bool TC>
 __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams P) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int upc = (P.H + (int) gridDim.x - 1) / (int) gridDim.x;
-    const Smem S = carve(smem_raw, P, upc);
+    Smem S;
+    TcSmem T;
+    if constexpr (TC) {
+        T = tc_carve(smem_raw, P);
+        S = as_smem(T);
+    } else {
+        const int upc = (P.H + (int) gridDim.x - 1) / (int) gridDim.x;
+        S = carve(smem_raw, P, upc);
+    }
     unsigned gen = 0u;   // the host zeroes the barrier words before every launch
     if (blockIdx.x == 0 && threadIdx.x == 0) *P.t_start = gtimer();
     // Test hook (PK_OPT_TEST_STALL): CTA 0 never arrives, every other CTA's
     // first barrier wait runs out after timeout_ns and records PK_ERR_TIMEOUT.
     if (P.test_stall && blockIdx.x == 0) return;
+    if constexpr (TC) {
+        if (P.stationary) tc_load_stationary(P, T);
+    }
     bool first = true;
     for (int iter = 0;; ++iter) {
         // Every utterance advances its frame pointer at least once per
@@ -663,17 +1054,20 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         const int n_emit = __ldcg(&P.ctl[C_NEMIT]);
         if (n_emit > 0) {
             for (int l = 0; l < P.L; ++l) {
-                phase_lstm(P, l, n_emit, S);
+                if constexpr (TC) tc_phase_lstm(P, l, n_emit, T);
+                else phase_lstm(P, l, n_emit, S);
                 if (!grid_barrier(P, gen, S)) return;
             }
         }
         const int sel = __ldcg(&P.ctl[C_SEL]);
         const int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
-        phase_pred(P, first, n_emit, sel, n_live, S);
+        if constexpr (TC) tc_phase_pred(P, first, n_emit, sel, n_live, T);
+        else phase_pred(P, first, n_emit, sel, n_live, S);
         if (!grid_barrier(P, gen, S)) return;
         first = false;
         if (n_live == 0) break;
-        phase_joint(P, sel, n_live, S);
+        if constexpr (TC) tc_phase_joint(P, sel, n_live, T);
+        else phase_joint(P, sel, n_live, S);
         if (grid_arrive(P, S)) {
             leader_decide(P, S);
             grid_release(P, gen);
@@ -697,19 +1091,30 @@ size_t step_loop_smem_bytes(int chunk, int ldx, int H, int grid) {
     return off;
 }
 
-cudaError_t step_loop_configure(size_t smem) {
-    return cudaFuncSetAttribute(step_loop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int) smem);
+size_t step_loop_tc_smem_bytes(unsigned sm_weights, int ldh) {
+    size_t off = (sm_weights + 15) & ~15u;
+    off += 2 * (size_t) kTcM * ldh * 2;
+    off += (size_t) kWarps * kTcRmax * 128 * 4;
+    off += (size_t) kTcRmax * 128 * 4;
+    off += 3 * 32 * 4 + (kWarps + 2) * 4 + 4 * 4;
+    return off;
 }
 
-cudaError_t step_loop_occupancy(size_t smem, int * blocks_per_sm) {
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, step_loop_kernel, kThreads, smem);
+cudaError_t step_loop_configure(size_t smem, int tc) {
+    return tc ? cudaFuncSetAttribute(step_loop_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem)
+              : cudaFuncSetAttribute(step_loop_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+}
+
+cudaError_t step_loop_occupancy(size_t smem, int tc, int * blocks_per_sm) {
+    return tc ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, step_loop_kernel<true>, kThreads, smem)
+              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, step_loop_kernel<false>, kThreads, smem);
 }
 
 cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s) {
     void * args[] = {const_cast<LoopParams *>(&p)};
-    return cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(step_loop_kernel),
-                                       dim3(grid), dim3(kThreads), args, smem, s);
+    const void * fn = p.tc ? reinterpret_cast<const void *>(step_loop_kernel<true>)
+                           : reinterpret_cast<const void *>(step_loop_kernel<false>);
+    return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kThreads), args, smem, s);
 }
 
 }  // namespace pk

@@ -11,6 +11,7 @@ pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 CASES = ["tdt_small", "tdt_msym2", "eou_small"]
+MATHS = ["tc", "f32"]
 
 
 def split(flat, counts):
@@ -33,10 +34,11 @@ def load_case(pk, name):
 
 
 @pytest.mark.parametrize("name", CASES)
-def test_golden_batch(built, name):
+@pytest.mark.parametrize("math", MATHS)
+def test_golden_batch(built, name, math):
     pk = built
     m, g = load_case(pk, name)
-    dec = pk.Decoder(m)
+    dec = pk.Decoder(m, math=math)
     r = dec.decode_batch(g["enc"], g["offsets"], g["n_frames"], max_symbols=int(g["max_symbols"]))
     toks = split(g["tokens"], g["token_counts"])
     for b in range(len(g["n_frames"])):
@@ -49,10 +51,11 @@ def test_golden_batch(built, name):
 
 
 @pytest.mark.parametrize("name", CASES)
-def test_golden_stream_windows(built, name):
+@pytest.mark.parametrize("math", MATHS)
+def test_golden_stream_windows(built, name, math):
     pk = built
     m, g = load_case(pk, name)
-    dec = pk.Decoder(m)
+    dec = pk.Decoder(m, math=math)
     s = dec.stream()
     e0 = g["enc"][:g["n_frames"][0]]
     wt = split(g["win_tokens"], g["win_token_counts"])
@@ -66,12 +69,13 @@ def test_golden_stream_windows(built, name):
         assert np.array_equal(r["bounds"], wb[k])
 
 
-def test_tdt_0_6b_teacher_forced(built, orc):
+@pytest.mark.parametrize("math", MATHS)
+def test_tdt_0_6b_teacher_forced(built, orc, math):
     """Config 1 geometry (TDT-0.6b-v3, q8_0, B=1, T=125): per-step logits and
     LSTM state within 2e-3, argmax identical except at margins < 1e-3."""
     pk = built
     m = pk.synth.tdt_0_6b(seed=1234)
-    dec = pk.Decoder(m)
+    dec = pk.Decoder(m, math=math)
     o = orc.Oracle(m)
     enc, _ = pk.synth.encoder_batch([125], m.d_enc, seed=99)
     st = parity.teacher_forced(dec, o, enc)
@@ -81,10 +85,11 @@ def test_tdt_0_6b_teacher_forced(built, orc):
     parity.compare_free_running(dec, o, enc, [0], [125], r["tokens"], [st["oracle"]["tokens"]])
 
 
-def test_tdt_0_6b_ragged_batch(built, orc):
+@pytest.mark.parametrize("math", MATHS)
+def test_tdt_0_6b_ragged_batch(built, orc, math):
     pk = built
     m = pk.synth.tdt_0_6b(seed=7)
-    dec = pk.Decoder(m)
+    dec = pk.Decoder(m, math=math)
     o = orc.Oracle(m)
     T = np.array([125, 60, 1, 0, 90, 33, 200, 7], np.int32)
     enc, offs = pk.synth.encoder_batch(T, m.d_enc, seed=5)
@@ -97,10 +102,11 @@ def test_tdt_0_6b_ragged_batch(built, orc):
 
 
 @pytest.mark.parametrize("wtype", ["f16", "q8_0"])
-def test_tdt_1_1b(built, orc, wtype):
+@pytest.mark.parametrize("math", MATHS)
+def test_tdt_1_1b(built, orc, wtype, math):
     pk = built
     m = pk.synth.tdt_1_1b(seed=3, wtype=wtype)
-    dec = pk.Decoder(m)
+    dec = pk.Decoder(m, math=math)
     o = orc.Oracle(m)
     T = pk.synth.lengths_uniform(12, 1, 90, seed=4)
     enc, offs = pk.synth.encoder_batch(T, m.d_enc, seed=6)
@@ -111,11 +117,12 @@ def test_tdt_1_1b(built, orc, wtype):
     parity.assert_tf_ok(st, "1.1b")
 
 
-def test_eou_120m_batch(built, orc):
+@pytest.mark.parametrize("math", MATHS)
+def test_eou_120m_batch(built, orc, math):
     """Config 3 geometry: EOU f16, 1-layer LSTM, no duration head, T=50."""
     pk = built
     m = pk.synth.eou_120m(seed=5)
-    dec = pk.Decoder(m)
+    dec = pk.Decoder(m, math=math)
     o = orc.Oracle(m)
     T = np.full(24, 50, np.int32)
     enc, offs = pk.synth.encoder_batch(T, m.d_enc, seed=8)
@@ -127,12 +134,13 @@ def test_eou_120m_batch(built, orc):
     parity.assert_tf_ok(st, "eou")
 
 
-def test_many_chunks_small_model(built, orc):
+@pytest.mark.parametrize("math", MATHS)
+def test_many_chunks_small_model(built, orc, math):
     """B=300 crosses several 32-utterance chunks and exercises live-list compaction."""
     pk = built
     m = pk.synth.make_decoder("tdt", vocab_size=200, d_enc=128, pred_hidden=128, joint_hidden=128,
                               seed=31, blank_bias=1.5)
-    dec = pk.Decoder(m)
+    dec = pk.Decoder(m, math=math)
     o = orc.Oracle(m)
     T = pk.synth.lengths_uniform(300, 0, 60, seed=9)
     enc, offs = pk.synth.encoder_batch(T, m.d_enc, seed=10)
@@ -143,10 +151,11 @@ def test_many_chunks_small_model(built, orc):
     assert all(np.array_equal(a, b) for a, b in zip(r["tokens"], r2["tokens"]))  # determinism
 
 
-def test_stream_state_matches_oracle(built, orc):
+@pytest.mark.parametrize("math", MATHS)
+def test_stream_state_matches_oracle(built, orc, math):
     pk = built
     m, g = load_case(pk, "tdt_small")
-    dec = pk.Decoder(m)
+    dec = pk.Decoder(m, math=math)
     o = orc.Oracle(m)
     s = dec.stream()
     ost = o.new_state()

@@ -52,7 +52,9 @@ def noalloc(pk, dec, enc_dev, T, msym, cap=None, d_enc=None):
 
 def check_model(pk, m, enc, offs, T, msym):
     import torch
-    dec = pk.Decoder(m)
+    # the no-alloc entry point runs the CUDA-core f32 step loop: compare with the
+    # same kernel variant of pk_decode_batch
+    dec = pk.Decoder(m, math="f32")
     ref = dec.decode_batch(enc, offs, T, max_symbols=msym)
     # two calls in a row per utterance, longest first so a short call follows a long one
     for b in sorted(range(len(T)), key=lambda i: -int(T[i])):
