@@ -351,6 +351,7 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
     t_wall = time.perf_counter()
     tot_ms = loop_ms = enc_ms = 0.0
     tokens = steps = iters = emit_iters = launches = 0
+    phase = np.zeros(8)
     lat = None
     for _ in range(args.steps):
         r = call(batch_dev, res_dev())
@@ -362,6 +363,7 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
         iters += r.loop_iterations
         emit_iters += r.emit_iterations
         launches += r.kernel_launches
+        phase += np.array(r.phase_ms[:], np.float64)
         lat = r.encproj_ms + fin[:Bn].astype(np.float64)
     barrier()
     wall_s = time.perf_counter() - t_wall
@@ -408,6 +410,10 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
             "decode_split_ms_per_step": {"encproj": enc_ms / args.steps, "loop": loop_ms / args.steps,
                                          "total": tot_ms / args.steps},
             "loop_iterations_per_step": iters / args.steps,
+            "loop_us_per_iteration": {
+                name: 1e3 * (phase[2 * i] + phase[2 * i + 1]) / max(1, iters)
+                for i, name in enumerate(["lstm", "pred_hidden", "joint", "leader"])},
+            "loop_wait_share": float((phase[1::2].sum()) / max(phase.sum(), 1e-9)),
             "gpu_launches": int(launches),
             "clocks": clk,
             "wall_s_timed": wall_s,

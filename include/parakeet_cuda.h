@@ -187,6 +187,10 @@ typedef struct pk_result {
     int64_t   loop_iterations;    /* batched step-loop iterations */
     int64_t   emit_iterations;    /* iterations in which at least one utterance emitted (LSTM ran) */
     int64_t   kernel_launches;    /* device kernels this call launched */
+    double    phase_ms[8];        /* step-loop breakdown seen by CTA 0 (%globaltimer): for the LSTM,
+                                     pred/hidden, joint and leader segments, [2i] = CTA 0's own work,
+                                     [2i+1] = the rest of the segment (waiting for the slowest CTA
+                                     and the grid barrier) */
     double    encproj_ms;         /* device time of the enc-proj GEMM (CUDA events) */
     double    loop_ms;            /* device time of the persistent step loop */
     double    total_ms;           /* device time of the whole call incl. copies */

@@ -61,6 +61,7 @@ class pk_result(C.Structure):
                 ("tokens_needed", C.c_int64), ("eou_bounds_needed", C.c_int64),
                 ("total_steps", C.c_int64), ("loop_iterations", C.c_int64),
                 ("emit_iterations", C.c_int64), ("kernel_launches", C.c_int64),
+                ("phase_ms", C.c_double * 8),
                 ("encproj_ms", C.c_double), ("loop_ms", C.c_double), ("total_ms", C.c_double)]
 
 

@@ -84,6 +84,8 @@ struct pk_ctx {
     DevBuf embed, w_ih[pk::kMaxLayers], w_hh[pk::kMaxLayers], b_ih[pk::kMaxLayers],
         b_hh[pk::kMaxLayers], enc_w, enc_b, pred_w, pred_b, out_w, out_b, durations, special;
     // per-call workspace
+    DevBuf prof;
+    DevBuf livef, h16, hid16;
     DevBuf enc, encp, h, c, predp, hid, ust, keys, live, emit, ctl, bar, tstart, finish, tok,
         tokregion, bnd, bndregion, frameoff, offsets, boffsets, compact, bcompact;
     DevBuf tr_logits, tr_h, tr_c, tr_tok, tr_dur, tr_ftok, tr_fdur;
@@ -94,7 +96,7 @@ struct pk_ctx {
                                    &keys, &live, &emit, &ctl, &bar, &tstart, &finish, &tok,
                                    &tokregion, &bnd, &bndregion, &frameoff, &offsets, &boffsets,
                                    &compact, &bcompact, &tr_logits, &tr_h, &tr_c, &tr_tok, &tr_dur,
-                                   &tr_ftok, &tr_fdur, &g0};
+                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &h16, &hid16};
         for (int i = 0; i < 2 + pk::kMaxLayers; ++i) { v.push_back(&tc_frag[i]); v.push_back(&tc_scale[i]); }
         for (int l = 0; l < pk::kMaxLayers; ++l) {
             v.push_back(&w_ih[l]); v.push_back(&w_hh[l]); v.push_back(&b_ih[l]); v.push_back(&b_hh[l]);
@@ -394,6 +396,7 @@ struct Run {
     // outputs
     std::vector<int32_t> ust;
     std::vector<int32_t> ctl;
+    unsigned long long prof[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     float ms_encproj = 0.f, ms_loop = 0.f;
     int launches = 0;          // kernels launched by this call
 };
@@ -423,15 +426,23 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(x->encp.ensure((size_t) frames * J * 4));
     PK_CK(x->h.ensure(2 * (size_t) L * Bs * H * 4));
     PK_CK(x->c.ensure((size_t) L * Bs * H * 4));
+    const bool use_tc = x->math == PK_MATH_TC && x->tc_ok;
+    if (use_tc) {
+        PK_CK(x->h16.ensure(2 * 2 * (size_t) L * Bs * H * 2));
+        PK_CK(x->hid16.ensure(2 * Bs * J * 2));
+    }
     PK_CK(x->predp.ensure(Bs * J * 4));
     PK_CK(x->hid.ensure(Bs * J * 4));
     PK_CK(x->ust.ensure(Bs * kUst * 4));
     PK_CK(x->keys.ensure(Bs * 2 * 8));
     PK_CK(x->live.ensure(2 * Bs * 4));
+    PK_CK(x->livef.ensure(2 * Bs * 8));
     PK_CK(x->emit.ensure(2 * Bs * 4));
     PK_CK(x->ctl.ensure(kCtl * 4));
     PK_CK(x->bar.ensure(2 * 4));
     PK_CK(x->tstart.ensure(8));
+    PK_CK(x->prof.ensure(8 * 8));
+    PK_CK(cudaMemsetAsync(x->prof.p, 0, 8 * 8, x->stream));
     PK_CK(x->finish.ensure(Bs * 8));
     PK_CK(x->tok.ensure((size_t) std::max<int64_t>(tok_total, 1) * 4));
     PK_CK(x->tokregion.ensure(Bs * 8));
@@ -456,6 +467,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
 
     // Host-built initial per-utterance state and lists.
     std::vector<int32_t> ust((size_t) B * kUst, 0), live, emit;
+    std::vector<int64_t> live_frame;
     for (int b = 0; b < B; ++b) {
         int32_t * u = &ust[(size_t) b * kUst];
         u[U_T] = r.t0[b];
@@ -466,7 +478,10 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         u[U_NBEFORE] = r.nbefore[b];
         u[U_NFRAMES] = r.n_frames[b];
         u[U_SYMX] = r.symx[b];
-        if (r.n_frames[b] > 0 && r.t0[b] < r.n_frames[b]) live.push_back(b);
+        if (r.n_frames[b] > 0 && r.t0[b] < r.n_frames[b]) {
+            live.push_back(b);
+            live_frame.push_back(r.frame_off[b] + r.t0[b]);
+        }
         if (r.fresh[b]) { emit.push_back(b); emit.push_back(x->blank | (1 << 31)); }
     }
     std::vector<int32_t> ctl(kCtl, 0);
@@ -478,8 +493,10 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         PK_CK(cudaMemcpyAsync(x->frameoff.p, r.frame_off, (size_t) B * 8, cudaMemcpyHostToDevice, s));
         PK_CK(cudaMemcpyAsync(x->tokregion.p, tokregion.data(), (size_t) B * 8, cudaMemcpyHostToDevice, s));
         PK_CK(cudaMemcpyAsync(x->bndregion.p, bndregion.data(), (size_t) B * 8, cudaMemcpyHostToDevice, s));
-        if (!live.empty())
+        if (!live.empty()) {
             PK_CK(cudaMemcpyAsync(x->live.p, live.data(), live.size() * 4, cudaMemcpyHostToDevice, s));
+            PK_CK(cudaMemcpyAsync(x->livef.p, live_frame.data(), live_frame.size() * 8, cudaMemcpyHostToDevice, s));
+        }
         if (!emit.empty())
             PK_CK(cudaMemcpyAsync(x->emit.p, emit.data(), emit.size() * 4, cudaMemcpyHostToDevice, s));
         PK_CK(cudaMemsetAsync(x->keys.p, 0, (size_t) B * 16, s));
@@ -490,6 +507,11 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     if (r.h_in) {
         PK_CK(cudaMemcpyAsync(x->h.p, r.h_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
         PK_CK(cudaMemcpyAsync(x->c.p, r.c_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
+        if (use_tc) {   // hi / lo split of the resumed state (B == 1: buffer 0 is [L][H])
+            unsigned short * h16 = x->h16.as<unsigned short>();
+            PK_CK(launch_split_f16(r.h_in, h16, h16 + (size_t) 2 * L * H, (int64_t) L * H, s));
+            ++r.launches;
+        }
     }
 
     LoopParams P{};
@@ -499,9 +521,10 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     P.chunk = x->chunk; P.ldx = x->ldx; P.timeout_ns = x->timeout_ns;
     P.test_stall = x->test_stall;
     x->test_stall = 0;   // one-shot
-    const bool use_tc = x->math == PK_MATH_TC && x->tc_ok;
     if (use_tc) {
         P.tc = 1;
+        P.h16 = x->h16.as<unsigned short>();
+        P.hid16 = x->hid16.as<unsigned short>();
         P.stationary = x->tc_stationary;
         P.sm_weights = x->tc_sm_weights;
         P.ldh = x->tc_ldh;
@@ -527,8 +550,10 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     P.h = x->h.as<float>(); P.c = x->c.as<float>(); P.predp = x->predp.as<float>();
     P.hid = x->hid.as<float>(); P.ust = x->ust.as<int32_t>();
     P.keys = x->keys.as<unsigned long long>(); P.live = x->live.as<int32_t>();
+    P.live_frame = x->livef.as<int64_t>();
     P.emit = x->emit.as<int32_t>(); P.ctl = x->ctl.as<int32_t>(); P.bar = x->bar.as<unsigned>();
     P.t_start = x->tstart.as<unsigned long long>(); P.finish_ns = x->finish.as<unsigned long long>();
+    P.prof = x->prof.as<unsigned long long>();
     P.tok_out = x->tok.as<int32_t>(); P.tok_region = x->tokregion.as<int64_t>();
     P.bnd_out = x->bnd.as<int32_t>(); P.bnd_region = x->bndregion.as<int64_t>();
     if (r.trace && r.trace->max_steps > 0 && B > 0) {
@@ -570,6 +595,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     r.ctl.assign(kCtl, 0);
     if (B > 0) PK_CK(cudaMemcpyAsync(r.ust.data(), x->ust.p, (size_t) B * kUst * 4, cudaMemcpyDeviceToHost, s));
     PK_CK(cudaMemcpyAsync(r.ctl.data(), x->ctl.p, kCtl * 4, cudaMemcpyDeviceToHost, s));
+    PK_CK(cudaMemcpyAsync(r.prof, x->prof.p, 8 * 8, cudaMemcpyDeviceToHost, s));
     PK_CK(cudaStreamSynchronize(s));
     PK_CK(cudaEventElapsedTime(&r.ms_encproj, x->ev[1], x->ev[2]));
     PK_CK(cudaEventElapsedTime(&r.ms_loop, x->ev[3], x->ev[4]));
@@ -610,6 +636,7 @@ pk_status emit_results(pk_ctx * x, Run & r, pk_result * res) {
     res->total_steps = nsteps;
     res->loop_iterations = r.ctl[C_ITERS];
     res->emit_iterations = r.ctl[C_EMITITERS];
+    for (int i = 0; i < 8; ++i) res->phase_ms[i] = (double) r.prof[i] * 1e-6;
     res->encproj_ms = r.ms_encproj;
     res->loop_ms = r.ms_loop;
     if (ntok > res->tokens_cap || (ntok > 0 && !res->tokens))

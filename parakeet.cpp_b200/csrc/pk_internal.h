@@ -99,14 +99,18 @@ struct LoopParams {
     float * h;                 // [2][L][B][H]
     float * c;                 // [L][B][H]
     float * predp;             // [B][J]
-    float * hid;               // [B][J]
+    float * hid;               // [B][J] (CUDA-core phases)
+    unsigned short * h16;      // [2 (hi, lo)][2][L][B][H] f16 split of h (tensor-core phases)
+    unsigned short * hid16;    // [2 (hi, lo)][B][J] f16 split of the joint hidden (tensor-core phases)
     int32_t * ust;             // [B][kUst]
     unsigned long long * keys; // [B][2] packed argmax keys (token, duration)
     int32_t * live;            // [2][B]
-    int32_t * emit;            // [B][2]: utterance, token | reset << 31
+    int64_t * live_frame;      // [2][B] encoder row (frame_offset + t) of each live entry
+    int32_t * emit;            // [B][2]: utterance, token | h-buffer << 30 | reset << 31
     int32_t * ctl;             // [kCtl]
     unsigned int * bar;        // [2]: arrival count, generation
     unsigned long long * t_start;   // [1] globaltimer at loop start
+    unsigned long long * prof;      // [8] CTA 0 phase breakdown (ns), see pk_result::phase_ms
     unsigned long long * finish_ns; // [B]
     // outputs
     int32_t * tok_out;         // per-utterance regions
@@ -143,6 +147,9 @@ cudaError_t launch_scan(const int32_t * ust, int B, int field, int64_t * offsets
 cudaError_t launch_gather(const int32_t * ust, int B, int field, const int32_t * src,
                           const int64_t * region, const int64_t * offsets, int32_t * dst,
                           cudaStream_t s);
+// hi = f16(x), lo = f16(x - hi) for n floats.
+cudaError_t launch_split_f16(const float * src, unsigned short * hi, unsigned short * lo, int64_t n,
+                             cudaStream_t s);
 cudaError_t launch_extract_field(const int32_t * ust, int B, int field, int32_t * dst,
                                  cudaStream_t s);
 

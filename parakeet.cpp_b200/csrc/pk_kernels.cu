@@ -162,6 +162,16 @@ __global__ void gather_kernel(const int32_t * __restrict__ ust, int field,
     for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = s[i];
 }
 
+__global__ void split_f16_kernel(const float * __restrict__ src, __half * __restrict__ hi,
+                                 __half * __restrict__ lo, int64_t n) {
+    const int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float x = src[i];
+    const __half h = __float2half_rn(x);
+    hi[i] = h;
+    lo[i] = __float2half_rn(x - __half2float(h));
+}
+
 __global__ void extract_field_kernel(const int32_t * __restrict__ ust, int B, int field,
                                      int32_t * __restrict__ dst) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -199,6 +209,14 @@ cudaError_t launch_gather(const int32_t * ust, int B, int field, const int32_t *
                           cudaStream_t s) {
     if (B <= 0) return cudaSuccess;
     gather_kernel<<<B, 128, 0, s>>>(ust, field, src, region, offsets, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_split_f16(const float * src, unsigned short * hi, unsigned short * lo, int64_t n,
+                             cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    split_f16_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, s>>>(src, reinterpret_cast<__half *>(hi),
+                                                                reinterpret_cast<__half *>(lo), n);
     return cudaGetLastError();
 }
 

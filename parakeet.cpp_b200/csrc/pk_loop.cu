@@ -163,6 +163,32 @@ __device__ __forceinline__ int pow2ceil(int n) {
 
 __device__ __forceinline__ int lg2_pow2(int p) { return 31 - __clz(p); }
 
+// Stage rows [0, cp) x [0, K) of f32 activations into xs (row stride ldx);
+// rows >= nc are zero. Eight independent loads per thread are in flight.
+template <class F>
+__device__ __forceinline__ void stage_f32(float * xs, int ldx, int cp, int nc, int K, F src) {
+    const int k4n = K >> 2;
+    const int total = cp * k4n;
+    constexpr int U = 8;
+    for (int base = 0; base < total; base += U * blockDim.x) {
+        float4 vv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = base + u * blockDim.x + threadIdx.x;
+            const int c = idx / k4n;
+            vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (idx < total && c < nc) vv[u] = src(c, 4 * (idx - c * k4n));
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = base + u * blockDim.x + threadIdx.x;
+            if (idx >= total) break;
+            const int c = idx / k4n;
+            *reinterpret_cast<float4 *>(xs + c * ldx + 4 * (idx - c * k4n)) = vv[u];
+        }
+    }
+}
+
 // ---- grid barrier -------------------------------------------------------------
 
 __device__ __forceinline__ bool grid_arrive(const LoopParams & P, const Smem & S) {
@@ -283,29 +309,21 @@ __device__ void phase_lstm(const LoopParams & P, int l, int n_emit, const Smem &
             const int utt = __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
             const int tr = __ldcg(&P.emit[2 * (cs + threadIdx.x) + 1]);
             S.s_utt[threadIdx.x] = utt;
-            S.s_aux[threadIdx.x] = tr & 0x7FFFFFFF;                              // token
-            S.s_aux2[threadIdx.x] = ((tr >> 31) & 1) | (__ldcg(&P.ust[utt * kUst + U_HBUF]) << 1);
+            S.s_aux[threadIdx.x] = tr & 0x3FFFFFFF;                              // token
+            S.s_aux2[threadIdx.x] = ((tr >> 31) & 1) | (((tr >> 30) & 1) << 1);   // reset | hbuf << 1
         }
         __syncthreads();
-        const int k4n = K2 / 4;
-        for (int idx = threadIdx.x; idx < cp * k4n; idx += blockDim.x) {
-            const int cc = idx / k4n;
-            const int k = 4 * (idx - cc * k4n);
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (cc < nc) {
-                const int utt = S.s_utt[cc];
-                const int reset = S.s_aux2[cc] & 1, hb = S.s_aux2[cc] >> 1;
-                if (k < H) {
-                    if (l == 0)
-                        v = __ldg(reinterpret_cast<const float4 *>(P.embed + (size_t) S.s_aux[cc] * H + k));
-                    else
-                        v = __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) hb * L + (l - 1)) * B + utt) * H + k));
-                } else if (!reset) {
-                    v = __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) (hb ^ 1) * L + l) * B + utt) * H + (k - H)));
-                }
+        stage_f32(S.xs, P.ldx, cp, nc, K2, [&](int cc, int k) {
+            const int utt = S.s_utt[cc];
+            const int reset = S.s_aux2[cc] & 1, hb = S.s_aux2[cc] >> 1;
+            if (k < H) {
+                if (l == 0)
+                    return __ldg(reinterpret_cast<const float4 *>(P.embed + (size_t) S.s_aux[cc] * H + k));
+                return __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) hb * L + (l - 1)) * B + utt) * H + k));
             }
-            *reinterpret_cast<float4 *>(S.xs + cc * P.ldx + k) = v;
-        }
+            if (reset) return make_float4(0.f, 0.f, 0.f, 0.f);
+            return __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) (hb ^ 1) * L + l) * B + utt) * H + (k - H)));
+        });
         __syncthreads();
         switch (cp) {
             case 1: lstm_rows<1>(P, l, u0, nu, upc, nc, S); break;
@@ -334,6 +352,55 @@ __device__ void phase_lstm(const LoopParams & P, int l, int n_emit, const Smem &
             P.h[(((size_t) hb * L + l) * B + utt) * H + j] = o_g * tanhf(c_new);
         }
         __syncthreads();
+    }
+}
+
+// hidden = relu((b_enc + W_enc enc_t) + (b_pred + W_pred pred)) (parakeet_tdt.cpp:168-171)
+// for every live utterance and this CTA's joint-hidden rows [j0, j0 + nr). Loads
+// are issued four items at a time to keep several L2 requests in flight.
+__device__ void joint_hidden(const LoopParams & P, int sel, int n_live, int j0, int nr) {
+    const int J = P.J, B = P.B;
+    const int * live = P.live + (size_t) sel * B;
+    const long long * lframe = reinterpret_cast<const long long *>(P.live_frame) + (size_t) sel * B;
+    const int total = n_live * nr;
+    for (int base = 0; base < total; base += 4 * blockDim.x) {
+        int utt[4], j[4];
+        long long fr[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int idx = base + u * blockDim.x + threadIdx.x;
+            utt[u] = -1;
+            if (idx < total) {
+                const int i = idx / nr;
+                j[u] = j0 + (idx - i * nr);
+                utt[u] = __ldcg(&live[i]);
+                fr[u] = __ldcg(&lframe[i]);
+            }
+        }
+        float e[4], q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (utt[u] >= 0) {
+                e[u] = __ldcg(P.encp + (size_t) fr[u] * J + j[u]);
+                q[u] = __ldcg(P.predp + (size_t) utt[u] * J + j[u]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (utt[u] >= 0) {
+                const float v = e[u] + q[u];
+                const float hv = (0.0f < v) ? v : 0.0f;
+                if (P.tc) {
+                    const __half hh = __float2half_rn(hv);
+                    const __half hl = __float2half_rn(hv - __half2float(hh));
+                    const size_t o = (size_t) utt[u] * J + j[u];
+                    reinterpret_cast<__half *>(P.hid16)[o] = hh;
+                    reinterpret_cast<__half *>(P.hid16)[(size_t) B * J + o] = hl;
+                } else {
+                    P.hid[(size_t) utt[u] * J + j[u]] = hv;
+                }
+            }
+        }
     }
 }
 
@@ -387,22 +454,22 @@ __device__ void phase_pred(const LoopParams & P, bool first, int n_emit, int sel
             const int nc = min(P.chunk, n_list - cs);
             const int cp = pow2ceil(nc);
             if (threadIdx.x < nc) {
-                const int utt = first ? __ldcg(&live[cs + threadIdx.x])
-                                      : __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
+                int utt, hb;
+                if (first) {
+                    utt = __ldcg(&live[cs + threadIdx.x]);
+                    hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+                } else {
+                    utt = __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
+                    hb = (__ldcg(&P.emit[2 * (cs + threadIdx.x) + 1]) >> 30) & 1;
+                }
                 S.s_utt[threadIdx.x] = utt;
-                S.s_aux2[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+                S.s_aux2[threadIdx.x] = hb;
             }
             __syncthreads();
-            const int k4n = H / 4;
-            for (int idx = threadIdx.x; idx < cp * k4n; idx += blockDim.x) {
-                const int cc = idx / k4n;
-                const int k = 4 * (idx - cc * k4n);
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (cc < nc)
-                    v = __ldcg(reinterpret_cast<const float4 *>(
-                        P.h + (((size_t) S.s_aux2[cc] * L + (L - 1)) * B + S.s_utt[cc]) * H + k));
-                *reinterpret_cast<float4 *>(S.xs + cc * P.ldx + k) = v;
-            }
+            stage_f32(S.xs, P.ldx, cp, nc, H, [&](int cc, int k) {
+                return __ldcg(reinterpret_cast<const float4 *>(
+                    P.h + (((size_t) S.s_aux2[cc] * L + (L - 1)) * B + S.s_utt[cc]) * H + k));
+            });
             __syncthreads();
             switch (cp) {
                 case 1: pred_rows<1>(P, j0, nr, nc, S); break;
@@ -414,16 +481,7 @@ __device__ void phase_pred(const LoopParams & P, bool first, int n_emit, int sel
             }
             __syncthreads();
         }
-        // hidden = relu((b_enc + W_enc enc_t) + (b_pred + W_pred pred)), :168-171
-        for (int idx = threadIdx.x; idx < n_live * nr; idx += blockDim.x) {
-            const int i = idx / nr, jj = idx - (idx / nr) * nr;
-            const int utt = __ldcg(&live[i]);
-            const int j = j0 + jj;
-            const int t = __ldcg(&P.ust[utt * kUst + U_T]);
-            const float v = __ldcg(P.encp + ((size_t) __ldg(P.frame_off + utt) + t) * J + j)
-                          + __ldcg(P.predp + (size_t) utt * J + j);
-            P.hid[(size_t) utt * J + j] = (0.0f < v) ? v : 0.0f;
-        }
+        joint_hidden(P, sel, n_live, j0, nr);
     }
     trace_state_dump(P, first, sel);
 }
@@ -475,15 +533,9 @@ __device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Sme
             S.s_aux[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
         }
         __syncthreads();
-        const int k4n = J / 4;
-        for (int idx = threadIdx.x; idx < cp * k4n; idx += blockDim.x) {
-            const int cc = idx / k4n;
-            const int k = 4 * (idx - cc * k4n);
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (cc < nc)
-                v = __ldcg(reinterpret_cast<const float4 *>(P.hid + (size_t) S.s_utt[cc] * J + k));
-            *reinterpret_cast<float4 *>(S.xs + cc * P.ldx + k) = v;
-        }
+        stage_f32(S.xs, P.ldx, cp, nc, J, [&](int cc, int k) {
+            return __ldcg(reinterpret_cast<const float4 *>(P.hid + (size_t) S.s_utt[cc] * J + k));
+        });
         __syncthreads();
         unsigned long long bt = 0ull, bd = 0ull;
         switch (cp) {
@@ -531,7 +583,8 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
     const int msym = P.max_sym;
     for (int r0 = 0; r0 < n_live; r0 += blockDim.x) {
         const int i = r0 + threadIdx.x;
-        int e = 0, lv = 0, utt = -1, etok = 0, ereset = 0;
+        int e = 0, lv = 0, utt = -1, etok = 0, ereset = 0, ehb = 0;
+        long long lframe = 0;
         if (i < n_live) {
             utt = __ldcg(&live_in[i]);
             int * u = P.ust + utt * kUst;
@@ -618,11 +671,15 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
                     P.ctl[C_ERRINFO] = utt;
                 }
             }
-            if (e) u[U_HBUF] = __ldcg(&u[U_HBUF]) ^ 1;
+            if (e) {
+                ehb = __ldcg(&u[U_HBUF]) ^ 1;
+                u[U_HBUF] = ehb;
+            }
             u[U_T] = t;
             u[U_SYM] = sym;
             u[U_NTOK] = ntok;
             lv = t < T ? 1 : 0;
+            if (lv) lframe = __ldg(P.frame_off + utt) + t;
             if (!lv) P.finish_ns[utt] = gtimer();
         }
         int tot_e = 0, tot_l = 0;
@@ -630,9 +687,12 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
         const int pl = block_excl_scan(lv, S, tot_l);
         if (e) {
             P.emit[2 * (base_emit + pe)] = utt;
-            P.emit[2 * (base_emit + pe) + 1] = etok | (ereset << 31);
+            P.emit[2 * (base_emit + pe) + 1] = etok | (ehb << 30) | (ereset << 31);
         }
-        if (lv) live_out[base_live + pl] = utt;
+        if (lv) {
+            live_out[base_live + pl] = utt;
+            P.live_frame[(size_t) (sel ^ 1) * B + base_live + pl] = lframe;
+        }
         base_emit += tot_e;
         base_live += tot_l;
     }
@@ -720,27 +780,30 @@ __device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, u
     hi = *reinterpret_cast<uint32_t *>(&hb);
 }
 
-// Stage up to 16 utterances' f32 activations [c][0..K) as f16 hi / lo.
+__device__ __forceinline__ void cp_async16(void * smem, const void * gmem, bool valid) {
+    const unsigned sa = (unsigned) __cvta_generic_to_shared(smem);
+    const int sz = valid ? 16 : 0;   // src-size 0: zero-fill, nothing read
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(sa), "l"(gmem), "r"(sz) : "memory");
+}
+
+// Stage up to 16 utterances' pre-split activations (f16 hi / lo rows written by
+// the producing phase) with 16-byte cp.async copies, all in flight at once.
+// src(c, k) returns the hi row pointer at element k (nullptr: zeros); the lo
+// row is `lo_off` halves after it. The caller synchronises the CTA afterwards.
 template <class F>
-__device__ __forceinline__ void tc_stage(const TcSmem & S, int ldh, int nc, int K, F src) {
-    const int k4n = K >> 2;
-    for (int idx = threadIdx.x; idx < kTcM * k4n; idx += blockDim.x) {
-        const int c = idx / k4n;
-        const int k = 4 * (idx - c * k4n);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (c < nc) v = src(c, k);
-        const __half2 h01 = __floats2half2_rn(v.x, v.y);
-        const __half2 h23 = __floats2half2_rn(v.z, v.w);
-        const float2 f01 = __half22float2(h01);
-        const float2 f23 = __half22float2(h23);
-        const __half2 l01 = __floats2half2_rn(v.x - f01.x, v.y - f01.y);
-        const __half2 l23 = __floats2half2_rn(v.z - f23.x, v.w - f23.y);
-        uint2 hv, lv;
-        hv.x = *reinterpret_cast<const uint32_t *>(&h01); hv.y = *reinterpret_cast<const uint32_t *>(&h23);
-        lv.x = *reinterpret_cast<const uint32_t *>(&l01); lv.y = *reinterpret_cast<const uint32_t *>(&l23);
-        *reinterpret_cast<uint2 *>(S.xs_hi + c * ldh + k) = hv;
-        *reinterpret_cast<uint2 *>(S.xs_lo + c * ldh + k) = lv;
+__device__ __forceinline__ void tc_stage_async(const TcSmem & S, int ldh, int nc, int K, size_t lo_off,
+                                               const __half * dummy, F src) {
+    const int k8n = K >> 3;
+    const int total = kTcM * k8n;
+    for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
+        const int c = idx / k8n;
+        const int k = 8 * (idx - c * k8n);
+        const __half * g = c < nc ? src(c, k) : nullptr;
+        const bool ok = g != nullptr;
+        cp_async16(S.xs_hi + c * ldh + k, ok ? g : dummy, ok);
+        cp_async16(S.xs_lo + c * ldh + k, ok ? g + lo_off : dummy, ok);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 __device__ __forceinline__ const uint8_t * tc_frag(const LoopParams & P, const TcSmem & S, const TcBlock & b) {
@@ -836,58 +899,71 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
             const int utt = __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
             const int tr = __ldcg(&P.emit[2 * (cs + threadIdx.x) + 1]);
             S.s_utt[threadIdx.x] = utt;
-            S.s_aux[threadIdx.x] = tr & 0x7FFFFFFF;
-            S.s_aux2[threadIdx.x] = ((tr >> 31) & 1) | (__ldcg(&P.ust[utt * kUst + U_HBUF]) << 1);
+            S.s_aux[threadIdx.x] = tr & 0x3FFFFFFF;
+            S.s_aux2[threadIdx.x] = ((tr >> 31) & 1) | (((tr >> 30) & 1) << 1);
         }
         __syncthreads();
+        // Prefetch the cell-update operands (biases / layer-0 table rows and the
+        // old cell state) before the GEMM so their latency overlaps it. One
+        // (utterance, unit) pair per thread: nc * nu <= 16 * upc <= blockDim.
+        const int my = threadIdx.x;
+        const bool act = my < nc * nu;
+        const int cc = act ? my / nu : 0, jj = act ? my - (my / nu) * nu : 0;
+        const int j = u0 + jj;
+        float pre[4] = {0.f, 0.f, 0.f, 0.f};
+        float c_old = 0.0f;
+        if (act) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int gr = q * H + j;
+                // ((b_ih + W_ih x) + b_hh) + W_hh h, with b_ih + W_ih x for layer 0 from the table
+                pre[q] = (l == 0) ? __ldg(P.g0 + (size_t) S.s_aux[cc] * 4 * H + gr) + __ldg(P.b_hh[0] + gr)
+                                  : __ldg(P.b_ih[l] + gr) + __ldg(P.b_hh[l] + gr);
+            }
+            if (!(S.s_aux2[cc] & 1)) c_old = __ldcg(P.c + ((size_t) l * B + S.s_utt[cc]) * H + j);
+        }
+        const __half * h16 = reinterpret_cast<const __half *>(P.h16);
+        const size_t lo_off = (size_t) 2 * L * B * H;
         if (l == 0) {
             // X = h_prev of layer 0 (zero on reset); W_ih0 . embed comes from the g0 table
-            tc_stage(S, P.ldh, nc, H, [&](int c, int k) {
+            tc_stage_async(S, P.ldh, nc, H, lo_off, h16, [&](int c, int k) -> const __half * {
                 const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
-                if (reset) return make_float4(0.f, 0.f, 0.f, 0.f);
-                return __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) (hb ^ 1) * L + 0) * B + utt) * H + k));
+                if (reset) return nullptr;
+                return h16 + (((size_t) (hb ^ 1) * L + 0) * B + utt) * H + k;
             });
         } else {
             // X = [h_new of layer l-1 | h_prev of layer l]
-            tc_stage(S, P.ldh, nc, 2 * H, [&](int c, int k) {
+            tc_stage_async(S, P.ldh, nc, 2 * H, lo_off, h16, [&](int c, int k) -> const __half * {
                 const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
-                if (k < H)
-                    return __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) hb * L + (l - 1)) * B + utt) * H + k));
-                if (reset) return make_float4(0.f, 0.f, 0.f, 0.f);
-                return __ldcg(reinterpret_cast<const float4 *>(P.h + (((size_t) (hb ^ 1) * L + l) * B + utt) * H + (k - H)));
+                if (k < H) return h16 + (((size_t) hb * L + (l - 1)) * B + utt) * H + k;
+                if (reset) return nullptr;
+                return h16 + (((size_t) (hb ^ 1) * L + l) * B + utt) * H + (k - H);
             });
         }
         __syncthreads();
         tc_gemm(P, S, bk, 0, bk.tiles);
         // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
-        for (int idx = threadIdx.x; idx < nc * nu; idx += blockDim.x) {
-            const int cc = idx / nu, jj = idx - (idx / nu) * nu;
-            const int j = u0 + jj;
+        if (act) {
             const int utt = S.s_utt[cc];
-            const int reset = S.s_aux2[cc] & 1, hb = S.s_aux2[cc] >> 1;
+            const int hb = S.s_aux2[cc] >> 1;
             float gate[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const int row = jj * 4 + q;
-                const float mm = S.C[(row >> 3) * 128 + (row & 7) * 16 + cc];
-                const int gr = q * H + j;
-                if (l == 0) {
-                    // ((b_ih + W_ih x) + b_hh) + W_hh h, with b_ih + W_ih x from the table
-                    const float gx = __ldg(P.g0 + (size_t) S.s_aux[cc] * 4 * H + gr);
-                    gate[q] = (gx + __ldg(P.b_hh[0] + gr)) + mm;
-                } else {
-                    gate[q] = (__ldg(P.b_ih[l] + gr) + __ldg(P.b_hh[l] + gr)) + mm;
-                }
+                gate[q] = pre[q] + S.C[(row >> 3) * 128 + (row & 7) * 16 + cc];
             }
             const float i_g = sigmoid_ref(gate[0]);
             const float f_g = sigmoid_ref(gate[1]);
             const float g_g = tanhf(gate[2]);
             const float o_g = sigmoid_ref(gate[3]);
-            float * cptr = P.c + ((size_t) l * B + utt) * H + j;
-            const float c_old = reset ? 0.0f : __ldcg(cptr);
             const float c_new = f_g * c_old + i_g * g_g;
-            *cptr = c_new;
-            P.h[(((size_t) hb * L + l) * B + utt) * H + j] = o_g * tanhf(c_new);
+            P.c[((size_t) l * B + utt) * H + j] = c_new;
+            const float hn = o_g * tanhf(c_new);
+            const size_t o = (((size_t) hb * L + l) * B + utt) * H + j;
+            P.h[o] = hn;
+            const __half hh = __float2half_rn(hn);
+            reinterpret_cast<__half *>(P.h16)[o] = hh;
+            reinterpret_cast<__half *>(P.h16)[(size_t) 2 * L * B * H + o] = __float2half_rn(hn - __half2float(hh));
         }
         __syncthreads();
     }
@@ -905,14 +981,21 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
         for (int cs = 0; cs < n_list; cs += kTcM) {
             const int nc = min(kTcM, n_list - cs);
             if (threadIdx.x < nc) {
-                const int utt = first ? __ldcg(&live[cs + threadIdx.x]) : __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
+                int utt, hb;
+                if (first) {
+                    utt = __ldcg(&live[cs + threadIdx.x]);
+                    hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+                } else {
+                    utt = __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
+                    hb = (__ldcg(&P.emit[2 * (cs + threadIdx.x) + 1]) >> 30) & 1;
+                }
                 S.s_utt[threadIdx.x] = utt;
-                S.s_aux2[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+                S.s_aux2[threadIdx.x] = hb;
             }
             __syncthreads();
-            tc_stage(S, P.ldh, nc, H, [&](int c, int k) {
-                return __ldcg(reinterpret_cast<const float4 *>(
-                    P.h + (((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H + k));
+            const __half * h16 = reinterpret_cast<const __half *>(P.h16);
+            tc_stage_async(S, P.ldh, nc, H, (size_t) 2 * L * B * H, h16, [&](int c, int k) -> const __half * {
+                return h16 + (((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H + k;
             });
             __syncthreads();
             for (int t0 = 0; t0 < P.tcp.tiles; t0 += kTcRmax) {
@@ -930,16 +1013,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
                 __syncthreads();
             }
         }
-        // hidden = relu((b_enc + W_enc enc_t) + (b_pred + W_pred pred)), :168-171
-        for (int idx = threadIdx.x; idx < n_live * nr; idx += blockDim.x) {
-            const int i = idx / nr, jj = idx - (idx / nr) * nr;
-            const int utt = __ldcg(&live[i]);
-            const int j = j0 + jj;
-            const int t = __ldcg(&P.ust[utt * kUst + U_T]);
-            const float v = __ldcg(P.encp + ((size_t) __ldg(P.frame_off + utt) + t) * J + j)
-                          + __ldcg(P.predp + (size_t) utt * J + j);
-            P.hid[(size_t) utt * J + j] = (0.0f < v) ? v : 0.0f;
-        }
+        joint_hidden(P, sel, n_live, j0, nr);
     }
     trace_state_dump(P, first, sel);
 }
@@ -960,8 +1034,9 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
             S.s_aux[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
         }
         __syncthreads();
-        tc_stage(S, P.ldh, nc, J, [&](int c, int k) {
-            return __ldcg(reinterpret_cast<const float4 *>(P.hid + (size_t) S.s_utt[c] * J + k));
+        const __half * hid16 = reinterpret_cast<const __half *>(P.hid16);
+        tc_stage_async(S, P.ldh, nc, J, (size_t) B * J, hid16, [&](int c, int k) -> const __half * {
+            return hid16 + (size_t) S.s_utt[c] * J + k;
         });
         __syncthreads();
         for (int t0 = 0; t0 < P.tcj.tiles; t0 += kTcRmax) {
@@ -1044,6 +1119,17 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         if (P.stationary) tc_load_stationary(P, T);
     }
     bool first = true;
+    // CTA 0 timestamps: per segment, its own work and the wait that follows
+    const bool prof = blockIdx.x == 0 && threadIdx.x == 0 && P.prof != nullptr;
+    unsigned long long pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    unsigned long long tseg = prof ? gtimer() : 0ull;
+    auto mark = [&](int slot) {
+        if (prof) {
+            const unsigned long long now = gtimer();
+            pacc[slot] += now - tseg;
+            tseg = now;
+        }
+    };
     for (int iter = 0;; ++iter) {
         // Every utterance advances its frame pointer at least once per
         // (max_sym + 1) iterations, so this bound only trips on a bug.
@@ -1056,27 +1142,39 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             for (int l = 0; l < P.L; ++l) {
                 if constexpr (TC) tc_phase_lstm(P, l, n_emit, T);
                 else phase_lstm(P, l, n_emit, S);
+                __syncthreads();
+                mark(0);
                 if (!grid_barrier(P, gen, S)) return;
+                mark(1);
             }
         }
         const int sel = __ldcg(&P.ctl[C_SEL]);
         const int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
         if constexpr (TC) tc_phase_pred(P, first, n_emit, sel, n_live, T);
         else phase_pred(P, first, n_emit, sel, n_live, S);
+        __syncthreads();
+        mark(2);
         if (!grid_barrier(P, gen, S)) return;
+        mark(3);
         first = false;
         if (n_live == 0) break;
         if constexpr (TC) tc_phase_joint(P, sel, n_live, T);
         else phase_joint(P, sel, n_live, S);
+        __syncthreads();
+        mark(4);
         if (grid_arrive(P, S)) {
             leader_decide(P, S);
+            mark(6);
             grid_release(P, gen);
         } else if (!grid_wait(P, gen, S)) {
             return;
         }
+        mark(7);
         ++gen;
         if (__ldcg(&P.ctl[C_ERR]) != 0) return;
     }
+    if (prof)
+        for (int i = 0; i < 8; ++i) P.prof[i] = pacc[i];
 }
 
 }  // namespace

@@ -35,7 +35,7 @@ std::mutex g_mu;
 unsigned char * g_addr[kNaMaxDevices] = {};
 
 struct Layout {
-    size_t encp, h, c, predp, hid, ust, keys, live, emit, ctl, bar, tstart, finish, tokregion,
+    size_t encp, h, c, predp, hid, ust, keys, live, livef, emit, ctl, bar, tstart, finish, tokregion,
         bndregion, frameoff, bnd, total;
 };
 
@@ -53,6 +53,7 @@ Layout layout(int J, int H, int L) {
     o.ust = take(kUst * 4);
     o.keys = take(2 * 8);
     o.live = take(2 * 4);
+    o.livef = take(2 * 8);
     o.emit = take(2 * 4);
     o.ctl = take(kCtl * 4);
     o.bar = take(2 * 4);
@@ -79,6 +80,9 @@ __global__ void noalloc_init_kernel(unsigned char * base, Layout o, int T, int b
     int32_t * live = reinterpret_cast<int32_t *>(base + o.live);
     live[0] = 0;
     live[1] = 0;
+    int64_t * livef = reinterpret_cast<int64_t *>(base + o.livef);
+    livef[0] = 0;   // frame row of the live utterance: frame_offset 0 + t 0
+    livef[1] = 0;
     ctl[C_NLIVE0] = T > 0 ? 1 : 0;
     int32_t * emit = reinterpret_cast<int32_t *>(base + o.emit);
     emit[0] = 0;
@@ -174,6 +178,7 @@ extern "C" PK_API pk_status pk_decode_noalloc(pk_ctx * ctx, const float * enc, i
     P.ust = reinterpret_cast<int32_t *>(base + o.ust);
     P.keys = reinterpret_cast<unsigned long long *>(base + o.keys);
     P.live = reinterpret_cast<int32_t *>(base + o.live);
+    P.live_frame = reinterpret_cast<int64_t *>(base + o.livef);
     P.emit = reinterpret_cast<int32_t *>(base + o.emit);
     P.ctl = reinterpret_cast<int32_t *>(base + o.ctl);
     P.bar = reinterpret_cast<unsigned *>(base + o.bar);
