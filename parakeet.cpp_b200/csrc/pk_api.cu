@@ -439,7 +439,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(x->livef.ensure(2 * Bs * 8));
     PK_CK(x->emit.ensure(2 * Bs * 4));
     PK_CK(x->ctl.ensure(kCtl * 4));
-    PK_CK(x->bar.ensure(2 * 4));
+    PK_CK(x->bar.ensure(4 * 4));
     PK_CK(x->tstart.ensure(8));
     PK_CK(x->prof.ensure(8 * 8));
     PK_CK(cudaMemsetAsync(x->prof.p, 0, 8 * 8, x->stream));
@@ -503,7 +503,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         PK_CK(cudaMemsetAsync(x->finish.p, 0, (size_t) B * 8, s));
     }
     PK_CK(cudaMemcpyAsync(x->ctl.p, ctl.data(), kCtl * 4, cudaMemcpyHostToDevice, s));
-    PK_CK(cudaMemsetAsync(x->bar.p, 0, 8, s));
+    PK_CK(cudaMemsetAsync(x->bar.p, 0, 16, s));
     if (r.h_in) {
         PK_CK(cudaMemcpyAsync(x->h.p, r.h_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
         PK_CK(cudaMemcpyAsync(x->c.p, r.c_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));

@@ -45,6 +45,7 @@ enum CtlField : int {
 
 constexpr int kTcM = 16;         // utterances per tensor-core pass (mma M)
 constexpr int kTcRmax = 8;       // 8-row weight tiles per tensor-core GEMM group
+constexpr int kTcRec = 256;     // records staged in shared memory per block of a phase
 
 // One phase's weights in the tensor-core layout. Rows owned by CTA k are
 // padded to `tiles` tiles of 8 rows; per (tile, 32-wide K block, lane) the
@@ -108,7 +109,7 @@ struct LoopParams {
     int64_t * live_frame;      // [2][B] encoder row (frame_offset + t) of each live entry
     int32_t * emit;            // [B][2]: utterance, token | h-buffer << 30 | reset << 31
     int32_t * ctl;             // [kCtl]
-    unsigned int * bar;        // [2]: arrival count, generation
+    unsigned int * bar;        // [4]: counter-barrier arrivals, unused, leader arrivals, leader generation
     unsigned long long * t_start;   // [1] globaltimer at loop start
     unsigned long long * prof;      // [8] CTA 0 phase breakdown (ns), see pk_result::phase_ms
     unsigned long long * finish_ns; // [B]

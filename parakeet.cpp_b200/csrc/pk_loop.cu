@@ -189,35 +189,25 @@ __device__ __forceinline__ void stage_f32(float * xs, int ldx, int cp, int nc, i
     }
 }
 
-// ---- grid barrier -------------------------------------------------------------
+// ---- grid barriers -----------------------------------------------------------
+//
+// Two kinds, on separate words of P.bar (zeroed by the host before each launch):
+//  * counter barriers (bar[0]): a monotonically increasing arrival count. Each
+//    CTA arrives with one acq_rel add and waits until the count reaches
+//    (k + 1) * gridDim.x for its k-th counter barrier. Nothing is reset, so an
+//    arrival costs one atomic and a wait one acquire-load loop.
+//  * the leader barrier (bar[2] arrivals, bar[3] generation): the last CTA to
+//    arrive runs the control step, resets the arrival word and publishes the
+//    next generation with a release store; the others wait for it.
 
-__device__ __forceinline__ bool grid_arrive(const LoopParams & P, const Smem & S) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned old = atom_add_acq_rel(&P.bar[0], 1u);
-        S.s_flag[0] = (old == gridDim.x - 1) ? 1 : 0;
-    }
-    __syncthreads();
-    return S.s_flag[0] != 0;
-}
-
-__device__ __forceinline__ void grid_release(const LoopParams & P, unsigned gen) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        atomicExch(&P.bar[0], 0u);
-        __threadfence();
-        st_release(&P.bar[1], gen + 1u);
-    }
-    __syncthreads();
-}
-
-// Returns false if the wait ran out or an error was flagged.
-__device__ __forceinline__ bool grid_wait(const LoopParams & P, unsigned gen, const Smem & S) {
+// Returns false if the wait ran out or an error was flagged (thread 0 decides).
+template <typename Done>
+__device__ __forceinline__ bool bounded_wait(const LoopParams & P, const Smem & S, Done done) {
     if (threadIdx.x == 0) {
         int ok = 1;
         const unsigned long long t0 = gtimer();
         unsigned it = 0;
-        while (ld_acquire(&P.bar[1]) == gen) {
+        while (!done()) {
             if ((++it & 63u) == 0u) {
                 if (__ldcg(&P.ctl[C_ERR]) != 0) { ok = 0; break; }
                 if ((long long) (gtimer() - t0) > P.timeout_ns) {
@@ -233,14 +223,38 @@ __device__ __forceinline__ bool grid_wait(const LoopParams & P, unsigned gen, co
     return S.s_flag[1] != 0;
 }
 
-__device__ __forceinline__ bool grid_barrier(const LoopParams & P, unsigned & gen, const Smem & S) {
-    if (grid_arrive(P, S)) {
-        grid_release(P, gen);
-    } else if (!grid_wait(P, gen, S)) {
-        return false;
-    }
-    ++gen;
+// k-th counter barrier of this launch (k counts from 0 in every CTA alike).
+__device__ __forceinline__ bool grid_barrier(const LoopParams & P, unsigned & k, const Smem & S) {
+    __syncthreads();
+    const unsigned target = (k + 1u) * gridDim.x;
+    if (threadIdx.x == 0) atom_add_acq_rel(&P.bar[0], 1u);
+    ++k;
+    if (!bounded_wait(P, S, [&] { return (int) (ld_acquire(&P.bar[0]) - target) >= 0; })) return false;
     return __ldcg(&P.ctl[C_ERR]) == 0;
+}
+
+__device__ __forceinline__ bool leader_arrive(const LoopParams & P, const Smem & S) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned old = atom_add_acq_rel(&P.bar[2], 1u);
+        S.s_flag[0] = (old == gridDim.x - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    return S.s_flag[0] != 0;
+}
+
+__device__ __forceinline__ void leader_release(const LoopParams & P, unsigned gen) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        atomicExch(&P.bar[2], 0u);
+        __threadfence();
+        st_release(&P.bar[3], gen + 1u);
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ bool leader_wait(const LoopParams & P, unsigned gen, const Smem & S) {
+    return bounded_wait(P, S, [&] { return ld_acquire(&P.bar[3]) != gen; });
 }
 
 // Block-wide exclusive scan of one int per thread.
@@ -724,9 +738,9 @@ struct TcSmem {
     __half * xs_lo;                 // [16][ldh]
     float * part;                   // [kWarps][kTcRmax][8][16]
     float * C;                      // [kTcRmax][8][16]
-    int * s_utt;                    // [32]
-    int * s_aux;                    // [32]
-    int * s_aux2;                   // [32]
+    int * s_utt;                    // [kTcRec] records of the current block
+    int * s_aux;                    // [kTcRec]
+    int * s_aux2;                   // [kTcRec]
     int * s_scan;                   // [kWarps + 2]
     int * s_flag;                   // [4]
 };
@@ -740,15 +754,22 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     s.xs_lo = reinterpret_cast<__half *>(raw + off); off += (size_t) kTcM * P.ldh * 2;
     s.part = reinterpret_cast<float *>(raw + off); off += (size_t) kWarps * kTcRmax * 128 * 4;
     s.C = reinterpret_cast<float *>(raw + off); off += (size_t) kTcRmax * 128 * 4;
-    s.s_utt = reinterpret_cast<int *>(raw + off); off += 32 * 4;
-    s.s_aux = reinterpret_cast<int *>(raw + off); off += 32 * 4;
-    s.s_aux2 = reinterpret_cast<int *>(raw + off); off += 32 * 4;
+    s.s_utt = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
+    s.s_aux = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
+    s.s_aux2 = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * 4;
     s.s_flag = reinterpret_cast<int *>(raw + off);
     return s;
 }
 
 // The barrier / scan helpers only use s_scan and s_flag.
+// The same view with the record arrays advanced to the pass starting at record p.
+__device__ __forceinline__ TcSmem tc_pass(const TcSmem & T, int p) {
+    TcSmem q = T;
+    q.s_utt += p; q.s_aux += p; q.s_aux2 += p;
+    return q;
+}
+
 __device__ __forceinline__ Smem as_smem(const TcSmem & T) {
     Smem s{};
     s.s_utt = T.s_utt; s.s_aux = T.s_aux; s.s_aux2 = T.s_aux2; s.s_scan = T.s_scan; s.s_flag = T.s_flag;
@@ -886,23 +907,25 @@ __device__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & 
     __syncthreads();
 }
 
-__device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcSmem & S) {
+__device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcSmem & T) {
     const int H = P.H, L = P.L, B = P.B;
     const int upc = P.upc;
     const int u0 = (int) blockIdx.x * upc;
     const int nu = max(0, min(H, u0 + upc) - u0);
     if (nu == 0) return;
     const TcBlock & bk = P.tcl[l];
-    for (int cs = 0; cs < n_emit; cs += kTcM) {
-        const int nc = min(kTcM, n_emit - cs);
-        if (threadIdx.x < nc) {
-            const int utt = __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
-            const int tr = __ldcg(&P.emit[2 * (cs + threadIdx.x) + 1]);
-            S.s_utt[threadIdx.x] = utt;
-            S.s_aux[threadIdx.x] = tr & 0x3FFFFFFF;
-            S.s_aux2[threadIdx.x] = ((tr >> 31) & 1) | (((tr >> 30) & 1) << 1);
-        }
-        __syncthreads();
+    for (int rb = 0; rb < n_emit; rb += kTcRec) {
+      const int nrb = min(kTcRec, n_emit - rb);
+      for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
+          const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + rb + i);
+          T.s_utt[i] = e.x;
+          T.s_aux[i] = e.y & 0x3FFFFFFF;
+          T.s_aux2[i] = ((e.y >> 31) & 1) | (((e.y >> 30) & 1) << 1);
+      }
+      __syncthreads();
+      for (int cs = 0; cs < nrb; cs += kTcM) {
+        const int nc = min(kTcM, nrb - cs);
+        const TcSmem S = tc_pass(T, cs);
         // Prefetch the cell-update operands (biases / layer-0 table rows and the
         // old cell state) before the GEMM so their latency overlaps it. One
         // (utterance, unit) pair per thread: nc * nu <= 16 * upc <= blockDim.
@@ -966,11 +989,12 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
             reinterpret_cast<__half *>(P.h16)[(size_t) 2 * L * B * H + o] = __float2half_rn(hn - __half2float(hh));
         }
         __syncthreads();
+      }
     }
 }
 
 __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int sel, int n_live,
-                              const TcSmem & S) {
+                              const TcSmem & T) {
     const int H = P.H, J = P.J, L = P.L, B = P.B;
     const int rpc = P.rpc_p;
     const int j0 = (int) blockIdx.x * rpc;
@@ -978,21 +1002,25 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
     const int * live = P.live + (size_t) sel * B;
     const int n_list = first ? n_live : n_emit;
     if (nr > 0) {
-        for (int cs = 0; cs < n_list; cs += kTcM) {
-            const int nc = min(kTcM, n_list - cs);
-            if (threadIdx.x < nc) {
-                int utt, hb;
-                if (first) {
-                    utt = __ldcg(&live[cs + threadIdx.x]);
-                    hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
-                } else {
-                    utt = __ldcg(&P.emit[2 * (cs + threadIdx.x)]);
-                    hb = (__ldcg(&P.emit[2 * (cs + threadIdx.x) + 1]) >> 30) & 1;
-                }
-                S.s_utt[threadIdx.x] = utt;
-                S.s_aux2[threadIdx.x] = hb;
+      for (int rb = 0; rb < n_list; rb += kTcRec) {
+        const int nrb = min(kTcRec, n_list - rb);
+        for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
+            int utt, hb;
+            if (first) {
+                utt = __ldcg(&live[rb + i]);
+                hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+            } else {
+                const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + rb + i);
+                utt = e.x;
+                hb = (e.y >> 30) & 1;
             }
-            __syncthreads();
+            T.s_utt[i] = utt;
+            T.s_aux2[i] = hb;
+        }
+        __syncthreads();
+        for (int cs = 0; cs < nrb; cs += kTcM) {
+            const int nc = min(kTcM, nrb - cs);
+            const TcSmem S = tc_pass(T, cs);
             const __half * h16 = reinterpret_cast<const __half *>(P.h16);
             tc_stage_async(S, P.ldh, nc, H, (size_t) 2 * L * B * H, h16, [&](int c, int k) -> const __half * {
                 return h16 + (((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H + k;
@@ -1013,12 +1041,13 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
                 __syncthreads();
             }
         }
+      }
         joint_hidden(P, sel, n_live, j0, nr);
     }
     trace_state_dump(P, first, sel);
 }
 
-__device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & S) {
+__device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & T) {
     const int J = P.J, B = P.B;
     const int rpc = P.rpc_j;
     const int r0 = (int) blockIdx.x * rpc;
@@ -1026,14 +1055,17 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
     if (nr == 0) return;
     const int * live = P.live + (size_t) sel * B;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int cs = 0; cs < n_live; cs += kTcM) {
-        const int nc = min(kTcM, n_live - cs);
-        if (threadIdx.x < nc) {
-            const int utt = __ldcg(&live[cs + threadIdx.x]);
-            S.s_utt[threadIdx.x] = utt;
-            S.s_aux[threadIdx.x] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
-        }
-        __syncthreads();
+    for (int rb = 0; rb < n_live; rb += kTcRec) {
+      const int nrb = min(kTcRec, n_live - rb);
+      for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
+          const int utt = __ldcg(&live[rb + i]);
+          T.s_utt[i] = utt;
+          if (P.trace_steps > 0) T.s_aux[i] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
+      }
+      __syncthreads();
+      for (int cs = 0; cs < nrb; cs += kTcM) {
+        const int nc = min(kTcM, nrb - cs);
+        const TcSmem S = tc_pass(T, cs);
         const __half * hid16 = reinterpret_cast<const __half *>(P.hid16);
         tc_stage_async(S, P.ldh, nc, J, (size_t) B * J, hid16, [&](int c, int k) -> const __half * {
             return hid16 + (size_t) S.s_utt[c] * J + k;
@@ -1079,6 +1111,7 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
             __syncthreads();
         }
     }
+    }
 }
 
 // Copy this CTA's slice of every tensor-core weight block into shared memory.
@@ -1110,7 +1143,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         const int upc = (P.H + (int) gridDim.x - 1) / (int) gridDim.x;
         S = carve(smem_raw, P, upc);
     }
-    unsigned gen = 0u;   // the host zeroes the barrier words before every launch
+    unsigned gen = 0u;   // leader generations; the host zeroes the barrier words before every launch
+    unsigned nbar = 0u;  // counter barriers passed
     if (blockIdx.x == 0 && threadIdx.x == 0) *P.t_start = gtimer();
     // Test hook (PK_OPT_TEST_STALL): CTA 0 never arrives, every other CTA's
     // first barrier wait runs out after timeout_ns and records PK_ERR_TIMEOUT.
@@ -1144,7 +1178,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
                 else phase_lstm(P, l, n_emit, S);
                 __syncthreads();
                 mark(0);
-                if (!grid_barrier(P, gen, S)) return;
+                if (!grid_barrier(P, nbar, S)) return;
                 mark(1);
             }
         }
@@ -1154,7 +1188,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         else phase_pred(P, first, n_emit, sel, n_live, S);
         __syncthreads();
         mark(2);
-        if (!grid_barrier(P, gen, S)) return;
+        if (!grid_barrier(P, nbar, S)) return;
         mark(3);
         first = false;
         if (n_live == 0) break;
@@ -1162,11 +1196,11 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         else phase_joint(P, sel, n_live, S);
         __syncthreads();
         mark(4);
-        if (grid_arrive(P, S)) {
+        if (leader_arrive(P, S)) {
             leader_decide(P, S);
             mark(6);
-            grid_release(P, gen);
-        } else if (!grid_wait(P, gen, S)) {
+            leader_release(P, gen);
+        } else if (!leader_wait(P, gen, S)) {
             return;
         }
         mark(7);
@@ -1194,7 +1228,7 @@ size_t step_loop_tc_smem_bytes(unsigned sm_weights, int ldh) {
     off += 2 * (size_t) kTcM * ldh * 2;
     off += (size_t) kWarps * kTcRmax * 128 * 4;
     off += (size_t) kTcRmax * 128 * 4;
-    off += 3 * 32 * 4 + (kWarps + 2) * 4 + 4 * 4;
+    off += 3 * kTcRec * 4 + (kWarps + 2) * 4 + 4 * 4;
     return off;
 }
 

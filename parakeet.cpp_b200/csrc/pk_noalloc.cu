@@ -56,7 +56,7 @@ Layout layout(int J, int H, int L) {
     o.livef = take(2 * 8);
     o.emit = take(2 * 4);
     o.ctl = take(kCtl * 4);
-    o.bar = take(2 * 4);
+    o.bar = take(4 * 4);
     o.tstart = take(8);
     o.finish = take(8);
     o.tokregion = take(8);
@@ -94,6 +94,8 @@ __global__ void noalloc_init_kernel(unsigned char * base, Layout o, int T, int b
     unsigned * bar = reinterpret_cast<unsigned *>(base + o.bar);
     bar[0] = 0u;
     bar[1] = 0u;
+    bar[2] = 0u;
+    bar[3] = 0u;
     *reinterpret_cast<unsigned long long *>(base + o.finish) = 0ull;
     *reinterpret_cast<int64_t *>(base + o.tokregion) = 0;
     *reinterpret_cast<int64_t *>(base + o.bndregion) = 0;
