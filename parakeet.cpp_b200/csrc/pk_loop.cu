@@ -743,6 +743,8 @@ struct TcSmem {
     int * s_aux2;                   // [kTcRec]
     int * s_scan;                   // [kWarps + 2]
     int * s_flag;                   // [4]
+    float * bj;                     // [rpc_j] this CTA's joint-out bias slice
+    float * bp;                     // [rpc_p] this CTA's pred-proj bias slice
 };
 
 __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams & P) {
@@ -758,7 +760,9 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     s.s_aux = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_aux2 = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * 4;
-    s.s_flag = reinterpret_cast<int *>(raw + off);
+    s.s_flag = reinterpret_cast<int *>(raw + off); off += 4 * 4;
+    s.bj = reinterpret_cast<float *>(raw + off); off += (size_t) P.rpc_j * 4;
+    s.bp = reinterpret_cast<float *>(raw + off);
     return s;
 }
 
@@ -779,11 +783,12 @@ __device__ __forceinline__ Smem as_smem(const TcSmem & T) {
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const __half * p) {
     const unsigned a = (unsigned) __cvta_generic_to_shared(p);
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a) : "memory");
 }
 
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+    // no side effects beyond its registers: left free for the scheduler
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
                  "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -801,28 +806,36 @@ __device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, u
     hi = *reinterpret_cast<uint32_t *>(&hb);
 }
 
-__device__ __forceinline__ void cp_async16(void * smem, const void * gmem, bool valid) {
+__device__ __forceinline__ void cp_async16(void * smem, const void * gmem) {
     const unsigned sa = (unsigned) __cvta_generic_to_shared(smem);
-    const int sz = valid ? 16 : 0;   // src-size 0: zero-fill, nothing read
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(sa), "l"(gmem), "r"(sz) : "memory");
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(sa), "l"(gmem) : "memory");
 }
 
-// Stage up to 16 utterances' pre-split activations (f16 hi / lo rows written by
-// the producing phase) with 16-byte cp.async copies, all in flight at once.
-// src(c, k) returns the hi row pointer at element k (nullptr: zeros); the lo
-// row is `lo_off` halves after it. The caller synchronises the CTA afterwards.
-template <class F>
-__device__ __forceinline__ void tc_stage_async(const TcSmem & S, int ldh, int nc, int K, size_t lo_off,
-                                               const __half * dummy, F src) {
+// Stage rows [0, nc) of the activation tile (f16 hi and lo halves, K columns)
+// into xs_hi / xs_lo; src(c, k) gives row c's 8 columns at k in the hi array
+// (the lo array is lo_off elements further on), or nullptr for a zero row.
+// Rows nc..15 keep whatever they held: every row of an mma output depends on
+// its own A row only, and outputs of rows >= nc are never read. Each thread
+// keeps one 16-byte column slot for the whole call (K <= 8 * blockDim.x).
+template <typename F>
+__device__ __forceinline__ void tc_stage_async(const TcSmem & S, int ldh, int nc, int K, size_t lo_off, F src) {
     const int k8n = K >> 3;
-    const int total = kTcM * k8n;
-    for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
-        const int c = idx / k8n;
-        const int k = 8 * (idx - c * k8n);
-        const __half * g = c < nc ? src(c, k) : nullptr;
-        const bool ok = g != nullptr;
-        cp_async16(S.xs_hi + c * ldh + k, ok ? g : dummy, ok);
-        cp_async16(S.xs_lo + c * ldh + k, ok ? g + lo_off : dummy, ok);
+    const int rpr = (int) blockDim.x / k8n;              // rows per round
+    const int c0 = (int) threadIdx.x / k8n;
+    const int k = 8 * ((int) threadIdx.x - c0 * k8n);
+    if (c0 < rpr) {
+        for (int c = c0; c < nc; c += rpr) {
+            const __half * g = src(c, k);
+            __half * dh = S.xs_hi + c * ldh + k;
+            __half * dl = S.xs_lo + c * ldh + k;
+            if (g != nullptr) {
+                cp_async16(dh, g);
+                cp_async16(dl, g + lo_off);
+            } else {
+                *reinterpret_cast<uint4 *>(dh) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4 *>(dl) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
 }
@@ -835,76 +848,107 @@ __device__ __forceinline__ const float * tc_scale(const LoopParams & P, const Tc
                         : b.scale + (size_t) blockIdx.x * b.cta_scales;
 }
 
-// C[r][col][c] (r < nt tiles starting at tile t0, col = row within the tile,
-// c = utterance) for the staged activations.
-__device__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt) {
+// C[r][col][c] (r < NT tiles starting at tile t0, col = row within the tile,
+// c = utterance) for the staged activations. Each warp takes a 1/8 slice of
+// the K blocks for all NT tiles; the slices are summed through shared memory.
+// NT is a compile-time constant so the per-tile work carries no predicates.
+template <int NT>
+__device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = lane & 3, g = lane >> 2;
     const int nkb = b.K >> 5;
     const int kb0 = (warp * nkb) / kWarps, kb1 = ((warp + 1) * nkb) / kWarps;
     const uint8_t * frag = tc_frag(P, S, b);
     const float * scale = tc_scale(P, S, b);
-    float acc[kTcRmax][4];
+    float acc[NT][4];
 #pragma unroll
-    for (int r = 0; r < kTcRmax; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+    for (int r = 0; r < NT; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
     const int mrow = ((lane >> 3) & 1) * 8 + (lane & 7);
     const int mk = (lane >> 4) * 8;
     const __half * ahp = S.xs_hi + mrow * P.ldh + mk;
     const __half * alp = S.xs_lo + mrow * P.ldh + mk;
-    for (int kb = kb0; kb < kb1; ++kb) {
-        uint32_t ah0[4], al0[4], ah1[4], al1[4];
-        ldsm_x4(ah0, ahp + kb * 32);
-        ldsm_x4(al0, alp + kb * 32);
-        ldsm_x4(ah1, ahp + kb * 32 + 16);
-        ldsm_x4(al1, alp + kb * 32 + 16);
+    if (b.is_i8) {
+        for (int kb = kb0; kb < kb1; ++kb) {
+            uint32_t ah0[4], al0[4], ah1[4], al1[4];
+            ldsm_x4(ah0, ahp + kb * 32);
+            ldsm_x4(al0, alp + kb * 32);
+            ldsm_x4(ah1, ahp + kb * 32 + 16);
+            ldsm_x4(al1, alp + kb * 32 + 16);
 #pragma unroll
-        for (int r = 0; r < kTcRmax; ++r) {
-            if (r < nt) {
-                const size_t fi = (size_t) ((t0 + r) * nkb + kb) * 32 + lane;
-                if (b.is_i8) {
-                    const uint2 w = *reinterpret_cast<const uint2 *>(frag + fi * 8);
-                    const float2 sc = *reinterpret_cast<const float2 *>(
-                        scale + (size_t) ((t0 + r) * nkb + kb) * 8 + 2 * t);
-                    float tmp[4] = {0.f, 0.f, 0.f, 0.f};
-                    uint32_t b0, b1;
-                    biased_i8x4_to_h2x2(w.x, b0, b1);
-                    mma16816(tmp, ah0, b0, b1);
-                    mma16816(tmp, al0, b0, b1);
-                    biased_i8x4_to_h2x2(w.y, b0, b1);
-                    mma16816(tmp, ah1, b0, b1);
-                    mma16816(tmp, al1, b0, b1);
-                    acc[r][0] = fmaf(sc.x, tmp[0], acc[r][0]);
-                    acc[r][1] = fmaf(sc.y, tmp[1], acc[r][1]);
-                    acc[r][2] = fmaf(sc.x, tmp[2], acc[r][2]);
-                    acc[r][3] = fmaf(sc.y, tmp[3], acc[r][3]);
-                } else {
-                    const uint4 w = *reinterpret_cast<const uint4 *>(frag + fi * 16);
-                    mma16816(acc[r], ah0, w.x, w.y);
-                    mma16816(acc[r], al0, w.x, w.y);
-                    mma16816(acc[r], ah1, w.z, w.w);
-                    mma16816(acc[r], al1, w.z, w.w);
-                }
+            for (int r = 0; r < NT; ++r) {
+                const size_t u = (size_t) (t0 + r) * nkb + kb;
+                const uint2 w = *reinterpret_cast<const uint2 *>(frag + (u * 32 + lane) * 8);
+                const float2 sc = *reinterpret_cast<const float2 *>(scale + u * 8 + 2 * t);
+                // two independent chains (hi, lo) of two k16 steps each; the
+                // q8_0 block scale is applied to their sum
+                float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
+                uint32_t b0, b1, b2, b3;
+                biased_i8x4_to_h2x2(w.x, b0, b1);
+                biased_i8x4_to_h2x2(w.y, b2, b3);
+                mma16816(th, ah0, b0, b1);
+                mma16816(tl, al0, b0, b1);
+                mma16816(th, ah1, b2, b3);
+                mma16816(tl, al1, b2, b3);
+                acc[r][0] = fmaf(sc.x, th[0] + tl[0], acc[r][0]);
+                acc[r][1] = fmaf(sc.y, th[1] + tl[1], acc[r][1]);
+                acc[r][2] = fmaf(sc.x, th[2] + tl[2], acc[r][2]);
+                acc[r][3] = fmaf(sc.y, th[3] + tl[3], acc[r][3]);
             }
         }
+    } else {
+        float accl[NT][4];   // lo-half chain
+#pragma unroll
+        for (int r = 0; r < NT; ++r) accl[r][0] = accl[r][1] = accl[r][2] = accl[r][3] = 0.0f;
+        for (int kb = kb0; kb < kb1; ++kb) {
+            uint32_t ah0[4], al0[4], ah1[4], al1[4];
+            ldsm_x4(ah0, ahp + kb * 32);
+            ldsm_x4(al0, alp + kb * 32);
+            ldsm_x4(ah1, ahp + kb * 32 + 16);
+            ldsm_x4(al1, alp + kb * 32 + 16);
+#pragma unroll
+            for (int r = 0; r < NT; ++r) {
+                const size_t u = (size_t) (t0 + r) * nkb + kb;
+                const uint4 w = *reinterpret_cast<const uint4 *>(frag + (u * 32 + lane) * 16);
+                mma16816(acc[r], ah0, w.x, w.y);
+                mma16816(accl[r], al0, w.x, w.y);
+                mma16816(acc[r], ah1, w.z, w.w);
+                mma16816(accl[r], al1, w.z, w.w);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < NT; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[r][q] += accl[r][q];
     }
 #pragma unroll
-    for (int r = 0; r < kTcRmax; ++r) {
-        if (r < nt) {
-            float * pp = S.part + ((warp * kTcRmax + r) * 8) * 16;
-            pp[(2 * t) * 16 + g] = acc[r][0];
-            pp[(2 * t + 1) * 16 + g] = acc[r][1];
-            pp[(2 * t) * 16 + g + 8] = acc[r][2];
-            pp[(2 * t + 1) * 16 + g + 8] = acc[r][3];
-        }
+    for (int r = 0; r < NT; ++r) {
+        float * pp = S.part + ((warp * kTcRmax + r) * 8) * 16;
+        pp[(2 * t) * 16 + g] = acc[r][0];
+        pp[(2 * t + 1) * 16 + g] = acc[r][1];
+        pp[(2 * t) * 16 + g + 8] = acc[r][2];
+        pp[(2 * t + 1) * 16 + g + 8] = acc[r][3];
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < nt * 128; idx += blockDim.x) {
+    for (int idx = threadIdx.x; idx < NT * 128; idx += blockDim.x) {
         float s = 0.0f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) s += S.part[w * kTcRmax * 128 + idx];
         S.C[idx] = s;
     }
     __syncthreads();
+}
+
+__device__ __forceinline__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt) {
+    switch (nt) {
+        case 1: tc_gemm_nt<1>(P, S, b, t0); break;
+        case 2: tc_gemm_nt<2>(P, S, b, t0); break;
+        case 3: tc_gemm_nt<3>(P, S, b, t0); break;
+        case 4: tc_gemm_nt<4>(P, S, b, t0); break;
+        case 5: tc_gemm_nt<5>(P, S, b, t0); break;
+        case 6: tc_gemm_nt<6>(P, S, b, t0); break;
+        case 7: tc_gemm_nt<7>(P, S, b, t0); break;
+        default: tc_gemm_nt<8>(P, S, b, t0); break;
+    }
 }
 
 __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcSmem & T) {
@@ -949,14 +993,14 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
         const size_t lo_off = (size_t) 2 * L * B * H;
         if (l == 0) {
             // X = h_prev of layer 0 (zero on reset); W_ih0 . embed comes from the g0 table
-            tc_stage_async(S, P.ldh, nc, H, lo_off, h16, [&](int c, int k) -> const __half * {
+            tc_stage_async(S, P.ldh, nc, H, lo_off, [&](int c, int k) -> const __half * {
                 const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
                 if (reset) return nullptr;
                 return h16 + (((size_t) (hb ^ 1) * L + 0) * B + utt) * H + k;
             });
         } else {
             // X = [h_new of layer l-1 | h_prev of layer l]
-            tc_stage_async(S, P.ldh, nc, 2 * H, lo_off, h16, [&](int c, int k) -> const __half * {
+            tc_stage_async(S, P.ldh, nc, 2 * H, lo_off, [&](int c, int k) -> const __half * {
                 const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
                 if (k < H) return h16 + (((size_t) hb * L + (l - 1)) * B + utt) * H + k;
                 if (reset) return nullptr;
@@ -1022,7 +1066,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             const int nc = min(kTcM, nrb - cs);
             const TcSmem S = tc_pass(T, cs);
             const __half * h16 = reinterpret_cast<const __half *>(P.h16);
-            tc_stage_async(S, P.ldh, nc, H, (size_t) 2 * L * B * H, h16, [&](int c, int k) -> const __half * {
+            tc_stage_async(S, P.ldh, nc, H, (size_t) 2 * L * B * H, [&](int c, int k) -> const __half * {
                 return h16 + (((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H + k;
             });
             __syncthreads();
@@ -1034,8 +1078,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
                     if (row < nr) {
                         const int r = row - t0 * 8;
                         const int j = j0 + row;
-                        P.predp[(size_t) S.s_utt[cc] * J + j] =
-                            __ldg(P.pred_b + j) + S.C[(r >> 3) * 128 + (r & 7) * 16 + cc];
+                        P.predp[(size_t) S.s_utt[cc] * J + j] = S.bp[row] + S.C[(r >> 3) * 128 + (r & 7) * 16 + cc];
                     }
                 }
                 __syncthreads();
@@ -1067,7 +1110,7 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
         const int nc = min(kTcM, nrb - cs);
         const TcSmem S = tc_pass(T, cs);
         const __half * hid16 = reinterpret_cast<const __half *>(P.hid16);
-        tc_stage_async(S, P.ldh, nc, J, (size_t) B * J, hid16, [&](int c, int k) -> const __half * {
+        tc_stage_async(S, P.ldh, nc, J, (size_t) B * J, [&](int c, int k) -> const __half * {
             return hid16 + (size_t) S.s_utt[c] * J + k;
         });
         __syncthreads();
@@ -1081,7 +1124,7 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
                     const int row = t0 * 8 + rr;
                     if (row >= nr) continue;
                     const int r = r0 + row;
-                    const float logit = __ldg(P.out_b + r) + S.C[(rr >> 3) * 128 + (rr & 7) * 16 + cc];
+                    const float logit = S.bj[row] + S.C[(rr >> 3) * 128 + (rr & 7) * 16 + cc];
                     if (P.trace_steps > 0) {
                         const int step = S.s_aux[cc];
                         if (step < P.trace_steps)
@@ -1150,6 +1193,20 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
     // first barrier wait runs out after timeout_ns and records PK_ERR_TIMEOUT.
     if (P.test_stall && blockIdx.x == 0) return;
     if constexpr (TC) {
+        // activation rows that a pass does not stage keep finite (zero) values
+        for (int i = threadIdx.x; i < kTcM * P.ldh / 8; i += blockDim.x) {
+            reinterpret_cast<uint4 *>(T.xs_hi)[i] = make_uint4(0u, 0u, 0u, 0u);
+            reinterpret_cast<uint4 *>(T.xs_lo)[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        for (int i = threadIdx.x; i < P.rpc_j; i += blockDim.x) {
+            const int r = (int) blockIdx.x * P.rpc_j + i;
+            T.bj[i] = r < P.Vo ? __ldg(P.out_b + r) : 0.0f;
+        }
+        for (int i = threadIdx.x; i < P.rpc_p; i += blockDim.x) {
+            const int j = (int) blockIdx.x * P.rpc_p + i;
+            T.bp[i] = j < P.J ? __ldg(P.pred_b + j) : 0.0f;
+        }
+        __syncthreads();
         if (P.stationary) tc_load_stationary(P, T);
     }
     bool first = true;
@@ -1223,12 +1280,13 @@ size_t step_loop_smem_bytes(int chunk, int ldx, int H, int grid) {
     return off;
 }
 
-size_t step_loop_tc_smem_bytes(unsigned sm_weights, int ldh) {
+size_t step_loop_tc_smem_bytes(unsigned sm_weights, int ldh, int rpc_j, int rpc_p) {
     size_t off = (sm_weights + 15) & ~15u;
     off += 2 * (size_t) kTcM * ldh * 2;
     off += (size_t) kWarps * kTcRmax * 128 * 4;
     off += (size_t) kTcRmax * 128 * 4;
     off += 3 * kTcRec * 4 + (kWarps + 2) * 4 + 4 * 4;
+    off += (size_t) (rpc_j + rpc_p) * 4;
     return off;
 }
 
