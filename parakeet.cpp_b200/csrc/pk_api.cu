@@ -328,14 +328,14 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
     const int kmax = std::max(std::max(J, H), L > 1 ? 2 * H : H);
     if (kmax > 8 * kThreads) return PK_OK;   // one 16-byte staging slot per thread and row
     x->tc_ldh = kmax + 8;
-    size_t need = step_loop_tc_smem_bytes(off, x->tc_ldh, rpc_j, rpc_p);
+    size_t need = step_loop_tc_smem_bytes(off, x->tc_ldh, rpc_j, rpc_p, upc);
     if (need <= smem_cap) {
         x->tc_stationary = 1;
         x->tc_sm_weights = off;
     } else {
         x->tc_stationary = 0;
         x->tc_sm_weights = 0;
-        need = step_loop_tc_smem_bytes(0, x->tc_ldh, rpc_j, rpc_p);
+        need = step_loop_tc_smem_bytes(0, x->tc_ldh, rpc_j, rpc_p, upc);
         if (need > smem_cap) return PK_OK;
     }
     x->tc_smem = need;

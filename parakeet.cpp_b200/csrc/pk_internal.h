@@ -132,7 +132,7 @@ struct LoopParams {
 // Launch wrappers (defined in the .cu files).
 cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s);
 size_t      step_loop_smem_bytes(int chunk, int ldx, int H, int grid);
-size_t      step_loop_tc_smem_bytes(unsigned sm_weights, int ldh, int rpc_j, int rpc_p);
+size_t      step_loop_tc_smem_bytes(unsigned sm_weights, int ldh, int rpc_j, int rpc_p, int upc);
 cudaError_t step_loop_configure(size_t smem, int tc);
 cudaError_t step_loop_occupancy(size_t smem, int tc, int * blocks_per_sm);
 

@@ -229,8 +229,7 @@ __device__ __forceinline__ bool grid_barrier(const LoopParams & P, unsigned & k,
     const unsigned target = (k + 1u) * gridDim.x;
     if (threadIdx.x == 0) atom_add_acq_rel(&P.bar[0], 1u);
     ++k;
-    if (!bounded_wait(P, S, [&] { return (int) (ld_acquire(&P.bar[0]) - target) >= 0; })) return false;
-    return __ldcg(&P.ctl[C_ERR]) == 0;
+    return bounded_wait(P, S, [&] { return (int) (ld_acquire(&P.bar[0]) - target) >= 0; });
 }
 
 __device__ __forceinline__ bool leader_arrive(const LoopParams & P, const Smem & S) {
@@ -246,8 +245,10 @@ __device__ __forceinline__ bool leader_arrive(const LoopParams & P, const Smem &
 __device__ __forceinline__ void leader_release(const LoopParams & P, unsigned gen) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        atomicExch(&P.bar[2], 0u);
-        __threadfence();
+        // nobody arrives again before observing the new generation, which the
+        // release store orders after this reset and after the CTA's decisions
+        // (made visible to thread 0 by the barrier above)
+        *reinterpret_cast<volatile unsigned *>(&P.bar[2]) = 0u;
         st_release(&P.bar[3], gen + 1u);
     }
     __syncthreads();
@@ -587,10 +588,13 @@ __device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Sme
 
 // ---- leader: greedy control for every live utterance -------------------------
 
-__device__ void leader_decide(const LoopParams & P, const Smem & S) {
+// The last CTA to reach the joint barrier decides every live utterance's step:
+// argmax keys -> token / duration, frame advance, token output, and the next
+// iteration's live and emit lists (compacted with one block scan). sel / n_live
+// are the current list selector and length; every CTA read them at the start of
+// the iteration and nothing has changed them since.
+__device__ void leader_decide(const LoopParams & P, const Smem & S, int sel, int n_live) {
     const int B = P.B;
-    const int sel = __ldcg(&P.ctl[C_SEL]);
-    const int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
     const int * live_in = P.live + (size_t) sel * B;
     int * live_out = P.live + (size_t) (sel ^ 1) * B;
     int base_emit = 0, base_live = 0;
@@ -602,8 +606,17 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
         if (i < n_live) {
             utt = __ldcg(&live_in[i]);
             int * u = P.ust + utt * kUst;
-            const unsigned long long kt = atomicExch(&P.keys[2 * utt + 0], 0ull);
-            const unsigned long long kd = P.is_tdt ? atomicExch(&P.keys[2 * utt + 1], 0ull) : 0ull;
+            // every load that depends only on utt goes out together (one round trip)
+            const unsigned long long kt = __ldcg(&P.keys[2 * utt + 0]);
+            const unsigned long long kd = P.is_tdt ? __ldcg(&P.keys[2 * utt + 1]) : 0ull;
+            const int4 u0 = __ldcg(reinterpret_cast<const int4 *>(u));
+            const int4 u1 = __ldcg(reinterpret_cast<const int4 *>(u) + 1);
+            const int4 u2 = __ldcg(reinterpret_cast<const int4 *>(u) + 2);
+            const long long foff = __ldg(P.frame_off + utt);
+            int uf[12] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w, u2.x, u2.y, u2.z, u2.w};
+            // the next joint phase max-reduces into cleared keys (ordered by the barrier release)
+            P.keys[2 * utt + 0] = 0ull;
+            if (P.is_tdt) P.keys[2 * utt + 1] = 0ull;
             int tok = key_index(kt);
             int di = P.is_tdt ? key_index(kd) : 0;
             if (kt == 0ull || tok < 0 || tok >= P.V1 || (P.is_tdt && (kd == 0ull || di < 0 || di >= P.Nd))) {
@@ -612,7 +625,7 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
                 tok = P.blank;
                 di = 0;
             }
-            const int step = __ldcg(&u[U_STEPS]);
+            const int step = uf[U_STEPS];
             if (P.trace_steps > 0 && step < P.trace_steps) {
                 const size_t ti = (size_t) utt * P.trace_steps + step;
                 if (P.tr_tok) P.tr_tok[ti] = tok;
@@ -627,10 +640,10 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
                 }
             }
             u[U_STEPS] = step + 1;
-            int t = __ldcg(&u[U_T]);
-            int sym = __ldcg(&u[U_SYM]);
-            int ntok = __ldcg(&u[U_NTOK]);
-            const int T = __ldcg(&u[U_NFRAMES]);
+            int t = uf[U_T];
+            int sym = uf[U_SYM];
+            int ntok = uf[U_NTOK];
+            const int T = uf[U_NFRAMES];
             bool emit_tok = false;
             if (P.is_tdt) {
                 // parakeet_tdt.cpp:938-968
@@ -654,9 +667,9 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
                     t += 1; sym = 0;
                 } else if (tok == P.eou) {
                     u[U_SYMX] = sym;
-                    const int total = __ldcg(&u[U_NBEFORE]) + ntok;
-                    if (total > __ldcg(&u[U_SEGSTART])) {
-                        const int nb = __ldcg(&u[U_NBND]);
+                    const int total = uf[U_NBEFORE] + ntok;
+                    if (total > uf[U_SEGSTART]) {
+                        const int nb = uf[U_NBND];
                         if (P.bnd_out != nullptr && nb < T) P.bnd_out[P.bnd_region[utt] + nb] = total;
                         u[U_NBND] = nb + 1;
                         u[U_SEGSTART] = total;
@@ -686,40 +699,36 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S) {
                 }
             }
             if (e) {
-                ehb = __ldcg(&u[U_HBUF]) ^ 1;
+                ehb = uf[U_HBUF] ^ 1;
                 u[U_HBUF] = ehb;
             }
             u[U_T] = t;
             u[U_SYM] = sym;
             u[U_NTOK] = ntok;
             lv = t < T ? 1 : 0;
-            if (lv) lframe = __ldg(P.frame_off + utt) + t;
+            if (lv) lframe = foff + t;
             if (!lv) P.finish_ns[utt] = gtimer();
         }
-        int tot_e = 0, tot_l = 0;
-        const int pe = block_excl_scan(e, S, tot_e);
-        const int pl = block_excl_scan(lv, S, tot_l);
+        // one scan for both lists: emit count in the low half, live count in the high half
+        int tot = 0;
+        const int pf = block_excl_scan(e | (lv << 16), S, tot);
+        const int pe = pf & 0xFFFF, pl = pf >> 16;
         if (e) {
-            P.emit[2 * (base_emit + pe)] = utt;
-            P.emit[2 * (base_emit + pe) + 1] = etok | (ehb << 30) | (ereset << 31);
+            reinterpret_cast<int2 *>(P.emit)[base_emit + pe] = make_int2(utt, etok | (ehb << 30) | (ereset << 31));
         }
         if (lv) {
             live_out[base_live + pl] = utt;
             P.live_frame[(size_t) (sel ^ 1) * B + base_live + pl] = lframe;
         }
-        base_emit += tot_e;
-        base_live += tot_l;
+        base_emit += tot & 0xFFFF;
+        base_live += tot >> 16;
     }
-    __syncthreads();
     if (threadIdx.x == 0) {
         P.ctl[C_NEMIT] = base_emit;
         P.ctl[C_NLIVE0 + (sel ^ 1)] = base_live;
         P.ctl[C_NDECIDED] = n_live;
         P.ctl[C_SEL] = sel ^ 1;
-        P.ctl[C_ITERS] = __ldcg(&P.ctl[C_ITERS]) + 1;
-        if (base_emit > 0) P.ctl[C_EMITITERS] = __ldcg(&P.ctl[C_EMITITERS]) + 1;
     }
-    __threadfence();
 }
 
 // ---- tensor-core phases (PK_MATH_TC) -------------------------------------------
@@ -738,6 +747,7 @@ struct TcSmem {
     __half * xs_lo;                 // [16][ldh]
     float * part;                   // [kWarps][kTcRmax][8][16]
     float * C;                      // [kTcRmax][8][16]
+    unsigned long long * mbar;      // staging completion barrier (bulk copies)
     int * s_utt;                    // [kTcRec] records of the current block
     int * s_aux;                    // [kTcRec]
     int * s_aux2;                   // [kTcRec]
@@ -745,6 +755,7 @@ struct TcSmem {
     int * s_flag;                   // [4]
     float * bj;                     // [rpc_j] this CTA's joint-out bias slice
     float * bp;                     // [rpc_p] this CTA's pred-proj bias slice
+    float * lb;                     // [L][4][upc] LSTM gate biases of this CTA's units
 };
 
 __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams & P) {
@@ -756,13 +767,15 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     s.xs_lo = reinterpret_cast<__half *>(raw + off); off += (size_t) kTcM * P.ldh * 2;
     s.part = reinterpret_cast<float *>(raw + off); off += (size_t) kWarps * kTcRmax * 128 * 4;
     s.C = reinterpret_cast<float *>(raw + off); off += (size_t) kTcRmax * 128 * 4;
+    s.mbar = reinterpret_cast<unsigned long long *>(raw + off); off += 16;
     s.s_utt = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_aux = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_aux2 = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * 4;
     s.s_flag = reinterpret_cast<int *>(raw + off); off += 4 * 4;
     s.bj = reinterpret_cast<float *>(raw + off); off += (size_t) P.rpc_j * 4;
-    s.bp = reinterpret_cast<float *>(raw + off);
+    s.bp = reinterpret_cast<float *>(raw + off); off += (size_t) P.rpc_p * 4;
+    s.lb = reinterpret_cast<float *>(raw + off);
     return s;
 }
 
@@ -806,38 +819,82 @@ __device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, u
     hi = *reinterpret_cast<uint32_t *>(&hb);
 }
 
-__device__ __forceinline__ void cp_async16(void * smem, const void * gmem) {
-    const unsigned sa = (unsigned) __cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(sa), "l"(gmem) : "memory");
-}
-
-// Stage rows [0, nc) of the activation tile (f16 hi and lo halves, K columns)
-// into xs_hi / xs_lo; src(c, k) gives row c's 8 columns at k in the hi array
-// (the lo array is lo_off elements further on), or nullptr for a zero row.
-// Rows nc..15 keep whatever they held: every row of an mma output depends on
-// its own A row only, and outputs of rows >= nc are never read. Each thread
-// keeps one 16-byte column slot for the whole call (K <= 8 * blockDim.x).
+// Stage rows [0, nc) of the activation tile into xs_hi / xs_lo with bulk
+// copies (the copy engine, completion counted on S.mbar). Row c is nseg
+// segments of seglen halves; src(c, s) gives segment s of row c in the hi
+// array (the lo array is lo_off halves further on), or nullptr for zeros.
+// Lane 0 of every warp issues the copies j = warp, warp + 8, ... and arrives
+// on the barrier once with its byte count. Rows nc..15 keep whatever they
+// held: each mma output row depends on its own A row only, and outputs of
+// rows >= nc are never read. Returns false (error flagged) if the copies did
+// not complete within timeout_ns.
 template <typename F>
-__device__ __forceinline__ void tc_stage_async(const TcSmem & S, int ldh, int nc, int K, size_t lo_off, F src) {
-    const int k8n = K >> 3;
-    const int rpr = (int) blockDim.x / k8n;              // rows per round
-    const int c0 = (int) threadIdx.x / k8n;
-    const int k = 8 * ((int) threadIdx.x - c0 * k8n);
-    if (c0 < rpr) {
-        for (int c = c0; c < nc; c += rpr) {
-            const __half * g = src(c, k);
-            __half * dh = S.xs_hi + c * ldh + k;
-            __half * dl = S.xs_lo + c * ldh + k;
-            if (g != nullptr) {
-                cp_async16(dh, g);
-                cp_async16(dl, g + lo_off);
-            } else {
-                *reinterpret_cast<uint4 *>(dh) = make_uint4(0u, 0u, 0u, 0u);
-                *reinterpret_cast<uint4 *>(dl) = make_uint4(0u, 0u, 0u, 0u);
+__device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S, int nc, int nseg, int seglen,
+                                         size_t lo_off, F src) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned ph = (unsigned) S.s_flag[2];
+    const int ncopy = nc * nseg * 2;
+    const unsigned bytes = (unsigned) seglen * 2u;
+    const unsigned mb = (unsigned) __cvta_generic_to_shared(S.mbar);
+    // Generic-proxy accesses of xs (ldmatrix reads in tc_gemm_nt, zero stores
+    // here and at kernel start) are each followed by fence.proxy.async in the
+    // thread that made them and by a CTA barrier before the next stage issues
+    // its copies, so the async writes below are ordered after them.
+    // zero segments (reset state): plain stores
+    for (int cs = warp; cs < nc * nseg; cs += kWarps) {
+        const int c = cs / nseg, sg = cs - c * nseg;
+        if (src(c, sg) == nullptr) {
+            for (int k = lane * 8; k < seglen; k += 32 * 8) {
+                *reinterpret_cast<uint4 *>(S.xs_hi + c * P.ldh + sg * seglen + k) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4 *>(S.xs_lo + c * P.ldh + sg * seglen + k) = make_uint4(0u, 0u, 0u, 0u);
             }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (lane == 0) {
+        unsigned mine = 0;
+        for (int j = warp; j < ncopy; j += kWarps) {
+            const int cs = j >> 1;
+            const int c = cs / nseg, sg = cs - c * nseg;
+            if (src(c, sg) != nullptr) mine += bytes;
+        }
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(mb), "r"(mine) : "memory");
+        for (int j = warp; j < ncopy; j += kWarps) {
+            const int cs = j >> 1, hl = j & 1;
+            const int c = cs / nseg, sg = cs - c * nseg;
+            const __half * g = src(c, sg);
+            if (g == nullptr) continue;
+            if (hl) g += lo_off;
+            __half * d = (hl ? S.xs_lo : S.xs_hi) + c * P.ldh + sg * seglen;
+            const unsigned da = (unsigned) __cvta_generic_to_shared(d);
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                         :: "r"(da), "l"(g), "r"(bytes), "r"(mb) : "memory");
+        }
+    }
+    if (threadIdx.x == 0) {
+        int ok = 0;
+        const unsigned long long t0 = gtimer();
+        for (unsigned it = 1;; ++it) {
+            unsigned done;
+            asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                         : "=r"(done) : "r"(mb), "r"(ph) : "memory");
+            if (done) { ok = 1; break; }
+            if ((it & 63u) == 0u && (long long) (gtimer() - t0) > P.timeout_ns) {
+                atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_TIMEOUT);
+                break;
+            }
+        }
+        S.s_flag[3] = ok;
+        S.s_flag[2] = (int) (ph ^ 1u);
+    }
+    __syncthreads();
+    if (S.s_flag[3] == 0) return false;
+    // the phase is complete: this test returns at once and orders the copied data for every thread
+    unsigned done;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(done) : "r"(mb), "r"(ph) : "memory");
+    (void) done;
+    return true;
 }
 
 __device__ __forceinline__ const uint8_t * tc_frag(const LoopParams & P, const TcSmem & S, const TcBlock & b) {
@@ -920,6 +977,8 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
 #pragma unroll
             for (int q = 0; q < 4; ++q) acc[r][q] += accl[r][q];
     }
+    // this thread's ldmatrix reads of xs come before the next stage's bulk writes
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 #pragma unroll
     for (int r = 0; r < NT; ++r) {
         float * pp = S.part + ((warp * kTcRmax + r) * 8) * 16;
@@ -977,37 +1036,37 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
         const bool act = my < nc * nu;
         const int cc = act ? my / nu : 0, jj = act ? my - (my / nu) * nu : 0;
         const int j = u0 + jj;
-        float pre[4] = {0.f, 0.f, 0.f, 0.f};
+        // Raw loads only: nothing consumes them before the cell update, so the
+        // warp does not wait for them here.
+        float g0v[4] = {0.f, 0.f, 0.f, 0.f};
         float c_old = 0.0f;
         if (act) {
+            if (l == 0) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int gr = q * H + j;
-                // ((b_ih + W_ih x) + b_hh) + W_hh h, with b_ih + W_ih x for layer 0 from the table
-                pre[q] = (l == 0) ? __ldg(P.g0 + (size_t) S.s_aux[cc] * 4 * H + gr) + __ldg(P.b_hh[0] + gr)
-                                  : __ldg(P.b_ih[l] + gr) + __ldg(P.b_hh[l] + gr);
+                for (int q = 0; q < 4; ++q) g0v[q] = __ldg(P.g0 + (size_t) S.s_aux[cc] * 4 * H + q * H + j);
             }
             if (!(S.s_aux2[cc] & 1)) c_old = __ldcg(P.c + ((size_t) l * B + S.s_utt[cc]) * H + j);
         }
         const __half * h16 = reinterpret_cast<const __half *>(P.h16);
         const size_t lo_off = (size_t) 2 * L * B * H;
+        bool staged;
         if (l == 0) {
             // X = h_prev of layer 0 (zero on reset); W_ih0 . embed comes from the g0 table
-            tc_stage_async(S, P.ldh, nc, H, lo_off, [&](int c, int k) -> const __half * {
+            staged = tc_stage(P, S, nc, 1, H, lo_off, [&](int c, int) -> const __half * {
                 const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
                 if (reset) return nullptr;
-                return h16 + (((size_t) (hb ^ 1) * L + 0) * B + utt) * H + k;
+                return h16 + (((size_t) (hb ^ 1) * L + 0) * B + utt) * H;
             });
         } else {
             // X = [h_new of layer l-1 | h_prev of layer l]
-            tc_stage_async(S, P.ldh, nc, 2 * H, lo_off, [&](int c, int k) -> const __half * {
+            staged = tc_stage(P, S, nc, 2, H, lo_off, [&](int c, int sg) -> const __half * {
                 const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
-                if (k < H) return h16 + (((size_t) hb * L + (l - 1)) * B + utt) * H + k;
+                if (sg == 0) return h16 + (((size_t) hb * L + (l - 1)) * B + utt) * H;
                 if (reset) return nullptr;
-                return h16 + (((size_t) (hb ^ 1) * L + l) * B + utt) * H + (k - H);
+                return h16 + (((size_t) (hb ^ 1) * L + l) * B + utt) * H;
             });
         }
-        __syncthreads();
+        if (!staged) return;
         tc_gemm(P, S, bk, 0, bk.tiles);
         // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
         if (act) {
@@ -1017,7 +1076,10 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const int row = jj * 4 + q;
-                gate[q] = pre[q] + S.C[(row >> 3) * 128 + (row & 7) * 16 + cc];
+                // ((b_ih + W_ih x) + b_hh) + W_hh h, with b_ih + W_ih x for layer 0 from
+                // the table; S.lb holds b_hh for layer 0 and b_ih + b_hh above it
+                const float pre = (l == 0 ? g0v[q] : 0.0f) + S.lb[(l * 4 + q) * upc + jj];
+                gate[q] = pre + S.C[(row >> 3) * 128 + (row & 7) * 16 + cc];
             }
             const float i_g = sigmoid_ref(gate[0]);
             const float f_g = sigmoid_ref(gate[1]);
@@ -1066,10 +1128,9 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             const int nc = min(kTcM, nrb - cs);
             const TcSmem S = tc_pass(T, cs);
             const __half * h16 = reinterpret_cast<const __half *>(P.h16);
-            tc_stage_async(S, P.ldh, nc, H, (size_t) 2 * L * B * H, [&](int c, int k) -> const __half * {
-                return h16 + (((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H + k;
-            });
-            __syncthreads();
+            if (!tc_stage(P, S, nc, 1, H, (size_t) 2 * L * B * H, [&](int c, int) -> const __half * {
+                    return h16 + (((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H;
+                })) return;
             for (int t0 = 0; t0 < P.tcp.tiles; t0 += kTcRmax) {
                 const int nt = min(kTcRmax, P.tcp.tiles - t0);
                 tc_gemm(P, S, P.tcp, t0, nt);
@@ -1110,10 +1171,9 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
         const int nc = min(kTcM, nrb - cs);
         const TcSmem S = tc_pass(T, cs);
         const __half * hid16 = reinterpret_cast<const __half *>(P.hid16);
-        tc_stage_async(S, P.ldh, nc, J, (size_t) B * J, [&](int c, int k) -> const __half * {
-            return hid16 + (size_t) S.s_utt[c] * J + k;
-        });
-        __syncthreads();
+        if (!tc_stage(P, S, nc, 1, J, (size_t) B * J, [&](int c, int) -> const __half * {
+                return hid16 + (size_t) S.s_utt[c] * J;
+            })) return;
         for (int t0 = 0; t0 < P.tcj.tiles; t0 += kTcRmax) {
             const int nt = min(kTcRmax, P.tcj.tiles - t0);
             tc_gemm(P, S, P.tcj, t0, nt);
@@ -1198,6 +1258,13 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             reinterpret_cast<uint4 *>(T.xs_hi)[i] = make_uint4(0u, 0u, 0u, 0u);
             reinterpret_cast<uint4 *>(T.xs_lo)[i] = make_uint4(0u, 0u, 0u, 0u);
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (threadIdx.x == 0) {
+            const unsigned mb = (unsigned) __cvta_generic_to_shared(T.mbar);
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(mb), "r"(kWarps) : "memory");
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            T.s_flag[2] = 0;   // staging barrier phase
+        }
         for (int i = threadIdx.x; i < P.rpc_j; i += blockDim.x) {
             const int r = (int) blockIdx.x * P.rpc_j + i;
             T.bj[i] = r < P.Vo ? __ldg(P.out_b + r) : 0.0f;
@@ -1206,10 +1273,21 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             const int j = (int) blockIdx.x * P.rpc_p + i;
             T.bp[i] = j < P.J ? __ldg(P.pred_b + j) : 0.0f;
         }
+        for (int i = threadIdx.x; i < P.L * 4 * P.upc; i += blockDim.x) {
+            const int l = i / (4 * P.upc), q = (i / P.upc) % 4, jj = i % P.upc;
+            const int j = (int) blockIdx.x * P.upc + jj;
+            float v = 0.0f;
+            if (j < P.H) {
+                const int gr = q * P.H + j;
+                v = l == 0 ? __ldg(P.b_hh[0] + gr) : __ldg(P.b_ih[l] + gr) + __ldg(P.b_hh[l] + gr);
+            }
+            T.lb[i] = v;
+        }
         __syncthreads();
         if (P.stationary) tc_load_stationary(P, T);
     }
     bool first = true;
+    int emit_iters = 0;
     // CTA 0 timestamps: per segment, its own work and the wait that follows
     const bool prof = blockIdx.x == 0 && threadIdx.x == 0 && P.prof != nullptr;
     unsigned long long pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -1228,7 +1306,19 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
             return;
         }
-        const int n_emit = __ldcg(&P.ctl[C_NEMIT]);
+        // control words C_ERR .. C_NDECIDED in one round trip (written by the
+        // host before the launch, then only by the leader)
+        const int4 cw0 = __ldcg(reinterpret_cast<const int4 *>(P.ctl));
+        const int4 cw1 = __ldcg(reinterpret_cast<const int4 *>(P.ctl) + 1);
+        if (cw0.x != 0) return;                 // C_ERR
+        const int sel = cw0.y;                  // C_SEL
+        const int n_live = sel ? cw0.w : cw0.z; // C_NLIVE1 / C_NLIVE0
+        const int n_emit = cw1.x;               // C_NEMIT
+        if (blockIdx.x == 0 && threadIdx.x == 0 && iter > 0) {
+            // plain stores (no read back): decided rounds so far, and how many of them emitted
+            P.ctl[C_ITERS] = iter;
+            if (n_emit > 0) P.ctl[C_EMITITERS] = ++emit_iters;
+        }
         if (n_emit > 0) {
             for (int l = 0; l < P.L; ++l) {
                 if constexpr (TC) tc_phase_lstm(P, l, n_emit, T);
@@ -1239,8 +1329,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
                 mark(1);
             }
         }
-        const int sel = __ldcg(&P.ctl[C_SEL]);
-        const int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
         if constexpr (TC) tc_phase_pred(P, first, n_emit, sel, n_live, T);
         else phase_pred(P, first, n_emit, sel, n_live, S);
         __syncthreads();
@@ -1254,7 +1342,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         __syncthreads();
         mark(4);
         if (leader_arrive(P, S)) {
-            leader_decide(P, S);
+            leader_decide(P, S, sel, n_live);
             mark(6);
             leader_release(P, gen);
         } else if (!leader_wait(P, gen, S)) {
@@ -1262,7 +1350,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         }
         mark(7);
         ++gen;
-        if (__ldcg(&P.ctl[C_ERR]) != 0) return;
     }
     if (prof)
         for (int i = 0; i < 8; ++i) P.prof[i] = pacc[i];
@@ -1280,13 +1367,15 @@ size_t step_loop_smem_bytes(int chunk, int ldx, int H, int grid) {
     return off;
 }
 
-size_t step_loop_tc_smem_bytes(unsigned sm_weights, int ldh, int rpc_j, int rpc_p) {
+size_t step_loop_tc_smem_bytes(unsigned sm_weights, int ldh, int rpc_j, int rpc_p, int upc) {
     size_t off = (sm_weights + 15) & ~15u;
     off += 2 * (size_t) kTcM * ldh * 2;
     off += (size_t) kWarps * kTcRmax * 128 * 4;
     off += (size_t) kTcRmax * 128 * 4;
+    off += 16;
     off += 3 * kTcRec * 4 + (kWarps + 2) * 4 + 4 * 4;
     off += (size_t) (rpc_j + rpc_p) * 4;
+    off += (size_t) kMaxLayers * 4 * upc * 4;
     return off;
 }
 
