@@ -80,6 +80,10 @@ struct pk_ctx {
     pk::TcBlock tcj{}, tcp{}, tcl[pk::kMaxLayers]{};
     DevBuf tc_frag[2 + pk::kMaxLayers], tc_scale[2 + pk::kMaxLayers], g0;
     uint64_t weight_bytes = 0;
+    // tensor-core enc-proj: f16 hi / lo weights and their TMA descriptor
+    int ep_ok = 0;
+    DevBuf ep_w16, ep_err;
+    alignas(64) unsigned char ep_tmap[128] = {};
     // weights (f32 on the device)
     DevBuf embed, w_ih[pk::kMaxLayers], w_hh[pk::kMaxLayers], b_ih[pk::kMaxLayers],
         b_hh[pk::kMaxLayers], enc_w, enc_b, pred_w, pred_b, out_w, out_b, durations, special;
@@ -96,7 +100,7 @@ struct pk_ctx {
                                    &keys, &live, &emit, &ctl, &bar, &tstart, &finish, &tok,
                                    &tokregion, &bnd, &bndregion, &frameoff, &offsets, &boffsets,
                                    &compact, &bcompact, &tr_logits, &tr_h, &tr_c, &tr_tok, &tr_dur,
-                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &h16, &hid16};
+                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &h16, &hid16, &ep_w16, &ep_err};
         for (int i = 0; i < 2 + pk::kMaxLayers; ++i) { v.push_back(&tc_frag[i]); v.push_back(&tc_scale[i]); }
         for (int l = 0; l < pk::kMaxLayers; ++l) {
             v.push_back(&w_ih[l]); v.push_back(&w_hh[l]); v.push_back(&b_ih[l]); v.push_back(&b_hh[l]);
@@ -346,6 +350,21 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
     return PK_OK;
 }
 
+// Tensor-core enc-proj (f16 hi / lo weights + TMA descriptor); leaves ep_ok = 0
+// (CUDA-core f32 enc-proj) when the shapes or the device do not allow it.
+void setup_encproj(pk_ctx * x, size_t smem_cap) {
+    x->ep_ok = 0;
+    if (!encproj_tc_supported(x->De, x->J) || encproj_tc_smem_bytes() > smem_cap) return;
+    if (x->ep_w16.ensure((size_t) 2 * x->J * x->De * 2) != cudaSuccess) return;
+    if (x->ep_err.ensure(sizeof(int)) != cudaSuccess) return;
+    if (cudaMemsetAsync(x->ep_err.p, 0, sizeof(int), x->stream) != cudaSuccess) return;
+    if (encproj_tc_prepare(x->enc_w.as<float>(), x->J, x->De, x->ep_w16.as<unsigned short>(), x->ep_tmap,
+                           x->stream) != cudaSuccess) return;
+    if (encproj_tc_configure() != cudaSuccess) return;
+    if (cudaStreamSynchronize(x->stream) != cudaSuccess) return;
+    x->ep_ok = 1;
+}
+
 pk_status validate_desc(const pk_model_desc * d) {
     if (!d) return fail(PK_ERR_INVALID, "null descriptor");
     if (d->model_type != PK_MODEL_TDT && d->model_type != PK_MODEL_EOU)
@@ -459,9 +478,14 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         encsrc = x->enc.as<float>();
     }
     PK_CK(cudaEventRecord(x->ev[1], s));
+    const bool ep_tc = use_tc && x->ep_ok && (reinterpret_cast<uintptr_t>(encsrc) & 15u) == 0;
     if (frames > 0) {
-        PK_CK(launch_encproj_f32(encsrc, frames, x->De, x->enc_w.as<float>(), x->enc_b.as<float>(), J,
-                                 x->encp.as<float>(), s));
+        if (ep_tc)
+            PK_CK(launch_encproj_tc(encsrc, frames, x->De, x->ep_tmap, J, x->enc_b.as<float>(), x->encp.as<float>(),
+                                    x->timeout_ns, x->ep_err.as<int>(), s));
+        else
+            PK_CK(launch_encproj_f32(encsrc, frames, x->De, x->enc_w.as<float>(), x->enc_b.as<float>(), J,
+                                     x->encp.as<float>(), s));
         ++r.launches;
     }
     PK_CK(cudaEventRecord(x->ev[2], s));
@@ -600,6 +624,14 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(cudaStreamSynchronize(s));
     PK_CK(cudaEventElapsedTime(&r.ms_encproj, x->ev[1], x->ev[2]));
     PK_CK(cudaEventElapsedTime(&r.ms_loop, x->ev[3], x->ev[4]));
+    if (ep_tc && frames > 0) {
+        int ep_err = 0;
+        PK_CK(copy_sync(x, &ep_err, x->ep_err.p, sizeof(int), cudaMemcpyDeviceToHost));
+        if (ep_err != 0) {
+            PK_CK(cudaMemsetAsync(x->ep_err.p, 0, sizeof(int), s));
+            return fail(PK_ERR_TIMEOUT, "enc-proj: a pipeline wait exceeded %lld us", x->timeout_ns / 1000);
+        }
+    }
     if (r.ctl[C_ERR] != 0) {
         const int code = r.ctl[C_ERR];
         if (code == PK_ERR_TIMEOUT)
@@ -831,6 +863,7 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
         return cleanup(fail(PK_ERR_CUDA, "step loop does not fit one CTA per SM"));
     st = setup_tc(x, d, (size_t) prop.sharedMemPerBlockOptin);
     if (st != PK_OK) return cleanup(st);
+    setup_encproj(x, (size_t) prop.sharedMemPerBlockOptin);
     x->math = x->tc_ok ? PK_MATH_TC : PK_MATH_F32;
     *out = x;
     return PK_OK;

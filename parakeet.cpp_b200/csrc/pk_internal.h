@@ -151,6 +151,15 @@ cudaError_t launch_gather(const int32_t * ust, int B, int field, const int32_t *
 // hi = f16(x), lo = f16(x - hi) for n floats.
 cudaError_t launch_split_f16(const float * src, unsigned short * hi, unsigned short * lo, int64_t n,
                              cudaStream_t s);
+// Tensor-core joint.enc projection (pk_encproj.cu): weights split into f16 hi / lo
+// halves once ([2J][K] f16 in w16, TMA descriptor of 128 bytes in tmap_out).
+bool        encproj_tc_supported(int K, int J);
+size_t      encproj_tc_smem_bytes();
+cudaError_t encproj_tc_configure();
+cudaError_t encproj_tc_prepare(const float * w, int J, int K, unsigned short * w16, void * tmap_out,
+                               cudaStream_t s);
+cudaError_t launch_encproj_tc(const float * enc, long long frames, int K, const void * tmap, int J,
+                              const float * bias, float * out, long long timeout_ns, int * err, cudaStream_t s);
 cudaError_t launch_extract_field(const int32_t * ust, int B, int field, int32_t * dst,
                                  cudaStream_t s);
 
