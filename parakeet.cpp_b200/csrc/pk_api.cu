@@ -74,7 +74,7 @@ struct pk_ctx {
     int math = PK_MATH_F32;
     int test_stall = 0;
     // tensor-core step loop
-    int tc_ok = 0, tc_stationary = 0, tc_ldh = 0, rpc_j = 0, rpc_p = 0, upc = 0;
+    int tc_ok = 0, tc_stationary = 0, tc_ldh = 0, rpc_j = 0, rpc_p = 0, upc = 0, tc_hint = 0;
     unsigned tc_sm_weights = 0;
     size_t tc_smem = 0;
     pk::TcBlock tcj{}, tcp{}, tcl[pk::kMaxLayers]{};
@@ -197,6 +197,12 @@ struct SrcMat {
         kk = k;
         return *a;
     }
+    int8_t q(int64_t row, int64_t k) const {
+        int64_t kk;
+        const pk_tensor & t = at(k, kk);
+        const uint8_t * blk = static_cast<const uint8_t *>(t.data) + (row * (t.ne0 / 32) + kk / 32) * 34;
+        return (int8_t) blk[2 + kk % 32];
+    }
     uint8_t q_biased(int64_t row, int64_t k) const {
         int64_t kk;
         const pk_tensor & t = at(k, kk);
@@ -216,10 +222,14 @@ struct SrcMat {
     }
 };
 
+// imma: q8_0 rows packed as raw int8 B fragments of mma.m16n8k32 (lane (g, t):
+// k = 4t..4t+3 then 16+4t..16+4t+3 of each 32-wide block); otherwise f16
+// fragments of mma.m16n8k16 (q8_0 stored q + 128, converted exactly in-kernel).
 template <class RowMap>
 pk_status build_tc_block(pk_ctx * x, int G, int tiles, int K, const SrcMat & src, RowMap rowmap,
-                         DevBuf & dfrag, DevBuf & dscale, pk::TcBlock & out) {
+                         DevBuf & dfrag, DevBuf & dscale, pk::TcBlock & out, bool imma = false) {
     const bool i8 = src.type() == PK_GGML_Q8_0;
+    imma = imma && i8;
     const int nkb = K / 32;
     const size_t per_lane = i8 ? 8 : 16;
     const size_t cta_bytes = (size_t) tiles * nkb * 32 * per_lane;
@@ -234,6 +244,13 @@ pk_status build_tc_block(pk_ctx * x, int G, int tiles, int K, const SrcMat & src
                     const int64_t row = rowmap(cta, tile * 8 + g);
                     uint8_t * dst = frag.data() + (size_t) cta * cta_bytes +
                                     (((size_t) tile * nkb + kb) * 32 + lane) * per_lane;
+                    if (imma) {
+                        for (int e = 0; e < 8; ++e) {
+                            const int64_t k = (int64_t) kb * 32 + (e < 4 ? 4 * t + e : 16 + 4 * t + e - 4);
+                            dst[e] = row < 0 ? (uint8_t) 0 : (uint8_t) src.q(row, k);
+                        }
+                        continue;
+                    }
                     for (int ks = 0; ks < 2; ++ks) {
                         const int64_t kk = (int64_t) kb * 32 + ks * 16;
                         const int64_t ks4[4] = {kk + 2 * t, kk + 2 * t + 1, kk + 2 * t + 8, kk + 2 * t + 9};
@@ -268,6 +285,7 @@ pk_status build_tc_block(pk_ctx * x, int G, int tiles, int K, const SrcMat & src
     out.tiles = tiles;
     out.K = K;
     out.is_i8 = i8 ? 1 : 0;
+    out.imma = imma ? 1 : 0;
     return PK_OK;
 }
 
@@ -282,6 +300,10 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
     if (!tc_type_ok(d->joint_out_w) || !tc_type_ok(d->joint_pred_w) || !tc_type_ok(d->lstm[0].w_hh)) return PK_OK;
     for (int l = 1; l < L; ++l)
         if (!tc_type_ok(d->lstm[l].w_ih) || d->lstm[l].w_ih.type != d->lstm[l].w_hh.type) return PK_OK;
+    // int16 activations on int8 tensor cores when every LSTM / pred-proj weight is q8_0
+    bool all_q8 = d->joint_pred_w.type == PK_GGML_Q8_0 && d->lstm[0].w_hh.type == PK_GGML_Q8_0;
+    for (int l = 1; l < L; ++l) all_q8 = all_q8 && d->lstm[l].w_ih.type == PK_GGML_Q8_0;
+    x->tc_hint = all_q8 ? 1 : 0;
     x->rpc_j = (x->Vo + G - 1) / G;
     x->rpc_p = (J + G - 1) / G;
     x->upc = (H + G - 1) / G;
@@ -297,7 +319,7 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
                           [&](int cta, int r) -> int64_t {
                               const int64_t row = (int64_t) cta * rpc_p + r;
                               return (r < rpc_p && row < J) ? row : -1; },
-                          x->tc_frag[1], x->tc_scale[1], x->tcp));
+                          x->tc_frag[1], x->tc_scale[1], x->tcp, x->tc_hint != 0));
     auto unit_rows = [&](int cta, int r) -> int64_t {
         const int jj = r / 4, q = r % 4;
         const int64_t unit = (int64_t) cta * upc + jj;
@@ -313,7 +335,7 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
             sl.a = &d->lstm[l].w_ih; sl.b = &d->lstm[l].w_hh; sl.ka = H;
         }
         PK_TRY(build_tc_block(x, G, tiles_l, l == 0 ? H : 2 * H, sl, unit_rows,
-                              x->tc_frag[2 + l], x->tc_scale[2 + l], x->tcl[l]));
+                              x->tc_frag[2 + l], x->tc_scale[2 + l], x->tcl[l], x->tc_hint != 0));
     }
     // g0[v][4H] = b_ih0 + W_ih0 . embed[v] for every token v (f32 GEMM on the device)
     PK_CK(x->g0.ensure((size_t) x->V1 * 4 * H * 4));
@@ -532,7 +554,11 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     if (r.h_in) {
         PK_CK(cudaMemcpyAsync(x->h.p, r.h_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
         PK_CK(cudaMemcpyAsync(x->c.p, r.c_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
-        if (use_tc) {   // hi / lo split of the resumed state (B == 1: buffer 0 is [L][H])
+        if (use_tc && x->tc_hint) {   // int16 digit planes of the resumed state (B == 1: buffer 0 is [L][H])
+            unsigned char * hq = x->h16.as<unsigned char>();
+            PK_CK(launch_split_int16(r.h_in, hq, hq + (size_t) 2 * L * H, (int64_t) L * H, s));
+            ++r.launches;
+        } else if (use_tc) {   // hi / lo split of the resumed state
             unsigned short * h16 = x->h16.as<unsigned short>();
             PK_CK(launch_split_f16(r.h_in, h16, h16 + (size_t) 2 * L * H, (int64_t) L * H, s));
             ++r.launches;
@@ -553,7 +579,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         P.stationary = x->tc_stationary;
         P.sm_weights = x->tc_sm_weights;
         P.ldh = x->tc_ldh;
-        P.rpc_j = x->rpc_j; P.rpc_p = x->rpc_p; P.upc = x->upc;
+        P.rpc_j = x->rpc_j; P.rpc_p = x->rpc_p; P.upc = x->upc; P.h_int = x->tc_hint;
         P.tcj = x->tcj; P.tcp = x->tcp;
         for (int l = 0; l < L; ++l) P.tcl[l] = x->tcl[l];
         P.g0 = x->g0.as<float>();

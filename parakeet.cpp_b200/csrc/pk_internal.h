@@ -60,6 +60,7 @@ struct TcBlock {
     int tiles;
     int K;                     // multiple of 32
     int is_i8;
+    int imma;                  // q8_0 packed as raw int8 B fragments of mma.m16n8k32 (int16 activations)
     unsigned sm_frag;          // offsets inside the stationary shared-memory region
     unsigned sm_scale;
 };
@@ -79,6 +80,7 @@ struct LoopParams {
     unsigned sm_weights;       // bytes of the stationary region
     int ldh;                   // halves per staged activation row (max K + 8)
     int rpc_j, rpc_p, upc;     // joint rows, pred rows, LSTM units per CTA
+    int h_int;                 // LSTM outputs staged as int16 fixed point (two int8 digit planes)
     TcBlock tcj, tcp, tcl[kMaxLayers];
     const float * g0;          // [V+1][4H]: b_ih0 + W_ih0 . embed[v] (layer-0 input projection)
     // weights (f32, row-major [out][in])
@@ -149,6 +151,9 @@ cudaError_t launch_gather(const int32_t * ust, int B, int field, const int32_t *
                           const int64_t * region, const int64_t * offsets, int32_t * dst,
                           cudaStream_t s);
 // hi = f16(x), lo = f16(x - hi) for n floats.
+// x -> round(x * 2^15) clamped to +-32767, stored as two int8 digit planes
+// (hi = value >> 8 signed, lo = value & 255 unsigned).
+cudaError_t launch_split_int16(const float * src, unsigned char * hi, unsigned char * lo, int64_t n, cudaStream_t s);
 cudaError_t launch_split_f16(const float * src, unsigned short * hi, unsigned short * lo, int64_t n,
                              cudaStream_t s);
 // Tensor-core joint.enc projection (pk_encproj.cu): weights split into f16 hi / lo

@@ -172,6 +172,15 @@ __global__ void split_f16_kernel(const float * __restrict__ src, __half * __rest
     lo[i] = __float2half_rn(x - __half2float(h));
 }
 
+__global__ void split_int16_kernel(const float * __restrict__ src, int8_t * __restrict__ hi,
+                                   uint8_t * __restrict__ lo, int64_t n) {
+    const int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int q = max(-32767, min(32767, __float2int_rn(src[i] * 32768.0f)));
+    hi[i] = (int8_t) (q >> 8);
+    lo[i] = (uint8_t) (q & 255);
+}
+
 __global__ void extract_field_kernel(const int32_t * __restrict__ ust, int B, int field,
                                      int32_t * __restrict__ dst) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -217,6 +226,13 @@ cudaError_t launch_split_f16(const float * src, unsigned short * hi, unsigned sh
     if (n <= 0) return cudaSuccess;
     split_f16_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, s>>>(src, reinterpret_cast<__half *>(hi),
                                                                 reinterpret_cast<__half *>(lo), n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_split_int16(const float * src, unsigned char * hi, unsigned char * lo, int64_t n,
+                               cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    split_int16_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, s>>>(src, reinterpret_cast<int8_t *>(hi), lo, n);
     return cudaGetLastError();
 }
 

@@ -807,6 +807,18 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// int8 tensor-core products (exact int32): A digit plane x raw q8_0 bytes.
+__device__ __forceinline__ void imma_s8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 // Four biased bytes (q + 128) -> two f16x2 holding q exactly: byte b placed
 // under the f16 exponent of 1024 gives 1024 + b, minus 1152 gives q.
 __device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, uint32_t & hi) {
@@ -924,7 +936,33 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
     const int mk = (lane >> 4) * 8;
     const __half * ahp = S.xs_hi + mrow * P.ldh + mk;
     const __half * alp = S.xs_lo + mrow * P.ldh + mk;
-    if (b.is_i8) {
+    if (b.imma) {
+        // A = int16 fixed point (x * 2^15) as two int8 digit planes in xs_hi (signed
+        // high byte) and xs_lo (unsigned low byte), 32 bytes per K block; one
+        // m16n8k32 per plane gives the block's exact int32 dot products.
+        for (int kb = kb0; kb < kb1; ++kb) {
+            uint32_t ah[4], al[4];
+            ldsm_x4(ah, ahp + kb * 16);
+            ldsm_x4(al, alp + kb * 16);
+#pragma unroll
+            for (int r = 0; r < NT; ++r) {
+                const size_t u = (size_t) (t0 + r) * nkb + kb;
+                const uint2 w = *reinterpret_cast<const uint2 *>(frag + (u * 32 + lane) * 8);
+                const float2 sc = *reinterpret_cast<const float2 *>(scale + u * 8 + 2 * t);
+                int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
+                imma_s8s8(dh, ah, w.x, w.y);
+                imma_u8s8(dl, al, w.x, w.y);
+                acc[r][0] = fmaf(sc.x, (float) (dh[0] * 256 + dl[0]), acc[r][0]);
+                acc[r][1] = fmaf(sc.y, (float) (dh[1] * 256 + dl[1]), acc[r][1]);
+                acc[r][2] = fmaf(sc.x, (float) (dh[2] * 256 + dl[2]), acc[r][2]);
+                acc[r][3] = fmaf(sc.y, (float) (dh[3] * 256 + dl[3]), acc[r][3]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < NT; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[r][q] *= 1.0f / 32768.0f;
+    } else if (b.is_i8) {
         for (int kb = kb0; kb < kb1; ++kb) {
             uint32_t ah0[4], al0[4], ah1[4], al1[4];
             ldsm_x4(ah0, ahp + kb * 32);
@@ -1047,23 +1085,29 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
             }
             if (!(S.s_aux2[cc] & 1)) c_old = __ldcg(P.c + ((size_t) l * B + S.s_utt[cc]) * H + j);
         }
-        const __half * h16 = reinterpret_cast<const __half *>(P.h16);
-        const size_t lo_off = (size_t) 2 * L * B * H;
+        // h rows: f16 hi / lo halves, or int16 digit planes (one byte each) when P.h_int
+        const int es = P.h_int ? 1 : 2;                       // bytes per element and half
+        const unsigned char * hb0 = reinterpret_cast<const unsigned char *>(P.h16);
+        const size_t lo_off = (size_t) 2 * L * B * H * es / 2;   // in halves
+        const int segh = H * es / 2;                            // segment length in halves
+        auto hrow = [&](int hbuf, int layer, int utt) -> const __half * {
+            return reinterpret_cast<const __half *>(hb0 + ((((size_t) hbuf * L + layer) * B + utt) * H) * es);
+        };
         bool staged;
         if (l == 0) {
             // X = h_prev of layer 0 (zero on reset); W_ih0 . embed comes from the g0 table
-            staged = tc_stage(P, S, nc, 1, H, lo_off, [&](int c, int) -> const __half * {
+            staged = tc_stage(P, S, nc, 1, segh, lo_off, [&](int c, int) -> const __half * {
                 const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
                 if (reset) return nullptr;
-                return h16 + (((size_t) (hb ^ 1) * L + 0) * B + utt) * H;
+                return hrow(hb ^ 1, 0, utt);
             });
         } else {
             // X = [h_new of layer l-1 | h_prev of layer l]
-            staged = tc_stage(P, S, nc, 2, H, lo_off, [&](int c, int sg) -> const __half * {
+            staged = tc_stage(P, S, nc, 2, segh, lo_off, [&](int c, int sg) -> const __half * {
                 const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
-                if (sg == 0) return h16 + (((size_t) hb * L + (l - 1)) * B + utt) * H;
+                if (sg == 0) return hrow(hb, l - 1, utt);
                 if (reset) return nullptr;
-                return h16 + (((size_t) (hb ^ 1) * L + l) * B + utt) * H;
+                return hrow(hb ^ 1, l, utt);
             });
         }
         if (!staged) return;
@@ -1090,9 +1134,16 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
             const float hn = o_g * tanhf(c_new);
             const size_t o = (((size_t) hb * L + l) * B + utt) * H + j;
             P.h[o] = hn;
-            const __half hh = __float2half_rn(hn);
-            reinterpret_cast<__half *>(P.h16)[o] = hh;
-            reinterpret_cast<__half *>(P.h16)[(size_t) 2 * L * B * H + o] = __float2half_rn(hn - __half2float(hh));
+            if (P.h_int) {
+                // int16 fixed point (|h| < 1), two digit planes
+                const int q16 = max(-32767, min(32767, __float2int_rn(hn * 32768.0f)));
+                reinterpret_cast<int8_t *>(P.h16)[o] = (int8_t) (q16 >> 8);
+                reinterpret_cast<uint8_t *>(P.h16)[(size_t) 2 * L * B * H + o] = (uint8_t) (q16 & 255);
+            } else {
+                const __half hh = __float2half_rn(hn);
+                reinterpret_cast<__half *>(P.h16)[o] = hh;
+                reinterpret_cast<__half *>(P.h16)[(size_t) 2 * L * B * H + o] = __float2half_rn(hn - __half2float(hh));
+            }
         }
         __syncthreads();
       }
@@ -1127,9 +1178,11 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
         for (int cs = 0; cs < nrb; cs += kTcM) {
             const int nc = min(kTcM, nrb - cs);
             const TcSmem S = tc_pass(T, cs);
-            const __half * h16 = reinterpret_cast<const __half *>(P.h16);
-            if (!tc_stage(P, S, nc, 1, H, (size_t) 2 * L * B * H, [&](int c, int) -> const __half * {
-                    return h16 + (((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H;
+            const int es = P.h_int ? 1 : 2;   // bytes per element and half (int16 digit planes / f16 hi, lo)
+            const unsigned char * hb0 = reinterpret_cast<const unsigned char *>(P.h16);
+            if (!tc_stage(P, S, nc, 1, H * es / 2, (size_t) 2 * L * B * H * es / 2, [&](int c, int) -> const __half * {
+                    return reinterpret_cast<const __half *>(
+                        hb0 + ((((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H) * es);
                 })) return;
             for (int t0 = 0; t0 < P.tcp.tiles; t0 += kTcRmax) {
                 const int nt = min(kTcRmax, P.tcp.tiles - t0);
