@@ -74,7 +74,8 @@ struct pk_ctx {
     int math = PK_MATH_F32;
     int test_stall = 0;
     // tensor-core step loop
-    int tc_ok = 0, tc_stationary = 0, tc_ldh = 0, rpc_j = 0, rpc_p = 0, upc = 0, tc_hint = 0;
+    int tc_ok = 0, tc_stationary = 0, rpc_j = 0, rpc_p = 0, upc = 0, tc_hint = 0;
+    int tc_rbh = 0, tc_rbj = 0, tc_rbx = 0;   // staged row bytes: h, hid, max
     unsigned tc_sm_weights = 0;
     size_t tc_smem = 0;
     pk::TcBlock tcj{}, tcp{}, tcl[pk::kMaxLayers]{};
@@ -89,7 +90,7 @@ struct pk_ctx {
         b_hh[pk::kMaxLayers], enc_w, enc_b, pred_w, pred_b, out_w, out_b, durations, special;
     // per-call workspace
     DevBuf prof;
-    DevBuf livef, h16, hid16;
+    DevBuf livef, hst, xnew, hidc;
     DevBuf enc, encp, h, c, predp, hid, ust, keys, live, emit, ctl, bar, tstart, finish, tok,
         tokregion, bnd, bndregion, frameoff, offsets, boffsets, compact, bcompact;
     DevBuf tr_logits, tr_h, tr_c, tr_tok, tr_dur, tr_ftok, tr_fdur;
@@ -100,7 +101,7 @@ struct pk_ctx {
                                    &keys, &live, &emit, &ctl, &bar, &tstart, &finish, &tok,
                                    &tokregion, &bnd, &bndregion, &frameoff, &offsets, &boffsets,
                                    &compact, &bcompact, &tr_logits, &tr_h, &tr_c, &tr_tok, &tr_dur,
-                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &h16, &hid16, &ep_w16, &ep_err};
+                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &hst, &xnew, &hidc, &ep_w16, &ep_err};
         for (int i = 0; i < 2 + pk::kMaxLayers; ++i) { v.push_back(&tc_frag[i]); v.push_back(&tc_scale[i]); }
         for (int l = 0; l < pk::kMaxLayers; ++l) {
             v.push_back(&w_ih[l]); v.push_back(&w_hh[l]); v.push_back(&b_ih[l]); v.push_back(&b_hh[l]);
@@ -351,17 +352,18 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
     place(x->tcj);
     place(x->tcp);
     for (int l = 0; l < L; ++l) place(x->tcl[l]);
-    const int kmax = std::max(std::max(J, H), L > 1 ? 2 * H : H);
-    if (kmax > 8 * kThreads) return PK_OK;   // one 16-byte staging slot per thread and row
-    x->tc_ldh = kmax + 8;
-    size_t need = step_loop_tc_smem_bytes(off, x->tc_ldh, rpc_j, rpc_p, upc);
+    // staged rows: [hi | lo] + 16 bytes, an odd multiple of 16 (conflict-free ldmatrix rows)
+    x->tc_rbh = 2 * H * (x->tc_hint ? 1 : 2) + 16;
+    x->tc_rbj = 4 * J + 16;
+    x->tc_rbx = std::max(x->tc_rbh, x->tc_rbj);
+    size_t need = step_loop_tc_smem_bytes(off, x->tc_rbx, rpc_j, rpc_p, upc);
     if (need <= smem_cap) {
         x->tc_stationary = 1;
         x->tc_sm_weights = off;
     } else {
         x->tc_stationary = 0;
         x->tc_sm_weights = 0;
-        need = step_loop_tc_smem_bytes(0, x->tc_ldh, rpc_j, rpc_p, upc);
+        need = step_loop_tc_smem_bytes(0, x->tc_rbx, rpc_j, rpc_p, upc);
         if (need > smem_cap) return PK_OK;
     }
     x->tc_smem = need;
@@ -470,8 +472,9 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(x->c.ensure((size_t) L * Bs * H * 4));
     const bool use_tc = x->math == PK_MATH_TC && x->tc_ok;
     if (use_tc) {
-        PK_CK(x->h16.ensure(2 * 2 * (size_t) L * Bs * H * 2));
-        PK_CK(x->hid16.ensure(2 * Bs * J * 2));
+        PK_CK(x->hst.ensure(2 * (size_t) L * Bs * x->tc_rbh));
+        PK_CK(x->xnew.ensure((size_t) L * Bs * x->tc_rbh));
+        PK_CK(x->hidc.ensure((size_t) Bs * x->tc_rbj));
     }
     PK_CK(x->predp.ensure(Bs * J * 4));
     PK_CK(x->hid.ensure(Bs * J * 4));
@@ -554,13 +557,8 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     if (r.h_in) {
         PK_CK(cudaMemcpyAsync(x->h.p, r.h_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
         PK_CK(cudaMemcpyAsync(x->c.p, r.c_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
-        if (use_tc && x->tc_hint) {   // int16 digit planes of the resumed state (B == 1: buffer 0 is [L][H])
-            unsigned char * hq = x->h16.as<unsigned char>();
-            PK_CK(launch_split_int16(r.h_in, hq, hq + (size_t) 2 * L * H, (int64_t) L * H, s));
-            ++r.launches;
-        } else if (use_tc) {   // hi / lo split of the resumed state
-            unsigned short * h16 = x->h16.as<unsigned short>();
-            PK_CK(launch_split_f16(r.h_in, h16, h16 + (size_t) 2 * L * H, (int64_t) L * H, s));
+        if (use_tc) {   // staged rows of the resumed state (B == 1: buffer 0, layer l is row l)
+            PK_CK(launch_stage_rows(r.h_in, L, H, x->tc_hint ? 1 : 2, x->tc_rbh, x->hst.as<unsigned char>(), s));
             ++r.launches;
         }
     }
@@ -574,11 +572,12 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     x->test_stall = 0;   // one-shot
     if (use_tc) {
         P.tc = 1;
-        P.h16 = x->h16.as<unsigned short>();
-        P.hid16 = x->hid16.as<unsigned short>();
+        P.hst = x->hst.as<unsigned char>();
+        P.xnew = x->xnew.as<unsigned char>();
+        P.hidc = x->hidc.as<unsigned char>();
         P.stationary = x->tc_stationary;
         P.sm_weights = x->tc_sm_weights;
-        P.ldh = x->tc_ldh;
+        P.rbh = x->tc_rbh; P.rbj = x->tc_rbj; P.rbx = x->tc_rbx;
         P.rpc_j = x->rpc_j; P.rpc_p = x->rpc_p; P.upc = x->upc; P.h_int = x->tc_hint;
         P.tcj = x->tcj; P.tcp = x->tcp;
         for (int l = 0; l < L; ++l) P.tcl[l] = x->tcl[l];

@@ -78,7 +78,7 @@ struct LoopParams {
     int tc;
     int stationary;            // copy TC weights into shared memory at kernel start
     unsigned sm_weights;       // bytes of the stationary region
-    int ldh;                   // halves per staged activation row (max K + 8)
+    int rbh, rbj, rbx;         // bytes per staged row: h (2 H es + 16), hid (4 J + 16), max of both
     int rpc_j, rpc_p, upc;     // joint rows, pred rows, LSTM units per CTA
     int h_int;                 // LSTM outputs staged as int16 fixed point (two int8 digit planes)
     TcBlock tcj, tcp, tcl[kMaxLayers];
@@ -103,8 +103,11 @@ struct LoopParams {
     float * c;                 // [L][B][H]
     float * predp;             // [B][J]
     float * hid;               // [B][J] (CUDA-core phases)
-    unsigned short * h16;      // [2 (hi, lo)][2][L][B][H] f16 split of h (tensor-core phases)
-    unsigned short * hid16;    // [2 (hi, lo)][B][J] f16 split of the joint hidden (tensor-core phases)
+    // tensor-core phases: activation rows in the staged layout [hi part | lo part | pad]
+    // (h: int16 digit planes of 1 byte or f16 halves, es bytes each; hid: f16)
+    unsigned char * hst;       // [2][L][B] rows of rbh bytes: h state per (buffer, layer, utterance)
+    unsigned char * xnew;      // [L][B] rows of rbh bytes: new h by emit-list index
+    unsigned char * hidc;      // [B] rows of rbj bytes: joint hidden by live-list index
     int32_t * ust;             // [B][kUst]
     unsigned long long * keys; // [B][2] packed argmax keys (token, duration)
     int32_t * live;            // [2][B]
@@ -134,7 +137,7 @@ struct LoopParams {
 // Launch wrappers (defined in the .cu files).
 cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s);
 size_t      step_loop_smem_bytes(int chunk, int ldx, int H, int grid);
-size_t      step_loop_tc_smem_bytes(unsigned sm_weights, int ldh, int rpc_j, int rpc_p, int upc);
+size_t      step_loop_tc_smem_bytes(unsigned sm_weights, int rbx, int rpc_j, int rpc_p, int upc);
 cudaError_t step_loop_configure(size_t smem, int tc);
 cudaError_t step_loop_occupancy(size_t smem, int tc, int * blocks_per_sm);
 
@@ -154,6 +157,10 @@ cudaError_t launch_gather(const int32_t * ust, int B, int field, const int32_t *
 // x -> round(x * 2^15) clamped to +-32767, stored as two int8 digit planes
 // (hi = value >> 8 signed, lo = value & 255 unsigned).
 cudaError_t launch_split_int16(const float * src, unsigned char * hi, unsigned char * lo, int64_t n, cudaStream_t s);
+// rows of H values (n_rows of them) -> staged-layout rows of rb bytes (hi part then
+// lo part): int16 digits (es = 1) or f16 halves (es = 2).
+cudaError_t launch_stage_rows(const float * src, int n_rows, int H, int es, int rb, unsigned char * dst,
+                              cudaStream_t s);
 cudaError_t launch_split_f16(const float * src, unsigned short * hi, unsigned short * lo, int64_t n,
                              cudaStream_t s);
 // Tensor-core joint.enc projection (pk_encproj.cu): weights split into f16 hi / lo

@@ -181,6 +181,24 @@ __global__ void split_int16_kernel(const float * __restrict__ src, int8_t * __re
     lo[i] = (uint8_t) (q & 255);
 }
 
+__global__ void stage_rows_kernel(const float * __restrict__ src, int n_rows, int H, int es, int rb,
+                                  unsigned char * __restrict__ dst) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows * H) return;
+    const int r = i / H, j = i - (i / H) * H;
+    const float x = src[i];
+    unsigned char * row = dst + (size_t) r * rb;
+    if (es == 1) {
+        const int q = max(-32767, min(32767, __float2int_rn(x * 32768.0f)));
+        row[j] = (unsigned char) (int8_t) (q >> 8);
+        row[H + j] = (unsigned char) (q & 255);
+    } else {
+        const __half h = __float2half_rn(x);
+        reinterpret_cast<__half *>(row)[j] = h;
+        reinterpret_cast<__half *>(row)[H + j] = __float2half_rn(x - __half2float(h));
+    }
+}
+
 __global__ void extract_field_kernel(const int32_t * __restrict__ ust, int B, int field,
                                      int32_t * __restrict__ dst) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -233,6 +251,14 @@ cudaError_t launch_split_int16(const float * src, unsigned char * hi, unsigned c
                                cudaStream_t s) {
     if (n <= 0) return cudaSuccess;
     split_int16_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, s>>>(src, reinterpret_cast<int8_t *>(hi), lo, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_stage_rows(const float * src, int n_rows, int H, int es, int rb, unsigned char * dst,
+                              cudaStream_t s) {
+    const int n = n_rows * H;
+    if (n <= 0) return cudaSuccess;
+    stage_rows_kernel<<<(n + 255) / 256, 256, 0, s>>>(src, n_rows, H, es, rb, dst);
     return cudaGetLastError();
 }
 

@@ -39,6 +39,31 @@ __device__ __forceinline__ unsigned long long gtimer() {
     return t;
 }
 
+// Sub-phase timing of CTA 0 in SM clock cycles, compiled in only with
+// -DPK_SUBPROF (development builds): SUBMARK(s) adds the cycles since the
+// previous mark to slot s (s < 0: restart the interval; -2: publish the slots
+// to g_subprof, -3: clear them).
+#ifdef PK_SUBPROF
+__device__ unsigned long long g_subprof[24];
+__device__ __forceinline__ void sub_mark(int slot) {
+    __shared__ long long s_t;
+    __shared__ unsigned long long s_acc[24];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const long long now = clock64();
+        if (slot >= 0 && slot < 24) s_acc[slot] += (unsigned long long) (now - s_t);
+        if (slot == -2)
+            for (int i = 0; i < 24; ++i) g_subprof[i] = s_acc[i];
+        if (slot == -3)
+            for (int i = 0; i < 24; ++i) s_acc[i] = 0;
+        if (slot == -4) s_acc[14] += 1;   // count (leader rounds run by CTA 0)
+        s_t = now;
+    }
+}
+#define SUBMARK(s) sub_mark(s)
+#else
+#define SUBMARK(s) do { } while (0)
+#endif
+
 __device__ __forceinline__ unsigned ld_acquire(const unsigned * p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -379,7 +404,7 @@ __device__ void joint_hidden(const LoopParams & P, int sel, int n_live, int j0, 
     const long long * lframe = reinterpret_cast<const long long *>(P.live_frame) + (size_t) sel * B;
     const int total = n_live * nr;
     for (int base = 0; base < total; base += 4 * blockDim.x) {
-        int utt[4], j[4];
+        int utt[4], j[4], li[4];
         long long fr[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -387,6 +412,7 @@ __device__ void joint_hidden(const LoopParams & P, int sel, int n_live, int j0, 
             utt[u] = -1;
             if (idx < total) {
                 const int i = idx / nr;
+                li[u] = i;
                 j[u] = j0 + (idx - i * nr);
                 utt[u] = __ldcg(&live[i]);
                 fr[u] = __ldcg(&lframe[i]);
@@ -406,11 +432,12 @@ __device__ void joint_hidden(const LoopParams & P, int sel, int n_live, int j0, 
                 const float v = e[u] + q[u];
                 const float hv = (0.0f < v) ? v : 0.0f;
                 if (P.tc) {
+                    // compact row of live index i in the staged layout: f16 hi | lo
                     const __half hh = __float2half_rn(hv);
                     const __half hl = __float2half_rn(hv - __half2float(hh));
-                    const size_t o = (size_t) utt[u] * J + j[u];
-                    reinterpret_cast<__half *>(P.hid16)[o] = hh;
-                    reinterpret_cast<__half *>(P.hid16)[(size_t) B * J + o] = hl;
+                    __half * row = reinterpret_cast<__half *>(P.hidc + (size_t) li[u] * P.rbj);
+                    row[j[u]] = hh;
+                    row[J + j[u]] = hl;
                 } else {
                     P.hid[(size_t) utt[u] * J + j[u]] = hv;
                 }
@@ -497,6 +524,7 @@ __device__ void phase_pred(const LoopParams & P, bool first, int n_emit, int sel
             __syncthreads();
         }
         joint_hidden(P, sel, n_live, j0, nr);
+        SUBMARK(8);
     }
     trace_state_dump(P, first, sel);
 }
@@ -733,18 +761,30 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S, int sel, int
 
 // ---- tensor-core phases (PK_MATH_TC) -------------------------------------------
 //
-// Each phase is a small GEMM C[rows of this CTA][16 utterances] = W . X^T with
-// mma.sync.m16n8k16 (A = activations, 16 utterances x 16 k; B = 8 weight rows x
-// 16 k; f32 accumulation). Weights are exact: q8_0 quants enter as f16 (|q| <=
-// 127 is exact) and the per-32-block scale is applied in f32 after each block;
-// f16 weights enter as-is. Activations are split into f16 hi + lo (x = hi + lo
-// to 22 significant bits), two MMAs per k-step. The 8 warps split K in 32-wide
-// blocks and their partial tiles are summed through shared memory.
+// Each phase is a small GEMM C[rows of this CTA][16 utterances] = W . X^T on the
+// warp-level tensor cores, 16 utterances (one pass) at a time, the 8 warps
+// splitting K in 32-wide blocks with a shared-memory reduction. Weights are
+// exact. Activations keep f32-level accuracy:
+//  * h (LSTM outputs, |h| < 1) with q8_0 weights: int16 fixed point h * 2^15 as
+//    two int8 digits (hi signed, lo unsigned); mma.m16n8k32 s8 / u8 x s8 gives
+//    each 32-wide q8_0 block's exact int32 product, scaled by the block's d.
+//  * otherwise (hid, or f16 weights): f16 hi + lo halves (x = hi + lo to 22
+//    significant bits), two mma.m16n8k16 per weight fragment; q8_0 weights enter
+//    as exact f16 integers with the block scale applied per 32-wide block.
+//
+// Activation rows live in HBM in the layout they take in shared memory: the hi
+// part, then the lo part, padded to a row stride (rbh for h, rbj for hid) of
+// 16 mod 128 bytes so that ldmatrix rows hit distinct banks. Producers write
+// them twice where a consumer reads a whole pass: the LSTM cell update writes
+// each new h both to the utterance's state row and to a compact row indexed by
+// its position in the emit list, and the joint hidden layer is written by
+// position in the live list, so the next phase stages a pass with a single
+// bulk copy. Only rows indexed by utterance (h_prev, read back at the
+// utterance's next emission) are copied row by row.
 
 struct TcSmem {
     unsigned char * w;              // stationary weights (P.sm_weights bytes)
-    __half * xs_hi;                 // [16][ldh]
-    __half * xs_lo;                 // [16][ldh]
+    unsigned char * xr[2];          // staging regions, 16 rows of P.rbx bytes each
     float * part;                   // [kWarps][kTcRmax][8][16]
     float * C;                      // [kTcRmax][8][16]
     unsigned long long * mbar;      // staging completion barrier (bulk copies)
@@ -763,8 +803,8 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     size_t off = 0;
     s.w = raw;
     off += (P.sm_weights + 15) & ~15u;
-    s.xs_hi = reinterpret_cast<__half *>(raw + off); off += (size_t) kTcM * P.ldh * 2;
-    s.xs_lo = reinterpret_cast<__half *>(raw + off); off += (size_t) kTcM * P.ldh * 2;
+    s.xr[0] = raw + off; off += (size_t) kTcM * P.rbx;
+    s.xr[1] = raw + off; off += (size_t) kTcM * P.rbx;
     s.part = reinterpret_cast<float *>(raw + off); off += (size_t) kWarps * kTcRmax * 128 * 4;
     s.C = reinterpret_cast<float *>(raw + off); off += (size_t) kTcRmax * 128 * 4;
     s.mbar = reinterpret_cast<unsigned long long *>(raw + off); off += 16;
@@ -780,7 +820,6 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
 }
 
 // The barrier / scan helpers only use s_scan and s_flag.
-// The same view with the record arrays advanced to the pass starting at record p.
 __device__ __forceinline__ TcSmem tc_pass(const TcSmem & T, int p) {
     TcSmem q = T;
     q.s_utt += p; q.s_aux += p; q.s_aux2 += p;
@@ -793,7 +832,7 @@ __device__ __forceinline__ Smem as_smem(const TcSmem & T) {
     return s;
 }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const __half * p) {
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const unsigned char * p) {
     const unsigned a = (unsigned) __cvta_generic_to_shared(p);
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a) : "memory");
@@ -831,58 +870,57 @@ __device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, u
     hi = *reinterpret_cast<uint32_t *>(&hb);
 }
 
-// Stage rows [0, nc) of the activation tile into xs_hi / xs_lo with bulk
-// copies (the copy engine, completion counted on S.mbar). Row c is nseg
-// segments of seglen halves; src(c, s) gives segment s of row c in the hi
-// array (the lo array is lo_off halves further on), or nullptr for zeros.
-// Lane 0 of every warp issues the copies j = warp, warp + 8, ... and arrives
-// on the barrier once with its byte count. Rows nc..15 keep whatever they
-// held: each mma output row depends on its own A row only, and outputs of
-// rows >= nc are never read. Returns false (error flagged) if the copies did
-// not complete within timeout_ns.
+// Stage one pass (rows [0, nc)) with bulk copies (the copy engine), completion
+// counted on S.mbar:
+//  * tile (optional): nc contiguous rows of tile_rb bytes into region 0 with one copy;
+//  * per-row: region `rreg` row c <- row_bytes bytes at rowsrc(c) (stride rows_rb),
+//    or zeros where rowsrc(c) is nullptr.
+// Lane 0 of every warp issues its share of the copies and arrives once with its
+// byte count. Rows nc..15 keep whatever they held: each mma output row depends
+// on its own A row only, and outputs of rows >= nc are never read. Generic-proxy
+// accesses of the regions (ldmatrix reads in tc_gemm_nt, the zero stores here
+// and at kernel start) are each followed by fence.proxy.async in the thread that
+// made them and by a CTA barrier before the next stage issues its copies.
+// Returns false (error flagged) if the copies did not complete within timeout_ns.
 template <typename F>
-__device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S, int nc, int nseg, int seglen,
-                                         size_t lo_off, F src) {
+__device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S, int nc,
+                                         const unsigned char * tile, unsigned tile_rb,
+                                         int rreg, unsigned row_bytes, unsigned rows_rb, F rowsrc) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned ph = (unsigned) S.s_flag[2];
-    const int ncopy = nc * nseg * 2;
-    const unsigned bytes = (unsigned) seglen * 2u;
     const unsigned mb = (unsigned) __cvta_generic_to_shared(S.mbar);
-    // Generic-proxy accesses of xs (ldmatrix reads in tc_gemm_nt, zero stores
-    // here and at kernel start) are each followed by fence.proxy.async in the
-    // thread that made them and by a CTA barrier before the next stage issues
-    // its copies, so the async writes below are ordered after them.
-    // zero segments (reset state): plain stores
-    for (int cs = warp; cs < nc * nseg; cs += kWarps) {
-        const int c = cs / nseg, sg = cs - c * nseg;
-        if (src(c, sg) == nullptr) {
-            for (int k = lane * 8; k < seglen; k += 32 * 8) {
-                *reinterpret_cast<uint4 *>(S.xs_hi + c * P.ldh + sg * seglen + k) = make_uint4(0u, 0u, 0u, 0u);
-                *reinterpret_cast<uint4 *>(S.xs_lo + c * P.ldh + sg * seglen + k) = make_uint4(0u, 0u, 0u, 0u);
+    if (rreg >= 0) {
+        for (int c = warp; c < nc; c += kWarps) {
+            if (rowsrc(c) == nullptr) {
+                unsigned char * d = S.xr[rreg] + (size_t) c * rows_rb;
+                for (unsigned k = lane * 16u; k < row_bytes; k += 32u * 16u)
+                    *reinterpret_cast<uint4 *>(d + k) = make_uint4(0u, 0u, 0u, 0u);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
     }
     if (lane == 0) {
-        unsigned mine = 0;
-        for (int j = warp; j < ncopy; j += kWarps) {
-            const int cs = j >> 1;
-            const int c = cs / nseg, sg = cs - c * nseg;
-            if (src(c, sg) != nullptr) mine += bytes;
-        }
+        unsigned mine = (warp == 0 && tile != nullptr) ? (unsigned) nc * tile_rb : 0u;
+        if (rreg >= 0)
+            for (int c = warp; c < nc; c += kWarps)
+                if (rowsrc(c) != nullptr) mine += row_bytes;
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(mb), "r"(mine) : "memory");
-        for (int j = warp; j < ncopy; j += kWarps) {
-            const int cs = j >> 1, hl = j & 1;
-            const int c = cs / nseg, sg = cs - c * nseg;
-            const __half * g = src(c, sg);
-            if (g == nullptr) continue;
-            if (hl) g += lo_off;
-            __half * d = (hl ? S.xs_lo : S.xs_hi) + c * P.ldh + sg * seglen;
-            const unsigned da = (unsigned) __cvta_generic_to_shared(d);
+        if (warp == 0 && tile != nullptr) {
+            const unsigned da = (unsigned) __cvta_generic_to_shared(S.xr[0]);
             asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                         :: "r"(da), "l"(g), "r"(bytes), "r"(mb) : "memory");
+                         :: "r"(da), "l"(tile), "r"((unsigned) nc * tile_rb), "r"(mb) : "memory");
+        }
+        if (rreg >= 0) {
+            for (int c = warp; c < nc; c += kWarps) {
+                const unsigned char * g = rowsrc(c);
+                if (g == nullptr) continue;
+                const unsigned da = (unsigned) __cvta_generic_to_shared(S.xr[rreg] + (size_t) c * rows_rb);
+                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                             :: "r"(da), "l"(g), "r"(row_bytes), "r"(mb) : "memory");
+            }
         }
     }
+    SUBMARK(15);
     if (threadIdx.x == 0) {
         int ok = 0;
         const unsigned long long t0 = gtimer();
@@ -897,16 +935,18 @@ __device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S,
             }
         }
         S.s_flag[3] = ok;
-        S.s_flag[2] = (int) (ph ^ 1u);
     }
     __syncthreads();
-    if (S.s_flag[3] == 0) return false;
-    // the phase is complete: this test returns at once and orders the copied data for every thread
-    unsigned done;
-    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                 : "=r"(done) : "r"(mb), "r"(ph) : "memory");
-    (void) done;
-    return true;
+    SUBMARK(16);
+    const bool ok = S.s_flag[3] != 0;
+    if (ok) {
+        // the phase is complete: this test returns at once and orders the copied data for every thread
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%0], %1; }"
+                     :: "r"(mb), "r"(ph) : "memory");
+    }
+    __syncthreads();   // everyone has read the phase bit before it flips
+    if (threadIdx.x == 0) S.s_flag[2] = (int) (ph ^ 1u);
+    return ok;
 }
 
 __device__ __forceinline__ const uint8_t * tc_frag(const LoopParams & P, const TcSmem & S, const TcBlock & b) {
@@ -917,12 +957,18 @@ __device__ __forceinline__ const float * tc_scale(const LoopParams & P, const Tc
                         : b.scale + (size_t) blockIdx.x * b.cta_scales;
 }
 
+// Where the staged A of a GEMM lives: K blocks below kb_split in region 0, the
+// rest in region 1; rb = row stride, lo = byte offset of the lo part in a row.
+struct ATile {
+    int rb0, lo0, rb1, lo1, kb_split;
+};
+
 // C[r][col][c] (r < NT tiles starting at tile t0, col = row within the tile,
 // c = utterance) for the staged activations. Each warp takes a 1/8 slice of
 // the K blocks for all NT tiles; the slices are summed through shared memory.
 // NT is a compile-time constant so the per-tile work carries no predicates.
 template <int NT>
-__device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0) {
+__device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, const ATile & A) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = lane & 3, g = lane >> 2;
     const int nkb = b.K >> 5;
@@ -933,17 +979,17 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
 #pragma unroll
     for (int r = 0; r < NT; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
     const int mrow = ((lane >> 3) & 1) * 8 + (lane & 7);
-    const int mk = (lane >> 4) * 8;
-    const __half * ahp = S.xs_hi + mrow * P.ldh + mk;
-    const __half * alp = S.xs_lo + mrow * P.ldh + mk;
+    const int mb16 = (lane >> 4) * 16;                 // byte column of this lane's ldmatrix row
+    const int kbytes = b.imma ? 32 : 64;               // bytes of one 32-wide K block per part
+    const unsigned char * a0 = S.xr[0] + mrow * A.rb0 + mb16;
+    const unsigned char * a1 = S.xr[1] + mrow * A.rb1 + mb16 - A.kb_split * kbytes;
     if (b.imma) {
-        // A = int16 fixed point (x * 2^15) as two int8 digit planes in xs_hi (signed
-        // high byte) and xs_lo (unsigned low byte), 32 bytes per K block; one
-        // m16n8k32 per plane gives the block's exact int32 dot products.
         for (int kb = kb0; kb < kb1; ++kb) {
+            const bool r0 = kb < A.kb_split;
+            const unsigned char * hp = (r0 ? a0 : a1) + kb * 32;
             uint32_t ah[4], al[4];
-            ldsm_x4(ah, ahp + kb * 16);
-            ldsm_x4(al, alp + kb * 16);
+            ldsm_x4(ah, hp);
+            ldsm_x4(al, hp + (r0 ? A.lo0 : A.lo1));
 #pragma unroll
             for (int r = 0; r < NT; ++r) {
                 const size_t u = (size_t) (t0 + r) * nkb + kb;
@@ -964,11 +1010,14 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
             for (int q = 0; q < 4; ++q) acc[r][q] *= 1.0f / 32768.0f;
     } else if (b.is_i8) {
         for (int kb = kb0; kb < kb1; ++kb) {
+            const bool r0 = kb < A.kb_split;
+            const unsigned char * hp = (r0 ? a0 : a1) + kb * 64;
+            const unsigned char * lp = hp + (r0 ? A.lo0 : A.lo1);
             uint32_t ah0[4], al0[4], ah1[4], al1[4];
-            ldsm_x4(ah0, ahp + kb * 32);
-            ldsm_x4(al0, alp + kb * 32);
-            ldsm_x4(ah1, ahp + kb * 32 + 16);
-            ldsm_x4(al1, alp + kb * 32 + 16);
+            ldsm_x4(ah0, hp);
+            ldsm_x4(al0, lp);
+            ldsm_x4(ah1, hp + 32);
+            ldsm_x4(al1, lp + 32);
 #pragma unroll
             for (int r = 0; r < NT; ++r) {
                 const size_t u = (size_t) (t0 + r) * nkb + kb;
@@ -995,11 +1044,14 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
 #pragma unroll
         for (int r = 0; r < NT; ++r) accl[r][0] = accl[r][1] = accl[r][2] = accl[r][3] = 0.0f;
         for (int kb = kb0; kb < kb1; ++kb) {
+            const bool r0 = kb < A.kb_split;
+            const unsigned char * hp = (r0 ? a0 : a1) + kb * 64;
+            const unsigned char * lp = hp + (r0 ? A.lo0 : A.lo1);
             uint32_t ah0[4], al0[4], ah1[4], al1[4];
-            ldsm_x4(ah0, ahp + kb * 32);
-            ldsm_x4(al0, alp + kb * 32);
-            ldsm_x4(ah1, ahp + kb * 32 + 16);
-            ldsm_x4(al1, alp + kb * 32 + 16);
+            ldsm_x4(ah0, hp);
+            ldsm_x4(al0, lp);
+            ldsm_x4(ah1, hp + 32);
+            ldsm_x4(al1, lp + 32);
 #pragma unroll
             for (int r = 0; r < NT; ++r) {
                 const size_t u = (size_t) (t0 + r) * nkb + kb;
@@ -1015,7 +1067,7 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
 #pragma unroll
             for (int q = 0; q < 4; ++q) acc[r][q] += accl[r][q];
     }
-    // this thread's ldmatrix reads of xs come before the next stage's bulk writes
+    // this thread's ldmatrix reads of the regions come before the next stage's bulk writes
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 #pragma unroll
     for (int r = 0; r < NT; ++r) {
@@ -1035,16 +1087,34 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
     __syncthreads();
 }
 
-__device__ __forceinline__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt) {
+__device__ __forceinline__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt,
+                                        const ATile & A) {
     switch (nt) {
-        case 1: tc_gemm_nt<1>(P, S, b, t0); break;
-        case 2: tc_gemm_nt<2>(P, S, b, t0); break;
-        case 3: tc_gemm_nt<3>(P, S, b, t0); break;
-        case 4: tc_gemm_nt<4>(P, S, b, t0); break;
-        case 5: tc_gemm_nt<5>(P, S, b, t0); break;
-        case 6: tc_gemm_nt<6>(P, S, b, t0); break;
-        case 7: tc_gemm_nt<7>(P, S, b, t0); break;
-        default: tc_gemm_nt<8>(P, S, b, t0); break;
+        case 1: tc_gemm_nt<1>(P, S, b, t0, A); break;
+        case 2: tc_gemm_nt<2>(P, S, b, t0, A); break;
+        case 3: tc_gemm_nt<3>(P, S, b, t0, A); break;
+        case 4: tc_gemm_nt<4>(P, S, b, t0, A); break;
+        case 5: tc_gemm_nt<5>(P, S, b, t0, A); break;
+        case 6: tc_gemm_nt<6>(P, S, b, t0, A); break;
+        case 7: tc_gemm_nt<7>(P, S, b, t0, A); break;
+        default: tc_gemm_nt<8>(P, S, b, t0, A); break;
+    }
+}
+
+// Bytes per h element and the h row layout: [hi | lo] parts of H elements each.
+__device__ __forceinline__ int h_es(const LoopParams & P) { return P.h_int ? 1 : 2; }
+
+// Write one new h value into a staged-layout row (state row or compact row).
+__device__ __forceinline__ void put_h(const LoopParams & P, unsigned char * row, int j, float hn) {
+    if (P.h_int) {
+        // int16 fixed point (|h| < 1): signed high digit, unsigned low digit
+        const int q16 = max(-32767, min(32767, __float2int_rn(hn * 32768.0f)));
+        row[j] = (unsigned char) (int8_t) (q16 >> 8);
+        row[P.H + j] = (unsigned char) (q16 & 255);
+    } else {
+        const __half hh = __float2half_rn(hn);
+        reinterpret_cast<__half *>(row)[j] = hh;
+        reinterpret_cast<__half *>(row)[P.H + j] = __float2half_rn(hn - __half2float(hh));
     }
 }
 
@@ -1055,6 +1125,16 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
     const int nu = max(0, min(H, u0 + upc) - u0);
     if (nu == 0) return;
     const TcBlock & bk = P.tcl[l];
+    const int es = h_es(P);
+    const unsigned hbytes = (unsigned) (2 * H * es);          // one staged h row: hi | lo
+    // state row of (h buffer, layer, utterance) and compact row of (layer, emit index)
+    auto hst = [&](int hb, int layer, int utt) -> unsigned char * {
+        return P.hst + ((((size_t) hb * L + layer) * B + utt) * P.rbh);
+    };
+    auto xnew = [&](int layer, int e) -> unsigned char * {
+        return P.xnew + (((size_t) layer * B + e) * P.rbh);
+    };
+    SUBMARK(-1);
     for (int rb = 0; rb < n_emit; rb += kTcRec) {
       const int nrb = min(kTcRec, n_emit - rb);
       for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
@@ -1064,18 +1144,18 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
           T.s_aux2[i] = ((e.y >> 31) & 1) | (((e.y >> 30) & 1) << 1);
       }
       __syncthreads();
+      SUBMARK(0);
       for (int cs = 0; cs < nrb; cs += kTcM) {
         const int nc = min(kTcM, nrb - cs);
         const TcSmem S = tc_pass(T, cs);
-        // Prefetch the cell-update operands (biases / layer-0 table rows and the
-        // old cell state) before the GEMM so their latency overlaps it. One
-        // (utterance, unit) pair per thread: nc * nu <= 16 * upc <= blockDim.
+        // Prefetch the cell-update operands (layer-0 table rows and the old cell
+        // state) before the GEMM so their latency overlaps it. One (utterance,
+        // unit) pair per thread: nc * nu <= 16 * upc <= blockDim. Raw loads only:
+        // nothing consumes them before the cell update.
         const int my = threadIdx.x;
         const bool act = my < nc * nu;
         const int cc = act ? my / nu : 0, jj = act ? my - (my / nu) * nu : 0;
         const int j = u0 + jj;
-        // Raw loads only: nothing consumes them before the cell update, so the
-        // warp does not wait for them here.
         float g0v[4] = {0.f, 0.f, 0.f, 0.f};
         float c_old = 0.0f;
         if (act) {
@@ -1085,33 +1165,23 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
             }
             if (!(S.s_aux2[cc] & 1)) c_old = __ldcg(P.c + ((size_t) l * B + S.s_utt[cc]) * H + j);
         }
-        // h rows: f16 hi / lo halves, or int16 digit planes (one byte each) when P.h_int
-        const int es = P.h_int ? 1 : 2;                       // bytes per element and half
-        const unsigned char * hb0 = reinterpret_cast<const unsigned char *>(P.h16);
-        const size_t lo_off = (size_t) 2 * L * B * H * es / 2;   // in halves
-        const int segh = H * es / 2;                            // segment length in halves
-        auto hrow = [&](int hbuf, int layer, int utt) -> const __half * {
-            return reinterpret_cast<const __half *>(hb0 + ((((size_t) hbuf * L + layer) * B + utt) * H) * es);
-        };
-        bool staged;
-        if (l == 0) {
-            // X = h_prev of layer 0 (zero on reset); W_ih0 . embed comes from the g0 table
-            staged = tc_stage(P, S, nc, 1, segh, lo_off, [&](int c, int) -> const __half * {
-                const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
-                if (reset) return nullptr;
-                return hrow(hb ^ 1, 0, utt);
-            });
-        } else {
-            // X = [h_new of layer l-1 | h_prev of layer l]
-            staged = tc_stage(P, S, nc, 2, segh, lo_off, [&](int c, int sg) -> const __half * {
-                const int utt = S.s_utt[c], reset = S.s_aux2[c] & 1, hb = S.s_aux2[c] >> 1;
-                if (sg == 0) return hrow(hb, l - 1, utt);
-                if (reset) return nullptr;
-                return hrow(hb ^ 1, l, utt);
-            });
-        }
-        if (!staged) return;
-        tc_gemm(P, S, bk, 0, bk.tiles);
+        SUBMARK(1);
+        // h_prev of layer l (zero on reset) goes row by row into the last region;
+        // above layer 0 the new h of layer l-1 comes first, one compact tile.
+        const int preg = l == 0 ? 0 : 1;
+        const unsigned char * tile = l == 0 ? nullptr : xnew(l - 1, rb + cs);
+        if (!tc_stage(P, S, nc, tile, (unsigned) P.rbh, preg, hbytes, (unsigned) P.rbh,
+                      [&](int c) -> const unsigned char * {
+                          const int utt = S.s_utt[c], a2 = S.s_aux2[c];
+                          if (a2 & 1) return nullptr;
+                          return hst((a2 >> 1) ^ 1, l, utt);
+                      })) return;
+        ATile A;
+        A.rb0 = A.rb1 = P.rbh;
+        A.lo0 = A.lo1 = H * es;
+        A.kb_split = l == 0 ? (bk.K >> 5) : (H >> 5);
+        tc_gemm(P, S, bk, 0, bk.tiles, A);
+        SUBMARK(3);
         // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
         if (act) {
             const int utt = S.s_utt[cc];
@@ -1132,20 +1202,12 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
             const float c_new = f_g * c_old + i_g * g_g;
             P.c[((size_t) l * B + utt) * H + j] = c_new;
             const float hn = o_g * tanhf(c_new);
-            const size_t o = (((size_t) hb * L + l) * B + utt) * H + j;
-            P.h[o] = hn;
-            if (P.h_int) {
-                // int16 fixed point (|h| < 1), two digit planes
-                const int q16 = max(-32767, min(32767, __float2int_rn(hn * 32768.0f)));
-                reinterpret_cast<int8_t *>(P.h16)[o] = (int8_t) (q16 >> 8);
-                reinterpret_cast<uint8_t *>(P.h16)[(size_t) 2 * L * B * H + o] = (uint8_t) (q16 & 255);
-            } else {
-                const __half hh = __float2half_rn(hn);
-                reinterpret_cast<__half *>(P.h16)[o] = hh;
-                reinterpret_cast<__half *>(P.h16)[(size_t) 2 * L * B * H + o] = __float2half_rn(hn - __half2float(hh));
-            }
+            P.h[(((size_t) hb * L + l) * B + utt) * H + j] = hn;
+            put_h(P, hst(hb, l, utt), j, hn);
+            put_h(P, xnew(l, rb + cs + cc), j, hn);
         }
         __syncthreads();
+        SUBMARK(4);
       }
     }
 }
@@ -1158,6 +1220,8 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
     const int nr = max(0, min(J, j0 + rpc) - j0);
     const int * live = P.live + (size_t) sel * B;
     const int n_list = first ? n_live : n_emit;
+    const int es = h_es(P);
+    SUBMARK(-1);
     if (nr > 0) {
       for (int rb = 0; rb < n_list; rb += kTcRec) {
         const int nrb = min(kTcRec, n_list - rb);
@@ -1175,18 +1239,31 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             T.s_aux2[i] = hb;
         }
         __syncthreads();
+        SUBMARK(5);
         for (int cs = 0; cs < nrb; cs += kTcM) {
             const int nc = min(kTcM, nrb - cs);
             const TcSmem S = tc_pass(T, cs);
-            const int es = P.h_int ? 1 : 2;   // bytes per element and half (int16 digit planes / f16 hi, lo)
-            const unsigned char * hb0 = reinterpret_cast<const unsigned char *>(P.h16);
-            if (!tc_stage(P, S, nc, 1, H * es / 2, (size_t) 2 * L * B * H * es / 2, [&](int c, int) -> const __half * {
-                    return reinterpret_cast<const __half *>(
-                        hb0 + ((((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * H) * es);
-                })) return;
+            // after the first iteration the pred list is the emit list: the last
+            // layer's new h is one compact tile; on the first iteration (the live
+            // list) rows come from the state, one by one
+            bool staged;
+            if (first) {
+                staged = tc_stage(P, S, nc, nullptr, 0u, 0, (unsigned) (2 * H * es), (unsigned) P.rbh,
+                                  [&](int c) -> const unsigned char * {
+                                      return P.hst + ((((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * P.rbh);
+                                  });
+            } else {
+                staged = tc_stage(P, S, nc, P.xnew + (((size_t) (L - 1) * B + rb + cs) * P.rbh), (unsigned) P.rbh,
+                                  -1, 0u, 0u, [&](int) -> const unsigned char * { return nullptr; });
+            }
+            if (!staged) return;
+            ATile A;
+            A.rb0 = A.rb1 = P.rbh;
+            A.lo0 = A.lo1 = H * es;
+            A.kb_split = P.tcp.K >> 5;
             for (int t0 = 0; t0 < P.tcp.tiles; t0 += kTcRmax) {
                 const int nt = min(kTcRmax, P.tcp.tiles - t0);
-                tc_gemm(P, S, P.tcp, t0, nt);
+                tc_gemm(P, S, P.tcp, t0, nt, A);
                 for (int idx = threadIdx.x; idx < nc * nt * 8; idx += blockDim.x) {
                     const int cc = idx / (nt * 8), row = t0 * 8 + (idx - cc * nt * 8);
                     if (row < nr) {
@@ -1196,10 +1273,12 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
                     }
                 }
                 __syncthreads();
+                SUBMARK(7);
             }
         }
       }
         joint_hidden(P, sel, n_live, j0, nr);
+        SUBMARK(8);
     }
     trace_state_dump(P, first, sel);
 }
@@ -1212,6 +1291,7 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
     if (nr == 0) return;
     const int * live = P.live + (size_t) sel * B;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    SUBMARK(-1);
     for (int rb = 0; rb < n_live; rb += kTcRec) {
       const int nrb = min(kTcRec, n_live - rb);
       for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
@@ -1220,16 +1300,21 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
           if (P.trace_steps > 0) T.s_aux[i] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
       }
       __syncthreads();
+      SUBMARK(9);
       for (int cs = 0; cs < nrb; cs += kTcM) {
         const int nc = min(kTcM, nrb - cs);
         const TcSmem S = tc_pass(T, cs);
-        const __half * hid16 = reinterpret_cast<const __half *>(P.hid16);
-        if (!tc_stage(P, S, nc, 1, J, (size_t) B * J, [&](int c, int) -> const __half * {
-                return hid16 + (size_t) S.s_utt[c] * J;
-            })) return;
+        // the joint hidden rows of this pass: one compact tile (live-list order)
+        if (!tc_stage(P, S, nc, P.hidc + (size_t) (rb + cs) * P.rbj, (unsigned) P.rbj, -1, 0u, 0u,
+                      [&](int) -> const unsigned char * { return nullptr; })) return;
+        ATile A;
+        A.rb0 = A.rb1 = P.rbj;
+        A.lo0 = A.lo1 = J * 2;
+        A.kb_split = P.tcj.K >> 5;
         for (int t0 = 0; t0 < P.tcj.tiles; t0 += kTcRmax) {
             const int nt = min(kTcRmax, P.tcj.tiles - t0);
-            tc_gemm(P, S, P.tcj, t0, nt);
+            tc_gemm(P, S, P.tcj, t0, nt, A);
+            SUBMARK(11);
             // warp w handles utterances w and w + 8; lanes walk the group's rows
             for (int cc = warp; cc < nc; cc += kWarps) {
                 unsigned long long bt = 0ull, bd = 0ull;
@@ -1265,8 +1350,9 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
                 }
             }
             __syncthreads();
+            SUBMARK(12);
         }
-    }
+      }
     }
 }
 
@@ -1307,9 +1393,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
     if (P.test_stall && blockIdx.x == 0) return;
     if constexpr (TC) {
         // activation rows that a pass does not stage keep finite (zero) values
-        for (int i = threadIdx.x; i < kTcM * P.ldh / 8; i += blockDim.x) {
-            reinterpret_cast<uint4 *>(T.xs_hi)[i] = make_uint4(0u, 0u, 0u, 0u);
-            reinterpret_cast<uint4 *>(T.xs_lo)[i] = make_uint4(0u, 0u, 0u, 0u);
+        for (int i = threadIdx.x; i < kTcM * P.rbx / 16; i += blockDim.x) {
+            reinterpret_cast<uint4 *>(T.xr[0])[i] = make_uint4(0u, 0u, 0u, 0u);
+            reinterpret_cast<uint4 *>(T.xr[1])[i] = make_uint4(0u, 0u, 0u, 0u);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (threadIdx.x == 0) {
@@ -1339,6 +1425,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         __syncthreads();
         if (P.stationary) tc_load_stationary(P, T);
     }
+    SUBMARK(-3);
     bool first = true;
     int emit_iters = 0;
     // CTA 0 timestamps: per segment, its own work and the wait that follows
@@ -1395,7 +1482,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         __syncthreads();
         mark(4);
         if (leader_arrive(P, S)) {
+            SUBMARK(-4);
             leader_decide(P, S, sel, n_live);
+            SUBMARK(13);
             mark(6);
             leader_release(P, gen);
         } else if (!leader_wait(P, gen, S)) {
@@ -1404,6 +1493,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         mark(7);
         ++gen;
     }
+    SUBMARK(-2);
     if (prof)
         for (int i = 0; i < 8; ++i) P.prof[i] = pacc[i];
 }
@@ -1420,9 +1510,9 @@ size_t step_loop_smem_bytes(int chunk, int ldx, int H, int grid) {
     return off;
 }
 
-size_t step_loop_tc_smem_bytes(unsigned sm_weights, int ldh, int rpc_j, int rpc_p, int upc) {
+size_t step_loop_tc_smem_bytes(unsigned sm_weights, int rbx, int rpc_j, int rpc_p, int upc) {
     size_t off = (sm_weights + 15) & ~15u;
-    off += 2 * (size_t) kTcM * ldh * 2;
+    off += 2 * (size_t) kTcM * rbx;
     off += (size_t) kWarps * kTcRmax * 128 * 4;
     off += (size_t) kTcRmax * 128 * 4;
     off += 16;
@@ -1450,3 +1540,10 @@ cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaSt
 }
 
 }  // namespace pk
+
+#ifdef PK_SUBPROF
+// Development builds only: the sub-phase cycle counters of the last launch.
+extern "C" __attribute__((visibility("default"))) int pk_debug_subprof(unsigned long long * out) {
+    return (int) cudaMemcpyFromSymbol(out, pk::g_subprof, sizeof(unsigned long long) * 24);
+}
+#endif
