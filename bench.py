@@ -273,7 +273,8 @@ def run_reference(args, model, enc, offs, T, config, rank):
     sample = (f"first {last['n_utt']} utterances of the batch, each truncated to {last['cap']} "
               f"frames ({last['frames']} frames), one utterance per thread")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": 0,
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "runs_on": "host CPU cores (rank 0)",
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / max(1, args.steps),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-init weights, N(0,1) encoder outputs)", "config": config,
