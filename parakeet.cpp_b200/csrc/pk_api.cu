@@ -448,6 +448,8 @@ struct Run {
 pk_status run_loop(pk_ctx * x, Run & r) {
     const int B = r.B, H = x->H, J = x->J, L = x->L;
     cudaStream_t s = x->stream;
+    // the loop's control word carries live and emit counts in 23 bits each
+    if (B >= (1 << 23)) return fail(PK_ERR_INVALID, "batch of %d utterances exceeds %d", B, (1 << 23) - 1);
     int64_t frames = 0;
     for (int b = 0; b < B; ++b) {
         if (r.n_frames[b] < 0) return fail(PK_ERR_INVALID, "n_frames[%d] < 0", b);
@@ -484,7 +486,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(x->livef.ensure(2 * Bs * 8));
     PK_CK(x->emit.ensure(2 * Bs * 4));
     PK_CK(x->ctl.ensure(kCtl * 4));
-    PK_CK(x->bar.ensure(4 * 4));
+    PK_CK(x->bar.ensure(8 * 4));
     PK_CK(x->tstart.ensure(8));
     PK_CK(x->prof.ensure(8 * 8));
     PK_CK(cudaMemsetAsync(x->prof.p, 0, 8 * 8, x->stream));
@@ -553,7 +555,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         PK_CK(cudaMemsetAsync(x->finish.p, 0, (size_t) B * 8, s));
     }
     PK_CK(cudaMemcpyAsync(x->ctl.p, ctl.data(), kCtl * 4, cudaMemcpyHostToDevice, s));
-    PK_CK(cudaMemsetAsync(x->bar.p, 0, 16, s));
+    PK_CK(cudaMemsetAsync(x->bar.p, 0, 32, s));
     if (r.h_in) {
         PK_CK(cudaMemcpyAsync(x->h.p, r.h_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
         PK_CK(cudaMemcpyAsync(x->c.p, r.c_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
@@ -704,6 +706,9 @@ pk_status emit_results(pk_ctx * x, Run & r, pk_result * res) {
         return fail(PK_ERR_CAPACITY, "boundary buffer holds %lld, %lld needed",
                     (long long) res->eou_bounds_cap, (long long) nbnd);
     const bool dev = res->results_on_device != 0;
+    if (dev && ((reinterpret_cast<uintptr_t>(res->tokens) | reinterpret_cast<uintptr_t>(res->steps) |
+                 reinterpret_cast<uintptr_t>(res->eou_bounds)) & 3u))
+        return fail(PK_ERR_INVALID, "device result buffers must be 4-byte aligned");
     PK_CK(launch_scan(x->ust.as<int32_t>(), B, U_NTOK, x->offsets.as<int64_t>(), s));
     ++r.launches;
     if (dev) {
@@ -769,6 +774,8 @@ pk_status batch_run(pk_ctx * x, const pk_batch * b, const pk_trace * trace, pk_r
         return fail(PK_ERR_DMODEL, "encoder d_model mismatch (%d vs %d)", b->d_enc, x->De);
     if (b->B < 0) return fail(PK_ERR_INVALID, "B < 0");
     if (b->B > 0 && (!b->frame_offsets || !b->n_frames)) return fail(PK_ERR_INVALID, "null offsets");
+    if (b->enc_on_device && (reinterpret_cast<uintptr_t>(b->enc) & 3u))
+        return fail(PK_ERR_INVALID, "device encoder output must be 4-byte aligned");
     PK_CK(cudaSetDevice(x->device));
     Run r;
     r.enc = b->enc;
@@ -986,6 +993,8 @@ namespace {
 pk_status stream_run(pk_stream * s, const float * enc, bool enc_dev, int n_frames, int msym,
                      int n_before, bool force_init, Run & r) {
     pk_ctx * x = s->ctx;
+    if (enc_dev && (reinterpret_cast<uintptr_t>(enc) & 3u))
+        return fail(PK_ERR_INVALID, "device encoder output must be 4-byte aligned");
     const bool fresh = force_init || !s->initialized;
     if (fresh) { s->sym = 0; s->carry = 0; s->last = -1; s->segstart = 0; s->symx = 0; }
     int t0 = 0;

@@ -114,7 +114,7 @@ struct LoopParams {
     int64_t * live_frame;      // [2][B] encoder row (frame_offset + t) of each live entry
     int32_t * emit;            // [B][2]: utterance, token | h-buffer << 30 | reset << 31
     int32_t * ctl;             // [kCtl]
-    unsigned int * bar;        // [4]: counter-barrier arrivals, unused, leader arrivals, leader generation
+    unsigned int * bar;        // [8]: counter-barrier arrivals, -, leader arrivals, -, 64-bit release word, -
     unsigned long long * t_start;   // [1] globaltimer at loop start
     unsigned long long * prof;      // [8] CTA 0 phase breakdown (ns), see pk_result::phase_ms
     unsigned long long * finish_ns; // [B]

@@ -37,6 +37,10 @@ __global__ void dequant_kernel(const uint8_t * __restrict__ src, int type, int64
 // build_enc_proj_graph, parakeet_tdt.cpp:433-483). 64x64 tiles, 4x4 per thread.
 constexpr int GB_M = 64, GB_N = 64, GB_K = 16;
 
+// VEC: A and W rows start on 16-byte boundaries (base aligned, K % 4 == 0), so
+// 4-float loads are used; otherwise every load is a scalar one (a caller's
+// device buffer need only be float-aligned).
+template <bool VEC>
 __global__ void __launch_bounds__(256) encproj_f32_kernel(const float * __restrict__ A, int64_t M,
                                                           int K, const float * __restrict__ W,
                                                           const float * __restrict__ bias, int N,
@@ -61,12 +65,13 @@ __global__ void __launch_bounds__(256) encproj_f32_kernel(const float * __restri
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (m < M) {
                 const float * p = A + m * K;
-                if (k + 3 < K) {
+                if (VEC && k + 3 < K) {
                     v = __ldg(reinterpret_cast<const float4 *>(p + k));
                 } else {
                     if (k < K) v.x = p[k];
                     if (k + 1 < K) v.y = p[k + 1];
                     if (k + 2 < K) v.z = p[k + 2];
+                    if (k + 3 < K) v.w = p[k + 3];
                 }
             }
             As[lk + 0][lr] = v.x; As[lk + 1][lr] = v.y; As[lk + 2][lr] = v.z; As[lk + 3][lr] = v.w;
@@ -77,12 +82,13 @@ __global__ void __launch_bounds__(256) encproj_f32_kernel(const float * __restri
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (n < N) {
                 const float * p = W + (int64_t) n * K;
-                if (k + 3 < K) {
+                if (VEC && k + 3 < K) {
                     v = __ldg(reinterpret_cast<const float4 *>(p + k));
                 } else {
                     if (k < K) v.x = p[k];
                     if (k + 1 < K) v.y = p[k + 1];
                     if (k + 2 < K) v.z = p[k + 2];
+                    if (k + 3 < K) v.w = p[k + 3];
                 }
             }
             Bs[lk + 0][lr] = v.x; Bs[lk + 1][lr] = v.y; Bs[lk + 2][lr] = v.z; Bs[lk + 3][lr] = v.w;
@@ -222,7 +228,10 @@ cudaError_t launch_encproj_f32(const float * enc, int64_t frames, int De, const 
                                const float * b, int J, float * out, cudaStream_t s) {
     if (frames <= 0) return cudaSuccess;
     dim3 grid((unsigned) ((frames + GB_M - 1) / GB_M), (unsigned) ((J + GB_N - 1) / GB_N));
-    encproj_f32_kernel<<<grid, 256, 0, s>>>(enc, frames, De, w, b, J, out);
+    const bool vec = De % 4 == 0 && (reinterpret_cast<uintptr_t>(enc) & 15u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
+    if (vec) encproj_f32_kernel<true><<<grid, 256, 0, s>>>(enc, frames, De, w, b, J, out);
+    else encproj_f32_kernel<false><<<grid, 256, 0, s>>>(enc, frames, De, w, b, J, out);
     return cudaGetLastError();
 }
 

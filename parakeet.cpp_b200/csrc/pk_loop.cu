@@ -74,6 +74,16 @@ __device__ __forceinline__ void st_release(unsigned * p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long * p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release64(unsigned long long * p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned * p, unsigned v) {
     unsigned old;
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
@@ -104,7 +114,7 @@ struct Smem {
     int * s_aux;                    // [32] token / step
     int * s_aux2;                   // [32] reset / h-buffer
     int * s_scan;                   // [kWarps + 2]
-    int * s_flag;                   // [4]
+    int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2-3 staging, 4-6 release word
 };
 
 __device__ __forceinline__ Smem carve(unsigned char * raw, const LoopParams & P, int upc) {
@@ -262,25 +272,50 @@ __device__ __forceinline__ bool leader_arrive(const LoopParams & P, const Smem &
     if (threadIdx.x == 0) {
         const unsigned old = atom_add_acq_rel(&P.bar[2], 1u);
         S.s_flag[0] = (old == gridDim.x - 1) ? 1 : 0;
+        S.s_flag[6] = 0;   // leader: errors seen while deciding
     }
     __syncthreads();
     return S.s_flag[0] != 0;
 }
 
-__device__ __forceinline__ void leader_release(const LoopParams & P, unsigned gen) {
+// The leader's release word (P.bar[4..5]) carries the next iteration's control
+// state, so the waiters need no further load: generation (16 bits) << 48 |
+// error << 47 | list selector << 46 | emit count << 23 | live count.
+__device__ __forceinline__ unsigned long long * release_word(const LoopParams & P) {
+    return reinterpret_cast<unsigned long long *>(P.bar + 4);
+}
+
+__device__ __forceinline__ unsigned long long pack_ctl(unsigned gen, int err, int sel, int n_emit, int n_live) {
+    return ((unsigned long long) (gen & 0xFFFFu) << 48) | ((unsigned long long) (err != 0) << 47) |
+           ((unsigned long long) (sel & 1) << 46) | ((unsigned long long) (unsigned) n_emit << 23) |
+           (unsigned long long) (unsigned) n_live;
+}
+
+__device__ __forceinline__ void leader_release(const LoopParams & P, unsigned long long word) {
     __syncthreads();
     if (threadIdx.x == 0) {
         // nobody arrives again before observing the new generation, which the
         // release store orders after this reset and after the CTA's decisions
         // (made visible to thread 0 by the barrier above)
         *reinterpret_cast<volatile unsigned *>(&P.bar[2]) = 0u;
-        st_release(&P.bar[3], gen + 1u);
+        st_release64(release_word(P), word);
     }
     __syncthreads();
 }
 
-__device__ __forceinline__ bool leader_wait(const LoopParams & P, unsigned gen, const Smem & S) {
-    return bounded_wait(P, S, [&] { return ld_acquire(&P.bar[3]) != gen; });
+// Waits for generation gen + 1; *word receives the release word.
+__device__ __forceinline__ bool leader_wait(const LoopParams & P, unsigned gen, const Smem & S,
+                                            unsigned long long & word) {
+    const unsigned next = (gen + 1u) & 0xFFFFu;
+    const bool ok = bounded_wait(P, S, [&] {
+        const unsigned long long w = ld_acquire64(release_word(P));
+        if ((unsigned) (w >> 48) != next) return false;
+        S.s_flag[4] = (int) (unsigned) w;
+        S.s_flag[5] = (int) (unsigned) (w >> 32);
+        return true;
+    });
+    word = ((unsigned long long) (unsigned) S.s_flag[5] << 32) | (unsigned) S.s_flag[4];
+    return ok;
 }
 
 // Block-wide exclusive scan of one int per thread.
@@ -621,8 +656,11 @@ __device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Sme
 // iteration's live and emit lists (compacted with one block scan). sel / n_live
 // are the current list selector and length; every CTA read them at the start of
 // the iteration and nothing has changed them since.
-__device__ void leader_decide(const LoopParams & P, const Smem & S, int sel, int n_live) {
+__device__ unsigned long long leader_decide(const LoopParams & P, const Smem & S, int sel, int n_live,
+                                           unsigned gen_next) {
     const int B = P.B;
+    // an error flagged anywhere so far travels with the release word
+    const int err0 = threadIdx.x == 0 ? __ldcg(&P.ctl[C_ERR]) : 0;
     const int * live_in = P.live + (size_t) sel * B;
     int * live_out = P.live + (size_t) (sel ^ 1) * B;
     int base_emit = 0, base_live = 0;
@@ -649,6 +687,7 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S, int sel, int
             int di = P.is_tdt ? key_index(kd) : 0;
             if (kt == 0ull || tok < 0 || tok >= P.V1 || (P.is_tdt && (kd == 0ull || di < 0 || di >= P.Nd))) {
                 atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+                atomicOr(&S.s_flag[6], 1);
                 P.ctl[C_ERRINFO] = utt;
                 tok = P.blank;
                 di = 0;
@@ -723,6 +762,7 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S, int sel, int
                     ++ntok;
                 } else {
                     atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+                atomicOr(&S.s_flag[6], 1);
                     P.ctl[C_ERRINFO] = utt;
                 }
             }
@@ -756,7 +796,11 @@ __device__ void leader_decide(const LoopParams & P, const Smem & S, int sel, int
         P.ctl[C_NLIVE0 + (sel ^ 1)] = base_live;
         P.ctl[C_NDECIDED] = n_live;
         P.ctl[C_SEL] = sel ^ 1;
+        if (err0 != 0) atomicOr(&S.s_flag[6], 1);
     }
+    __syncthreads();
+    const int err = S.s_flag[6];
+    return pack_ctl(gen_next, err, sel ^ 1, base_emit, base_live);
 }
 
 // ---- tensor-core phases (PK_MATH_TC) -------------------------------------------
@@ -792,7 +836,7 @@ struct TcSmem {
     int * s_aux;                    // [kTcRec]
     int * s_aux2;                   // [kTcRec]
     int * s_scan;                   // [kWarps + 2]
-    int * s_flag;                   // [4]
+    int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2-3 staging, 4-6 release word
     float * bj;                     // [rpc_j] this CTA's joint-out bias slice
     float * bp;                     // [rpc_p] this CTA's pred-proj bias slice
     float * lb;                     // [L][4][upc] LSTM gate biases of this CTA's units
@@ -812,7 +856,7 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     s.s_aux = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_aux2 = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * 4;
-    s.s_flag = reinterpret_cast<int *>(raw + off); off += 4 * 4;
+    s.s_flag = reinterpret_cast<int *>(raw + off); off += 8 * 4;
     s.bj = reinterpret_cast<float *>(raw + off); off += (size_t) P.rpc_j * 4;
     s.bp = reinterpret_cast<float *>(raw + off); off += (size_t) P.rpc_p * 4;
     s.lb = reinterpret_cast<float *>(raw + off);
@@ -1439,6 +1483,14 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             tseg = now;
         }
     };
+    // control state of the first iteration from the host-written words; later
+    // ones arrive with the leader's release word
+    unsigned long long cw;
+    {
+        const int4 cw0 = __ldcg(reinterpret_cast<const int4 *>(P.ctl));
+        const int4 cw1 = __ldcg(reinterpret_cast<const int4 *>(P.ctl) + 1);
+        cw = pack_ctl(0u, cw0.x, cw0.y, cw1.x, cw0.y ? cw0.w : cw0.z);
+    }
     for (int iter = 0;; ++iter) {
         // Every utterance advances its frame pointer at least once per
         // (max_sym + 1) iterations, so this bound only trips on a bug.
@@ -1446,14 +1498,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
             return;
         }
-        // control words C_ERR .. C_NDECIDED in one round trip (written by the
-        // host before the launch, then only by the leader)
-        const int4 cw0 = __ldcg(reinterpret_cast<const int4 *>(P.ctl));
-        const int4 cw1 = __ldcg(reinterpret_cast<const int4 *>(P.ctl) + 1);
-        if (cw0.x != 0) return;                 // C_ERR
-        const int sel = cw0.y;                  // C_SEL
-        const int n_live = sel ? cw0.w : cw0.z; // C_NLIVE1 / C_NLIVE0
-        const int n_emit = cw1.x;               // C_NEMIT
+        if ((cw >> 47) & 1ull) return;          // error flagged
+        const int sel = (int) ((cw >> 46) & 1ull);
+        const int n_emit = (int) ((cw >> 23) & 0x7FFFFFull);
+        const int n_live = (int) (cw & 0x7FFFFFull);
         if (blockIdx.x == 0 && threadIdx.x == 0 && iter > 0) {
             // plain stores (no read back): decided rounds so far, and how many of them emitted
             P.ctl[C_ITERS] = iter;
@@ -1483,11 +1531,11 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         mark(4);
         if (leader_arrive(P, S)) {
             SUBMARK(-4);
-            leader_decide(P, S, sel, n_live);
+            cw = leader_decide(P, S, sel, n_live, gen + 1u);
             SUBMARK(13);
             mark(6);
-            leader_release(P, gen);
-        } else if (!leader_wait(P, gen, S)) {
+            leader_release(P, cw);
+        } else if (!leader_wait(P, gen, S, cw)) {
             return;
         }
         mark(7);
@@ -1506,7 +1554,7 @@ size_t step_loop_smem_bytes(int chunk, int ldx, int H, int grid) {
     off += (size_t) chunk * upc * 4 * sizeof(float);
     off = (off + 15) & ~(size_t) 15;
     off += (size_t) kWarps * 32 * 2 * sizeof(unsigned long long);
-    off += 3 * 32 * sizeof(int) + (kWarps + 2) * sizeof(int) + 4 * sizeof(int);
+    off += 3 * 32 * sizeof(int) + (kWarps + 2) * sizeof(int) + 8 * sizeof(int);
     return off;
 }
 
@@ -1516,7 +1564,7 @@ size_t step_loop_tc_smem_bytes(unsigned sm_weights, int rbx, int rpc_j, int rpc_
     off += (size_t) kWarps * kTcRmax * 128 * 4;
     off += (size_t) kTcRmax * 128 * 4;
     off += 16;
-    off += 3 * kTcRec * 4 + (kWarps + 2) * 4 + 4 * 4;
+    off += 3 * kTcRec * 4 + (kWarps + 2) * 4 + 8 * 4;
     off += (size_t) (rpc_j + rpc_p) * 4;
     off += (size_t) kMaxLayers * 4 * upc * 4;
     return off;

@@ -56,7 +56,7 @@ Layout layout(int J, int H, int L) {
     o.livef = take(2 * 8);
     o.emit = take(2 * 4);
     o.ctl = take(kCtl * 4);
-    o.bar = take(4 * 4);
+    o.bar = take(8 * 4);
     o.tstart = take(8);
     o.finish = take(8);
     o.tokregion = take(8);
@@ -92,10 +92,7 @@ __global__ void noalloc_init_kernel(unsigned char * base, Layout o, int T, int b
     keys[0] = 0ull;
     keys[1] = 0ull;
     unsigned * bar = reinterpret_cast<unsigned *>(base + o.bar);
-    bar[0] = 0u;
-    bar[1] = 0u;
-    bar[2] = 0u;
-    bar[3] = 0u;
+    for (int i = 0; i < 8; ++i) bar[i] = 0u;
     *reinterpret_cast<unsigned long long *>(base + o.finish) = 0ull;
     *reinterpret_cast<int64_t *>(base + o.tokregion) = 0;
     *reinterpret_cast<int64_t *>(base + o.bndregion) = 0;
@@ -137,6 +134,9 @@ extern "C" PK_API pk_status pk_decode_noalloc(pk_ctx * ctx, const float * enc, i
     CtxView v;
     ctx_view(ctx, &v);
     if (d_enc != v.De) return na_fail(PK_ERR_DMODEL, "pk_decode_noalloc: encoder d_model mismatch");
+    if ((reinterpret_cast<uintptr_t>(enc) | reinterpret_cast<uintptr_t>(tokens) | reinterpret_cast<uintptr_t>(n_tokens) |
+         reinterpret_cast<uintptr_t>(steps)) & 3u)
+        return na_fail(PK_ERR_INVALID, "pk_decode_noalloc: device pointers must be 4-byte aligned");
     if (n_frames < 0 || n_frames > PK_NOALLOC_MAX_FRAMES)
         return na_fail(PK_ERR_INVALID, "pk_decode_noalloc: n_frames outside [0, PK_NOALLOC_MAX_FRAMES = 4096]");
     if (v.J > kNaMaxDim || v.H > kNaMaxDim)

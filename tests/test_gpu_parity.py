@@ -204,6 +204,31 @@ def test_device_resident_input(built):
     assert all(np.array_equal(a, b) for a, b in zip(ref["tokens"], r["tokens"]))
 
 
+def test_device_input_encproj_paths(built, orc):
+    """TDT-0.6b geometry runs the tensor-core enc-proj for host input and for a 16-byte
+    aligned device pointer, and the CUDA-core enc-proj for a device pointer that is only
+    4-byte aligned; all three must agree with the oracle."""
+    import torch
+    pk = built
+    m = pk.synth.tdt_0_6b(seed=21)
+    dec = pk.Decoder(m)
+    o = orc.Oracle(m)
+    T = np.array([70, 45, 96], np.int32)
+    enc, offs = pk.synth.encoder_batch(T, m.d_enc, seed=8)
+    ro = o.decode_batch(enc, offs, T)
+    r_host = dec.decode_batch(enc, offs, T)
+    t = torch.from_numpy(enc).cuda()
+    r_al = dec.decode_batch(t.data_ptr(), offs, T, enc_on_device=True)
+    t2 = torch.zeros(enc.size + 1, dtype=torch.float32, device="cuda")
+    t2[1:] = t.reshape(-1)
+    torch.cuda.synchronize()
+    r_mis = dec.decode_batch(t2.data_ptr() + 4, offs, T, enc_on_device=True)
+    torch.cuda.synchronize()
+    for r in (r_host, r_al, r_mis):
+        parity.compare_free_running(dec, o, enc, offs, T, r["tokens"], ro["tokens"])
+    assert all(np.array_equal(a, b) for a, b in zip(r_host["tokens"], r_al["tokens"]))
+
+
 def test_error_paths(built):
     pk = built
     m, g = load_case(pk, "tdt_small")
