@@ -835,6 +835,7 @@ struct TcSmem {
     int * s_utt;                    // [kTcRec] records of the current block
     int * s_aux;                    // [kTcRec]
     int * s_aux2;                   // [kTcRec]
+    int * s_lutt;                   // [kTcRec] first block of the live list (loaded with the emit records)
     int * s_scan;                   // [kWarps + 2]
     int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2-3 staging, 4-6 release word
     float * bj;                     // [rpc_j] this CTA's joint-out bias slice
@@ -855,6 +856,7 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     s.s_utt = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_aux = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_aux2 = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
+    s.s_lutt = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * 4;
     s.s_flag = reinterpret_cast<int *>(raw + off); off += 8 * 4;
     s.bj = reinterpret_cast<float *>(raw + off); off += (size_t) P.rpc_j * 4;
@@ -1162,6 +1164,28 @@ __device__ __forceinline__ void put_h(const LoopParams & P, unsigned char * row,
     }
 }
 
+// Records of one emit-list block: utterance, token, reset | h buffer << 1.
+__device__ __forceinline__ void tc_emit_record(const LoopParams & P, const TcSmem & T, int i, int g) {
+    const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + g);
+    T.s_utt[i] = e.x;
+    T.s_aux[i] = e.y & 0x3FFFFFFF;
+    T.s_aux2[i] = ((e.y >> 31) & 1) | (((e.y >> 30) & 1) << 1);
+}
+
+// Start of an iteration: the first block of the emit list (LSTM and pred-proj
+// records) and of the live list (joint records) in one round trip. When a list
+// fits one block the phases use these copies instead of reloading.
+__device__ __forceinline__ void tc_load_records(const LoopParams & P, const TcSmem & T, int sel, int n_emit,
+                                                int n_live) {
+    const int ne = min(kTcRec, n_emit), nl = min(kTcRec, n_live);
+    const int * live = P.live + (size_t) sel * P.B;
+    for (int i = threadIdx.x; i < max(ne, nl); i += blockDim.x) {
+        if (i < ne) tc_emit_record(P, T, i, i);
+        if (i < nl) T.s_lutt[i] = __ldcg(&live[i]);
+    }
+    __syncthreads();
+}
+
 __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcSmem & T) {
     const int H = P.H, L = P.L, B = P.B;
     const int upc = P.upc;
@@ -1181,13 +1205,10 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
     SUBMARK(-1);
     for (int rb = 0; rb < n_emit; rb += kTcRec) {
       const int nrb = min(kTcRec, n_emit - rb);
-      for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
-          const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + rb + i);
-          T.s_utt[i] = e.x;
-          T.s_aux[i] = e.y & 0x3FFFFFFF;
-          T.s_aux2[i] = ((e.y >> 31) & 1) | (((e.y >> 30) & 1) << 1);
+      if (n_emit > kTcRec) {   // otherwise the records loaded at the start of the iteration are in place
+          for (int i = threadIdx.x; i < nrb; i += blockDim.x) tc_emit_record(P, T, i, rb + i);
+          __syncthreads();
       }
-      __syncthreads();
       SUBMARK(0);
       for (int cs = 0; cs < nrb; cs += kTcM) {
         const int nc = min(kTcM, nrb - cs);
@@ -1269,20 +1290,20 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
     if (nr > 0) {
       for (int rb = 0; rb < n_list; rb += kTcRec) {
         const int nrb = min(kTcRec, n_list - rb);
-        for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
-            int utt, hb;
-            if (first) {
-                utt = __ldcg(&live[rb + i]);
-                hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
-            } else {
-                const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + rb + i);
-                utt = e.x;
-                hb = (e.y >> 30) & 1;
+        // records hold the h buffer as s_aux2 >> 1 (the LSTM's record format); after
+        // the first iteration, a list that fits one block is already in place
+        if (first || n_list > kTcRec) {
+            for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
+                if (first) {
+                    const int utt = __ldcg(&live[rb + i]);
+                    T.s_utt[i] = utt;
+                    T.s_aux2[i] = __ldcg(&P.ust[utt * kUst + U_HBUF]) << 1;
+                } else {
+                    tc_emit_record(P, T, i, rb + i);
+                }
             }
-            T.s_utt[i] = utt;
-            T.s_aux2[i] = hb;
+            __syncthreads();
         }
-        __syncthreads();
         SUBMARK(5);
         for (int cs = 0; cs < nrb; cs += kTcM) {
             const int nc = min(kTcM, nrb - cs);
@@ -1294,7 +1315,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             if (first) {
                 staged = tc_stage(P, S, nc, nullptr, 0u, 0, (unsigned) (2 * H * es), (unsigned) P.rbh,
                                   [&](int c) -> const unsigned char * {
-                                      return P.hst + ((((size_t) S.s_aux2[c] * L + (L - 1)) * B + S.s_utt[c]) * P.rbh);
+                                      return P.hst + ((((size_t) (S.s_aux2[c] >> 1) * L + (L - 1)) * B + S.s_utt[c]) * P.rbh);
                                   });
             } else {
                 staged = tc_stage(P, S, nc, P.xnew + (((size_t) (L - 1) * B + rb + cs) * P.rbh), (unsigned) P.rbh,
@@ -1338,16 +1359,21 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
     SUBMARK(-1);
     for (int rb = 0; rb < n_live; rb += kTcRec) {
       const int nrb = min(kTcRec, n_live - rb);
-      for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
-          const int utt = __ldcg(&live[rb + i]);
-          T.s_utt[i] = utt;
-          if (P.trace_steps > 0) T.s_aux[i] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
+      // a live list that fits one block was loaded at the start of the iteration
+      if (n_live > kTcRec || P.trace_steps > 0) {
+          for (int i = threadIdx.x; i < nrb; i += blockDim.x) {
+              const int utt = n_live > kTcRec ? __ldcg(&live[rb + i]) : T.s_lutt[i];
+              T.s_utt[i] = utt;
+              if (P.trace_steps > 0) T.s_aux[i] = __ldcg(&P.ust[utt * kUst + U_STEPS]);
+          }
+          __syncthreads();
       }
-      __syncthreads();
+      int * lrec = (n_live > kTcRec || P.trace_steps > 0) ? T.s_utt : T.s_lutt;
       SUBMARK(9);
       for (int cs = 0; cs < nrb; cs += kTcM) {
         const int nc = min(kTcM, nrb - cs);
-        const TcSmem S = tc_pass(T, cs);
+        TcSmem S = tc_pass(T, cs);
+        S.s_utt = lrec + cs;
         // the joint hidden rows of this pass: one compact tile (live-list order)
         if (!tc_stage(P, S, nc, P.hidc + (size_t) (rb + cs) * P.rbj, (unsigned) P.rbj, -1, 0u, 0u,
                       [&](int) -> const unsigned char * { return nullptr; })) return;
@@ -1507,6 +1533,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             P.ctl[C_ITERS] = iter;
             if (n_emit > 0) P.ctl[C_EMITITERS] = ++emit_iters;
         }
+        if constexpr (TC) tc_load_records(P, T, sel, n_emit, n_live);
         if (n_emit > 0) {
             for (int l = 0; l < P.L; ++l) {
                 if constexpr (TC) tc_phase_lstm(P, l, n_emit, T);
@@ -1564,7 +1591,7 @@ size_t step_loop_tc_smem_bytes(unsigned sm_weights, int rbx, int rpc_j, int rpc_
     off += (size_t) kWarps * kTcRmax * 128 * 4;
     off += (size_t) kTcRmax * 128 * 4;
     off += 16;
-    off += 3 * kTcRec * 4 + (kWarps + 2) * 4 + 8 * 4;
+    off += 4 * kTcRec * 4 + (kWarps + 2) * 4 + 8 * 4;
     off += (size_t) (rpc_j + rpc_p) * 4;
     off += (size_t) kMaxLayers * 4 * upc * 4;
     return off;
