@@ -433,10 +433,13 @@ __device__ void phase_lstm(const LoopParams & P, int l, int n_emit, const Smem &
 // hidden = relu((b_enc + W_enc enc_t) + (b_pred + W_pred pred)) (parakeet_tdt.cpp:168-171)
 // for every live utterance and this CTA's joint-hidden rows [j0, j0 + nr). Loads
 // are issued four items at a time to keep several L2 requests in flight.
-__device__ void joint_hidden(const LoopParams & P, int sel, int n_live, int j0, int nr) {
+// lutt / lfr: the live list and its encoder rows already in shared memory (the
+// whole list), or nullptr to read them from global memory.
+__device__ void joint_hidden(const LoopParams & P, int sel, int n_live, int j0, int nr,
+                             const int * lutt = nullptr, const long long * lfr = nullptr) {
     const int J = P.J, B = P.B;
-    const int * live = P.live + (size_t) sel * B;
-    const long long * lframe = reinterpret_cast<const long long *>(P.live_frame) + (size_t) sel * B;
+    const int * live = lutt ? lutt : P.live + (size_t) sel * B;
+    const long long * lframe = lfr ? lfr : reinterpret_cast<const long long *>(P.live_frame) + (size_t) sel * B;
     const int total = n_live * nr;
     for (int base = 0; base < total; base += 4 * blockDim.x) {
         int utt[4], j[4], li[4];
@@ -449,8 +452,8 @@ __device__ void joint_hidden(const LoopParams & P, int sel, int n_live, int j0, 
                 const int i = idx / nr;
                 li[u] = i;
                 j[u] = j0 + (idx - i * nr);
-                utt[u] = __ldcg(&live[i]);
-                fr[u] = __ldcg(&lframe[i]);
+                utt[u] = lutt ? live[i] : __ldcg(&live[i]);
+                fr[u] = lfr ? lframe[i] : __ldcg(&lframe[i]);
             }
         }
         float e[4], q[4];
@@ -656,8 +659,9 @@ __device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Sme
 // iteration's live and emit lists (compacted with one block scan). sel / n_live
 // are the current list selector and length; every CTA read them at the start of
 // the iteration and nothing has changed them since.
+// live_smem: the whole live list already in shared memory, or nullptr.
 __device__ unsigned long long leader_decide(const LoopParams & P, const Smem & S, int sel, int n_live,
-                                           unsigned gen_next) {
+                                           unsigned gen_next, const int * live_smem = nullptr) {
     const int B = P.B;
     // an error flagged anywhere so far travels with the release word
     const int err0 = threadIdx.x == 0 ? __ldcg(&P.ctl[C_ERR]) : 0;
@@ -670,7 +674,7 @@ __device__ unsigned long long leader_decide(const LoopParams & P, const Smem & S
         int e = 0, lv = 0, utt = -1, etok = 0, ereset = 0, ehb = 0;
         long long lframe = 0;
         if (i < n_live) {
-            utt = __ldcg(&live_in[i]);
+            utt = live_smem ? live_smem[i] : __ldcg(&live_in[i]);
             int * u = P.ust + utt * kUst;
             // every load that depends only on utt goes out together (one round trip)
             const unsigned long long kt = __ldcg(&P.keys[2 * utt + 0]);
@@ -836,6 +840,7 @@ struct TcSmem {
     int * s_aux;                    // [kTcRec]
     int * s_aux2;                   // [kTcRec]
     int * s_lutt;                   // [kTcRec] first block of the live list (loaded with the emit records)
+    long long * s_lframe;           // [kTcRec] its encoder rows
     int * s_scan;                   // [kWarps + 2]
     int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2-3 staging, 4-6 release word
     float * bj;                     // [rpc_j] this CTA's joint-out bias slice
@@ -857,6 +862,7 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     s.s_aux = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_aux2 = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_lutt = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
+    s.s_lframe = reinterpret_cast<long long *>(raw + off); off += kTcRec * 8;
     s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * 4;
     s.s_flag = reinterpret_cast<int *>(raw + off); off += 8 * 4;
     s.bj = reinterpret_cast<float *>(raw + off); off += (size_t) P.rpc_j * 4;
@@ -1181,7 +1187,10 @@ __device__ __forceinline__ void tc_load_records(const LoopParams & P, const TcSm
     const int * live = P.live + (size_t) sel * P.B;
     for (int i = threadIdx.x; i < max(ne, nl); i += blockDim.x) {
         if (i < ne) tc_emit_record(P, T, i, i);
-        if (i < nl) T.s_lutt[i] = __ldcg(&live[i]);
+        if (i < nl) {
+            T.s_lutt[i] = __ldcg(&live[i]);
+            T.s_lframe[i] = __ldcg(reinterpret_cast<const long long *>(P.live_frame) + (size_t) sel * P.B + i);
+        }
     }
     __syncthreads();
 }
@@ -1342,7 +1351,8 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             }
         }
       }
-        joint_hidden(P, sel, n_live, j0, nr);
+        if (n_live <= kTcRec) joint_hidden(P, sel, n_live, j0, nr, T.s_lutt, T.s_lframe);
+        else joint_hidden(P, sel, n_live, j0, nr);
         SUBMARK(8);
     }
     trace_state_dump(P, first, sel);
@@ -1558,7 +1568,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         mark(4);
         if (leader_arrive(P, S)) {
             SUBMARK(-4);
-            cw = leader_decide(P, S, sel, n_live, gen + 1u);
+            const int * lsm = nullptr;
+            if constexpr (TC) lsm = n_live <= kTcRec ? T.s_lutt : nullptr;
+            cw = leader_decide(P, S, sel, n_live, gen + 1u, lsm);
             SUBMARK(13);
             mark(6);
             leader_release(P, cw);
@@ -1591,7 +1603,7 @@ size_t step_loop_tc_smem_bytes(unsigned sm_weights, int rbx, int rpc_j, int rpc_
     off += (size_t) kWarps * kTcRmax * 128 * 4;
     off += (size_t) kTcRmax * 128 * 4;
     off += 16;
-    off += 4 * kTcRec * 4 + (kWarps + 2) * 4 + 8 * 4;
+    off += 4 * kTcRec * 4 + kTcRec * 8 + (kWarps + 2) * 4 + 8 * 4;
     off += (size_t) (rpc_j + rpc_p) * 4;
     off += (size_t) kMaxLayers * 4 * upc * 4;
     return off;
