@@ -84,6 +84,11 @@ __device__ __forceinline__ void st_release64(unsigned long long * p, unsigned lo
     asm volatile("st.release.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
 }
 
+// Arrival without waiting for the old value (fire-and-forget, release ordered).
+__device__ __forceinline__ void red_add_release(unsigned * p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned * p, unsigned v) {
     unsigned old;
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
@@ -228,9 +233,10 @@ __device__ __forceinline__ void stage_f32(float * xs, int ldx, int cp, int nc, i
 //
 // Two kinds, on separate words of P.bar (zeroed by the host before each launch):
 //  * counter barriers (bar[0]): a monotonically increasing arrival count. Each
-//    CTA arrives with one acq_rel add and waits until the count reaches
+//    CTA arrives with one release-ordered reduction (no reply awaited) and waits
+//    until the count reaches
 //    (k + 1) * gridDim.x for its k-th counter barrier. Nothing is reset, so an
-//    arrival costs one atomic and a wait one acquire-load loop.
+//    arrival costs one reduction and a wait one acquire-load loop.
 //  * the leader barrier (bar[2] arrivals, bar[3] generation): the last CTA to
 //    arrive runs the control step, resets the arrival word and publishes the
 //    next generation with a release store; the others wait for it.
@@ -262,7 +268,7 @@ __device__ __forceinline__ bool bounded_wait(const LoopParams & P, const Smem & 
 __device__ __forceinline__ bool grid_barrier(const LoopParams & P, unsigned & k, const Smem & S) {
     __syncthreads();
     const unsigned target = (k + 1u) * gridDim.x;
-    if (threadIdx.x == 0) atom_add_acq_rel(&P.bar[0], 1u);
+    if (threadIdx.x == 0) red_add_release(&P.bar[0], 1u);
     ++k;
     return bounded_wait(P, S, [&] { return (int) (ld_acquire(&P.bar[0]) - target) >= 0; });
 }
