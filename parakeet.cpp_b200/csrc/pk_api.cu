@@ -75,7 +75,8 @@ struct pk_ctx {
     int test_stall = 0;
     // tensor-core step loop
     int tc_ok = 0, tc_stationary = 0, rpc_j = 0, rpc_p = 0, upc = 0, tc_hint = 0;
-    int tc_rbh = 0, tc_rbj = 0, tc_rbx = 0;   // staged row bytes: h, hid, max
+    int tc_rbh = 0, tc_rbj = 0;   // staged row bytes: h, hid
+    int tc_area = 0, tc_mb = 1;   // shared-memory staging area bytes, m16 blocks per pass
     unsigned tc_sm_weights = 0;
     size_t tc_smem = 0;
     pk::TcBlock tcj{}, tcp{}, tcl[pk::kMaxLayers]{};
@@ -355,15 +356,33 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
     // staged rows: [hi | lo] + 16 bytes, an odd multiple of 16 (conflict-free ldmatrix rows)
     x->tc_rbh = 2 * H * (x->tc_hint ? 1 : 2) + 16;
     x->tc_rbj = 4 * J + 16;
-    x->tc_rbx = std::max(x->tc_rbh, x->tc_rbj);
-    size_t need = step_loop_tc_smem_bytes(off, x->tc_rbx, rpc_j, rpc_p, upc);
-    if (need <= smem_cap) {
-        x->tc_stationary = 1;
-        x->tc_sm_weights = off;
-    } else {
-        x->tc_stationary = 0;
+    // staging area for a pass of 16 * mb utterances: the joint hidden rows, or the
+    // LSTM's one or two h segments, or afterwards the GEMM's per-warp partial sums
+    auto area_for = [&](int mb) -> int {
+        const size_t pr = (size_t) kTcM * mb;
+        const size_t part = (size_t) kWarps * (mb == 2 ? 7 : kTcRmax) * 8 * pr * 4;
+        const size_t a = std::max({pr * x->tc_rbj, (L > 1 ? 2 : 1) * pr * x->tc_rbh, part});
+        return (int) ((a + 15) & ~(size_t) 15);
+    };
+    // passes of 32 when every GEMM of the loop has at most 7 tiles per call and
+    // 32 utterances x the CTA's units fit one thread each in the cell update
+    const bool mb2_ok = tiles_l <= 7 && kTcM * 2 * upc <= kThreads;
+    size_t need = 0;
+    x->tc_stationary = 0;
+    for (int mb = mb2_ok ? 2 : 1; mb >= 1 && !x->tc_stationary; --mb) {
+        need = step_loop_tc_smem_bytes(off, area_for(mb), rpc_j, rpc_p, upc);
+        if (need <= smem_cap) {
+            x->tc_stationary = 1;
+            x->tc_sm_weights = off;
+            x->tc_mb = mb;
+            x->tc_area = area_for(mb);
+        }
+    }
+    if (!x->tc_stationary) {
         x->tc_sm_weights = 0;
-        need = step_loop_tc_smem_bytes(0, x->tc_rbx, rpc_j, rpc_p, upc);
+        x->tc_mb = 1;
+        x->tc_area = area_for(1);
+        need = step_loop_tc_smem_bytes(0, x->tc_area, rpc_j, rpc_p, upc);
         if (need > smem_cap) return PK_OK;
     }
     x->tc_smem = need;
@@ -579,7 +598,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         P.hidc = x->hidc.as<unsigned char>();
         P.stationary = x->tc_stationary;
         P.sm_weights = x->tc_sm_weights;
-        P.rbh = x->tc_rbh; P.rbj = x->tc_rbj; P.rbx = x->tc_rbx;
+        P.rbh = x->tc_rbh; P.rbj = x->tc_rbj; P.area = x->tc_area; P.mb = x->tc_mb;
         P.rpc_j = x->rpc_j; P.rpc_p = x->rpc_p; P.upc = x->upc; P.h_int = x->tc_hint;
         P.tcj = x->tcj; P.tcp = x->tcp;
         for (int l = 0; l < L; ++l) P.tcl[l] = x->tcl[l];

@@ -78,7 +78,9 @@ struct LoopParams {
     int tc;
     int stationary;            // copy TC weights into shared memory at kernel start
     unsigned sm_weights;       // bytes of the stationary region
-    int rbh, rbj, rbx;         // bytes per staged row: h (2 H es + 16), hid (4 J + 16), max of both
+    int rbh, rbj;              // bytes per staged row: h (2 H es + 16), hid (4 J + 16)
+    int area;                  // bytes of the shared-memory staging area (multiple of 16)
+    int mb;                    // m16 blocks per pass: passes of 16 * mb utterances
     int rpc_j, rpc_p, upc;     // joint rows, pred rows, LSTM units per CTA
     int h_int;                 // LSTM outputs staged as int16 fixed point (two int8 digit planes)
     TcBlock tcj, tcp, tcl[kMaxLayers];
@@ -137,7 +139,7 @@ struct LoopParams {
 // Launch wrappers (defined in the .cu files).
 cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s);
 size_t      step_loop_smem_bytes(int chunk, int ldx, int H, int grid);
-size_t      step_loop_tc_smem_bytes(unsigned sm_weights, int rbx, int rpc_j, int rpc_p, int upc);
+size_t      step_loop_tc_smem_bytes(unsigned sm_weights, int area, int rpc_j, int rpc_p, int upc);
 cudaError_t step_loop_configure(size_t smem, int tc);
 cudaError_t step_loop_occupancy(size_t smem, int tc, int * blocks_per_sm);
 

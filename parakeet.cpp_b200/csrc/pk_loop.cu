@@ -838,9 +838,9 @@ __device__ unsigned long long leader_decide(const LoopParams & P, const Smem & S
 
 struct TcSmem {
     unsigned char * w;              // stationary weights (P.sm_weights bytes)
-    unsigned char * xr[2];          // staging regions, 16 rows of P.rbx bytes each
-    float * part;                   // [kWarps][kTcRmax][8][16]
-    float * C;                      // [kTcRmax][8][16]
+    unsigned char * area;           // staging area (P.area bytes): the pass's activation rows, then the
+                                    // GEMM's per-warp partial sums once the rows have been read
+    float * C;                      // [kTcRmax][8][16 * mb] reduced GEMM output
     unsigned long long * mbar;      // staging completion barrier (bulk copies)
     int * s_utt;                    // [kTcRec] records of the current block
     int * s_aux;                    // [kTcRec]
@@ -859,10 +859,8 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     size_t off = 0;
     s.w = raw;
     off += (P.sm_weights + 15) & ~15u;
-    s.xr[0] = raw + off; off += (size_t) kTcM * P.rbx;
-    s.xr[1] = raw + off; off += (size_t) kTcM * P.rbx;
-    s.part = reinterpret_cast<float *>(raw + off); off += (size_t) kWarps * kTcRmax * 128 * 4;
-    s.C = reinterpret_cast<float *>(raw + off); off += (size_t) kTcRmax * 128 * 4;
+    s.area = raw + off; off += (size_t) P.area;
+    s.C = reinterpret_cast<float *>(raw + off); off += (size_t) kTcRmax * 128 * 2 * 4;
     s.mbar = reinterpret_cast<unsigned long long *>(raw + off); off += 16;
     s.s_utt = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_aux = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
@@ -928,11 +926,11 @@ __device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, u
     hi = *reinterpret_cast<uint32_t *>(&hb);
 }
 
-// Stage one pass (rows [0, nc)) with bulk copies (the copy engine), completion
-// counted on S.mbar:
-//  * tile (optional): nc contiguous rows of tile_rb bytes into region 0 with one copy;
-//  * per-row: region `rreg` row c <- row_bytes bytes at rowsrc(c) (stride rows_rb),
-//    or zeros where rowsrc(c) is nullptr.
+// Stage one pass (rows [0, nc), nc <= 16 * mb) with bulk copies (the copy
+// engine), completion counted on S.mbar:
+//  * tile (optional): nc contiguous rows of tile_rb bytes to dtile with one copy;
+//  * per-row (drows != nullptr): drows + c * rows_rb <- row_bytes bytes at
+//    rowsrc(c), or zeros where rowsrc(c) is nullptr.
 // Lane 0 of every warp issues its share of the copies and arrives once with its
 // byte count. Rows nc..15 keep whatever they held: each mma output row depends
 // on its own A row only, and outputs of rows >= nc are never read. Generic-proxy
@@ -942,15 +940,15 @@ __device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, u
 // Returns false (error flagged) if the copies did not complete within timeout_ns.
 template <typename F>
 __device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S, int nc,
-                                         const unsigned char * tile, unsigned tile_rb,
-                                         int rreg, unsigned row_bytes, unsigned rows_rb, F rowsrc) {
+                                         const unsigned char * tile, unsigned tile_rb, unsigned char * dtile,
+                                         unsigned char * drows, unsigned row_bytes, unsigned rows_rb, F rowsrc) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned ph = (unsigned) S.s_flag[2];
     const unsigned mb = (unsigned) __cvta_generic_to_shared(S.mbar);
-    if (rreg >= 0) {
+    if (drows != nullptr) {
         for (int c = warp; c < nc; c += kWarps) {
             if (rowsrc(c) == nullptr) {
-                unsigned char * d = S.xr[rreg] + (size_t) c * rows_rb;
+                unsigned char * d = drows + (size_t) c * rows_rb;
                 for (unsigned k = lane * 16u; k < row_bytes; k += 32u * 16u)
                     *reinterpret_cast<uint4 *>(d + k) = make_uint4(0u, 0u, 0u, 0u);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -959,20 +957,20 @@ __device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S,
     }
     if (lane == 0) {
         unsigned mine = (warp == 0 && tile != nullptr) ? (unsigned) nc * tile_rb : 0u;
-        if (rreg >= 0)
+        if (drows != nullptr)
             for (int c = warp; c < nc; c += kWarps)
                 if (rowsrc(c) != nullptr) mine += row_bytes;
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(mb), "r"(mine) : "memory");
         if (warp == 0 && tile != nullptr) {
-            const unsigned da = (unsigned) __cvta_generic_to_shared(S.xr[0]);
+            const unsigned da = (unsigned) __cvta_generic_to_shared(dtile);
             asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                          :: "r"(da), "l"(tile), "r"((unsigned) nc * tile_rb), "r"(mb) : "memory");
         }
-        if (rreg >= 0) {
+        if (drows != nullptr) {
             for (int c = warp; c < nc; c += kWarps) {
                 const unsigned char * g = rowsrc(c);
                 if (g == nullptr) continue;
-                const unsigned da = (unsigned) __cvta_generic_to_shared(S.xr[rreg] + (size_t) c * rows_rb);
+                const unsigned da = (unsigned) __cvta_generic_to_shared(drows + (size_t) c * rows_rb);
                 asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                              :: "r"(da), "l"(g), "r"(row_bytes), "r"(mb) : "memory");
             }
@@ -1015,17 +1013,23 @@ __device__ __forceinline__ const float * tc_scale(const LoopParams & P, const Tc
                         : b.scale + (size_t) blockIdx.x * b.cta_scales;
 }
 
-// Where the staged A of a GEMM lives: K blocks below kb_split in region 0, the
-// rest in region 1; rb = row stride, lo = byte offset of the lo part in a row.
+// Where the staged A of a GEMM lives: K blocks below kb_split in the rows at
+// r0, the rest in the rows at r1 (row stride rb bytes; lo part lo bytes into a
+// row). m16 block m of the pass starts 16 * m rows further on.
 struct ATile {
-    int rb0, lo0, rb1, lo1, kb_split;
+    const unsigned char * r0;
+    const unsigned char * r1;
+    int rb, lo, kb_split;
 };
 
 // C[r][col][c] (r < NT tiles starting at tile t0, col = row within the tile,
-// c = utterance) for the staged activations. Each warp takes a 1/8 slice of
-// the K blocks for all NT tiles; the slices are summed through shared memory.
-// NT is a compile-time constant so the per-tile work carries no predicates.
-template <int NT>
+// c < 16 * MB = utterance of the pass) for the staged activations. Each warp
+// takes a 1/8 slice of the K blocks for all NT tiles and MB m16 blocks (the
+// weight fragments are loaded once for the MB blocks); the slices are summed
+// through shared memory, in the staging area, whose rows are no longer needed
+// once every warp has finished its ldmatrix reads. NT and MB are compile-time
+// constants so the per-tile work carries no predicates.
+template <int NT, int MB>
 __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, const ATile & A) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = lane & 3, g = lane >> 2;
@@ -1033,129 +1037,164 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
     const int kb0 = (warp * nkb) / kWarps, kb1 = ((warp + 1) * nkb) / kWarps;
     const uint8_t * frag = tc_frag(P, S, b);
     const float * scale = tc_scale(P, S, b);
-    float acc[NT][4];
+    float acc[NT][MB][4];
 #pragma unroll
-    for (int r = 0; r < NT; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+    for (int r = 0; r < NT; ++r)
+#pragma unroll
+        for (int m = 0; m < MB; ++m) acc[r][m][0] = acc[r][m][1] = acc[r][m][2] = acc[r][m][3] = 0.0f;
     const int mrow = ((lane >> 3) & 1) * 8 + (lane & 7);
     const int mb16 = (lane >> 4) * 16;                 // byte column of this lane's ldmatrix row
     const int kbytes = b.imma ? 32 : 64;               // bytes of one 32-wide K block per part
-    const unsigned char * a0 = S.xr[0] + mrow * A.rb0 + mb16;
-    const unsigned char * a1 = S.xr[1] + mrow * A.rb1 + mb16 - A.kb_split * kbytes;
+    const size_t mstep = (size_t) 16 * A.rb;           // bytes between m16 blocks
+    const unsigned char * a0 = A.r0 + mrow * A.rb + mb16;
+    const unsigned char * a1 = A.r1 + mrow * A.rb + mb16 - A.kb_split * kbytes;
     if (b.imma) {
         for (int kb = kb0; kb < kb1; ++kb) {
-            const bool r0 = kb < A.kb_split;
-            const unsigned char * hp = (r0 ? a0 : a1) + kb * 32;
-            uint32_t ah[4], al[4];
-            ldsm_x4(ah, hp);
-            ldsm_x4(al, hp + (r0 ? A.lo0 : A.lo1));
+            const unsigned char * hp = (kb < A.kb_split ? a0 : a1) + kb * 32;
+            uint32_t ah[MB][4], al[MB][4];
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                ldsm_x4(ah[m], hp + m * mstep);
+                ldsm_x4(al[m], hp + m * mstep + A.lo);
+            }
 #pragma unroll
             for (int r = 0; r < NT; ++r) {
                 const size_t u = (size_t) (t0 + r) * nkb + kb;
                 const uint2 w = *reinterpret_cast<const uint2 *>(frag + (u * 32 + lane) * 8);
                 const float2 sc = *reinterpret_cast<const float2 *>(scale + u * 8 + 2 * t);
-                int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
-                imma_s8s8(dh, ah, w.x, w.y);
-                imma_u8s8(dl, al, w.x, w.y);
-                acc[r][0] = fmaf(sc.x, (float) (dh[0] * 256 + dl[0]), acc[r][0]);
-                acc[r][1] = fmaf(sc.y, (float) (dh[1] * 256 + dl[1]), acc[r][1]);
-                acc[r][2] = fmaf(sc.x, (float) (dh[2] * 256 + dl[2]), acc[r][2]);
-                acc[r][3] = fmaf(sc.y, (float) (dh[3] * 256 + dl[3]), acc[r][3]);
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
+                    imma_s8s8(dh, ah[m], w.x, w.y);
+                    imma_u8s8(dl, al[m], w.x, w.y);
+                    acc[r][m][0] = fmaf(sc.x, (float) (dh[0] * 256 + dl[0]), acc[r][m][0]);
+                    acc[r][m][1] = fmaf(sc.y, (float) (dh[1] * 256 + dl[1]), acc[r][m][1]);
+                    acc[r][m][2] = fmaf(sc.x, (float) (dh[2] * 256 + dl[2]), acc[r][m][2]);
+                    acc[r][m][3] = fmaf(sc.y, (float) (dh[3] * 256 + dl[3]), acc[r][m][3]);
+                }
             }
         }
 #pragma unroll
         for (int r = 0; r < NT; ++r)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) acc[r][q] *= 1.0f / 32768.0f;
+            for (int m = 0; m < MB; ++m)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[r][m][q] *= 1.0f / 32768.0f;
     } else if (b.is_i8) {
         for (int kb = kb0; kb < kb1; ++kb) {
-            const bool r0 = kb < A.kb_split;
-            const unsigned char * hp = (r0 ? a0 : a1) + kb * 64;
-            const unsigned char * lp = hp + (r0 ? A.lo0 : A.lo1);
-            uint32_t ah0[4], al0[4], ah1[4], al1[4];
-            ldsm_x4(ah0, hp);
-            ldsm_x4(al0, lp);
-            ldsm_x4(ah1, hp + 32);
-            ldsm_x4(al1, lp + 32);
+            const unsigned char * hp = (kb < A.kb_split ? a0 : a1) + kb * 64;
+            uint32_t ah0[MB][4], al0[MB][4], ah1[MB][4], al1[MB][4];
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                ldsm_x4(ah0[m], hp + m * mstep);
+                ldsm_x4(al0[m], hp + m * mstep + A.lo);
+                ldsm_x4(ah1[m], hp + m * mstep + 32);
+                ldsm_x4(al1[m], hp + m * mstep + A.lo + 32);
+            }
 #pragma unroll
             for (int r = 0; r < NT; ++r) {
                 const size_t u = (size_t) (t0 + r) * nkb + kb;
                 const uint2 w = *reinterpret_cast<const uint2 *>(frag + (u * 32 + lane) * 8);
                 const float2 sc = *reinterpret_cast<const float2 *>(scale + u * 8 + 2 * t);
-                // two independent chains (hi, lo) of two k16 steps each; the
-                // q8_0 block scale is applied to their sum
-                float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
                 uint32_t b0, b1, b2, b3;
                 biased_i8x4_to_h2x2(w.x, b0, b1);
                 biased_i8x4_to_h2x2(w.y, b2, b3);
-                mma16816(th, ah0, b0, b1);
-                mma16816(tl, al0, b0, b1);
-                mma16816(th, ah1, b2, b3);
-                mma16816(tl, al1, b2, b3);
-                acc[r][0] = fmaf(sc.x, th[0] + tl[0], acc[r][0]);
-                acc[r][1] = fmaf(sc.y, th[1] + tl[1], acc[r][1]);
-                acc[r][2] = fmaf(sc.x, th[2] + tl[2], acc[r][2]);
-                acc[r][3] = fmaf(sc.y, th[3] + tl[3], acc[r][3]);
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    // two independent chains (hi, lo) of two k16 steps each; the
+                    // q8_0 block scale is applied to their sum
+                    float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(th, ah0[m], b0, b1);
+                    mma16816(tl, al0[m], b0, b1);
+                    mma16816(th, ah1[m], b2, b3);
+                    mma16816(tl, al1[m], b2, b3);
+                    acc[r][m][0] = fmaf(sc.x, th[0] + tl[0], acc[r][m][0]);
+                    acc[r][m][1] = fmaf(sc.y, th[1] + tl[1], acc[r][m][1]);
+                    acc[r][m][2] = fmaf(sc.x, th[2] + tl[2], acc[r][m][2]);
+                    acc[r][m][3] = fmaf(sc.y, th[3] + tl[3], acc[r][m][3]);
+                }
             }
         }
     } else {
-        float accl[NT][4];   // lo-half chain
-#pragma unroll
-        for (int r = 0; r < NT; ++r) accl[r][0] = accl[r][1] = accl[r][2] = accl[r][3] = 0.0f;
         for (int kb = kb0; kb < kb1; ++kb) {
-            const bool r0 = kb < A.kb_split;
-            const unsigned char * hp = (r0 ? a0 : a1) + kb * 64;
-            const unsigned char * lp = hp + (r0 ? A.lo0 : A.lo1);
-            uint32_t ah0[4], al0[4], ah1[4], al1[4];
-            ldsm_x4(ah0, hp);
-            ldsm_x4(al0, lp);
-            ldsm_x4(ah1, hp + 32);
-            ldsm_x4(al1, lp + 32);
+            const unsigned char * hp = (kb < A.kb_split ? a0 : a1) + kb * 64;
+            uint32_t ah0[MB][4], al0[MB][4], ah1[MB][4], al1[MB][4];
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                ldsm_x4(ah0[m], hp + m * mstep);
+                ldsm_x4(al0[m], hp + m * mstep + A.lo);
+                ldsm_x4(ah1[m], hp + m * mstep + 32);
+                ldsm_x4(al1[m], hp + m * mstep + A.lo + 32);
+            }
 #pragma unroll
             for (int r = 0; r < NT; ++r) {
                 const size_t u = (size_t) (t0 + r) * nkb + kb;
                 const uint4 w = *reinterpret_cast<const uint4 *>(frag + (u * 32 + lane) * 16);
-                mma16816(acc[r], ah0, w.x, w.y);
-                mma16816(accl[r], al0, w.x, w.y);
-                mma16816(acc[r], ah1, w.z, w.w);
-                mma16816(accl[r], al1, w.z, w.w);
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    mma16816(acc[r][m], ah0[m], w.x, w.y);
+                    mma16816(acc[r][m], al0[m], w.x, w.y);
+                    mma16816(acc[r][m], ah1[m], w.z, w.w);
+                    mma16816(acc[r][m], al1[m], w.z, w.w);
+                }
             }
         }
-#pragma unroll
-        for (int r = 0; r < NT; ++r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[r][q] += accl[r][q];
     }
-    // this thread's ldmatrix reads of the regions come before the next stage's bulk writes
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // every warp's ldmatrix reads are done before the partial sums overwrite the rows
+    __syncthreads();
+    constexpr int W = 16 * MB;                         // utterance columns of a partial tile
+    float * part = reinterpret_cast<float *>(S.area);  // [kWarps][NT][8][W]
 #pragma unroll
     for (int r = 0; r < NT; ++r) {
-        float * pp = S.part + ((warp * kTcRmax + r) * 8) * 16;
-        pp[(2 * t) * 16 + g] = acc[r][0];
-        pp[(2 * t + 1) * 16 + g] = acc[r][1];
-        pp[(2 * t) * 16 + g + 8] = acc[r][2];
-        pp[(2 * t + 1) * 16 + g + 8] = acc[r][3];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            float * pp = part + ((warp * NT + r) * 8) * W + m * 16;
+            pp[(2 * t) * W + g] = acc[r][m][0];
+            pp[(2 * t + 1) * W + g] = acc[r][m][1];
+            pp[(2 * t) * W + g + 8] = acc[r][m][2];
+            pp[(2 * t + 1) * W + g + 8] = acc[r][m][3];
+        }
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < NT * 128; idx += blockDim.x) {
+    for (int idx = threadIdx.x; idx < NT * 8 * W; idx += blockDim.x) {
         float s = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) s += S.part[w * kTcRmax * 128 + idx];
+        for (int w = 0; w < kWarps; ++w) s += part[w * NT * 8 * W + idx];
         S.C[idx] = s;
     }
+    // this thread's generic accesses of the area come before the next stage's bulk writes
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
 }
 
+// C layout: row r of the pass's tile group, utterance c -> C[(r >> 3) * 8 * W + (r & 7) * W + c].
+__device__ __forceinline__ int c_index(int r, int c, int W) { return (r >> 3) * 8 * W + (r & 7) * W + c; }
+
+// mbp: m16 blocks of this pass (2 only when the pass has more than 16
+// utterances and the loop was set up for 32-utterance passes).
 __device__ __forceinline__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt,
-                                        const ATile & A) {
+                                        const ATile & A, int mbp) {
+    if (mbp == 2) {
+        switch (nt) {
+            case 1: tc_gemm_nt<1, 2>(P, S, b, t0, A); break;
+            case 2: tc_gemm_nt<2, 2>(P, S, b, t0, A); break;
+            case 3: tc_gemm_nt<3, 2>(P, S, b, t0, A); break;
+            case 4: tc_gemm_nt<4, 2>(P, S, b, t0, A); break;
+            case 5: tc_gemm_nt<5, 2>(P, S, b, t0, A); break;
+            case 6: tc_gemm_nt<6, 2>(P, S, b, t0, A); break;
+            default: tc_gemm_nt<7, 2>(P, S, b, t0, A); break;
+        }
+        return;
+    }
     switch (nt) {
-        case 1: tc_gemm_nt<1>(P, S, b, t0, A); break;
-        case 2: tc_gemm_nt<2>(P, S, b, t0, A); break;
-        case 3: tc_gemm_nt<3>(P, S, b, t0, A); break;
-        case 4: tc_gemm_nt<4>(P, S, b, t0, A); break;
-        case 5: tc_gemm_nt<5>(P, S, b, t0, A); break;
-        case 6: tc_gemm_nt<6>(P, S, b, t0, A); break;
-        case 7: tc_gemm_nt<7>(P, S, b, t0, A); break;
-        default: tc_gemm_nt<8>(P, S, b, t0, A); break;
+        case 1: tc_gemm_nt<1, 1>(P, S, b, t0, A); break;
+        case 2: tc_gemm_nt<2, 1>(P, S, b, t0, A); break;
+        case 3: tc_gemm_nt<3, 1>(P, S, b, t0, A); break;
+        case 4: tc_gemm_nt<4, 1>(P, S, b, t0, A); break;
+        case 5: tc_gemm_nt<5, 1>(P, S, b, t0, A); break;
+        case 6: tc_gemm_nt<6, 1>(P, S, b, t0, A); break;
+        case 7: tc_gemm_nt<7, 1>(P, S, b, t0, A); break;
+        default: tc_gemm_nt<8, 1>(P, S, b, t0, A); break;
     }
 }
 
@@ -1209,6 +1248,7 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
     if (nu == 0) return;
     const TcBlock & bk = P.tcl[l];
     const int es = h_es(P);
+    const int PR = kTcM * P.mb;                               // utterances per pass
     const unsigned hbytes = (unsigned) (2 * H * es);          // one staged h row: hi | lo
     // state row of (h buffer, layer, utterance) and compact row of (layer, emit index)
     auto hst = [&](int hb, int layer, int utt) -> unsigned char * {
@@ -1225,12 +1265,13 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
           __syncthreads();
       }
       SUBMARK(0);
-      for (int cs = 0; cs < nrb; cs += kTcM) {
-        const int nc = min(kTcM, nrb - cs);
+      for (int cs = 0; cs < nrb; cs += PR) {
+        const int nc = min(PR, nrb - cs);
         const TcSmem S = tc_pass(T, cs);
+        const int mbp = nc > kTcM ? 2 : 1;          // m16 blocks computed for this pass
         // Prefetch the cell-update operands (layer-0 table rows and the old cell
         // state) before the GEMM so their latency overlaps it. One (utterance,
-        // unit) pair per thread: nc * nu <= 16 * upc <= blockDim. Raw loads only:
+        // unit) pair per thread: nc * nu <= PR * upc <= blockDim. Raw loads only:
         // nothing consumes them before the cell update.
         const int my = threadIdx.x;
         const bool act = my < nc * nu;
@@ -1248,19 +1289,21 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
         SUBMARK(1);
         // h_prev of layer l (zero on reset) goes row by row into the last region;
         // above layer 0 the new h of layer l-1 comes first, one compact tile.
-        const int preg = l == 0 ? 0 : 1;
+        unsigned char * reg1 = S.area + (size_t) PR * P.rbh;
         const unsigned char * tile = l == 0 ? nullptr : xnew(l - 1, rb + cs);
-        if (!tc_stage(P, S, nc, tile, (unsigned) P.rbh, preg, hbytes, (unsigned) P.rbh,
+        if (!tc_stage(P, S, nc, tile, (unsigned) P.rbh, S.area, l == 0 ? S.area : reg1, hbytes, (unsigned) P.rbh,
                       [&](int c) -> const unsigned char * {
                           const int utt = S.s_utt[c], a2 = S.s_aux2[c];
                           if (a2 & 1) return nullptr;
                           return hst((a2 >> 1) ^ 1, l, utt);
                       })) return;
         ATile A;
-        A.rb0 = A.rb1 = P.rbh;
-        A.lo0 = A.lo1 = H * es;
+        A.r0 = S.area;
+        A.r1 = reg1;
+        A.rb = P.rbh;
+        A.lo = H * es;
         A.kb_split = l == 0 ? (bk.K >> 5) : (H >> 5);
-        tc_gemm(P, S, bk, 0, bk.tiles, A);
+        tc_gemm(P, S, bk, 0, bk.tiles, A, mbp);
         SUBMARK(3);
         // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
         if (act) {
@@ -1273,7 +1316,7 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
                 // ((b_ih + W_ih x) + b_hh) + W_hh h, with b_ih + W_ih x for layer 0 from
                 // the table; S.lb holds b_hh for layer 0 and b_ih + b_hh above it
                 const float pre = (l == 0 ? g0v[q] : 0.0f) + S.lb[(l * 4 + q) * upc + jj];
-                gate[q] = pre + S.C[(row >> 3) * 128 + (row & 7) * 16 + cc];
+                gate[q] = pre + S.C[c_index(row, cc, kTcM * mbp)];
             }
             const float i_g = sigmoid_ref(gate[0]);
             const float f_g = sigmoid_ref(gate[1]);
@@ -1301,6 +1344,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
     const int * live = P.live + (size_t) sel * B;
     const int n_list = first ? n_live : n_emit;
     const int es = h_es(P);
+    const int PR = kTcM * P.mb;                 // utterances per pass
     SUBMARK(-1);
     if (nr > 0) {
       for (int rb = 0; rb < n_list; rb += kTcRec) {
@@ -1320,36 +1364,39 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             __syncthreads();
         }
         SUBMARK(5);
-        for (int cs = 0; cs < nrb; cs += kTcM) {
-            const int nc = min(kTcM, nrb - cs);
+        for (int cs = 0; cs < nrb; cs += PR) {
+            const int nc = min(PR, nrb - cs);
             const TcSmem S = tc_pass(T, cs);
+            const int mbp = nc > kTcM ? 2 : 1;          // m16 blocks computed for this pass
+            const int TG = mbp == 2 ? 7 : kTcRmax;      // weight tiles per GEMM call
             // after the first iteration the pred list is the emit list: the last
             // layer's new h is one compact tile; on the first iteration (the live
             // list) rows come from the state, one by one
             bool staged;
             if (first) {
-                staged = tc_stage(P, S, nc, nullptr, 0u, 0, (unsigned) (2 * H * es), (unsigned) P.rbh,
+                staged = tc_stage(P, S, nc, nullptr, 0u, S.area, S.area, (unsigned) (2 * H * es), (unsigned) P.rbh,
                                   [&](int c) -> const unsigned char * {
                                       return P.hst + ((((size_t) (S.s_aux2[c] >> 1) * L + (L - 1)) * B + S.s_utt[c]) * P.rbh);
                                   });
             } else {
                 staged = tc_stage(P, S, nc, P.xnew + (((size_t) (L - 1) * B + rb + cs) * P.rbh), (unsigned) P.rbh,
-                                  -1, 0u, 0u, [&](int) -> const unsigned char * { return nullptr; });
+                                  S.area, nullptr, 0u, 0u, [&](int) -> const unsigned char * { return nullptr; });
             }
             if (!staged) return;
             ATile A;
-            A.rb0 = A.rb1 = P.rbh;
-            A.lo0 = A.lo1 = H * es;
+            A.r0 = A.r1 = S.area;
+            A.rb = P.rbh;
+            A.lo = H * es;
             A.kb_split = P.tcp.K >> 5;
-            for (int t0 = 0; t0 < P.tcp.tiles; t0 += kTcRmax) {
-                const int nt = min(kTcRmax, P.tcp.tiles - t0);
-                tc_gemm(P, S, P.tcp, t0, nt, A);
+            for (int t0 = 0; t0 < P.tcp.tiles; t0 += TG) {
+                const int nt = min(TG, P.tcp.tiles - t0);
+                tc_gemm(P, S, P.tcp, t0, nt, A, mbp);
                 for (int idx = threadIdx.x; idx < nc * nt * 8; idx += blockDim.x) {
                     const int cc = idx / (nt * 8), row = t0 * 8 + (idx - cc * nt * 8);
                     if (row < nr) {
                         const int r = row - t0 * 8;
                         const int j = j0 + row;
-                        P.predp[(size_t) S.s_utt[cc] * J + j] = S.bp[row] + S.C[(r >> 3) * 128 + (r & 7) * 16 + cc];
+                        P.predp[(size_t) S.s_utt[cc] * J + j] = S.bp[row] + S.C[c_index(r, cc, kTcM * mbp)];
                     }
                 }
                 __syncthreads();
@@ -1372,6 +1419,7 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
     if (nr == 0) return;
     const int * live = P.live + (size_t) sel * B;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int PR = kTcM * P.mb;                 // utterances per pass
     SUBMARK(-1);
     for (int rb = 0; rb < n_live; rb += kTcRec) {
       const int nrb = min(kTcRec, n_live - rb);
@@ -1386,29 +1434,32 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
       }
       int * lrec = (n_live > kTcRec || P.trace_steps > 0) ? T.s_utt : T.s_lutt;
       SUBMARK(9);
-      for (int cs = 0; cs < nrb; cs += kTcM) {
-        const int nc = min(kTcM, nrb - cs);
+      for (int cs = 0; cs < nrb; cs += PR) {
+        const int nc = min(PR, nrb - cs);
         TcSmem S = tc_pass(T, cs);
         S.s_utt = lrec + cs;
+        const int mbp = nc > kTcM ? 2 : 1;              // m16 blocks computed for this pass
+        const int TG = mbp == 2 ? 7 : kTcRmax;          // weight tiles per GEMM call
         // the joint hidden rows of this pass: one compact tile (live-list order)
-        if (!tc_stage(P, S, nc, P.hidc + (size_t) (rb + cs) * P.rbj, (unsigned) P.rbj, -1, 0u, 0u,
+        if (!tc_stage(P, S, nc, P.hidc + (size_t) (rb + cs) * P.rbj, (unsigned) P.rbj, S.area, nullptr, 0u, 0u,
                       [&](int) -> const unsigned char * { return nullptr; })) return;
         ATile A;
-        A.rb0 = A.rb1 = P.rbj;
-        A.lo0 = A.lo1 = J * 2;
+        A.r0 = A.r1 = S.area;
+        A.rb = P.rbj;
+        A.lo = J * 2;
         A.kb_split = P.tcj.K >> 5;
-        for (int t0 = 0; t0 < P.tcj.tiles; t0 += kTcRmax) {
-            const int nt = min(kTcRmax, P.tcj.tiles - t0);
-            tc_gemm(P, S, P.tcj, t0, nt, A);
+        for (int t0 = 0; t0 < P.tcj.tiles; t0 += TG) {
+            const int nt = min(TG, P.tcj.tiles - t0);
+            tc_gemm(P, S, P.tcj, t0, nt, A, mbp);
             SUBMARK(11);
-            // warp w handles utterances w and w + 8; lanes walk the group's rows
+            // warp w handles utterances w, w + 8, ...; lanes walk the group's rows
             for (int cc = warp; cc < nc; cc += kWarps) {
                 unsigned long long bt = 0ull, bd = 0ull;
                 for (int rr = lane; rr < nt * 8; rr += 32) {
                     const int row = t0 * 8 + rr;
                     if (row >= nr) continue;
                     const int r = r0 + row;
-                    const float logit = S.bj[row] + S.C[(rr >> 3) * 128 + (rr & 7) * 16 + cc];
+                    const float logit = S.bj[row] + S.C[c_index(rr, cc, kTcM * mbp)];
                     if (P.trace_steps > 0) {
                         const int step = S.s_aux[cc];
                         if (step < P.trace_steps)
@@ -1479,10 +1530,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
     if (P.test_stall && blockIdx.x == 0) return;
     if constexpr (TC) {
         // activation rows that a pass does not stage keep finite (zero) values
-        for (int i = threadIdx.x; i < kTcM * P.rbx / 16; i += blockDim.x) {
-            reinterpret_cast<uint4 *>(T.xr[0])[i] = make_uint4(0u, 0u, 0u, 0u);
-            reinterpret_cast<uint4 *>(T.xr[1])[i] = make_uint4(0u, 0u, 0u, 0u);
-        }
+        for (int i = threadIdx.x; i < P.area / 16; i += blockDim.x)
+            reinterpret_cast<uint4 *>(T.area)[i] = make_uint4(0u, 0u, 0u, 0u);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (threadIdx.x == 0) {
             const unsigned mb = (unsigned) __cvta_generic_to_shared(T.mbar);
@@ -1603,11 +1652,10 @@ size_t step_loop_smem_bytes(int chunk, int ldx, int H, int grid) {
     return off;
 }
 
-size_t step_loop_tc_smem_bytes(unsigned sm_weights, int rbx, int rpc_j, int rpc_p, int upc) {
+size_t step_loop_tc_smem_bytes(unsigned sm_weights, int area, int rpc_j, int rpc_p, int upc) {
     size_t off = (sm_weights + 15) & ~15u;
-    off += 2 * (size_t) kTcM * rbx;
-    off += (size_t) kWarps * kTcRmax * 128 * 4;
-    off += (size_t) kTcRmax * 128 * 4;
+    off += (size_t) area;
+    off += (size_t) kTcRmax * 128 * 2 * 4;
     off += 16;
     off += 4 * kTcRec * 4 + kTcRec * 8 + (kWarps + 2) * 4 + 8 * 4;
     off += (size_t) (rpc_j + rpc_p) * 4;
