@@ -1275,6 +1275,7 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
         // nothing consumes them before the cell update.
         const int my = threadIdx.x;
         const bool act = my < nc * nu;
+        // unit fastest: consecutive threads prefetch consecutive table / state entries
         const int cc = act ? my / nu : 0, jj = act ? my - (my / nu) * nu : 0;
         const int j = u0 + jj;
         float g0v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1392,7 +1393,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
                 const int nt = min(TG, P.tcp.tiles - t0);
                 tc_gemm(P, S, P.tcp, t0, nt, A, mbp);
                 for (int idx = threadIdx.x; idx < nc * nt * 8; idx += blockDim.x) {
-                    const int cc = idx / (nt * 8), row = t0 * 8 + (idx - cc * nt * 8);
+                    const int rr = idx / nc, cc = idx - rr * nc, row = t0 * 8 + rr;   // utterance fastest
                     if (row < nr) {
                         const int r = row - t0 * 8;
                         const int j = j0 + row;
@@ -1452,39 +1453,51 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
             const int nt = min(TG, P.tcj.tiles - t0);
             tc_gemm(P, S, P.tcj, t0, nt, A, mbp);
             SUBMARK(11);
-            // warp w handles utterances w, w + 8, ...; lanes walk the group's rows
-            for (int cc = warp; cc < nc; cc += kWarps) {
+            // thread = (utterance c, row group rg): consecutive threads read
+            // consecutive C columns; row-group partial keys meet in the staging
+            // area (free again once C is reduced), then one thread per
+            // utterance folds them into the global keys
+            {
+                const int W = kTcM * mbp, RG = kThreads / W;
+                const int c = threadIdx.x % W, rg = threadIdx.x / W;
                 unsigned long long bt = 0ull, bd = 0ull;
-                for (int rr = lane; rr < nt * 8; rr += 32) {
-                    const int row = t0 * 8 + rr;
-                    if (row >= nr) continue;
-                    const int r = r0 + row;
-                    const float logit = S.bj[row] + S.C[c_index(rr, cc, kTcM * mbp)];
-                    if (P.trace_steps > 0) {
-                        const int step = S.s_aux[cc];
-                        if (step < P.trace_steps)
-                            P.tr_logits[((size_t) S.s_utt[cc] * P.trace_steps + step) * P.Vo + r] = logit;
-                    }
-                    if (r < P.V1) {
-                        const unsigned long long k = make_key(logit, r);
-                        bt = k > bt ? k : bt;
-                    } else {
-                        const unsigned long long k = make_key(logit, r - P.V1);
-                        bd = k > bd ? k : bd;
+                if (c < nc) {
+                    for (int rr = rg; rr < nt * 8; rr += RG) {
+                        const int row = t0 * 8 + rr;
+                        if (row >= nr) break;
+                        const int r = r0 + row;
+                        const float logit = S.bj[row] + S.C[c_index(rr, c, W)];
+                        if (P.trace_steps > 0) {
+                            const int step = S.s_aux[c];
+                            if (step < P.trace_steps)
+                                P.tr_logits[((size_t) S.s_utt[c] * P.trace_steps + step) * P.Vo + r] = logit;
+                        }
+                        if (r < P.V1) {
+                            const unsigned long long k = make_key(logit, r);
+                            bt = k > bt ? k : bt;
+                        } else {
+                            const unsigned long long k = make_key(logit, r - P.V1);
+                            bd = k > bd ? k : bd;
+                        }
                     }
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const unsigned long long ot = __shfl_xor_sync(0xFFFFFFFFu, bt, o);
-                    const unsigned long long od = __shfl_xor_sync(0xFFFFFFFFu, bd, o);
-                    bt = ot > bt ? ot : bt;
-                    bd = od > bd ? od : bd;
-                }
-                if (lane == 0) {
-                    const int utt = S.s_utt[cc];
+                unsigned long long * kp = reinterpret_cast<unsigned long long *>(S.area);
+                kp[2 * threadIdx.x] = bt;
+                kp[2 * threadIdx.x + 1] = bd;
+                __syncthreads();
+                if (threadIdx.x < nc) {
+                    for (int g = 1; g < RG; ++g) {
+                        const unsigned long long ot = kp[2 * (g * W + threadIdx.x)];
+                        const unsigned long long od = kp[2 * (g * W + threadIdx.x) + 1];
+                        bt = ot > bt ? ot : bt;
+                        bd = od > bd ? od : bd;
+                    }
+                    const int utt = S.s_utt[threadIdx.x];
                     if (bt) atomicMax(&P.keys[2 * utt + 0], bt);
                     if (bd) atomicMax(&P.keys[2 * utt + 1], bd);
                 }
+                // generic accesses of the area before the next stage's bulk writes
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             }
             __syncthreads();
             SUBMARK(12);
