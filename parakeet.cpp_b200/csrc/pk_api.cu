@@ -360,7 +360,7 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
     // LSTM's one or two h segments, or afterwards the GEMM's per-warp partial sums
     auto area_for = [&](int mb) -> int {
         const size_t pr = (size_t) kTcM * mb;
-        const size_t part = (size_t) kWarps * (mb == 2 ? 7 : kTcRmax) * 8 * pr * 4;
+        const size_t part = (size_t) kWarps * (mb == 2 ? 7 : kTcRmax) * 8 * (pr + 4) * 4;   // rows padded by 4
         const size_t a = std::max({pr * x->tc_rbj, (L > 1 ? 2 : 1) * pr * x->tc_rbh, part});
         return (int) ((a + 15) & ~(size_t) 15);
     };

@@ -928,7 +928,7 @@ __device__ __forceinline__ void biased_i8x4_to_h2x2(uint32_t v, uint32_t & lo, u
 
 // Stage one pass (rows [0, nc), nc <= 16 * mb) with bulk copies (the copy
 // engine), completion counted on S.mbar:
-//  * tile (optional): nc contiguous rows of tile_rb bytes to dtile with one copy;
+//  * tile (optional): nc contiguous rows of tile_rb bytes to dtile, one slice per warp;
 //  * per-row (drows != nullptr): drows + c * rows_rb <- row_bytes bytes at
 //    rowsrc(c), or zeros where rowsrc(c) is nullptr.
 // Lane 0 of every warp issues its share of the copies and arrives once with its
@@ -956,15 +956,20 @@ __device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S,
         }
     }
     if (lane == 0) {
-        unsigned mine = (warp == 0 && tile != nullptr) ? (unsigned) nc * tile_rb : 0u;
+        // the tile goes in one 16-byte-aligned slice per warp: one issuing
+        // thread reaches about half the shared-memory fill rate that eight do
+        const unsigned ttot = tile != nullptr ? (unsigned) nc * tile_rb : 0u;
+        const unsigned tchunk = ((ttot / kWarps) + 15u) & ~15u;
+        const unsigned tbeg = min(ttot, (unsigned) warp * tchunk), tlen = min(ttot, tbeg + tchunk) - tbeg;
+        unsigned mine = tlen;
         if (drows != nullptr)
             for (int c = warp; c < nc; c += kWarps)
                 if (rowsrc(c) != nullptr) mine += row_bytes;
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(mb), "r"(mine) : "memory");
-        if (warp == 0 && tile != nullptr) {
-            const unsigned da = (unsigned) __cvta_generic_to_shared(dtile);
+        if (tlen > 0u) {
+            const unsigned da = (unsigned) __cvta_generic_to_shared(dtile + tbeg);
             asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                         :: "r"(da), "l"(tile), "r"((unsigned) nc * tile_rb), "r"(mb) : "memory");
+                         :: "r"(da), "l"(tile + tbeg), "r"(tlen), "r"(mb) : "memory");
         }
         if (drows != nullptr) {
             for (int c = warp; c < nc; c += kWarps) {
@@ -1029,12 +1034,16 @@ struct ATile {
 // through shared memory, in the staging area, whose rows are no longer needed
 // once every warp has finished its ldmatrix reads. NT and MB are compile-time
 // constants so the per-tile work carries no predicates.
+// kw (4 or 8): warps that split K. Fewer warps halve the partial sums to
+// reduce; the tensor pipe stays busy with one warp per scheduler for the
+// joint's many tiles and for passes of one m16 block.
 template <int NT, int MB>
-__device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, const ATile & A) {
+__device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, const ATile & A,
+                           int kw) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = lane & 3, g = lane >> 2;
     const int nkb = b.K >> 5;
-    const int kb0 = (warp * nkb) / kWarps, kb1 = ((warp + 1) * nkb) / kWarps;
+    const int kb0 = warp < kw ? (warp * nkb) / kw : 0, kb1 = warp < kw ? ((warp + 1) * nkb) / kw : 0;
     const uint8_t * frag = tc_frag(P, S, b);
     const float * scale = tc_scale(P, S, b);
     float acc[NT][MB][4];
@@ -1101,17 +1110,17 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
                 biased_i8x4_to_h2x2(w.y, b2, b3);
 #pragma unroll
                 for (int m = 0; m < MB; ++m) {
-                    // two independent chains (hi, lo) of two k16 steps each; the
-                    // q8_0 block scale is applied to their sum
-                    float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
+                    // one chain over the block's hi and lo parts (two k16 steps
+                    // each); the q8_0 block scale is applied to the sum
+                    float th[4] = {0.f, 0.f, 0.f, 0.f};
                     mma16816(th, ah0[m], b0, b1);
-                    mma16816(tl, al0[m], b0, b1);
+                    mma16816(th, al0[m], b0, b1);
                     mma16816(th, ah1[m], b2, b3);
-                    mma16816(tl, al1[m], b2, b3);
-                    acc[r][m][0] = fmaf(sc.x, th[0] + tl[0], acc[r][m][0]);
-                    acc[r][m][1] = fmaf(sc.y, th[1] + tl[1], acc[r][m][1]);
-                    acc[r][m][2] = fmaf(sc.x, th[2] + tl[2], acc[r][m][2]);
-                    acc[r][m][3] = fmaf(sc.y, th[3] + tl[3], acc[r][m][3]);
+                    mma16816(th, al1[m], b2, b3);
+                    acc[r][m][0] = fmaf(sc.x, th[0], acc[r][m][0]);
+                    acc[r][m][1] = fmaf(sc.y, th[1], acc[r][m][1]);
+                    acc[r][m][2] = fmaf(sc.x, th[2], acc[r][m][2]);
+                    acc[r][m][3] = fmaf(sc.y, th[3], acc[r][m][3]);
                 }
             }
         }
@@ -1143,23 +1152,28 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
     // every warp's ldmatrix reads are done before the partial sums overwrite the rows
     __syncthreads();
     constexpr int W = 16 * MB;                         // utterance columns of a partial tile
-    float * part = reinterpret_cast<float *>(S.area);  // [kWarps][NT][8][W]
+    // rows padded to W + 4 floats: a store's 32 lanes (rows 2t / 2t + 1, columns g)
+    // then fall on 32 distinct banks (2 (W + 4) = 8 mod 32)
+    constexpr int WP = W + 4;
+    float * part = reinterpret_cast<float *>(S.area);  // [kw][NT][8][WP]
+    if (warp < kw) {
 #pragma unroll
-    for (int r = 0; r < NT; ++r) {
+        for (int r = 0; r < NT; ++r) {
 #pragma unroll
-        for (int m = 0; m < MB; ++m) {
-            float * pp = part + ((warp * NT + r) * 8) * W + m * 16;
-            pp[(2 * t) * W + g] = acc[r][m][0];
-            pp[(2 * t + 1) * W + g] = acc[r][m][1];
-            pp[(2 * t) * W + g + 8] = acc[r][m][2];
-            pp[(2 * t + 1) * W + g + 8] = acc[r][m][3];
+            for (int m = 0; m < MB; ++m) {
+                float * pp = part + ((warp * NT + r) * 8) * WP + m * 16;
+                pp[(2 * t) * WP + g] = acc[r][m][0];
+                pp[(2 * t + 1) * WP + g] = acc[r][m][1];
+                pp[(2 * t) * WP + g + 8] = acc[r][m][2];
+                pp[(2 * t + 1) * WP + g + 8] = acc[r][m][3];
+            }
         }
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < NT * 8 * W; idx += blockDim.x) {
+        const int pi = (idx / W) * WP + idx % W;
         float s = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) s += part[w * NT * 8 * W + idx];
+        for (int w = 0; w < kw; ++w) s += part[w * NT * 8 * WP + pi];
         S.C[idx] = s;
     }
     // this thread's generic accesses of the area come before the next stage's bulk writes
@@ -1173,28 +1187,28 @@ __device__ __forceinline__ int c_index(int r, int c, int W) { return (r >> 3) * 
 // mbp: m16 blocks of this pass (2 only when the pass has more than 16
 // utterances and the loop was set up for 32-utterance passes).
 __device__ __forceinline__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt,
-                                        const ATile & A, int mbp) {
+                                        const ATile & A, int mbp, int kw) {
     if (mbp == 2) {
         switch (nt) {
-            case 1: tc_gemm_nt<1, 2>(P, S, b, t0, A); break;
-            case 2: tc_gemm_nt<2, 2>(P, S, b, t0, A); break;
-            case 3: tc_gemm_nt<3, 2>(P, S, b, t0, A); break;
-            case 4: tc_gemm_nt<4, 2>(P, S, b, t0, A); break;
-            case 5: tc_gemm_nt<5, 2>(P, S, b, t0, A); break;
-            case 6: tc_gemm_nt<6, 2>(P, S, b, t0, A); break;
-            default: tc_gemm_nt<7, 2>(P, S, b, t0, A); break;
+            case 1: tc_gemm_nt<1, 2>(P, S, b, t0, A, kw); break;
+            case 2: tc_gemm_nt<2, 2>(P, S, b, t0, A, kw); break;
+            case 3: tc_gemm_nt<3, 2>(P, S, b, t0, A, kw); break;
+            case 4: tc_gemm_nt<4, 2>(P, S, b, t0, A, kw); break;
+            case 5: tc_gemm_nt<5, 2>(P, S, b, t0, A, kw); break;
+            case 6: tc_gemm_nt<6, 2>(P, S, b, t0, A, kw); break;
+            default: tc_gemm_nt<7, 2>(P, S, b, t0, A, kw); break;
         }
         return;
     }
     switch (nt) {
-        case 1: tc_gemm_nt<1, 1>(P, S, b, t0, A); break;
-        case 2: tc_gemm_nt<2, 1>(P, S, b, t0, A); break;
-        case 3: tc_gemm_nt<3, 1>(P, S, b, t0, A); break;
-        case 4: tc_gemm_nt<4, 1>(P, S, b, t0, A); break;
-        case 5: tc_gemm_nt<5, 1>(P, S, b, t0, A); break;
-        case 6: tc_gemm_nt<6, 1>(P, S, b, t0, A); break;
-        case 7: tc_gemm_nt<7, 1>(P, S, b, t0, A); break;
-        default: tc_gemm_nt<8, 1>(P, S, b, t0, A); break;
+        case 1: tc_gemm_nt<1, 1>(P, S, b, t0, A, kw); break;
+        case 2: tc_gemm_nt<2, 1>(P, S, b, t0, A, kw); break;
+        case 3: tc_gemm_nt<3, 1>(P, S, b, t0, A, kw); break;
+        case 4: tc_gemm_nt<4, 1>(P, S, b, t0, A, kw); break;
+        case 5: tc_gemm_nt<5, 1>(P, S, b, t0, A, kw); break;
+        case 6: tc_gemm_nt<6, 1>(P, S, b, t0, A, kw); break;
+        case 7: tc_gemm_nt<7, 1>(P, S, b, t0, A, kw); break;
+        default: tc_gemm_nt<8, 1>(P, S, b, t0, A, kw); break;
     }
 }
 
@@ -1304,7 +1318,7 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
         A.rb = P.rbh;
         A.lo = H * es;
         A.kb_split = l == 0 ? (bk.K >> 5) : (H >> 5);
-        tc_gemm(P, S, bk, 0, bk.tiles, A, mbp);
+        tc_gemm(P, S, bk, 0, bk.tiles, A, mbp, mbp == 2 ? kWarps : 4);
         SUBMARK(3);
         // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
         if (act) {
@@ -1391,7 +1405,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             A.kb_split = P.tcp.K >> 5;
             for (int t0 = 0; t0 < P.tcp.tiles; t0 += TG) {
                 const int nt = min(TG, P.tcp.tiles - t0);
-                tc_gemm(P, S, P.tcp, t0, nt, A, mbp);
+                tc_gemm(P, S, P.tcp, t0, nt, A, mbp, mbp == 2 ? kWarps : 4);
                 for (int idx = threadIdx.x; idx < nc * nt * 8; idx += blockDim.x) {
                     const int rr = idx / nc, cc = idx - rr * nc, row = t0 * 8 + rr;   // utterance fastest
                     if (row < nr) {
@@ -1419,7 +1433,6 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
     const int nr = max(0, min(P.Vo, r0 + rpc) - r0);
     if (nr == 0) return;
     const int * live = P.live + (size_t) sel * B;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int PR = kTcM * P.mb;                 // utterances per pass
     SUBMARK(-1);
     for (int rb = 0; rb < n_live; rb += kTcRec) {
@@ -1451,7 +1464,7 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
         A.kb_split = P.tcj.K >> 5;
         for (int t0 = 0; t0 < P.tcj.tiles; t0 += TG) {
             const int nt = min(TG, P.tcj.tiles - t0);
-            tc_gemm(P, S, P.tcj, t0, nt, A, mbp);
+            tc_gemm(P, S, P.tcj, t0, nt, A, mbp, 4);
             SUBMARK(11);
             // thread = (utterance c, row group rg): consecutive threads read
             // consecutive C columns; row-group partial keys meet in the staging
