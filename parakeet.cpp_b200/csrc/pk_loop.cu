@@ -1229,6 +1229,11 @@ __device__ __forceinline__ void put_h(const LoopParams & P, unsigned char * row,
     }
 }
 
+// Bring bytes (a multiple of 16, 16-byte aligned) at p into L2, no completion tracked.
+__device__ __forceinline__ void prefetch_l2(const void * p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
+
 // Records of one emit-list block: utterance, token, reset | h buffer << 1.
 __device__ __forceinline__ void tc_emit_record(const LoopParams & P, const TcSmem & T, int i, int g) {
     const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + g);
@@ -1252,6 +1257,11 @@ __device__ __forceinline__ void tc_load_records(const LoopParams & P, const TcSm
         }
     }
     __syncthreads();
+    // The joint-hidden step reads each live utterance's enc-proj row after the
+    // LSTM phases: pull the rows into L2 now (one bulk prefetch per row, spread
+    // over the CTAs), since the enc-proj table of a long batch exceeds L2.
+    for (int i = (int) blockIdx.x + (int) threadIdx.x * (int) gridDim.x; i < nl; i += (int) (blockDim.x * gridDim.x))
+        prefetch_l2(P.encp + (size_t) T.s_lframe[i] * P.J, (unsigned) P.J * 4u);
 }
 
 __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcSmem & T) {
@@ -1426,6 +1436,56 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
     trace_state_dump(P, first, sel);
 }
 
+// Joint epilogue of one GEMM call: logits = bias + C for this CTA's rows, the
+// best (token, duration) key per utterance max-reduced into P.keys. Thread =
+// (utterance c, row group rg): consecutive threads read consecutive C columns;
+// row-group partial keys meet in the staging area (free again once C is
+// reduced), then one thread per utterance folds them (unrolled, loads in
+// flight together) into the global keys. W = utterance columns of C.
+template <int W>
+__device__ __forceinline__ void joint_keys(const LoopParams & P, const TcSmem & S, int nc, int nt, int t0, int nr,
+                                           int r0) {
+    constexpr int RG = kThreads / W;
+    const int c = threadIdx.x % W, rg = threadIdx.x / W;
+    unsigned long long bt = 0ull, bd = 0ull;
+    if (c < nc) {
+        for (int rr = rg; rr < nt * 8; rr += RG) {
+            const int row = t0 * 8 + rr;
+            if (row >= nr) break;
+            const int r = r0 + row;
+            const float logit = S.bj[row] + S.C[c_index(rr, c, W)];
+            if (P.trace_steps > 0) {
+                const int step = S.s_aux[c];
+                if (step < P.trace_steps)
+                    P.tr_logits[((size_t) S.s_utt[c] * P.trace_steps + step) * P.Vo + r] = logit;
+            }
+            if (r < P.V1) {
+                const unsigned long long k = make_key(logit, r);
+                bt = k > bt ? k : bt;
+            } else {
+                const unsigned long long k = make_key(logit, r - P.V1);
+                bd = k > bd ? k : bd;
+            }
+        }
+    }
+    ulonglong2 * kp = reinterpret_cast<ulonglong2 *>(S.area);
+    kp[threadIdx.x] = make_ulonglong2(bt, bd);
+    __syncthreads();
+    if (threadIdx.x < nc) {
+#pragma unroll
+        for (int g = 1; g < RG; ++g) {
+            const ulonglong2 o = kp[g * W + threadIdx.x];
+            bt = o.x > bt ? o.x : bt;
+            bd = o.y > bd ? o.y : bd;
+        }
+        const int utt = S.s_utt[threadIdx.x];
+        if (bt) atomicMax(&P.keys[2 * utt + 0], bt);
+        if (bd) atomicMax(&P.keys[2 * utt + 1], bd);
+    }
+    // generic accesses of the area before the next stage's bulk writes
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & T) {
     const int J = P.J, B = P.B;
     const int rpc = P.rpc_j;
@@ -1466,52 +1526,8 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
             const int nt = min(TG, P.tcj.tiles - t0);
             tc_gemm(P, S, P.tcj, t0, nt, A, mbp, 4);
             SUBMARK(11);
-            // thread = (utterance c, row group rg): consecutive threads read
-            // consecutive C columns; row-group partial keys meet in the staging
-            // area (free again once C is reduced), then one thread per
-            // utterance folds them into the global keys
-            {
-                const int W = kTcM * mbp, RG = kThreads / W;
-                const int c = threadIdx.x % W, rg = threadIdx.x / W;
-                unsigned long long bt = 0ull, bd = 0ull;
-                if (c < nc) {
-                    for (int rr = rg; rr < nt * 8; rr += RG) {
-                        const int row = t0 * 8 + rr;
-                        if (row >= nr) break;
-                        const int r = r0 + row;
-                        const float logit = S.bj[row] + S.C[c_index(rr, c, W)];
-                        if (P.trace_steps > 0) {
-                            const int step = S.s_aux[c];
-                            if (step < P.trace_steps)
-                                P.tr_logits[((size_t) S.s_utt[c] * P.trace_steps + step) * P.Vo + r] = logit;
-                        }
-                        if (r < P.V1) {
-                            const unsigned long long k = make_key(logit, r);
-                            bt = k > bt ? k : bt;
-                        } else {
-                            const unsigned long long k = make_key(logit, r - P.V1);
-                            bd = k > bd ? k : bd;
-                        }
-                    }
-                }
-                unsigned long long * kp = reinterpret_cast<unsigned long long *>(S.area);
-                kp[2 * threadIdx.x] = bt;
-                kp[2 * threadIdx.x + 1] = bd;
-                __syncthreads();
-                if (threadIdx.x < nc) {
-                    for (int g = 1; g < RG; ++g) {
-                        const unsigned long long ot = kp[2 * (g * W + threadIdx.x)];
-                        const unsigned long long od = kp[2 * (g * W + threadIdx.x) + 1];
-                        bt = ot > bt ? ot : bt;
-                        bd = od > bd ? od : bd;
-                    }
-                    const int utt = S.s_utt[threadIdx.x];
-                    if (bt) atomicMax(&P.keys[2 * utt + 0], bt);
-                    if (bd) atomicMax(&P.keys[2 * utt + 1], bd);
-                }
-                // generic accesses of the area before the next stage's bulk writes
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            }
+            if (mbp == 2) joint_keys<2 * kTcM>(P, S, nc, nt, t0, nr, r0);
+            else joint_keys<kTcM>(P, S, nc, nt, t0, nr, r0);
             __syncthreads();
             SUBMARK(12);
         }
