@@ -500,7 +500,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(x->predp.ensure(Bs * J * 4));
     PK_CK(x->hid.ensure(Bs * J * 4));
     PK_CK(x->ust.ensure(Bs * kUst * 4));
-    PK_CK(x->keys.ensure(Bs * 2 * 8));
+    PK_CK(x->keys.ensure(Bs * 4 * 8));   // two alternating [B][2] argmax key buffers
     PK_CK(x->live.ensure(2 * Bs * 4));
     PK_CK(x->livef.ensure(2 * Bs * 8));
     PK_CK(x->emit.ensure(2 * Bs * 4));
@@ -570,7 +570,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         }
         if (!emit.empty())
             PK_CK(cudaMemcpyAsync(x->emit.p, emit.data(), emit.size() * 4, cudaMemcpyHostToDevice, s));
-        PK_CK(cudaMemsetAsync(x->keys.p, 0, (size_t) B * 16, s));
+        PK_CK(cudaMemsetAsync(x->keys.p, 0, (size_t) B * 32, s));
         PK_CK(cudaMemsetAsync(x->finish.p, 0, (size_t) B * 8, s));
     }
     PK_CK(cudaMemcpyAsync(x->ctl.p, ctl.data(), kCtl * 4, cudaMemcpyHostToDevice, s));

@@ -111,7 +111,7 @@ struct LoopParams {
     unsigned char * xnew;      // [L][B] rows of rbh bytes: new h by emit-list index
     unsigned char * hidc;      // [B] rows of rbj bytes: joint hidden by live-list index
     int32_t * ust;             // [B][kUst]
-    unsigned long long * keys; // [B][2] packed argmax keys (token, duration)
+    unsigned long long * keys; // [2][B][2] packed argmax keys (token, duration), buffer = iteration & 1
     int32_t * live;            // [2][B]
     int64_t * live_frame;      // [2][B] encoder row (frame_offset + t) of each live entry
     int32_t * emit;            // [B][2]: utterance, token | h-buffer << 30 | reset << 31

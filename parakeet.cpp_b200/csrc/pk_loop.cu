@@ -603,7 +603,7 @@ __device__ void joint_rows(const LoopParams & P, int r0, int nr, int nc, const S
     }
 }
 
-__device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Smem & S) {
+__device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Smem & S, unsigned long long * keys) {
     const int J = P.J, B = P.B;
     const int rpc = (P.Vo + (int) gridDim.x - 1) / (int) gridDim.x;
     const int r0 = (int) blockIdx.x * rpc;
@@ -651,11 +651,96 @@ __device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Sme
                 kd = b > kd ? b : kd;
             }
             const int utt = S.s_utt[threadIdx.x];
-            if (kt) atomicMax(&P.keys[2 * utt + 0], kt);
-            if (kd) atomicMax(&P.keys[2 * utt + 1], kd);
+            if (kt) atomicMax(&keys[2 * utt + 0], kt);
+            if (kd) atomicMax(&keys[2 * utt + 1], kd);
         }
         __syncthreads();
     }
+}
+
+// ---- greedy control ---------------------------------------------------------
+
+// One utterance's step for the decided (token, duration index) and its current
+// symbol count: frame advance, new symbol count and the emit record.
+//  * TDT, parakeet_tdt.cpp:938-968: blank advances by max(1, dur); a token is
+//    emitted and advances when dur > 0 or max_symbols is reached.
+//  * EOU, parakeet_eou.cpp:271-333: blank / EOB / a special piece end the frame;
+//    EOU ends the frame, resets the prediction net (re-primed on blank) and may
+//    record a boundary; any other token is emitted. kind tells the state writer
+//    which side effects follow: 0 frame end, 1 end of utterance, 2 token,
+//    3 token that reaches max_symbols (and ends the frame).
+struct Decision {
+    int adv, sym, e, etok, ereset, emit_tok, kind;
+};
+
+__device__ __forceinline__ Decision decide_core(const LoopParams & P, int tok, int di, int s0) {
+    Decision d{0, s0, 0, 0, 0, 0, 0};
+    const int msym = P.max_sym;
+    if (P.is_tdt) {
+        const int dur = P.Nd > 0 ? __ldg(P.durations + di) : di;
+        const int adv = dur > 1 ? dur : 1;
+        if (tok == P.blank) {
+            d.adv = adv; d.sym = 0;
+        } else {
+            d.emit_tok = 1; d.e = 1; d.etok = tok;
+            ++d.sym;
+            if (dur > 0 || d.sym >= msym) { d.adv = adv; d.sym = 0; }
+        }
+    } else if (tok == P.blank || tok == P.eob) {
+        d.adv = 1; d.sym = 0;
+    } else if (tok == P.eou) {
+        d.kind = 1; d.e = 1; d.etok = P.blank; d.ereset = 1; d.adv = 1; d.sym = 0;
+    } else if (tok < P.n_special && __ldg(P.special + tok)) {
+        d.adv = 1; d.sym = 0;
+    } else {
+        d.kind = 2; d.emit_tok = 1; d.e = 1; d.etok = tok;
+        ++d.sym;
+        if (d.sym >= msym) { d.kind = 3; d.adv = 1; d.sym = 0; }
+    }
+    return d;
+}
+
+// EOU state side effects of a decision (uf: the utterance's state before it).
+// The frame loop resets symbols_this_step at each frame start; U_SYMX keeps the
+// value a frame ended with (what the reference's state holds after the window).
+__device__ __forceinline__ void eou_effects(const LoopParams & P, int * u, const int * uf, int utt,
+                                            const Decision & d, int s0, int ntok, int tok, int T) {
+    if (d.kind == 0) {
+        u[U_SYMX] = s0;
+    } else if (d.kind == 1) {
+        u[U_SYMX] = s0;
+        const int total = uf[U_NBEFORE] + ntok;
+        if (total > uf[U_SEGSTART]) {
+            const int nb = uf[U_NBND];
+            if (P.bnd_out != nullptr && nb < T) P.bnd_out[P.bnd_region[utt] + nb] = total;
+            u[U_NBND] = nb + 1;
+            u[U_SEGSTART] = total;
+        }
+        u[U_LAST] = P.blank;
+    } else {
+        u[U_LAST] = tok;
+        if (d.kind == 3) u[U_SYMX] = s0 + 1;
+    }
+}
+
+// An argmax key that no joint row produced, or an index out of range.
+__device__ __forceinline__ bool keys_bad(const LoopParams & P, unsigned long long kt, unsigned long long kd,
+                                         int tok, int di) {
+    return kt == 0ull || tok < 0 || tok >= P.V1 || (P.is_tdt && (kd == 0ull || di < 0 || di >= P.Nd));
+}
+
+// Append an emitted token to the utterance's output region; false (error
+// flagged) when the region (T * max_symbols tokens) is full.
+__device__ __forceinline__ bool put_token(const LoopParams & P, int utt, int tok, int & ntok, int T) {
+    const int cap = T * (P.max_sym > 0 ? P.max_sym : 1);
+    if (ntok < cap) {
+        P.tok_out[P.tok_region[utt] + ntok] = tok;
+        ++ntok;
+        return true;
+    }
+    atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+    P.ctl[C_ERRINFO] = utt;
+    return false;
 }
 
 // ---- leader: greedy control for every live utterance -------------------------
@@ -666,15 +751,16 @@ __device__ void phase_joint(const LoopParams & P, int sel, int n_live, const Sme
 // are the current list selector and length; every CTA read them at the start of
 // the iteration and nothing has changed them since.
 // live_smem: the whole live list already in shared memory, or nullptr.
+// keys: this iteration's argmax key buffer (cleared here for its next use).
 __device__ unsigned long long leader_decide(const LoopParams & P, const Smem & S, int sel, int n_live,
-                                           unsigned gen_next, const int * live_smem = nullptr) {
+                                           unsigned gen_next, unsigned long long * keys,
+                                           const int * live_smem = nullptr) {
     const int B = P.B;
     // an error flagged anywhere so far travels with the release word
     const int err0 = threadIdx.x == 0 ? __ldcg(&P.ctl[C_ERR]) : 0;
     const int * live_in = P.live + (size_t) sel * B;
     int * live_out = P.live + (size_t) (sel ^ 1) * B;
     int base_emit = 0, base_live = 0;
-    const int msym = P.max_sym;
     for (int r0 = 0; r0 < n_live; r0 += blockDim.x) {
         const int i = r0 + threadIdx.x;
         int e = 0, lv = 0, utt = -1, etok = 0, ereset = 0, ehb = 0;
@@ -683,19 +769,20 @@ __device__ unsigned long long leader_decide(const LoopParams & P, const Smem & S
             utt = live_smem ? live_smem[i] : __ldcg(&live_in[i]);
             int * u = P.ust + utt * kUst;
             // every load that depends only on utt goes out together (one round trip)
-            const unsigned long long kt = __ldcg(&P.keys[2 * utt + 0]);
-            const unsigned long long kd = P.is_tdt ? __ldcg(&P.keys[2 * utt + 1]) : 0ull;
+            const unsigned long long kt = __ldcg(&keys[2 * utt + 0]);
+            const unsigned long long kd = P.is_tdt ? __ldcg(&keys[2 * utt + 1]) : 0ull;
             const int4 u0 = __ldcg(reinterpret_cast<const int4 *>(u));
             const int4 u1 = __ldcg(reinterpret_cast<const int4 *>(u) + 1);
             const int4 u2 = __ldcg(reinterpret_cast<const int4 *>(u) + 2);
             const long long foff = __ldg(P.frame_off + utt);
             int uf[12] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w, u2.x, u2.y, u2.z, u2.w};
-            // the next joint phase max-reduces into cleared keys (ordered by the barrier release)
-            P.keys[2 * utt + 0] = 0ull;
-            if (P.is_tdt) P.keys[2 * utt + 1] = 0ull;
+            // the next joint phase on this buffer max-reduces into cleared keys
+            // (ordered by the barrier release)
+            keys[2 * utt + 0] = 0ull;
+            if (P.is_tdt) keys[2 * utt + 1] = 0ull;
             int tok = key_index(kt);
             int di = P.is_tdt ? key_index(kd) : 0;
-            if (kt == 0ull || tok < 0 || tok >= P.V1 || (P.is_tdt && (kd == 0ull || di < 0 || di >= P.Nd))) {
+            if (keys_bad(P, kt, kd, tok, di)) {
                 atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
                 atomicOr(&S.s_flag[6], 1);
                 P.ctl[C_ERRINFO] = utt;
@@ -717,64 +804,16 @@ __device__ unsigned long long leader_decide(const LoopParams & P, const Smem & S
                 }
             }
             u[U_STEPS] = step + 1;
-            int t = uf[U_T];
-            int sym = uf[U_SYM];
-            int ntok = uf[U_NTOK];
+            const int s0 = uf[U_SYM];
             const int T = uf[U_NFRAMES];
-            bool emit_tok = false;
-            if (P.is_tdt) {
-                // parakeet_tdt.cpp:938-968
-                const int dur = P.Nd > 0 ? __ldg(P.durations + di) : di;
-                const int adv = dur > 1 ? dur : 1;
-                if (tok == P.blank) {
-                    t += adv;
-                    sym = 0;
-                } else {
-                    emit_tok = true;
-                    e = 1; etok = tok;
-                    ++sym;
-                    if (dur > 0 || sym >= msym) { t += adv; sym = 0; }
-                }
-            } else {
-                // parakeet_eou.cpp:271-333. The frame loop resets symbols_this_step
-                // at each frame start; U_SYMX keeps the value a frame ended with
-                // (what the reference's state holds after the window).
-                if (tok == P.blank || tok == P.eob) {
-                    u[U_SYMX] = sym;
-                    t += 1; sym = 0;
-                } else if (tok == P.eou) {
-                    u[U_SYMX] = sym;
-                    const int total = uf[U_NBEFORE] + ntok;
-                    if (total > uf[U_SEGSTART]) {
-                        const int nb = uf[U_NBND];
-                        if (P.bnd_out != nullptr && nb < T) P.bnd_out[P.bnd_region[utt] + nb] = total;
-                        u[U_NBND] = nb + 1;
-                        u[U_SEGSTART] = total;
-                    }
-                    e = 1; etok = P.blank; ereset = 1;
-                    u[U_LAST] = P.blank;
-                    t += 1; sym = 0;
-                } else if (tok < P.n_special && __ldg(P.special + tok)) {
-                    u[U_SYMX] = sym;
-                    t += 1; sym = 0;
-                } else {
-                    emit_tok = true;
-                    e = 1; etok = tok;
-                    u[U_LAST] = tok;
-                    ++sym;
-                    if (sym >= msym) { u[U_SYMX] = sym; t += 1; sym = 0; }
-                }
-            }
-            if (emit_tok) {
-                const int cap = T * (msym > 0 ? msym : 1);
-                if (ntok < cap) {
-                    P.tok_out[P.tok_region[utt] + ntok] = tok;
-                    ++ntok;
-                } else {
-                    atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
-                atomicOr(&S.s_flag[6], 1);
-                    P.ctl[C_ERRINFO] = utt;
-                }
+            const Decision d = decide_core(P, tok, di, s0);
+            const int t = uf[U_T] + d.adv;
+            const int sym = d.sym;
+            e = d.e; etok = d.etok; ereset = d.ereset;
+            int ntok = uf[U_NTOK];
+            if (!P.is_tdt) eou_effects(P, u, uf, utt, d, s0, ntok, tok, T);
+            if (d.emit_tok) {
+                if (!put_token(P, utt, tok, ntok, T)) atomicOr(&S.s_flag[6], 1);
             }
             if (e) {
                 ehb = uf[U_HBUF] ^ 1;
@@ -847,6 +886,8 @@ struct TcSmem {
     int * s_aux2;                   // [kTcRec]
     int * s_lutt;                   // [kTcRec] first block of the live list (loaded with the emit records)
     long long * s_lframe;           // [kTcRec] its encoder rows
+    int2 * s_lst;                   // [kTcRec] its control state in replicated mode:
+                                    // (frames left, symbol count | h buffer << 30)
     int * s_scan;                   // [kWarps + 2]
     int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2-3 staging, 4-6 release word
     float * bj;                     // [rpc_j] this CTA's joint-out bias slice
@@ -867,6 +908,7 @@ __device__ __forceinline__ TcSmem tc_carve(unsigned char * raw, const LoopParams
     s.s_aux2 = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_lutt = reinterpret_cast<int *>(raw + off); off += kTcRec * 4;
     s.s_lframe = reinterpret_cast<long long *>(raw + off); off += kTcRec * 8;
+    s.s_lst = reinterpret_cast<int2 *>(raw + off); off += kTcRec * 8;
     s.s_scan = reinterpret_cast<int *>(raw + off); off += (kWarps + 2) * 4;
     s.s_flag = reinterpret_cast<int *>(raw + off); off += 8 * 4;
     s.bj = reinterpret_cast<float *>(raw + off); off += (size_t) P.rpc_j * 4;
@@ -1242,6 +1284,21 @@ __device__ __forceinline__ void tc_emit_record(const LoopParams & P, const TcSme
     T.s_aux2[i] = ((e.y >> 31) & 1) | (((e.y >> 30) & 1) << 1);
 }
 
+// The joint-hidden step reads each live utterance's enc-proj row after the
+// LSTM phases: pull the rows of the live entries in shared memory into L2 at
+// the start of the iteration (one bulk prefetch per row, spread over the CTAs),
+// since the enc-proj table of a long batch exceeds L2.
+__device__ __forceinline__ void tc_prefetch_encp(const LoopParams & P, const TcSmem & T, int nl) {
+    for (int i = (int) blockIdx.x + (int) threadIdx.x * (int) gridDim.x; i < nl; i += (int) (blockDim.x * gridDim.x))
+        prefetch_l2(P.encp + (size_t) T.s_lframe[i] * P.J, (unsigned) P.J * 4u);
+}
+
+// Iterations whose live list fits shared memory end with a decision that every
+// CTA computes itself (no leader round trip); trace runs keep the leader.
+__device__ __forceinline__ bool rep_mode(const LoopParams & P, int n_live) {
+    return P.trace_steps <= 0 && n_live <= kTcRec;
+}
+
 // Start of an iteration: the first block of the emit list (LSTM and pred-proj
 // records) and of the live list (joint records) in one round trip. When a list
 // fits one block the phases use these copies instead of reloading.
@@ -1249,19 +1306,116 @@ __device__ __forceinline__ void tc_load_records(const LoopParams & P, const TcSm
                                                 int n_live) {
     const int ne = min(kTcRec, n_emit), nl = min(kTcRec, n_live);
     const int * live = P.live + (size_t) sel * P.B;
+    // the iteration ends with a replicated decision: each CTA takes its own copy
+    // of the live utterances' control state (kept in shared memory from then on)
+    const bool rep = rep_mode(P, n_live);
     for (int i = threadIdx.x; i < max(ne, nl); i += blockDim.x) {
         if (i < ne) tc_emit_record(P, T, i, i);
         if (i < nl) {
-            T.s_lutt[i] = __ldcg(&live[i]);
+            const int utt = __ldcg(&live[i]);
+            T.s_lutt[i] = utt;
             T.s_lframe[i] = __ldcg(reinterpret_cast<const long long *>(P.live_frame) + (size_t) sel * P.B + i);
+            if (rep) {
+                const int * u = P.ust + utt * kUst;
+                const int t = __ldcg(u + U_T), sym = __ldcg(u + U_SYM), hb = __ldcg(u + U_HBUF);
+                const int nf = __ldcg(u + U_NFRAMES);
+                T.s_lst[i] = make_int2(nf - t, sym | (hb << 30));
+            }
         }
     }
     __syncthreads();
-    // The joint-hidden step reads each live utterance's enc-proj row after the
-    // LSTM phases: pull the rows into L2 now (one bulk prefetch per row, spread
-    // over the CTAs), since the enc-proj table of a long batch exceeds L2.
-    for (int i = (int) blockIdx.x + (int) threadIdx.x * (int) gridDim.x; i < nl; i += (int) (blockDim.x * gridDim.x))
-        prefetch_l2(P.encp + (size_t) T.s_lframe[i] * P.J, (unsigned) P.J * 4u);
+    tc_prefetch_encp(P, T, nl);
+}
+
+// Replicated decision (tensor-core loop, n_live <= kTcRec, no trace): every CTA
+// decides every live utterance from the argmax keys and its own shared-memory
+// copy of (frames left, symbol count, h buffer), and compacts the next emit and
+// live lists in place in shared memory, so no leader round trip, list write-out
+// or record reload separates the joint from the next LSTM phase. The decisions
+// are the leader's (decide_core on the same keys). The last CTA (the one with
+// the fewest rows in every phase) alone applies what the leader writes
+// (utterance state, tokens, boundaries, finish times, control words) and clears
+// these utterances' entries of the other key buffer, which every CTA finished
+// reading one iteration ago and the joint after next fills.
+// Returns the next iteration's control word.
+__device__ unsigned long long rep_decide(const LoopParams & P, const TcSmem & T, int sel, int n_live,
+                                         const unsigned long long * keys, unsigned long long * keys_other) {
+    const bool writer = blockIdx.x == gridDim.x - 1;
+    const int i = threadIdx.x;   // n_live <= kTcRec == blockDim.x: one entry per thread
+    int e = 0, lv = 0, utt = -1, etok = 0, ereset = 0, hb = 0, rem = 0, sym = 0, err = 0;
+    long long lframe = 0;
+    if (i < n_live) {
+        utt = T.s_lutt[i];
+        const int2 st = T.s_lst[i];
+        int * u = P.ust + utt * kUst;
+        // the writer's state loads go out with the key loads (one round trip)
+        int4 u0 = make_int4(0, 0, 0, 0), u1 = u0, u2 = u0;
+        if (writer) {
+            u0 = __ldcg(reinterpret_cast<const int4 *>(u));
+            u1 = __ldcg(reinterpret_cast<const int4 *>(u) + 1);
+            u2 = __ldcg(reinterpret_cast<const int4 *>(u) + 2);
+        }
+        const unsigned long long kt = __ldcg(&keys[2 * utt + 0]);
+        const unsigned long long kd = P.is_tdt ? __ldcg(&keys[2 * utt + 1]) : 0ull;
+        int tok = key_index(kt);
+        int di = P.is_tdt ? key_index(kd) : 0;
+        if (keys_bad(P, kt, kd, tok, di)) {   // the same keys, so the same verdict, in every CTA
+            err = 1;
+            if (writer) {
+                atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+                P.ctl[C_ERRINFO] = utt;
+            }
+            tok = P.blank;
+            di = 0;
+        }
+        const int s0 = st.y & 0x3FFFFFFF;
+        hb = (st.y >> 30) & 1;
+        const Decision d = decide_core(P, tok, di, s0);
+        rem = st.x - d.adv;
+        sym = d.sym;
+        e = d.e; etok = d.etok; ereset = d.ereset;
+        if (e) hb ^= 1;
+        lv = rem > 0 ? 1 : 0;
+        lframe = T.s_lframe[i] + d.adv;
+        if (writer) {
+            const int uf[12] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w, u2.x, u2.y, u2.z, u2.w};
+            keys_other[2 * utt + 0] = 0ull;
+            if (P.is_tdt) keys_other[2 * utt + 1] = 0ull;
+            u[U_STEPS] = uf[U_STEPS] + 1;
+            int ntok = uf[U_NTOK];
+            if (!P.is_tdt) eou_effects(P, u, uf, utt, d, s0, ntok, tok, uf[U_NFRAMES]);
+            if (d.emit_tok && !put_token(P, utt, tok, ntok, uf[U_NFRAMES])) err = 1;
+            if (e) u[U_HBUF] = hb;
+            u[U_T] = uf[U_T] + d.adv;
+            u[U_SYM] = sym;
+            u[U_NTOK] = ntok;
+            if (!lv) P.finish_ns[utt] = gtimer();
+        }
+    }
+    // every thread has read its entry before the scan's first barrier, so the
+    // compacted lists can overwrite the current ones in place
+    int tot = 0;
+    const int pf = block_excl_scan(e | (lv << 16), as_smem(T), tot);
+    const int pe = pf & 0xFFFF, pl = pf >> 16;
+    const int n_emit = tot & 0xFFFF, n_next = tot >> 16;
+    if (e) {
+        T.s_utt[pe] = utt;
+        T.s_aux[pe] = etok;
+        T.s_aux2[pe] = ereset | (hb << 1);
+    }
+    if (lv) {
+        T.s_lutt[pl] = utt;
+        T.s_lframe[pl] = lframe;
+        T.s_lst[pl] = make_int2(rem, sym | (hb << 30));
+    }
+    if (writer && threadIdx.x == 0) {
+        P.ctl[C_NEMIT] = n_emit;
+        P.ctl[C_NLIVE0 + (sel ^ 1)] = n_next;
+        P.ctl[C_NDECIDED] = n_live;
+        P.ctl[C_SEL] = sel ^ 1;
+    }
+    const int any_err = __syncthreads_or(err);
+    return pack_ctl(0u, any_err, sel ^ 1, n_emit, n_next);
 }
 
 __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcSmem & T) {
@@ -1437,14 +1591,14 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
 }
 
 // Joint epilogue of one GEMM call: logits = bias + C for this CTA's rows, the
-// best (token, duration) key per utterance max-reduced into P.keys. Thread =
+// best (token, duration) key per utterance max-reduced into keys. Thread =
 // (utterance c, row group rg): consecutive threads read consecutive C columns;
 // row-group partial keys meet in the staging area (free again once C is
 // reduced), then one thread per utterance folds them (unrolled, loads in
 // flight together) into the global keys. W = utterance columns of C.
 template <int W>
 __device__ __forceinline__ void joint_keys(const LoopParams & P, const TcSmem & S, int nc, int nt, int t0, int nr,
-                                           int r0) {
+                                           int r0, unsigned long long * keys) {
     constexpr int RG = kThreads / W;
     const int c = threadIdx.x % W, rg = threadIdx.x / W;
     unsigned long long bt = 0ull, bd = 0ull;
@@ -1479,14 +1633,14 @@ __device__ __forceinline__ void joint_keys(const LoopParams & P, const TcSmem & 
             bd = o.y > bd ? o.y : bd;
         }
         const int utt = S.s_utt[threadIdx.x];
-        if (bt) atomicMax(&P.keys[2 * utt + 0], bt);
-        if (bd) atomicMax(&P.keys[2 * utt + 1], bd);
+        if (bt) atomicMax(&keys[2 * utt + 0], bt);
+        if (bd) atomicMax(&keys[2 * utt + 1], bd);
     }
     // generic accesses of the area before the next stage's bulk writes
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & T) {
+__device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & T, unsigned long long * keys) {
     const int J = P.J, B = P.B;
     const int rpc = P.rpc_j;
     const int r0 = (int) blockIdx.x * rpc;
@@ -1526,8 +1680,8 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
             const int nt = min(TG, P.tcj.tiles - t0);
             tc_gemm(P, S, P.tcj, t0, nt, A, mbp, 4);
             SUBMARK(11);
-            if (mbp == 2) joint_keys<2 * kTcM>(P, S, nc, nt, t0, nr, r0);
-            else joint_keys<kTcM>(P, S, nc, nt, t0, nr, r0);
+            if (mbp == 2) joint_keys<2 * kTcM>(P, S, nc, nt, t0, nr, r0, keys);
+            else joint_keys<kTcM>(P, S, nc, nt, t0, nr, r0, keys);
             __syncthreads();
             SUBMARK(12);
         }
@@ -1604,6 +1758,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
     }
     SUBMARK(-3);
     bool first = true;
+    bool rep = false;    // lists and control state held in shared memory (replicated decisions)
     int emit_iters = 0;
     // CTA 0 timestamps: per segment, its own work and the wait that follows
     const bool prof = blockIdx.x == 0 && threadIdx.x == 0 && P.prof != nullptr;
@@ -1640,7 +1795,11 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             P.ctl[C_ITERS] = iter;
             if (n_emit > 0) P.ctl[C_EMITITERS] = ++emit_iters;
         }
-        if constexpr (TC) tc_load_records(P, T, sel, n_emit, n_live);
+        // this iteration's argmax key buffer (two, alternating)
+        unsigned long long * keys = P.keys + (size_t) (iter & 1) * 2 * P.B;
+        if constexpr (TC) {
+            if (!rep) tc_load_records(P, T, sel, n_emit, n_live);
+        }
         if (n_emit > 0) {
             for (int l = 0; l < P.L; ++l) {
                 if constexpr (TC) tc_phase_lstm(P, l, n_emit, T);
@@ -1659,15 +1818,26 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         mark(3);
         first = false;
         if (n_live == 0) break;
-        if constexpr (TC) tc_phase_joint(P, sel, n_live, T);
-        else phase_joint(P, sel, n_live, S);
+        if constexpr (TC) tc_phase_joint(P, sel, n_live, T, keys);
+        else phase_joint(P, sel, n_live, S, keys);
         __syncthreads();
         mark(4);
-        if (leader_arrive(P, S)) {
+        bool rep_now = false;
+        if constexpr (TC) rep_now = rep_mode(P, n_live);
+        if (rep_now) {
+            if (!grid_barrier(P, nbar, S)) return;
+            mark(5);
+            SUBMARK(-4);
+            cw = rep_decide(P, T, sel, n_live, keys, P.keys + (size_t) ((iter + 1) & 1) * 2 * P.B);
+            SUBMARK(13);
+            tc_prefetch_encp(P, T, (int) (cw & 0x7FFFFFull));
+            rep = true;
+            mark(6);
+        } else if (leader_arrive(P, S)) {
             SUBMARK(-4);
             const int * lsm = nullptr;
             if constexpr (TC) lsm = n_live <= kTcRec ? T.s_lutt : nullptr;
-            cw = leader_decide(P, S, sel, n_live, gen + 1u, lsm);
+            cw = leader_decide(P, S, sel, n_live, gen + 1u, keys, lsm);
             SUBMARK(13);
             mark(6);
             leader_release(P, cw);
@@ -1699,7 +1869,7 @@ size_t step_loop_tc_smem_bytes(unsigned sm_weights, int area, int rpc_j, int rpc
     off += (size_t) area;
     off += (size_t) kTcRmax * 128 * 2 * 4;
     off += 16;
-    off += 4 * kTcRec * 4 + kTcRec * 8 + (kWarps + 2) * 4 + 8 * 4;
+    off += 4 * kTcRec * 4 + 2 * kTcRec * 8 + (kWarps + 2) * 4 + 8 * 4;
     off += (size_t) (rpc_j + rpc_p) * 4;
     off += (size_t) kMaxLayers * 4 * upc * 4;
     return off;

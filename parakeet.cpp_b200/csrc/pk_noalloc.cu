@@ -51,7 +51,7 @@ Layout layout(int J, int H, int L) {
     o.predp = take((size_t) J * 4);
     o.hid = take((size_t) J * 4);
     o.ust = take(kUst * 4);
-    o.keys = take(2 * 8);
+    o.keys = take(4 * 8);   // two alternating argmax key buffers
     o.live = take(2 * 4);
     o.livef = take(2 * 8);
     o.emit = take(2 * 4);
@@ -89,8 +89,7 @@ __global__ void noalloc_init_kernel(unsigned char * base, Layout o, int T, int b
     emit[1] = blank | (1 << 31);
     ctl[C_NEMIT] = fresh ? 1 : 0;
     unsigned long long * keys = reinterpret_cast<unsigned long long *>(base + o.keys);
-    keys[0] = 0ull;
-    keys[1] = 0ull;
+    for (int i = 0; i < 4; ++i) keys[i] = 0ull;
     unsigned * bar = reinterpret_cast<unsigned *>(base + o.bar);
     for (int i = 0; i < 8; ++i) bar[i] = 0u;
     *reinterpret_cast<unsigned long long *>(base + o.finish) = 0ull;
