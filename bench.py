@@ -413,7 +413,7 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
             "loop_iterations_per_step": iters / args.steps,
             "loop_us_per_iteration": {
                 name: 1e3 * (phase[2 * i] + phase[2 * i + 1]) / max(1, iters)
-                for i, name in enumerate(["lstm", "pred_hidden", "joint", "leader"])},
+                for i, name in enumerate(["lstm", "pred_hidden", "joint", "decision"])},
             "loop_wait_share": float((phase[1::2].sum()) / max(phase.sum(), 1e-9)),
             "gpu_launches": int(launches),
             "clocks": clk,
