@@ -903,7 +903,7 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
     x->grid = x->sm_count;
     x->ldx = ((std::max(2 * x->H, x->J) + 3) / 4) * 4;
     x->chunk = 32;
-    const size_t smem_cap = std::min<size_t>(prop.sharedMemPerBlockOptin, 200 * 1024);
+    const size_t smem_cap = std::min<size_t>(prop.sharedMemPerBlockOptin - step_loop_static_smem(0), 200 * 1024);
     while (x->chunk > 1 && step_loop_smem_bytes(x->chunk, x->ldx, x->H, x->grid) > smem_cap) x->chunk >>= 1;
     x->smem = step_loop_smem_bytes(x->chunk, x->ldx, x->H, x->grid);
     if (x->smem > smem_cap) return cleanup(fail(PK_ERR_MODEL, "hidden sizes too large for shared memory"));
@@ -912,7 +912,8 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
     int per_sm = 0;
     if (step_loop_occupancy(x->smem, 0, &per_sm) != cudaSuccess || per_sm < 1)
         return cleanup(fail(PK_ERR_CUDA, "step loop does not fit one CTA per SM"));
-    st = setup_tc(x, d, (size_t) prop.sharedMemPerBlockOptin);
+    // dynamic shared memory may use what the kernel's static arrays leave
+    st = setup_tc(x, d, (size_t) prop.sharedMemPerBlockOptin - step_loop_static_smem(1));
     if (st != PK_OK) return cleanup(st);
     setup_encproj(x, (size_t) prop.sharedMemPerBlockOptin);
     x->math = x->tc_ok ? PK_MATH_TC : PK_MATH_F32;

@@ -141,6 +141,7 @@ cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaSt
 size_t      step_loop_smem_bytes(int chunk, int ldx, int H, int grid);
 size_t      step_loop_tc_smem_bytes(unsigned sm_weights, int area, int rpc_j, int rpc_p, int upc);
 cudaError_t step_loop_configure(size_t smem, int tc);
+size_t step_loop_static_smem(int tc);   // static shared memory of the step-loop kernel
 cudaError_t step_loop_occupancy(size_t smem, int tc, int * blocks_per_sm);
 
 cudaError_t launch_encproj_f32(const float * enc, int64_t frames, int De, const float * w,

@@ -984,6 +984,7 @@ template <typename F>
 __device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S, int nc,
                                          const unsigned char * tile, unsigned tile_rb, unsigned char * dtile,
                                          unsigned char * drows, unsigned row_bytes, unsigned rows_rb, F rowsrc) {
+    SUBMARK(17);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned ph = (unsigned) S.s_flag[2];
     const unsigned mb = (unsigned) __cvta_generic_to_shared(S.mbar);
@@ -1632,12 +1633,15 @@ __device__ __forceinline__ void joint_keys(const LoopParams & P, const TcSmem & 
             bt = o.x > bt ? o.x : bt;
             bd = o.y > bd ? o.y : bd;
         }
+    }
+    // generic accesses of the area before the next stage's bulk writes; ahead of
+    // the global reductions so that it does not wait for them
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (threadIdx.x < nc) {
         const int utt = S.s_utt[threadIdx.x];
         if (bt) atomicMax(&keys[2 * utt + 0], bt);
         if (bd) atomicMax(&keys[2 * utt + 1], bd);
     }
-    // generic accesses of the area before the next stage's bulk writes
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & T, unsigned long long * keys) {
@@ -1761,14 +1765,18 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
     bool rep = false;    // lists and control state held in shared memory (replicated decisions)
     int emit_iters = 0;
     // CTA 0 timestamps: per segment, its own work and the wait that follows
+    // (accumulators in shared memory: registers are the loop's scarcest resource)
+    __shared__ unsigned long long pacc[9];   // 8 segments, then the last timestamp
     const bool prof = blockIdx.x == 0 && threadIdx.x == 0 && P.prof != nullptr;
-    unsigned long long pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    unsigned long long tseg = prof ? gtimer() : 0ull;
+    if (prof) {
+        for (int i = 0; i < 8; ++i) pacc[i] = 0ull;
+        pacc[8] = gtimer();
+    }
     auto mark = [&](int slot) {
         if (prof) {
             const unsigned long long now = gtimer();
-            pacc[slot] += now - tseg;
-            tseg = now;
+            pacc[slot] += now - pacc[8];
+            pacc[8] = now;
         }
     };
     // control state of the first iteration from the host-written words; later
@@ -1878,6 +1886,13 @@ size_t step_loop_tc_smem_bytes(unsigned sm_weights, int area, int rpc_j, int rpc
 cudaError_t step_loop_configure(size_t smem, int tc) {
     return tc ? cudaFuncSetAttribute(step_loop_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem)
               : cudaFuncSetAttribute(step_loop_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+}
+
+size_t step_loop_static_smem(int tc) {
+    cudaFuncAttributes a{};
+    const cudaError_t e = tc ? cudaFuncGetAttributes(&a, step_loop_kernel<true>)
+                             : cudaFuncGetAttributes(&a, step_loop_kernel<false>);
+    return e == cudaSuccess ? a.sharedSizeBytes : 0;
 }
 
 cudaError_t step_loop_occupancy(size_t smem, int tc, int * blocks_per_sm) {
