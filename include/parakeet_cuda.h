@@ -303,6 +303,61 @@ PK_API pk_status pk_decode_noalloc(pk_ctx * ctx, const float * enc, int32_t n_fr
                                    int32_t max_symbols_per_step, int32_t * tokens, int32_t tokens_cap,
                                    int32_t * n_tokens, int32_t * steps);
 
+/* ---- Beside the token loop: CTC greedy decode and detokenize -----------------
+ *
+ * Both work on B utterances at once on one device. Host arrays are plain
+ * pointers; a `*_on_device` flag says whether the large input (logits,
+ * tokens) is a device pointer on the handle's device (4-byte aligned) or host
+ * memory. Outputs are written to host memory. */
+
+typedef struct pk_ctc pk_ctc;
+
+/* Replaces the per-utterance calls of ctc_greedy_decode / ctc_greedy_decode_window
+ * (src/parakeet_ctc.cpp:1820-1865, called at src/parakeet_engine.cpp:299 and
+ * src/main.cpp:777). vocab_size = logits row width (tokens + blank). */
+PK_API pk_status pk_ctc_create(int device, int32_t vocab_size, int32_t blank_id, pk_ctc ** out);
+PK_API void      pk_ctc_destroy(pk_ctc * c);
+
+/* logits: [sum n_frames][vocab_size] f32, utterance b at rows frame_offsets[b] ..
+ * frame_offsets[b] + n_frames[b] - 1. Each frame's argmax is the first index of
+ * its maximum (`>` scan from index 0, so a NaN at index 0 wins and other NaNs
+ * never do); a frame emits its argmax when it is not blank and differs from the
+ * previous frame's argmax. prev_inout[b] (host) is the argmax of the frame
+ * before the window (-1 for a fresh utterance) and receives the window's last
+ * argmax (ctc_greedy_decode_window's inout_prev_token). tokens (host, tokens_cap
+ * entries) receive the emitted tokens of all utterances back to back,
+ * token_offsets (host, B + 1) their start indices, first_frame (host, may be
+ * NULL) each token's frame index within its utterance's window. tokens_needed
+ * (host, may be NULL) receives the total; PK_ERR_CAPACITY when it exceeds
+ * tokens_cap (prev_inout is then left unchanged). */
+PK_API pk_status pk_ctc_greedy(pk_ctc * c, const float * logits, int32_t logits_on_device,
+                               const int64_t * frame_offsets, const int32_t * n_frames, int32_t B,
+                               int32_t * prev_inout, int32_t * tokens, int64_t tokens_cap,
+                               int64_t * token_offsets, int32_t * first_frame, int64_t * tokens_needed);
+
+typedef struct pk_vocab pk_vocab;
+
+/* Replaces parakeet::detokenize (src/sentencepiece_bpe.cpp:9-37) with its
+ * BpeVocab (src/sentencepiece_bpe.h): piece v is the byte string
+ * piece_bytes[piece_offsets[v] .. piece_offsets[v + 1]) (UTF-8, as the GGUF
+ * tokenizer stores it). blank / bos / eos / pad ids (-1: none) are skipped. */
+PK_API pk_status pk_vocab_create(int device, const uint8_t * piece_bytes, const int64_t * piece_offsets,
+                                 int32_t n_pieces, int32_t blank_id, int32_t bos_id, int32_t eos_id,
+                                 int32_t pad_id, pk_vocab ** out);
+PK_API void      pk_vocab_destroy(pk_vocab * v);
+
+/* tokens: [token_offsets[B]] int32 (host, or device when tokens_on_device),
+ * utterance b = tokens[token_offsets[b] .. token_offsets[b + 1]) (token_offsets
+ * on the host). Ids outside [0, n_pieces) and the special ids are skipped; each
+ * U+2581 (E2 96 81) inside a piece becomes one space; leading spaces of each
+ * utterance's text are removed. text (host, text_cap bytes) receives the B
+ * texts back to back (no terminators), text_offsets (host, B + 1) their start
+ * offsets, text_needed (host, may be NULL) the total; PK_ERR_CAPACITY when it
+ * exceeds text_cap. */
+PK_API pk_status pk_detokenize(pk_vocab * v, const int32_t * tokens, int32_t tokens_on_device,
+                               const int64_t * token_offsets, int32_t B, char * text, int64_t text_cap,
+                               int64_t * text_offsets, int64_t * text_needed);
+
 #ifdef __cplusplus
 }
 #endif

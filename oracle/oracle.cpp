@@ -498,4 +498,58 @@ double orc_decode_batch(const orc_model * m, const float * enc, const int64_t * 
     return failed.load() ? -1.0 : wall;
 }
 
+// ctc_greedy_decode_window (src/parakeet_ctc.cpp:1831-1865): per frame the
+// first index of the maximum (`>` scan from index 0), emitted when it is not
+// blank and differs from the previous frame's; prev carries across windows.
+int32_t orc_ctc_greedy_window(const float * logits, int32_t n_frames, int32_t vocab_size, int32_t blank_id,
+                              int32_t * prev, int32_t * tokens, int32_t cap, int32_t * n_tokens,
+                              int32_t * first_frame) {
+    int32_t p = *prev;
+    for (int32_t t = 0; t < n_frames; ++t) {
+        const float * row = logits + (size_t) t * vocab_size;
+        int32_t best = 0;
+        float best_score = row[0];
+        for (int32_t i = 1; i < vocab_size; ++i) {
+            if (row[i] > best_score) { best_score = row[i]; best = i; }
+        }
+        if (best != blank_id && best != p) {
+            if (*n_tokens >= cap) return -1;
+            if (first_frame) first_frame[*n_tokens] = t;
+            tokens[(*n_tokens)++] = best;
+        }
+        p = best;
+    }
+    *prev = p;
+    return 0;
+}
+
+// detokenize (src/sentencepiece_bpe.cpp:9-37): skip ids outside the vocabulary
+// and the blank / bos / eos / pad ids; copy each piece with every E2 96 81
+// (U+2581) replaced by one space; drop the text's leading spaces.
+int64_t orc_detokenize(const uint8_t * bytes, const int64_t * offsets, int32_t n_pieces, int32_t blank_id,
+                       int32_t bos_id, int32_t eos_id, int32_t pad_id, const int32_t * tokens, int64_t n_tokens,
+                       char * text, int64_t cap) {
+    std::string out;
+    for (int64_t k = 0; k < n_tokens; ++k) {
+        const int32_t id = tokens[k];
+        if (id < 0 || id >= n_pieces) continue;
+        if (id == blank_id || id == bos_id || id == eos_id || id == pad_id) continue;
+        const int64_t a = offsets[id], e = offsets[id + 1];
+        for (int64_t i = a; i < e;) {
+            if (bytes[i] == 0xE2 && i + 2 < e && bytes[i + 1] == 0x96 && bytes[i + 2] == 0x81) {
+                out.push_back(' ');
+                i += 3;
+            } else {
+                out.push_back((char) bytes[i]);
+                ++i;
+            }
+        }
+    }
+    size_t start = 0;
+    while (start < out.size() && out[start] == ' ') ++start;
+    const int64_t n = (int64_t) (out.size() - start);
+    if (text) std::memcpy(text, out.data() + start, (size_t) std::min<int64_t>(n, cap));
+    return n;
+}
+
 }  // extern "C"

@@ -100,6 +100,21 @@ double      orc_decode_batch(const orc_model * m, const float * enc, const int64
                              int32_t * bounds, const int64_t * bound_region, int32_t * n_bounds,
                              double * ms);
 
+/* ctc_greedy_decode_window (src/parakeet_ctc.cpp:1831-1865): frames
+ * [0, n_frames) of logits [n_frames][vocab_size]; *prev in/out. Tokens are
+ * appended at tokens[*n_tokens] (and their frames at first_frame[*n_tokens] when
+ * first_frame != NULL); returns -1 if `cap` would be exceeded, else 0. */
+int32_t     orc_ctc_greedy_window(const float * logits, int32_t n_frames, int32_t vocab_size,
+                                  int32_t blank_id, int32_t * prev, int32_t * tokens, int32_t cap,
+                                  int32_t * n_tokens, int32_t * first_frame);
+
+/* detokenize (src/sentencepiece_bpe.cpp:9-37) with a BpeVocab of n_pieces byte
+ * strings (piece v = bytes[offsets[v] .. offsets[v + 1])). Writes at most `cap`
+ * bytes of text; returns the text length (which may exceed cap). */
+int64_t     orc_detokenize(const uint8_t * bytes, const int64_t * offsets, int32_t n_pieces,
+                           int32_t blank_id, int32_t bos_id, int32_t eos_id, int32_t pad_id,
+                           const int32_t * tokens, int64_t n_tokens, char * text, int64_t cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,10 @@ def lib():
         L.orc_eou_decode_window.argtypes = [P, P, I32, I32, I32, P, P, I32, P, P, I32, P, P, P]
         L.orc_decode_batch.restype = C.c_double
         L.orc_decode_batch.argtypes = [P, P, P, P, I32, I32, I32, P, P, P, P, P, P, P, P]
+        L.orc_ctc_greedy_window.restype = I32
+        L.orc_ctc_greedy_window.argtypes = [P, I32, I32, I32, P, P, I32, P, P]
+        L.orc_detokenize.restype = C.c_int64
+        L.orc_detokenize.argtypes = [P, P, I32, I32, I32, I32, I32, P, C.c_int64, P, C.c_int64]
         _lib = L
     return _lib
 
@@ -189,3 +193,32 @@ class Oracle:
         if not self.is_tdt:
             res["bounds"] = [bounds[bregion[b]:bregion[b] + nb[b]].copy() for b in range(B)]
         return res
+
+
+def ctc_greedy_window(logits: np.ndarray, blank_id: int, prev: int = -1):
+    """ctc_greedy_decode_window (src/parakeet_ctc.cpp:1831-1865) on [frames][vocab]
+    logits. Returns (tokens, first frames, new prev)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    T, V = logits.shape
+    toks = np.zeros(max(T, 1), np.int32)
+    frs = np.zeros(max(T, 1), np.int32)
+    n = C.c_int32(0)
+    pv = C.c_int32(prev)
+    rc = lib().orc_ctc_greedy_window(_p(logits), T, V, blank_id, C.byref(pv), _p(toks), T, C.byref(n), _p(frs))
+    assert rc == 0
+    return toks[:n.value].copy(), frs[:n.value].copy(), pv.value
+
+
+def detokenize(pieces, tokens, blank_id=-1, bos_id=-1, eos_id=-1, pad_id=-1) -> bytes:
+    """parakeet::detokenize (src/sentencepiece_bpe.cpp:9-37) over byte-string pieces."""
+    bs = [p.encode("utf-8") if isinstance(p, str) else bytes(p) for p in pieces]
+    offs = np.zeros(len(bs) + 1, np.int64)
+    offs[1:] = np.cumsum([len(b) for b in bs])
+    buf = np.frombuffer(b"".join(bs) or b"\0", dtype=np.uint8).copy()
+    t = np.ascontiguousarray(tokens, dtype=np.int32)
+    n = lib().orc_detokenize(_p(buf), _p(offs), len(bs), blank_id, bos_id, eos_id, pad_id,
+                             _p(t) if len(t) else None, len(t), None, 0)
+    out = np.zeros(max(n, 1), np.uint8)
+    lib().orc_detokenize(_p(buf), _p(offs), len(bs), blank_id, bos_id, eos_id, pad_id,
+                         _p(t) if len(t) else None, len(t), _p(out), n)
+    return out[:n].tobytes()

@@ -58,6 +58,10 @@ def lib():
             "pk_stream_window": ([P, P, I32, I32, I32, I32, I32, P, I32, P, P, P, I32, P], I32),
             "pk_stream_get_state": ([P, P], I32), "pk_stream_set_state": ([P, P], I32),
             "pk_shard_lpt": ([P, I32, I32, P], I32),
+            "pk_ctc_create": ([I32, I32, I32, P], I32), "pk_ctc_destroy": ([P], None),
+            "pk_ctc_greedy": ([P, P, I32, P, P, I32, P, P, I64, P, P, P], I32),
+            "pk_vocab_create": ([I32, P, P, I32, I32, I32, I32, I32, P], I32), "pk_vocab_destroy": ([P], None),
+            "pk_detokenize": ([P, P, I32, P, I32, P, I64, P, P], I32),
         }
         for name, (args, res) in sigs.items():
             f = getattr(L, name)
@@ -280,3 +284,95 @@ class Stream:
 
 
 from . import multi  # noqa: E402,F401  (needs shard_lpt defined above)
+
+
+class CtcGreedy:
+    """Batched CTC greedy decode (ctc_greedy_decode / ctc_greedy_decode_window,
+    src/parakeet_ctc.cpp:1820-1865) on one GPU through the C ABI."""
+
+    def __init__(self, vocab_size: int, blank_id: int, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().pk_ctc_create(device, vocab_size, blank_id, C.byref(h)), "pk_ctc_create")
+        self._h = h
+        self.vocab_size, self.blank_id = vocab_size, blank_id
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().pk_ctc_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def decode(self, logits, frame_offsets, n_frames, prev=None, on_device=False, with_frames=False):
+        """logits: [frames][vocab] float32 (numpy, or a device pointer int with on_device).
+        Returns (token lists, frame lists or None, new prev array)."""
+        n_frames = np.ascontiguousarray(n_frames, dtype=np.int32)
+        B = len(n_frames)
+        foff = np.ascontiguousarray(frame_offsets, dtype=np.int64)
+        prev = np.full(B, -1, np.int32) if prev is None else np.array(prev, dtype=np.int32, copy=True)
+        cap = int(n_frames.sum())
+        toks = np.zeros(max(cap, 1), np.int32)
+        frs = np.zeros(max(cap, 1), np.int32) if with_frames else None
+        toff = np.zeros(B + 1, np.int64)
+        need = C.c_int64(0)
+        if on_device:
+            lp = C.c_void_p(int(logits))
+        else:
+            logits = np.ascontiguousarray(logits, dtype=np.float32)
+            lp = _p(logits)
+        _check(lib().pk_ctc_greedy(self._h, lp, 1 if on_device else 0, _p(foff), _p(n_frames), B, _p(prev),
+                                   _p(toks), cap, _p(toff), _p(frs) if with_frames else None, C.byref(need)),
+               "pk_ctc_greedy")
+        out = [toks[toff[b]:toff[b + 1]].copy() for b in range(B)]
+        fo = [frs[toff[b]:toff[b + 1]].copy() for b in range(B)] if with_frames else None
+        return out, fo, prev
+
+
+class Vocab:
+    """SentencePiece BPE detokenizer (parakeet::detokenize, src/sentencepiece_bpe.cpp:9-37)
+    with the vocabulary held on one GPU."""
+
+    def __init__(self, pieces, blank_id=-1, bos_id=-1, eos_id=-1, pad_id=-1, device: int = 0):
+        bs = [p.encode("utf-8") if isinstance(p, str) else bytes(p) for p in pieces]
+        offs = np.zeros(len(bs) + 1, np.int64)
+        offs[1:] = np.cumsum([len(b) for b in bs])
+        buf = np.frombuffer(b"".join(bs) or b"\0", dtype=np.uint8).copy()
+        h = C.c_void_p()
+        _check(lib().pk_vocab_create(device, _p(buf), _p(offs), len(bs), blank_id, bos_id, eos_id, pad_id,
+                                     C.byref(h)), "pk_vocab_create")
+        self._h = h
+        self.n = len(bs)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().pk_vocab_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def detokenize(self, token_lists) -> list:
+        """token_lists: sequences of int ids, one per utterance. Returns bytes per utterance."""
+        B = len(token_lists)
+        lens = [len(t) for t in token_lists]
+        toff = np.zeros(B + 1, np.int64)
+        toff[1:] = np.cumsum(lens)
+        toks = np.ascontiguousarray(np.concatenate([np.asarray(t, np.int32) for t in token_lists])
+                                    if sum(lens) else np.zeros(1, np.int32), dtype=np.int32)
+        tof = np.zeros(B + 1, np.int64)
+        need = C.c_int64(0)
+        rc = lib().pk_detokenize(self._h, _p(toks), 0, _p(toff), B, None, 0, _p(tof), C.byref(need))
+        if rc not in (0, 7):   # PK_ERR_CAPACITY: size query
+            _check(rc, "pk_detokenize")
+        cap = int(need.value)
+        text = np.zeros(max(cap, 1), np.uint8)
+        _check(lib().pk_detokenize(self._h, _p(toks), 0, _p(toff), B, _p(text), cap, _p(tof), C.byref(need)),
+               "pk_detokenize")
+        return [text[tof[b]:tof[b + 1]].tobytes() for b in range(B)]
