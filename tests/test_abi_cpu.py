@@ -81,6 +81,34 @@ def test_create_without_device_fails_cleanly(pk):
     assert e.value.status in (pk.abi.PK_ERR_NO_DEVICE, pk.abi.PK_ERR_CUDA)
 
 
+def test_text_entry_points_check_arguments(pk):
+    """pk_ctc_* / pk_vocab_* / pk_detokenize reject bad arguments before touching a device."""
+    L = pk.lib()
+    E = pk.abi
+    h = C.c_void_p()
+    assert L.pk_ctc_create(0, 0, 0, C.byref(h)) == E.PK_ERR_INVALID            # empty vocabulary
+    assert L.pk_ctc_create(0, 10, 10, C.byref(h)) == E.PK_ERR_INVALID          # blank out of range
+    assert L.pk_ctc_create(0, 10, 3, None) == E.PK_ERR_INVALID
+    assert L.pk_ctc_greedy(None, None, 0, None, None, 1, None, None, 0, None, None, None) == E.PK_ERR_INVALID
+    offs = np.array([0, 2, 1], np.int64)                                         # decreasing
+    assert L.pk_vocab_create(0, None, offs.ctypes.data, 2, -1, -1, -1, -1, C.byref(h)) == E.PK_ERR_INVALID
+    assert L.pk_detokenize(None, None, 0, None, 1, None, 0, None, None) == E.PK_ERR_INVALID
+    L.pk_ctc_destroy(None)
+    L.pk_vocab_destroy(None)
+
+
+def test_text_create_without_device_fails_cleanly(pk):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    with pytest.raises(pk.PkError) as e:
+        pk.CtcGreedy(10, 3)
+    assert e.value.status == pk.abi.PK_ERR_NO_DEVICE
+    with pytest.raises(pk.PkError) as e:
+        pk.Vocab(["a", "b"])
+    assert e.value.status == pk.abi.PK_ERR_NO_DEVICE
+
+
 def test_gguf_round_trip(pk, tmp_path):
     m = pk.synth.make_decoder("eou", vocab_size=40, d_enc=32, pred_hidden=32, joint_hidden=64,
                               n_layers=1, wtype="f16", eou_id=36, eob_id=37)
