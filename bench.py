@@ -222,8 +222,12 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="override utterances per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--path", default="tdt", choices=["tdt", "ctc"],
+                    help="tdt: the token loop (the headline); ctc: CTC greedy decode beside it (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 0)
+    if args.path == "ctc":
+        return run_ctc(args)
 
     cfg = dict(CONFIGS[args.config])
     wtype = args.wtype or cfg["wtype"]
@@ -250,6 +254,89 @@ def main():
     if args.impl == "reference":
         return run_reference(args, model, enc, offs, T, config, rank)
     return run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wtype)
+
+
+def run_ctc(args):
+    """CTC greedy decode (pk_ctc_greedy, src/parakeet_ctc.cpp:1820-1865) over a config-2 sized batch
+    of synthetic CTC logits (V = 1025: 1024 pieces + blank, N(0,1) with the blank raised by 2,
+    mostly-blank frames as a CTC head gives): frames/s device-resident and end to end, the HBM
+    roofline of reading the logits, and the oracle on one host thread. One GPU."""
+    import torch
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"path": "ctc", "unavailable": "the CTC measurement runs on one GPU"}))
+        return 0
+    pk = pkg()
+    cfg = CONFIGS[args.config]
+    B = args.batch or cfg["B"]
+    T = global_lengths(pk, cfg, B).astype(np.int32)
+    offs = np.zeros(B, np.int64)
+    offs[1:] = np.cumsum(T[:-1])
+    F, V, blank = int(T.sum()), 1025, 1024
+    g = torch.Generator(device="cuda").manual_seed(7)
+    logits = torch.randn(F, V, device="cuda", generator=g)
+    logits[:, blank] += 2.0
+    host = logits.cpu().pin_memory()
+    ctc = pk.CtcGreedy(V, blank)
+    for _ in range(max(args.warmup, 3)):
+        ctc.decode(logits.data_ptr(), offs, T, on_device=True)
+    clocks = ClockSampler(0)
+    clocks.start()
+    ms = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        toks, _, _ = ctc.decode(logits.data_ptr(), offs, T, on_device=True)
+        e1.record()
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    clk = clocks.stop()
+    ms_e2e = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        toks_h, _, _ = ctc.decode(host.numpy(), offs, T)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_e2e.append(e0.elapsed_time(e1))
+    same = all(np.array_equal(a, b) for a, b in zip(toks, toks_h))
+    t = float(np.mean(ms))
+    peak, peak_kind = read_peaks()
+    achieved = F * V * 4 / (t * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        orc = oracle_mod()
+        L = host.numpy()
+        n = fr = 0
+        t0 = time.perf_counter()
+        while n < B and time.perf_counter() - t0 < min(args.cpu_budget_s, 20.0):
+            orc.ctc_greedy_window(L[offs[n]:offs[n] + T[n]], blank, -1)
+            fr += int(T[n])
+            n += 1
+        wall = time.perf_counter() - t0
+        cpu = {"value": fr / wall, "unit": "frames/s", "cores": 1, "kind": "port",
+               "sample": f"first {n} utterances of the batch ({fr} frames), orc_ctc_greedy_window on one thread"}
+    print(json.dumps({
+        "path": "ctc", "metric": "ctc_greedy_frames_per_sec", "value": F / (t * 1e-3), "unit": "frames/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": t,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1) logits, blank raised by 2", "config": {
+            "workload": f"CTC greedy, B={B} utterances of config-{args.config} lengths, V={V}",
+            "frames": F, "l2": f"logits {F * V * 4 / 1e6:.0f} MB per step (L2 is 126 MB)"},
+        "tokens_per_step": int(sum(len(x) for x in toks)), "clocks": clk,
+        "e2e": {"value": F / (float(np.mean(ms_e2e)) * 1e-3), "unit": "frames/s",
+                "h2d_bytes_per_step": F * V * 4, "d2h_bytes_per_step": int(sum(len(x) for x in toks)) * 4 + (B + 1) * 8,
+                "tokens_match_device_run": same},
+        "gpu_launches": 4 * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "ctc_argmax_kernel (+ collapse / scan / gather in the same call)",
+                     "note": f"algorithmic bytes = logits read once (4 B x V per frame); time = the whole call "
+                             f"(host synchronisations included); peak {peak_kind}"},
+        "cpu_baseline": cpu,
+    }))
+    return 0
 
 
 def run_reference(args, model, enc, offs, T, config, rank):
