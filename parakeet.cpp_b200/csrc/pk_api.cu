@@ -361,12 +361,20 @@ pk_status setup_tc(pk_ctx * x, const pk_model_desc * d, size_t smem_cap) {
     auto area_for = [&](int mb) -> int {
         const size_t pr = (size_t) kTcM * mb;
         const size_t part = (size_t) kWarps * (mb == 2 ? 7 : kTcRmax) * 8 * (pr + 4) * 4;   // rows padded by 4
-        const size_t a = std::max({pr * x->tc_rbj, (L > 1 ? 2 : 1) * pr * x->tc_rbh, part});
+        // a joint or pred-proj slice of more tiles than one GEMM call takes is done
+        // call by call on one staged tile: its partial sums (and the argmax keys) go after it
+        const int tg = mb == 2 ? 7 : kTcRmax;
+        const size_t jkeep = x->tcj.tiles <= tg ? 0
+            : pr * x->tc_rbj + std::max<size_t>((size_t) 4 * tg * 8 * (pr + 4) * 4, kThreads * 16) + 16;
+        const size_t pkeep = x->tcp.tiles <= tg ? 0
+            : pr * x->tc_rbh + std::max<size_t>((size_t) (mb == 2 ? kWarps : 4) * tg * 8 * (pr + 4) * 4,
+                                                kThreads * 16) + 16;
+        const size_t a = std::max({pr * x->tc_rbj, (L > 1 ? 2 : 1) * pr * x->tc_rbh, part, jkeep, pkeep});
         return (int) ((a + 15) & ~(size_t) 15);
     };
-    // passes of 32 when every GEMM of the loop has at most 7 tiles per call and
+    // passes of 32 when the LSTM slice fits one two-block GEMM call (7 tiles) and
     // 32 utterances x the CTA's units fit one thread each in the cell update
-    const bool mb2_ok = tiles_l <= 7 && kTcM * 2 * upc <= kThreads;
+    const bool mb2_ok = tiles_l <= 7 && kTcM * 2 * upc <= kThreads;   // one call per LSTM pass
     size_t need = 0;
     x->tc_stationary = 0;
     for (int mb = mb2_ok ? 2 : 1; mb >= 1 && !x->tc_stationary; --mb) {

@@ -1080,9 +1080,12 @@ struct ATile {
 // kw (4 or 8): warps that split K. Fewer warps halve the partial sums to
 // reduce; the tensor pipe stays busy with one warp per scheduler for the
 // joint's many tiles and for passes of one m16 block.
+// part_end: the partial sums go to the end of the staging area, so that the
+// activation rows at its start survive the call (the phase's next call on
+// further tiles reads them again).
 template <int NT, int MB>
 __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, const ATile & A,
-                           int kw) {
+                           int kw, bool part_end) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = lane & 3, g = lane >> 2;
     const int nkb = b.K >> 5;
@@ -1198,7 +1201,8 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
     // rows padded to W + 4 floats: a store's 32 lanes (rows 2t / 2t + 1, columns g)
     // then fall on 32 distinct banks (2 (W + 4) = 8 mod 32)
     constexpr int WP = W + 4;
-    float * part = reinterpret_cast<float *>(S.area);  // [kw][NT][8][WP]
+    const int part_off = part_end ? ((P.area - kw * NT * 8 * WP * 4) & ~15) : 0;
+    float * part = reinterpret_cast<float *>(S.area + part_off);  // [kw][NT][8][WP]
     if (warp < kw) {
 #pragma unroll
         for (int r = 0; r < NT; ++r) {
@@ -1228,30 +1232,31 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
 __device__ __forceinline__ int c_index(int r, int c, int W) { return (r >> 3) * 8 * W + (r & 7) * W + c; }
 
 // mbp: m16 blocks of this pass (2 only when the pass has more than 16
-// utterances and the loop was set up for 32-utterance passes).
+// utterances and the loop was set up for 32-utterance passes). Two-block calls
+// take at most 7 tiles, one-block calls 8 (callers split larger groups).
 __device__ __forceinline__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt,
-                                        const ATile & A, int mbp, int kw) {
+                                        const ATile & A, int mbp, int kw, bool part_end = false) {
     if (mbp == 2) {
         switch (nt) {
-            case 1: tc_gemm_nt<1, 2>(P, S, b, t0, A, kw); break;
-            case 2: tc_gemm_nt<2, 2>(P, S, b, t0, A, kw); break;
-            case 3: tc_gemm_nt<3, 2>(P, S, b, t0, A, kw); break;
-            case 4: tc_gemm_nt<4, 2>(P, S, b, t0, A, kw); break;
-            case 5: tc_gemm_nt<5, 2>(P, S, b, t0, A, kw); break;
-            case 6: tc_gemm_nt<6, 2>(P, S, b, t0, A, kw); break;
-            default: tc_gemm_nt<7, 2>(P, S, b, t0, A, kw); break;
+            case 1: tc_gemm_nt<1, 2>(P, S, b, t0, A, kw, part_end); break;
+            case 2: tc_gemm_nt<2, 2>(P, S, b, t0, A, kw, part_end); break;
+            case 3: tc_gemm_nt<3, 2>(P, S, b, t0, A, kw, part_end); break;
+            case 4: tc_gemm_nt<4, 2>(P, S, b, t0, A, kw, part_end); break;
+            case 5: tc_gemm_nt<5, 2>(P, S, b, t0, A, kw, part_end); break;
+            case 6: tc_gemm_nt<6, 2>(P, S, b, t0, A, kw, part_end); break;
+            default: tc_gemm_nt<7, 2>(P, S, b, t0, A, kw, part_end); break;
         }
         return;
     }
     switch (nt) {
-        case 1: tc_gemm_nt<1, 1>(P, S, b, t0, A, kw); break;
-        case 2: tc_gemm_nt<2, 1>(P, S, b, t0, A, kw); break;
-        case 3: tc_gemm_nt<3, 1>(P, S, b, t0, A, kw); break;
-        case 4: tc_gemm_nt<4, 1>(P, S, b, t0, A, kw); break;
-        case 5: tc_gemm_nt<5, 1>(P, S, b, t0, A, kw); break;
-        case 6: tc_gemm_nt<6, 1>(P, S, b, t0, A, kw); break;
-        case 7: tc_gemm_nt<7, 1>(P, S, b, t0, A, kw); break;
-        default: tc_gemm_nt<8, 1>(P, S, b, t0, A, kw); break;
+        case 1: tc_gemm_nt<1, 1>(P, S, b, t0, A, kw, part_end); break;
+        case 2: tc_gemm_nt<2, 1>(P, S, b, t0, A, kw, part_end); break;
+        case 3: tc_gemm_nt<3, 1>(P, S, b, t0, A, kw, part_end); break;
+        case 4: tc_gemm_nt<4, 1>(P, S, b, t0, A, kw, part_end); break;
+        case 5: tc_gemm_nt<5, 1>(P, S, b, t0, A, kw, part_end); break;
+        case 6: tc_gemm_nt<6, 1>(P, S, b, t0, A, kw, part_end); break;
+        case 7: tc_gemm_nt<7, 1>(P, S, b, t0, A, kw, part_end); break;
+        default: tc_gemm_nt<8, 1>(P, S, b, t0, A, kw, part_end); break;
     }
 }
 
@@ -1570,7 +1575,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             A.kb_split = P.tcp.K >> 5;
             for (int t0 = 0; t0 < P.tcp.tiles; t0 += TG) {
                 const int nt = min(TG, P.tcp.tiles - t0);
-                tc_gemm(P, S, P.tcp, t0, nt, A, mbp, mbp == 2 ? kWarps : 4);
+                tc_gemm(P, S, P.tcp, t0, nt, A, mbp, mbp == 2 ? kWarps : 4, P.tcp.tiles > TG);
                 for (int idx = threadIdx.x; idx < nc * nt * 8; idx += blockDim.x) {
                     const int rr = idx / nc, cc = idx - rr * nc, row = t0 * 8 + rr;   // utterance fastest
                     if (row < nr) {
@@ -1623,9 +1628,13 @@ __device__ __forceinline__ void joint_keys(const LoopParams & P, const TcSmem & 
             }
         }
     }
-    ulonglong2 * kp = reinterpret_cast<ulonglong2 *>(S.area);
+    // (at the end of the area: with several calls per pass, the staged rows at its
+    // start feed the next one)
+    ulonglong2 * kp = reinterpret_cast<ulonglong2 *>(S.area + ((P.area - kThreads * 16) & ~15));
     kp[threadIdx.x] = make_ulonglong2(bt, bd);
+    SUBMARK(18);
     __syncthreads();
+    SUBMARK(19);
     if (threadIdx.x < nc) {
 #pragma unroll
         for (int g = 1; g < RG; ++g) {
@@ -1636,12 +1645,15 @@ __device__ __forceinline__ void joint_keys(const LoopParams & P, const TcSmem & 
     }
     // generic accesses of the area before the next stage's bulk writes; ahead of
     // the global reductions so that it does not wait for them
+    SUBMARK(20);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    SUBMARK(21);
     if (threadIdx.x < nc) {
         const int utt = S.s_utt[threadIdx.x];
         if (bt) atomicMax(&keys[2 * utt + 0], bt);
         if (bd) atomicMax(&keys[2 * utt + 1], bd);
     }
+    SUBMARK(22);
 }
 
 __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & T, unsigned long long * keys) {
@@ -1682,7 +1694,7 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
         A.kb_split = P.tcj.K >> 5;
         for (int t0 = 0; t0 < P.tcj.tiles; t0 += TG) {
             const int nt = min(TG, P.tcj.tiles - t0);
-            tc_gemm(P, S, P.tcj, t0, nt, A, mbp, 4);
+            tc_gemm(P, S, P.tcj, t0, nt, A, mbp, 4, P.tcj.tiles > TG);
             SUBMARK(11);
             if (mbp == 2) joint_keys<2 * kTcM>(P, S, nc, nt, t0, nr, r0, keys);
             else joint_keys<kTcM>(P, S, nc, nt, t0, nr, r0, keys);

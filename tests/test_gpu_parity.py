@@ -101,6 +101,35 @@ def test_tdt_0_6b_ragged_batch(built, orc, math):
     assert r["steps"][3] == 0 and len(r["tokens"][3]) == 0
 
 
+def test_tdt_0_6b_two_block_passes(built, orc):
+    """40 live utterances: 32-utterance passes (two m16 blocks) in every phase, and a
+    joint slice of 7 tiles per CTA that the GEMM covers in two calls on one staged tile."""
+    pk = built
+    m = pk.synth.tdt_0_6b(seed=17)
+    dec = pk.Decoder(m, math="tc")
+    o = orc.Oracle(m)
+    T = pk.synth.lengths_uniform(40, 20, 70, seed=4)
+    enc, offs = pk.synth.encoder_batch(T, m.d_enc, seed=6)
+    r = dec.decode_batch(enc, offs, T)
+    ro = o.decode_batch(enc, offs, T)
+    parity.compare_free_running(dec, o, enc, offs, T, r["tokens"], ro["tokens"])
+
+
+def test_joint_slice_in_several_calls(built, orc):
+    """A 9000-piece vocabulary gives each CTA 61 joint rows (8 tiles): 32-utterance
+    passes cover them in two GEMM calls on one staged tile."""
+    pk = built
+    m = pk.synth.make_decoder("tdt", vocab_size=9000, d_enc=128, pred_hidden=128, joint_hidden=128,
+                              seed=23, blank_bias=1.0)
+    dec = pk.Decoder(m, math="tc")
+    o = orc.Oracle(m)
+    T = pk.synth.lengths_uniform(40, 10, 40, seed=8)
+    enc, offs = pk.synth.encoder_batch(T, m.d_enc, seed=12)
+    r = dec.decode_batch(enc, offs, T)
+    ro = o.decode_batch(enc, offs, T)
+    parity.compare_free_running(dec, o, enc, offs, T, r["tokens"], ro["tokens"])
+
+
 @pytest.mark.parametrize("wtype", ["f16", "q8_0"])
 @pytest.mark.parametrize("math", MATHS)
 def test_tdt_1_1b(built, orc, wtype, math):
