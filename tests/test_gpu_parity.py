@@ -163,6 +163,24 @@ def test_eou_120m_batch(built, orc, math):
     parity.assert_tf_ok(st, "eou")
 
 
+def test_eou_leader_then_replicated_decisions(built, orc):
+    """300 EOU utterances: the loop starts with more live utterances than a CTA keeps
+    in shared memory (leader decisions), then switches to decisions every CTA makes
+    itself as utterances finish; tokens and EOU boundaries must match the oracle."""
+    pk = built
+    m = pk.synth.make_decoder("eou", vocab_size=64, d_enc=64, pred_hidden=64, joint_hidden=64,
+                              n_layers=1, wtype="f16", seed=29, blank_bias=0.5)
+    dec = pk.Decoder(m, math="tc")
+    o = orc.Oracle(m)
+    T = pk.synth.lengths_uniform(300, 1, 60, seed=31)
+    enc, offs = pk.synth.encoder_batch(T, m.d_enc, seed=33)
+    r = dec.decode_batch(enc, offs, T)
+    ro = o.decode_batch(enc, offs, T)
+    parity.compare_free_running(dec, o, enc, offs, T, r["tokens"], ro["tokens"],
+                                gpu_bounds=r["bounds"], oracle_bounds=ro["bounds"])
+    assert sum(len(b) for b in ro["bounds"]) > 0      # the case does reach EOU
+
+
 @pytest.mark.parametrize("math", MATHS)
 def test_many_chunks_small_model(built, orc, math):
     """B=300 crosses several 32-utterance chunks and exercises live-list compaction."""
