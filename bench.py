@@ -96,7 +96,9 @@ def host_cores():
 # ---------------------------------------------------------------- clocks ----
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region.
+    start() returns once the first sample is in, so that a timed region shorter than the
+    sampling period still has one (taken as it begins)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -116,6 +118,9 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.perf_counter()
+            while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 3.0:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
 
