@@ -119,7 +119,7 @@ struct Smem {
     int * s_aux;                    // [32] token / step
     int * s_aux2;                   // [32] reset / h-buffer
     int * s_scan;                   // [kWarps + 2]
-    int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2-3 staging, 4-6 release word
+    int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2 staging phase, 4-6 release word
 };
 
 __device__ __forceinline__ Smem carve(unsigned char * raw, const LoopParams & P, int upc) {
@@ -889,7 +889,7 @@ struct TcSmem {
     int2 * s_lst;                   // [kTcRec] its control state in replicated mode:
                                     // (frames left, symbol count | h buffer << 30)
     int * s_scan;                   // [kWarps + 2]
-    int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2-3 staging, 4-6 release word
+    int * s_flag;                   // [8]: 0 leader arrival, 1 wait status, 2 staging phase, 4-6 release word
     float * bj;                     // [rpc_j] this CTA's joint-out bias slice
     float * bp;                     // [rpc_p] this CTA's pred-proj bias slice
     float * lb;                     // [L][4][upc] LSTM gate biases of this CTA's units
@@ -1025,31 +1025,25 @@ __device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S,
         }
     }
     SUBMARK(15);
-    if (threadIdx.x == 0) {
-        int ok = 0;
+    // every thread waits for the phase itself (the completed wait orders the copied
+    // data for it), each with the same bound; one barrier agrees on the outcome
+    int fail = 0;
+    {
         const unsigned long long t0 = gtimer();
         for (unsigned it = 1;; ++it) {
             unsigned done;
             asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
                          : "=r"(done) : "r"(mb), "r"(ph) : "memory");
-            if (done) { ok = 1; break; }
-            if ((it & 63u) == 0u && (long long) (gtimer() - t0) > P.timeout_ns) {
-                atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_TIMEOUT);
-                break;
-            }
+            if (done) break;
+            if ((it & 63u) == 0u && (long long) (gtimer() - t0) > P.timeout_ns) { fail = 1; break; }
         }
-        S.s_flag[3] = ok;
     }
-    __syncthreads();
+    const bool ok = __syncthreads_or(fail) == 0;   // everyone has read the phase bit before it flips
     SUBMARK(16);
-    const bool ok = S.s_flag[3] != 0;
-    if (ok) {
-        // the phase is complete: this test returns at once and orders the copied data for every thread
-        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%0], %1; }"
-                     :: "r"(mb), "r"(ph) : "memory");
+    if (threadIdx.x == 0) {
+        if (!ok) atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_TIMEOUT);
+        S.s_flag[2] = (int) (ph ^ 1u);
     }
-    __syncthreads();   // everyone has read the phase bit before it flips
-    if (threadIdx.x == 0) S.s_flag[2] = (int) (ph ^ 1u);
     return ok;
 }
 
