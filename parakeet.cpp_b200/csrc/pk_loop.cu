@@ -1074,12 +1074,13 @@ struct ATile {
 // kw (4 or 8): warps that split K. Fewer warps halve the partial sums to
 // reduce; the tensor pipe stays busy with one warp per scheduler for the
 // joint's many tiles and for passes of one m16 block.
-// part_end: the partial sums go to the end of the staging area, so that the
-// activation rows at its start survive the call (the phase's next call on
-// further tiles reads them again).
+// keep: bytes of activation rows at the start of the staging area. When the
+// partial sums fit after them they go to the end of the area, the rows survive
+// the call (a phase's next call on further tiles reads them again) and no CTA
+// barrier has to separate the warps' last row reads from the partial writes.
 template <int NT, int MB>
 __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, const ATile & A,
-                           int kw, bool part_end) {
+                           int kw, int keep) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = lane & 3, g = lane >> 2;
     const int nkb = b.K >> 5;
@@ -1189,14 +1190,15 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
             }
         }
     }
-    // every warp's ldmatrix reads are done before the partial sums overwrite the rows
-    __syncthreads();
     constexpr int W = 16 * MB;                         // utterance columns of a partial tile
     // rows padded to W + 4 floats: a store's 32 lanes (rows 2t / 2t + 1, columns g)
     // then fall on 32 distinct banks (2 (W + 4) = 8 mod 32)
     constexpr int WP = W + 4;
-    const int part_off = part_end ? ((P.area - kw * NT * 8 * WP * 4) & ~15) : 0;
-    float * part = reinterpret_cast<float *>(S.area + part_off);  // [kw][NT][8][WP]
+    const int end_off = (P.area - kw * NT * 8 * WP * 4) & ~15;
+    const bool at_end = keep > 0 && end_off >= keep;
+    // otherwise every warp's ldmatrix reads are done before the partial sums overwrite the rows
+    if (!at_end) __syncthreads();
+    float * part = reinterpret_cast<float *>(S.area + (at_end ? end_off : 0));  // [kw][NT][8][WP]
     if (warp < kw) {
 #pragma unroll
         for (int r = 0; r < NT; ++r) {
@@ -1229,28 +1231,28 @@ __device__ __forceinline__ int c_index(int r, int c, int W) { return (r >> 3) * 
 // utterances and the loop was set up for 32-utterance passes). Two-block calls
 // take at most 7 tiles, one-block calls 8 (callers split larger groups).
 __device__ __forceinline__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt,
-                                        const ATile & A, int mbp, int kw, bool part_end = false) {
+                                        const ATile & A, int mbp, int kw, int keep = 0) {
     if (mbp == 2) {
         switch (nt) {
-            case 1: tc_gemm_nt<1, 2>(P, S, b, t0, A, kw, part_end); break;
-            case 2: tc_gemm_nt<2, 2>(P, S, b, t0, A, kw, part_end); break;
-            case 3: tc_gemm_nt<3, 2>(P, S, b, t0, A, kw, part_end); break;
-            case 4: tc_gemm_nt<4, 2>(P, S, b, t0, A, kw, part_end); break;
-            case 5: tc_gemm_nt<5, 2>(P, S, b, t0, A, kw, part_end); break;
-            case 6: tc_gemm_nt<6, 2>(P, S, b, t0, A, kw, part_end); break;
-            default: tc_gemm_nt<7, 2>(P, S, b, t0, A, kw, part_end); break;
+            case 1: tc_gemm_nt<1, 2>(P, S, b, t0, A, kw, keep); break;
+            case 2: tc_gemm_nt<2, 2>(P, S, b, t0, A, kw, keep); break;
+            case 3: tc_gemm_nt<3, 2>(P, S, b, t0, A, kw, keep); break;
+            case 4: tc_gemm_nt<4, 2>(P, S, b, t0, A, kw, keep); break;
+            case 5: tc_gemm_nt<5, 2>(P, S, b, t0, A, kw, keep); break;
+            case 6: tc_gemm_nt<6, 2>(P, S, b, t0, A, kw, keep); break;
+            default: tc_gemm_nt<7, 2>(P, S, b, t0, A, kw, keep); break;
         }
         return;
     }
     switch (nt) {
-        case 1: tc_gemm_nt<1, 1>(P, S, b, t0, A, kw, part_end); break;
-        case 2: tc_gemm_nt<2, 1>(P, S, b, t0, A, kw, part_end); break;
-        case 3: tc_gemm_nt<3, 1>(P, S, b, t0, A, kw, part_end); break;
-        case 4: tc_gemm_nt<4, 1>(P, S, b, t0, A, kw, part_end); break;
-        case 5: tc_gemm_nt<5, 1>(P, S, b, t0, A, kw, part_end); break;
-        case 6: tc_gemm_nt<6, 1>(P, S, b, t0, A, kw, part_end); break;
-        case 7: tc_gemm_nt<7, 1>(P, S, b, t0, A, kw, part_end); break;
-        default: tc_gemm_nt<8, 1>(P, S, b, t0, A, kw, part_end); break;
+        case 1: tc_gemm_nt<1, 1>(P, S, b, t0, A, kw, keep); break;
+        case 2: tc_gemm_nt<2, 1>(P, S, b, t0, A, kw, keep); break;
+        case 3: tc_gemm_nt<3, 1>(P, S, b, t0, A, kw, keep); break;
+        case 4: tc_gemm_nt<4, 1>(P, S, b, t0, A, kw, keep); break;
+        case 5: tc_gemm_nt<5, 1>(P, S, b, t0, A, kw, keep); break;
+        case 6: tc_gemm_nt<6, 1>(P, S, b, t0, A, kw, keep); break;
+        case 7: tc_gemm_nt<7, 1>(P, S, b, t0, A, kw, keep); break;
+        default: tc_gemm_nt<8, 1>(P, S, b, t0, A, kw, keep); break;
     }
 }
 
@@ -1482,7 +1484,8 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
         A.rb = P.rbh;
         A.lo = H * es;
         A.kb_split = l == 0 ? (bk.K >> 5) : (H >> 5);
-        tc_gemm(P, S, bk, 0, bk.tiles, A, mbp, mbp == 2 ? kWarps : 4);
+        tc_gemm(P, S, bk, 0, bk.tiles, A, mbp, mbp == 2 ? kWarps : 4,
+                l == 0 ? nc * P.rbh : PR * P.rbh + nc * P.rbh);
         SUBMARK(3);
         // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
         if (act) {
@@ -1569,7 +1572,7 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             A.kb_split = P.tcp.K >> 5;
             for (int t0 = 0; t0 < P.tcp.tiles; t0 += TG) {
                 const int nt = min(TG, P.tcp.tiles - t0);
-                tc_gemm(P, S, P.tcp, t0, nt, A, mbp, mbp == 2 ? kWarps : 4, P.tcp.tiles > TG);
+                tc_gemm(P, S, P.tcp, t0, nt, A, mbp, mbp == 2 ? kWarps : 4, nc * P.rbh);
                 for (int idx = threadIdx.x; idx < nc * nt * 8; idx += blockDim.x) {
                     const int rr = idx / nc, cc = idx - rr * nc, row = t0 * 8 + rr;   // utterance fastest
                     if (row < nr) {
@@ -1688,7 +1691,7 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
         A.kb_split = P.tcj.K >> 5;
         for (int t0 = 0; t0 < P.tcj.tiles; t0 += TG) {
             const int nt = min(TG, P.tcj.tiles - t0);
-            tc_gemm(P, S, P.tcj, t0, nt, A, mbp, 4, P.tcj.tiles > TG);
+            tc_gemm(P, S, P.tcj, t0, nt, A, mbp, 4, nc * P.rbj);
             SUBMARK(11);
             if (mbp == 2) joint_keys<2 * kTcM>(P, S, nc, nt, t0, nr, r0, keys);
             else joint_keys<kTcM>(P, S, nc, nt, t0, nr, r0, keys);
@@ -1818,7 +1821,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
             for (int l = 0; l < P.L; ++l) {
                 if constexpr (TC) tc_phase_lstm(P, l, n_emit, T);
                 else phase_lstm(P, l, n_emit, S);
-                __syncthreads();
                 mark(0);
                 if (!grid_barrier(P, nbar, S)) return;
                 mark(1);
@@ -1826,7 +1828,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         }
         if constexpr (TC) tc_phase_pred(P, first, n_emit, sel, n_live, T);
         else phase_pred(P, first, n_emit, sel, n_live, S);
-        __syncthreads();
         mark(2);
         if (!grid_barrier(P, nbar, S)) return;
         mark(3);
@@ -1834,7 +1835,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         if (n_live == 0) break;
         if constexpr (TC) tc_phase_joint(P, sel, n_live, T, keys);
         else phase_joint(P, sel, n_live, S, keys);
-        __syncthreads();
         mark(4);
         bool rep_now = false;
         if constexpr (TC) rep_now = rep_mode(P, n_live);
