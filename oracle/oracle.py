@@ -222,3 +222,30 @@ def detokenize(pieces, tokens, blank_id=-1, bos_id=-1, eos_id=-1, pad_id=-1) -> 
     lib().orc_detokenize(_p(buf), _p(offs), len(bs), blank_id, bos_id, eos_id, pad_id,
                          _p(t) if len(t) else None, len(t), _p(out), n)
     return out[:n].tobytes()
+
+
+REF_PATH = os.path.join(HERE, "_ref", "libref_detok.so")
+_ref = None
+
+
+def ref_detokenize(pieces, tokens, blank_id=-1, bos_id=-1, eos_id=-1, pad_id=-1):
+    """The reference's own detokenize (src/sentencepiece_bpe.cpp, built into _ref/ by
+    `make ref` from the reference's sources), or None when that library is absent."""
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_PATH):
+            return None
+        _ref = C.CDLL(REF_PATH)
+        P, I32, I64 = C.c_void_p, C.c_int32, C.c_int64
+        _ref.ref_detokenize.restype = I64
+        _ref.ref_detokenize.argtypes = [P, P, I32, I32, I32, I32, I32, P, I64, P, I64]
+    bs = [p.encode("utf-8") if isinstance(p, str) else bytes(p) for p in pieces]
+    offs = np.zeros(len(bs) + 1, np.int64)
+    offs[1:] = np.cumsum([len(b) for b in bs])
+    buf = np.frombuffer(b"".join(bs) or b"\0", dtype=np.uint8).copy()
+    t = np.ascontiguousarray(tokens, dtype=np.int32)
+    args = (_p(buf), _p(offs), len(bs), blank_id, bos_id, eos_id, pad_id, _p(t) if len(t) else None, len(t))
+    n = _ref.ref_detokenize(*args, None, 0)
+    out = np.zeros(max(n, 1), np.uint8)
+    _ref.ref_detokenize(*args, _p(out), n)
+    return out[:n].tobytes()

@@ -58,6 +58,29 @@ def test_oracle_ctc_matches_python_scan(orc):
         assert toks.tolist() == et and frs.tolist() == ef and pv == ep
 
 
+def _random_vocab(rng, n):
+    alphabet = [b"a", b"b", b"c", b" ", MARK.encode(), "é".encode(), "中".encode(), b"\xe2\x96", b"\x81"]
+    pieces = []
+    for v in range(n):
+        k = int(rng.integers(0, 6))
+        pieces.append(b"".join(alphabet[int(i)] for i in rng.integers(0, len(alphabet), size=k)))
+    return pieces
+
+
+def test_oracle_detokenize_matches_reference_build(orc):
+    """orc_detokenize against the reference's own detokenize, compiled from its sources
+    into oracle/_ref (oracle/Makefile target `ref`)."""
+    if orc.ref_detokenize(["a"], [0]) is None:
+        pytest.skip("oracle/_ref/libref_detok.so not built (the reference tree is absent)")
+    rng = np.random.default_rng(41)
+    for trial in range(20):
+        pieces = _random_vocab(rng, int(rng.integers(1, 300)))
+        n = len(pieces)
+        ids = {k: int(rng.integers(-1, n)) for k in ("blank_id", "bos_id", "eos_id", "pad_id")}
+        toks = rng.integers(-3, n + 3, size=int(rng.integers(0, 500))).astype(np.int32)
+        assert orc.detokenize(pieces, toks, **ids) == orc.ref_detokenize(pieces, toks, **ids), trial
+
+
 def test_oracle_detokenize_known_answer(orc):
     P = ["<blk>", MARK + "hel", "lo", MARK + "wor", "ld", MARK, "x" + MARK + "y", "<s>"]
     out = orc.detokenize(P, [5, 5, 1, 2, 3, 4, 0, 7, 6, 99, -3], blank_id=0, bos_id=7)
@@ -170,12 +193,7 @@ def test_ctc_greedy_device_input_and_capacity(built, orc):
 
 
 def _vocab(rng, n):
-    alphabet = [b"a", b"b", b"c", b" ", MARK.encode(), "é".encode(), "中".encode(), b"\xe2\x96", b"\x81"]
-    pieces = []
-    for v in range(n):
-        k = int(rng.integers(0, 6))
-        pieces.append(b"".join(alphabet[int(i)] for i in rng.integers(0, len(alphabet), size=k)))
-    return pieces
+    return _random_vocab(rng, n)
 
 
 @pytest.mark.gpu
@@ -196,6 +214,8 @@ def test_detokenize_matches_oracle(built, orc):
     got = voc.detokenize(lists)
     for b in range(B):
         assert got[b] == orc.detokenize(pieces, lists[b], **specials), b
+        ref = orc.ref_detokenize(pieces, lists[b], **specials)   # the reference's own build, when present
+        assert ref is None or got[b] == ref, b
     voc.close()
 
 
