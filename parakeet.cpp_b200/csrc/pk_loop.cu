@@ -1484,7 +1484,7 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
         A.rb = P.rbh;
         A.lo = H * es;
         A.kb_split = l == 0 ? (bk.K >> 5) : (H >> 5);
-        tc_gemm(P, S, bk, 0, bk.tiles, A, mbp, mbp == 2 ? kWarps : 4,
+        tc_gemm(P, S, bk, 0, bk.tiles, A, mbp, 4,
                 l == 0 ? nc * P.rbh : PR * P.rbh + nc * P.rbh);
         SUBMARK(3);
         // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
