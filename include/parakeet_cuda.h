@@ -204,6 +204,35 @@ PK_API pk_status pk_decode_batch(pk_ctx * ctx, const pk_batch * batch, pk_result
 /* Upper bound on tokens a batch can emit: sum_b n_frames[b] * max(1, max_symbols). */
 PK_API int64_t   pk_tokens_capacity(const int32_t * n_frames, int32_t B, int32_t max_symbols_per_step);
 
+/* --- input prefetch (pipelined serving) ----------------------------------- */
+
+/* No counterpart in the reference: its Engine takes one request at a time and
+ * has no device copy to overlap (include/parakeet/engine.h:35-55).
+ *
+ * Starts copying a batch's HOST encoder outputs (frames 0 .. max_b
+ * frame_offsets[b] + n_frames[b]) to the device on a copy stream of the context
+ * and returns without waiting for the copy. Prefetched copies form a queue of at
+ * most two; a third prefetch replaces the oldest. The next decode call with host
+ * input (pk_decode_batch, pk_decode_trace, pk_stream_window) whose `enc` pointer
+ * is the queue head's and whose frames the head covers uses that copy (the
+ * device waits for it) instead of copying itself; a call with any other host
+ * input empties the queue and copies as usual. Calls with device input leave
+ * the queue alone. So the copy of batch k+1 overlaps the decode of batch k:
+ *
+ *     pk_prefetch_batch(ctx, &b[0]);
+ *     for (k = 0; k < n; ++k) {
+ *         if (k + 1 < n) pk_prefetch_batch(ctx, &b[k + 1]);
+ *         pk_decode_batch(ctx, &b[k], &res[k]);
+ *     }
+ *
+ * The host buffer must stay valid and unchanged until the decode that uses its
+ * copy returns. Pinned host memory makes the copy asynchronous; pageable memory
+ * is copied before this call returns. When it returns, the copy of the prefetch
+ * two calls earlier has completed. A batch with enc_on_device = 1 is rejected
+ * (PK_ERR_INVALID). The decode's total_ms does not include a prefetched copy
+ * except for any wait for it to finish. */
+PK_API pk_status pk_prefetch_batch(pk_ctx * ctx, const pk_batch * batch);
+
 /* --- teacher-forced trace (parity harness) -------------------------------- */
 
 /* Runs the same kernel as pk_decode_batch but, when forced_token is given,

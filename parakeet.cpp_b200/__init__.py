@@ -53,6 +53,7 @@ def lib():
             "pk_get_info": ([P, P], I32), "pk_set_option": ([P, I32, I64], I32),
             "pk_last_error": ([], C.c_char_p), "pk_abi_version": ([], I32),
             "pk_decode_batch": ([P, P, P], I32), "pk_tokens_capacity": ([P, I32, I32], I64),
+            "pk_prefetch_batch": ([P, P], I32),
             "pk_decode_trace": ([P, P, P, P], I32), "pk_stream_create": ([P, P], I32),
             "pk_stream_destroy": ([P], None), "pk_stream_reset": ([P], I32),
             "pk_stream_window": ([P, P, I32, I32, I32, I32, I32, P, I32, P, P, P, I32, P], I32),
@@ -178,6 +179,20 @@ class Decoder:
         if want_finish:
             out["finish_ms"] = fin[:B].copy()
         return out
+
+    def prefetch(self, enc, offs, n_frames, d_enc: Optional[int] = None):
+        """pk_prefetch_batch: start copying host encoder outputs for the next
+        decode_batch call with the same array (see the header for the queue rules).
+        The arrays are kept alive here until two later prefetches have been made,
+        by which time their copy has completed."""
+        b, keep = self.make_batch(enc, offs, n_frames, d_enc=d_enc)
+        _check(lib().pk_prefetch_batch(self.h, C.byref(b)), "pk_prefetch_batch")
+        self._prefetched = (getattr(self, "_prefetched", ()) + (keep,))[-2:]
+        return keep[0]
+
+    def prefetch_raw(self, batch: abi.pk_batch) -> int:
+        """Direct pk_prefetch_batch call on a prepared struct (benchmarks)."""
+        return int(lib().pk_prefetch_batch(self.h, C.byref(batch)))
 
     def decode_batch_raw(self, batch: abi.pk_batch, result: abi.pk_result) -> int:
         """Direct pk_decode_batch call on prepared structs (benchmarks)."""

@@ -96,13 +96,29 @@ struct pk_ctx {
         tokregion, bnd, bndregion, frameoff, offsets, boffsets, compact, bcompact;
     DevBuf tr_logits, tr_h, tr_c, tr_tok, tr_dur, tr_ftok, tr_fdur;
     cudaEvent_t ev[6] = {};
+    // prefetched host encoder outputs: a queue of up to two staged copies made on a
+    // copy stream (pk_prefetch_batch); copy n records cev[n & 1]
+    cudaStream_t cstream = nullptr;
+    cudaEvent_t cev[2] = {};
+    uint64_t n_copies = 0;
+    DevBuf stg[2];
+    const float * stg_src[2] = {nullptr, nullptr};
+    int64_t stg_frames[2] = {0, 0};
+    uint64_t stg_seq[2] = {0, 0};   // 0: empty; else 1 + the copy's number (queue order)
+    int stg_head() const {          // oldest staged copy, or -1
+        if (!stg_seq[0] && !stg_seq[1]) return -1;
+        if (!stg_seq[0]) return 1;
+        if (!stg_seq[1]) return 0;
+        return stg_seq[0] < stg_seq[1] ? 0 : 1;
+    }
     std::vector<DevBuf *> all_bufs() {
         std::vector<DevBuf *> v = {&embed, &enc_w, &enc_b, &pred_w, &pred_b, &out_w, &out_b,
                                    &durations, &special, &enc, &encp, &h, &c, &predp, &hid, &ust,
                                    &keys, &live, &emit, &ctl, &bar, &tstart, &finish, &tok,
                                    &tokregion, &bnd, &bndregion, &frameoff, &offsets, &boffsets,
                                    &compact, &bcompact, &tr_logits, &tr_h, &tr_c, &tr_tok, &tr_dur,
-                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &hst, &xnew, &hidc, &ep_w16, &ep_err};
+                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &hst, &xnew, &hidc, &ep_w16, &ep_err,
+                                   &stg[0], &stg[1]};
         for (int i = 0; i < 2 + pk::kMaxLayers; ++i) { v.push_back(&tc_frag[i]); v.push_back(&tc_scale[i]); }
         for (int l = 0; l < pk::kMaxLayers; ++l) {
             v.push_back(&w_ih[l]); v.push_back(&w_hh[l]); v.push_back(&b_ih[l]); v.push_back(&b_hh[l]);
@@ -527,9 +543,19 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(cudaEventRecord(x->ev[0], s));
     const float * encsrc = r.enc;
     if (frames > 0 && !r.enc_dev) {
-        PK_CK(x->enc.ensure((size_t) frames * x->De * 4));
-        PK_CK(cudaMemcpyAsync(x->enc.p, r.enc, (size_t) frames * x->De * 4, cudaMemcpyHostToDevice, s));
-        encsrc = x->enc.as<float>();
+        const int q = x->stg_head();
+        if (q >= 0 && x->stg_src[q] == r.enc && x->stg_frames[q] >= frames) {
+            // the queue head is this input, prefetched: wait for its copy on the device
+            PK_CK(cudaStreamWaitEvent(s, x->cev[(x->stg_seq[q] - 1) & 1], 0));
+            encsrc = x->stg[q].as<float>();
+            x->stg_seq[q] = 0;
+        } else {
+            // other host input: prefetched copies are out of order with the calls, drop them
+            x->stg_seq[0] = x->stg_seq[1] = 0;
+            PK_CK(x->enc.ensure((size_t) frames * x->De * 4));
+            PK_CK(cudaMemcpyAsync(x->enc.p, r.enc, (size_t) frames * x->De * 4, cudaMemcpyHostToDevice, s));
+            encsrc = x->enc.as<float>();
+        }
     }
     PK_CK(cudaEventRecord(x->ev[1], s));
     const bool ep_tc = use_tc && x->ep_ok && (reinterpret_cast<uintptr_t>(encsrc) & 15u) == 0;
@@ -933,10 +959,14 @@ void pk_destroy(pk_ctx * x) {
     if (!x) return;
     cudaSetDevice(x->device);
     if (x->stream) cudaStreamSynchronize(x->stream);
+    if (x->cstream) cudaStreamSynchronize(x->cstream);
     for (DevBuf * b : x->all_bufs()) b->release();
     for (auto & e : x->ev)
         if (e) cudaEventDestroy(e);
+    for (auto & e : x->cev)
+        if (e) cudaEventDestroy(e);
     if (x->stream) cudaStreamDestroy(x->stream);
+    if (x->cstream) cudaStreamDestroy(x->cstream);
     delete x;
 }
 
@@ -984,6 +1014,51 @@ int64_t pk_tokens_capacity(const int32_t * n_frames, int32_t B, int32_t msym) {
 
 pk_status pk_decode_batch(pk_ctx * x, const pk_batch * b, pk_result * res) {
     return batch_run(x, b, nullptr, res);
+}
+
+pk_status pk_prefetch_batch(pk_ctx * x, const pk_batch * b) {
+    if (!x || !b) return fail(PK_ERR_INVALID, "null argument");
+    if (b->enc_on_device) return fail(PK_ERR_INVALID, "prefetch takes host encoder outputs");
+    if (b->d_enc != x->De)
+        return fail(PK_ERR_DMODEL, "encoder d_model mismatch (%d vs %d)", b->d_enc, x->De);
+    if (b->B < 0) return fail(PK_ERR_INVALID, "B < 0");
+    if (b->B > 0 && (!b->frame_offsets || !b->n_frames)) return fail(PK_ERR_INVALID, "null offsets");
+    int64_t frames = 0;
+    for (int i = 0; i < b->B; ++i) {
+        if (b->n_frames[i] < 0) return fail(PK_ERR_INVALID, "n_frames[%d] < 0", i);
+        if (b->n_frames[i] > 0) {
+            if (b->frame_offsets[i] < 0) return fail(PK_ERR_INVALID, "frame_offsets[%d] < 0", i);
+            frames = std::max<int64_t>(frames, b->frame_offsets[i] + b->n_frames[i]);
+        }
+    }
+    if (frames == 0) return PK_OK;            // nothing the decode would copy
+    if (!b->enc) return fail(PK_ERR_INVALID, "null encoder output");
+    PK_CK(cudaSetDevice(x->device));
+    if (!x->cstream) {
+        PK_CK(cudaStreamCreateWithFlags(&x->cstream, cudaStreamNonBlocking));
+        for (auto & e : x->cev) PK_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    // copy n reuses copy n-2's event: wait for that copy (so its host buffer and,
+    // if it was never used, its slot are free), which also bounds the copies in flight.
+    // The compute stream is idle between calls (every call synchronises it); waiting
+    // for it covers work a failed call left behind that may still read a slot.
+    const uint64_t n = x->n_copies;
+    PK_CK(cudaEventSynchronize(x->cev[n & 1]));
+    PK_CK(cudaStreamSynchronize(x->stream));
+    const int q = !x->stg_seq[0] ? 0 : !x->stg_seq[1] ? 1 : (x->stg_seq[0] < x->stg_seq[1] ? 0 : 1);
+    x->stg_seq[q] = 0;
+    const size_t bytes = (size_t) frames * x->De * 4;
+    if (x->stg[q].cap < bytes) {
+        PK_CK(cudaStreamSynchronize(x->cstream));   // the other slot's copy may still read into its buffer
+        PK_CK(x->stg[q].ensure(bytes));
+    }
+    PK_CK(cudaMemcpyAsync(x->stg[q].p, b->enc, bytes, cudaMemcpyHostToDevice, x->cstream));
+    PK_CK(cudaEventRecord(x->cev[n & 1], x->cstream));
+    x->n_copies = n + 1;
+    x->stg_src[q] = b->enc;
+    x->stg_frames[q] = frames;
+    x->stg_seq[q] = n + 1;
+    return PK_OK;
 }
 
 pk_status pk_decode_trace(pk_ctx * x, const pk_batch * b, pk_trace * t, pk_result * res) {

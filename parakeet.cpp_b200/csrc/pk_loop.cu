@@ -70,10 +70,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned * p) {
     return v;
 }
 
-__device__ __forceinline__ void st_release(unsigned * p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long * p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
