@@ -888,6 +888,12 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
         return cleanup(fail(PK_ERR_CUDA, "stream creation failed"));
     for (auto & e : x->ev)
         if (cudaEventCreate(&e) != cudaSuccess) return cleanup(fail(PK_ERR_CUDA, "event creation failed"));
+    // the copy stream of pk_prefetch_batch (created here so that no prefetch pays for it)
+    if (cudaStreamCreateWithFlags(&x->cstream, cudaStreamNonBlocking) != cudaSuccess)
+        return cleanup(fail(PK_ERR_CUDA, "stream creation failed"));
+    for (auto & e : x->cev)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+            return cleanup(fail(PK_ERR_CUDA, "event creation failed"));
     DevBuf scratch;
     pk_status st = PK_OK;
     auto up = [&](const pk_tensor & t, int64_t keep, DevBuf & dst, const char * name) {
@@ -1034,10 +1040,6 @@ pk_status pk_prefetch_batch(pk_ctx * x, const pk_batch * b) {
     if (frames == 0) return PK_OK;            // nothing the decode would copy
     if (!b->enc) return fail(PK_ERR_INVALID, "null encoder output");
     PK_CK(cudaSetDevice(x->device));
-    if (!x->cstream) {
-        PK_CK(cudaStreamCreateWithFlags(&x->cstream, cudaStreamNonBlocking));
-        for (auto & e : x->cev) PK_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    }
     // copy n reuses copy n-2's event: wait for that copy (so its host buffer and,
     // if it was never used, its slot are free), which also bounds the copies in flight.
     // The compute stream is idle between calls (every call synchronises it); waiting
