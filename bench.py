@@ -14,7 +14,7 @@ enc-proj GEMM, the persistent step-loop kernel, token compaction.
           previous step decodes; time = host wall clock around the K calls.
           e2e.serial: one call at a time, its copies inside the call.
 
-Default workload (N=1): BASELINE config 2, TDT-0.6b-v3 q8_0, B=64,
+Default workload (N=1): benchmark configuration 2, TDT-0.6b-v3 q8_0, B=64,
 T ~ U[60, 1875]. For N>1 (torchrun, one rank per GPU) each rank decodes its LPT
 shard of a global batch of B*N utterances (weak scaling, no collective on the
 decode path).
