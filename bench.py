@@ -14,14 +14,17 @@ enc-proj GEMM, the persistent step-loop kernel, token compaction.
           previous step decodes; time = host wall clock around the K calls.
           e2e.serial: one call at a time, its copies inside the call.
 
-Default workload (N=1): benchmark configuration 2, TDT-0.6b-v3 q8_0, B=64,
-T ~ U[60, 1875]. For N>1 (torchrun, one rank per GPU) each rank decodes its LPT
-shard of a global batch of B*N utterances (weak scaling, no collective on the
-decode path).
+Default workload: benchmark configuration 5, TDT-0.6b-v3 q8_0, a global batch of
+4096 utterances with log-normal lengths (median 250 frames, sigma 0.8, clipped to
+[25, 3750]), blank bias +2. With N GPUs (torchrun, one rank per GPU) each rank
+decodes its LPT shard of the same 4096 utterances (strong scaling: N = 8 is the
+stated 4096-over-8 case; no collective on the decode path). Configurations 1-4
+keep their per-GPU batch (weak scaling).
 
---impl reference times the reference's CPU decoder (the oracle port of
-src/parakeet_tdt.cpp / src/parakeet_eou.cpp; the reference itself cannot be
-built here: it needs the un-vendored ggml) on all host cores.
+--impl reference times the reference's own CPU decoder (src/parakeet_tdt.cpp /
+src/parakeet_eou.cpp compiled unchanged into oracle/_ref/libref_decoder.so
+against a host-only ggml stand-in; the oracle restatement when that library is
+absent) on all host cores.
 """
 import argparse
 import importlib.util
@@ -49,10 +52,18 @@ CONFIGS = {
               desc="EOU-120m f16, B=256, T=50"),
     "4": dict(model="tdt_1_1b", wtype="q8_0", B=1024, lengths=("const", 750), blank_bias=2.0,
               desc="TDT-1.1b, B=1024, T=750"),
-    "5": dict(model="tdt_0_6b", wtype="q8_0", B=512, lengths=("lognormal",), blank_bias=2.0,
-              desc="TDT-0.6b-v3 q8_0, 512 per GPU (4096 over 8), T lognormal(250, 0.8) in [25, 3750]"),
+    "5": dict(model="tdt_0_6b", wtype="q8_0", B=4096, lengths=("lognormal",), blank_bias=2.0, global_batch=True,
+              desc="TDT-0.6b-v3 q8_0, global batch 4096 split over the GPUs, T lognormal(250, 0.8) in [25, 3750]"),
 }
+DEFAULT_CONFIG = "5"
 METRIC = "tdt_greedy_decode_tokens_per_sec"
+# What the default (tensor-core) step loop computes in, by weight type: exact weights,
+# h as int16 fixed point in two int8 digits for the q8_0 LSTM / pred-proj (int8 MMA,
+# int32 per 32-wide block, f32 block scale), the joint hidden layer as f16 hi + lo
+# (22 significant bits) against exact f16 weights, f32 accumulation and state.
+DTYPE = {"q8_0": "q8_0 weights; int16 fixed-point h (int8 MMA) in LSTM/pred-proj; f16 hi+lo joint; f32 accumulate",
+         "f16": "f16 weights; f16 hi+lo activations; f32 accumulate",
+         "f32": "f32"}
 
 
 def load(name, path, pkg_dir=None):
@@ -224,10 +235,11 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
     ap.add_argument("--wtype", default=None)
     ap.add_argument("--blank-bias", type=float, default=None)
-    ap.add_argument("--batch", type=int, default=None, help="override utterances per GPU")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the batch (global for configuration 5, per GPU otherwise)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--path", default="tdt", choices=["tdt", "ctc"],
@@ -248,16 +260,25 @@ def main():
 
     pk = pkg()
     model = make_model(pk, cfg, wtype, blank_bias)
-    B_total = B * world
+    strong = bool(cfg.get("global_batch"))
+    B_total = B if strong else B * world
     T_all = global_lengths(pk, cfg, B_total)
     idx = pk.multi.shard_indices(T_all, world)[rank] if world > 1 else np.arange(B_total)
+    if args.impl == "reference":
+        # the CPU arm decodes a bounded sample: the rank's first utterances, one per host thread
+        idx = idx[:host_cores()]
     T = T_all[idx].astype(np.int32)
-    enc, offs = pk.synth.encoder_batch(T, model.d_enc, seed=99 + rank)
+    if strong:
+        # every utterance has the same frames whichever rank decodes it
+        enc, offs = pk.synth.encoder_pooled(T, idx, model.d_enc, seed=99)
+    else:
+        enc, offs = pk.synth.encoder_batch(T, model.d_enc, seed=99 + rank)
     config = {"workload": cfg["desc"] + (f" (wtype {wtype})" if wtype != cfg["wtype"] else ""),
               "config": args.config, "utterances_per_gpu": int(len(T)), "global_batch": int(B_total),
-              "frames_per_gpu": int(T.sum()), "blank_bias": blank_bias,
+              "frames_per_gpu": int(T.sum()), "frames_global": int(T_all.sum()), "blank_bias": blank_bias,
               "l2": f"inputs {enc.nbytes / 1e6:.0f} MB of encoder output per step (L2 is 126 MB)",
               "parallelism": f"utterance shards x{world}" if world > 1 else "single GPU"}
+    args.scaling = "strong" if strong else "weak"
 
     if args.impl == "reference":
         return run_reference(args, model, enc, offs, T, config, rank)
@@ -347,11 +368,31 @@ def run_ctc(args):
     return 0
 
 
+def cpu_model():
+    """Host CPU model name (lscpu), or None."""
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for ln in out.splitlines():
+            if ln.startswith("Model name:"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return None
+
+
+def reference_decoder(model):
+    """The reference's own CPU decoder (oracle/_ref/libref_decoder.so, built from the
+    reference's sources) when present, else the oracle restatement: (decoder, kind)."""
+    orc = oracle_mod()
+    if orc.ref_decoder_available():
+        return orc.Reference(model), "reference"
+    return orc.Oracle(model), "port"
+
+
 def run_reference(args, model, enc, offs, T, config, rank):
     if rank != 0:
         return 0
-    orc = oracle_mod()
-    o = orc.Oracle(model)
+    o, kind = reference_decoder(model)
     threads = host_cores()
     budget = max(1.0, 150.0 / max(1, args.steps + min(args.warmup, 1)))
     for _ in range(min(args.warmup, 1)):
@@ -365,17 +406,20 @@ def run_reference(args, model, enc, offs, T, config, rank):
         steps += last["steps"]
         wall += last["wall_s"]
     v = toks / wall if wall > 0 else 0.0
+    what = ("the reference's tdt_greedy_decode / eou_greedy_decode (src/parakeet_tdt.cpp, src/parakeet_eou.cpp "
+            "built unchanged with -O3 -ffast-math -funroll-loops)" if kind == "reference" else
+            "the oracle restatement of the reference's CPU decoder")
     sample = (f"first {last['n_utt']} utterances of the batch, each truncated to {last['cap']} "
-              f"frames ({last['frames']} frames), one utterance per thread")
+              f"frames ({last['frames']} frames), one utterance per thread, {what}")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "runs_on": "host CPU cores (rank 0)",
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / max(1, args.steps),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-init weights, N(0,1) encoder outputs)", "config": config,
         "steps_per_sec": steps / wall if wall > 0 else 0.0,
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "cpu_model": cpu_model(), "sample": sample},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
     return 0
@@ -525,7 +569,7 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": DTYPE[wtype],
             "data": "synthetic (seeded random-init weights of the named geometry, N(0,1) encoder outputs)",
             "config": config,
             "steps_per_sec": steps_all / (tot_ms / 1e3) if tot_ms > 0 else 0.0,
@@ -561,12 +605,12 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
                                  f"peak {peak_kind}"},
         }
     if world == 1 and not args.no_cpu_baseline and rank == 0:
-        orc = oracle_mod()
-        o = orc.Oracle(model)
+        o, kind = reference_decoder(model)
         threads = host_cores()
         cs = cpu_sample_run(o, enc, offs, T, threads, args.cpu_budget_s)
         result["cpu_baseline"] = {
-            "value": cs["tokens"] / cs["wall_s"], "unit": "tokens/s", "cores": threads, "kind": "port",
+            "value": cs["tokens"] / cs["wall_s"], "unit": "tokens/s", "cores": threads, "kind": kind,
+            "cpu_model": cpu_model(),
             "sample": f"first {cs['n_utt']} utterances of the batch truncated to {cs['cap']} frames "
                       f"({cs['frames']} frames, {cs['tokens']} tokens, {cs['wall_s']:.1f} s wall), "
                       f"one utterance per thread, -O3 -ffast-math -funroll-loops",

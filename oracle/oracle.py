@@ -249,3 +249,148 @@ def ref_detokenize(pieces, tokens, blank_id=-1, bos_id=-1, eos_id=-1, pad_id=-1)
     out = np.zeros(max(n, 1), np.uint8)
     _ref.ref_detokenize(*args, _p(out), n)
     return out[:n].tobytes()
+
+
+# ---- the reference's own decoder (src/parakeet_tdt.cpp, src/parakeet_eou.cpp) ----
+#
+# Built by `make ref` from the reference's sources, unchanged, against the
+# host-only ggml stand-in in oracle/ggml_host/ (oracle/_ref/libref_decoder.so).
+
+REF_DECODER_PATH = os.path.join(HERE, "_ref", "libref_decoder.so")
+_refdec = None
+
+
+def ref_decoder_available() -> bool:
+    return os.path.exists(REF_DECODER_PATH)
+
+
+def _ref_lib():
+    global _refdec
+    if _refdec is None:
+        if not os.path.exists(REF_DECODER_PATH):
+            raise FileNotFoundError(REF_DECODER_PATH + " (make -C oracle ref with PARAKEET_REFERENCE_DIR set)")
+        L = C.CDLL(REF_DECODER_PATH)
+        P, I32 = C.c_void_p, C.c_int32
+        L.ref_create.restype = P
+        L.ref_create.argtypes = [P, C.c_char_p, I32]
+        L.ref_destroy.argtypes = [P]
+        L.ref_state_new.restype = P
+        L.ref_state_new.argtypes = []
+        L.ref_state_free.argtypes = [P]
+        L.ref_state_get.argtypes = [P, P, P, P, P, P]
+        L.ref_decode_window.restype = I32
+        L.ref_decode_window.argtypes = [P, P, P, I32, I32, I32, P, I32, P, P, P, I32, P]
+        L.ref_decode_batch.restype = C.c_double
+        L.ref_decode_batch.argtypes = [P, P, P, P, I32, I32, I32, P, P, P, P, P, P, P, P]
+        _refdec = L
+    return _refdec
+
+
+class RefState:
+    """A TdtDecodeState / EouDecodeState of the reference (default-constructed:
+    uninitialised, so its first window runs tdt_init_state / eou_init_state)."""
+
+    def __init__(self, ref):
+        self.ref = ref
+        self.h = C.c_void_p(_ref_lib().ref_state_new())
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None):
+                _ref_lib().ref_state_free(self.h)
+        except Exception:
+            pass
+
+    def get(self):
+        r = self.ref
+        h = np.zeros((r.L, r.H), np.float32)
+        c = np.zeros((r.L, r.H), np.float32)
+        p = np.zeros(r.H, np.float32)
+        ints = np.zeros(5, np.int32)
+        _ref_lib().ref_state_get(r.h, self.h, _p(h), _p(c), _p(p), _p(ints))
+        return {"h": h, "c": c, "pred": p, "symbols_this_step": int(ints[0]), "initialized": int(ints[1]),
+                "carry_frames": int(ints[2]), "last_token": int(ints[3]), "segment_start_token": int(ints[4])}
+
+
+class Reference:
+    """The reference's own CPU decoder for one synthetic model (same interface as
+    Oracle.decode_window / decode_batch, without traces: the reference exposes
+    no per-step logits, only its decoder state between windows)."""
+
+    def __init__(self, model, desc=None):
+        self.model = model
+        self._desc = desc if desc is not None else _abi().ModelDesc(model)
+        err = C.create_string_buffer(256)
+        h = _ref_lib().ref_create(self._desc.ref(), err, 256)
+        if not h:
+            raise RuntimeError("ref_create: " + err.value.decode())
+        self.h = C.c_void_p(h)
+        self.is_tdt = model.model_type == "tdt"
+        self.H = model.pred_hidden
+        self.L = model.n_layers
+        self.De = model.d_enc
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None):
+                _ref_lib().ref_destroy(self.h)
+        except Exception:
+            pass
+
+    def new_state(self) -> RefState:
+        return RefState(self)
+
+    def decode_window(self, enc: np.ndarray, st: Optional[RefState] = None, max_symbols: Optional[int] = None,
+                      tokens_before: Optional[np.ndarray] = None, d_enc: Optional[int] = None):
+        """One tdt_decode_window / eou_decode_window. `tokens_before` is the running
+        out_tokens list the reference appends to (EOU boundaries count it)."""
+        if st is None:
+            st = self.new_state()
+        enc = np.ascontiguousarray(enc, np.float32)
+        T = int(enc.shape[0]) if enc.ndim == 2 else 0
+        msym = self.model.max_symbols_per_step if max_symbols is None else max_symbols
+        before = np.zeros(0, np.int32) if tokens_before is None else np.asarray(tokens_before, np.int32)
+        n0 = len(before)
+        cap = max(1, T * max(1, msym)) + n0
+        toks = np.zeros(cap, np.int32)
+        toks[:n0] = before
+        bounds = np.zeros(max(1, T), np.int32)
+        nt, nb, steps = C.c_int32(n0), C.c_int32(0), C.c_int32(0)
+        rc = _ref_lib().ref_decode_window(self.h, st.h, _p(enc), T, self.De if d_enc is None else d_enc, msym,
+                                          _p(toks), cap, C.byref(nt), C.byref(steps), _p(bounds), len(bounds),
+                                          C.byref(nb))
+        return {"rc": int(rc), "tokens": toks[n0:nt.value].copy(), "steps": int(steps.value),
+                "bounds": bounds[:nb.value].copy(), "state": st}
+
+    def decode_batch(self, enc: np.ndarray, offs: np.ndarray, n_frames: np.ndarray,
+                     n_threads: int = 0, max_symbols: Optional[int] = None):
+        """tdt_greedy_decode / eou_greedy_decode of a ragged batch on host threads."""
+        n_frames = np.ascontiguousarray(n_frames, np.int32)
+        offs = np.ascontiguousarray(offs, np.int64)
+        B = len(n_frames)
+        msym = self.model.max_symbols_per_step if max_symbols is None else max_symbols
+        region = np.zeros(B, np.int64)
+        if B > 1:
+            region[1:] = np.cumsum(n_frames.astype(np.int64) * max(1, msym))[:-1]
+        cap = int(n_frames.astype(np.int64).sum() * max(1, msym)) + 1
+        toks = np.zeros(cap, np.int32)
+        ntok = np.zeros(B, np.int32)
+        steps = np.zeros(B, np.int32)
+        ms = np.zeros(B, np.float64)
+        bounds = nb = bregion = None
+        if not self.is_tdt:
+            bregion = np.zeros(B, np.int64)
+            if B > 1:
+                bregion[1:] = np.cumsum(n_frames.astype(np.int64))[:-1]
+            bounds = np.zeros(int(n_frames.astype(np.int64).sum()) + 1, np.int32)
+            nb = np.zeros(B, np.int32)
+        wall = _ref_lib().ref_decode_batch(self.h, _p(np.ascontiguousarray(enc, np.float32)), _p(offs),
+                                           _p(n_frames), B, msym, n_threads, _p(toks), _p(region),
+                                           _p(ntok), _p(steps), _p(bounds), _p(bregion), _p(nb), _p(ms))
+        if wall < 0:
+            raise RuntimeError("ref_decode_batch failed")
+        tokens = [toks[region[b]:region[b] + ntok[b]].copy() for b in range(B)]
+        res = {"tokens": tokens, "steps": steps, "ms": ms, "wall_ms": wall}
+        if not self.is_tdt:
+            res["bounds"] = [bounds[bregion[b]:bregion[b] + nb[b]].copy() for b in range(B)]
+        return res
