@@ -20,6 +20,7 @@
 #include "ggml-backend.h"
 
 #include "parakeet_cuda.h"
+#include "ref_model.hpp"
 
 #include <algorithm>
 #include <atomic>
@@ -49,41 +50,9 @@ void log_impl(enum ggml_log_level, const char * fmt, ...) {
 }
 }  // namespace parakeet
 
-namespace {
-
-struct Blob {
-    ggml_tensor t{};
-    std::vector<uint8_t> bytes;
-};
-
-}  // namespace
-
-struct ref_model {
-    parakeet::ParakeetCtcModel model;
-    std::vector<std::unique_ptr<Blob>> blobs;
+struct ref_model : refmodel::Model {
     parakeet::TdtRuntimeWeights tdt;
     parakeet::EouRuntimeWeights eou;
-    bool is_tdt = true;
-    int max_symbols = 10;
-
-    ggml_tensor * tensor(const pk_tensor & src) {
-        if (!src.data) return nullptr;
-        auto b = std::make_unique<Blob>();
-        b->bytes.assign(static_cast<const uint8_t *>(src.data), static_cast<const uint8_t *>(src.data) + src.nbytes);
-        ggml_tensor & t = b->t;
-        t.type = (ggml_type) src.type;
-        t.ne[0] = src.ne0;
-        t.ne[1] = src.ne1 > 0 ? src.ne1 : 1;
-        t.ne[2] = t.ne[3] = 1;
-        const ggml_type_traits * tr = ggml_get_type_traits(t.type);
-        t.nb[0] = tr ? tr->type_size : 0;
-        t.nb[1] = tr ? (size_t) (t.ne[0] / tr->blck_size) * tr->type_size : 0;
-        t.nb[2] = t.nb[1] * (size_t) t.ne[1];
-        t.nb[3] = t.nb[2];
-        t.data = b->bytes.data();
-        blobs.push_back(std::move(b));
-        return &blobs.back()->t;
-    }
 };
 
 struct ref_state {
@@ -100,64 +69,14 @@ ref_model * ref_create(const pk_model_desc * d, char * err, int32_t errlen) {
     };
     if (!d) return fail("null descriptor");
     auto m = std::make_unique<ref_model>();
+    m->fill(*d);
     parakeet::ParakeetCtcModel & M = m->model;
-    m->is_tdt = d->model_type == PK_MODEL_TDT;
-    M.model_type = m->is_tdt ? parakeet::ParakeetModelType::TDT : parakeet::ParakeetModelType::EOU;
-    M.encoder_cfg.d_model = d->d_enc;
-    M.vocab_size = d->vocab_size;
-    M.blank_id = d->blank_id;
-    M.eou_id = d->eou_id;
-    M.eob_id = d->eob_id;
-    // Tokenizer pieces only matter for the EOU "<...>" skip rule (parakeet_eou.cpp:315-319)
-    // and detokenize; the descriptor carries which pieces are special.
-    M.vocab.pieces.resize((size_t) std::max(0, d->n_vocab_pieces));
-    for (int32_t i = 0; i < d->n_vocab_pieces; ++i)
-        M.vocab.pieces[(size_t) i] = (d->special_piece && d->special_piece[i]) ? "<s" + std::to_string(i) + ">"
-                                                                               : "p" + std::to_string(i);
-    M.vocab.blank_id = d->blank_id;
-    std::vector<parakeet::TdtLstmLayer> lstm((size_t) std::max(0, d->n_layers));
-    for (int32_t l = 0; l < d->n_layers; ++l) {
-        lstm[(size_t) l].w_ih = m->tensor(d->lstm[l].w_ih);
-        lstm[(size_t) l].w_hh = m->tensor(d->lstm[l].w_hh);
-        lstm[(size_t) l].b_ih = m->tensor(d->lstm[l].b_ih);
-        lstm[(size_t) l].b_hh = m->tensor(d->lstm[l].b_hh);
-    }
-    m->max_symbols = d->max_symbols_per_step;
     try {
         if (m->is_tdt) {
-            M.encoder_cfg.tdt_pred_hidden = d->pred_hidden;
-            M.encoder_cfg.tdt_joint_hidden = d->joint_hidden;
-            M.encoder_cfg.tdt_pred_rnn_layers = d->n_layers;
-            M.encoder_cfg.tdt_num_durations = d->num_durations;
-            M.tdt_durations.assign(d->durations, d->durations + d->num_durations);
-            auto & w = M.tdt;
-            w.predict_embed = m->tensor(d->embed);
-            w.lstm = lstm;
-            w.joint_enc_w = m->tensor(d->joint_enc_w);
-            w.joint_enc_b = m->tensor(d->joint_enc_b);
-            w.joint_pred_w = m->tensor(d->joint_pred_w);
-            w.joint_pred_b = m->tensor(d->joint_pred_b);
-            w.joint_out_w = m->tensor(d->joint_out_w);
-            w.joint_out_b = m->tensor(d->joint_out_b);
-            const int rc = parakeet::tdt_prepare_runtime(M, m->tdt);
-            if (rc != 0) return fail("tdt_prepare_runtime failed");
+            if (parakeet::tdt_prepare_runtime(M, m->tdt) != 0) return fail("tdt_prepare_runtime failed");
             if (m->tdt.use_graphs) return fail("tdt_prepare_runtime chose the graph branch");
         } else {
-            M.encoder_cfg.eou_pred_hidden = d->pred_hidden;
-            M.encoder_cfg.eou_joint_hidden = d->joint_hidden;
-            M.encoder_cfg.eou_pred_rnn_layers = d->n_layers;
-            M.encoder_cfg.eou_max_symbols_per_step = d->max_symbols_per_step;
-            auto & w = M.eou;
-            w.predict_embed = m->tensor(d->embed);
-            w.lstm = lstm;
-            w.joint_enc_w = m->tensor(d->joint_enc_w);
-            w.joint_enc_b = m->tensor(d->joint_enc_b);
-            w.joint_pred_w = m->tensor(d->joint_pred_w);
-            w.joint_pred_b = m->tensor(d->joint_pred_b);
-            w.joint_out_w = m->tensor(d->joint_out_w);
-            w.joint_out_b = m->tensor(d->joint_out_b);
-            const int rc = parakeet::eou_prepare_runtime(M, m->eou);
-            if (rc != 0) return fail("eou_prepare_runtime failed");
+            if (parakeet::eou_prepare_runtime(M, m->eou) != 0) return fail("eou_prepare_runtime failed");
         }
     } catch (const std::exception & e) {
         return fail(e.what());
