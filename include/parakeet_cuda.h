@@ -125,9 +125,13 @@ enum {
     PK_OPT_TIMEOUT_US  = 1,  /* bound (microseconds) on every device-side grid-barrier wait */
     PK_OPT_MATH        = 2,  /* PK_MATH_* */
     PK_OPT_MAX_SYMBOLS = 3,  /* default max_symbols_per_step override (> 0) */
-    PK_OPT_TEST_STALL  = 4   /* test hook: 1 = CTA 0 of the next step loop never arrives at its first
+    PK_OPT_TEST_STALL  = 4,  /* test hook: 1 = CTA 0 of the next step loop never arrives at its first
                                 grid barrier, so the other CTAs' bounded waits run out and the call
                                 returns PK_ERR_TIMEOUT (exercises failure detection without a fault) */
+    PK_OPT_BULK_MIN_LIVE = 5 /* tensor-core math: iterations with at least this many live utterances run
+                                on the tcgen05 bulk loop (two-dimensional tiles, accumulators in tensor
+                                memory), the rest on the persistent loop; default 256, 0 = never,
+                                1 = every iteration of a fresh batch (trace runs too) */
 };
 
 /* Static information about a context. */
@@ -192,8 +196,10 @@ typedef struct pk_result {
                                      [2i+1] = the rest of the segment (waiting for the slowest CTA
                                      and the grid barrier) */
     double    encproj_ms;         /* device time of the enc-proj GEMM (CUDA events) */
-    double    loop_ms;            /* device time of the persistent step loop */
+    double    loop_ms;            /* device time of the step loop (bulk and persistent loops together) */
     double    total_ms;           /* device time of the whole call incl. copies */
+    double    bulk_ms;            /* device time of the tcgen05 bulk loop (PK_OPT_BULK_MIN_LIVE), 0 if it did not run */
+    int64_t   bulk_iterations;    /* loop iterations that ran on the bulk loop (included in loop_iterations) */
 } pk_result;
 
 /* Greedy decode of B fresh utterances (each starts from tdt_init_state /

@@ -98,8 +98,10 @@ class Decoder:
     """A libparakeet_cuda context holding one repacked decoder on one device."""
 
     def __init__(self, model, device: int = 0, desc: Optional[abi.ModelDesc] = None,
-                 math: Optional[str] = None):
-        """math: None (library default: tensor cores when the weights allow), "tc" or "f32"."""
+                 math: Optional[str] = None, bulk_min_live: Optional[int] = None):
+        """math: None (library default: tensor cores when the weights allow), "tc" or "f32".
+        bulk_min_live: PK_OPT_BULK_MIN_LIVE (None: the library default; 0 never runs the
+        tcgen05 bulk loop, 1 runs it for every iteration of a fresh batch)."""
         self.model = model
         self._desc = desc if desc is not None else abi.ModelDesc(model)
         h = C.c_void_p()
@@ -110,6 +112,8 @@ class Decoder:
         self.info = info
         if math is not None:
             self.set_option(abi.PK_OPT_MATH, {"tc": abi.PK_MATH_TC, "f32": abi.PK_MATH_F32}[math])
+        if bulk_min_live is not None:
+            self.set_option(abi.PK_OPT_BULK_MIN_LIVE, int(bulk_min_live))
 
     def close(self):
         if getattr(self, "h", None) is not None and self.h.value:
@@ -173,7 +177,8 @@ class Decoder:
         out = {"tokens": [toks[offs_out[i]:offs_out[i + 1]].copy() for i in range(B)],
                "steps": steps[:B].copy(), "total_steps": int(r.total_steps),
                "loop_iterations": int(r.loop_iterations), "encproj_ms": r.encproj_ms,
-               "loop_ms": r.loop_ms, "total_ms": r.total_ms, "tokens_needed": int(r.tokens_needed)}
+               "loop_ms": r.loop_ms, "total_ms": r.total_ms, "tokens_needed": int(r.tokens_needed),
+               "bulk_ms": r.bulk_ms, "bulk_iterations": int(r.bulk_iterations)}
         if bounds is not None:
             out["bounds"] = [bounds[boffs[i]:boffs[i + 1]].copy() for i in range(B)]
         if want_finish:

@@ -9,7 +9,7 @@ import numpy as np
 PK_OK, PK_ERR_DMODEL, PK_ERR_INVALID, PK_ERR_MODEL, PK_ERR_CUDA = 0, 1, 2, 3, 4
 PK_ERR_OOM, PK_ERR_TIMEOUT, PK_ERR_CAPACITY, PK_ERR_NO_DEVICE, PK_ERR_DEVICE = 5, 6, 7, 8, 9
 PK_MODEL_TDT, PK_MODEL_EOU = 1, 2
-PK_OPT_TIMEOUT_US, PK_OPT_MATH, PK_OPT_MAX_SYMBOLS, PK_OPT_TEST_STALL = 1, 2, 3, 4
+PK_OPT_TIMEOUT_US, PK_OPT_MATH, PK_OPT_MAX_SYMBOLS, PK_OPT_TEST_STALL, PK_OPT_BULK_MIN_LIVE = 1, 2, 3, 4, 5
 PK_MATH_F32, PK_MATH_TC = 0, 1
 
 STATUS_NAMES = {0: "PK_OK", 1: "PK_ERR_DMODEL", 2: "PK_ERR_INVALID", 3: "PK_ERR_MODEL",
@@ -62,7 +62,8 @@ class pk_result(C.Structure):
                 ("total_steps", C.c_int64), ("loop_iterations", C.c_int64),
                 ("emit_iterations", C.c_int64), ("kernel_launches", C.c_int64),
                 ("phase_ms", C.c_double * 8),
-                ("encproj_ms", C.c_double), ("loop_ms", C.c_double), ("total_ms", C.c_double)]
+                ("encproj_ms", C.c_double), ("loop_ms", C.c_double), ("total_ms", C.c_double),
+                ("bulk_ms", C.c_double), ("bulk_iterations", C.c_int64)]
 
 
 class pk_trace(C.Structure):

@@ -89,13 +89,18 @@ struct pk_ctx {
     // weights (f32 on the device)
     DevBuf embed, w_ih[pk::kMaxLayers], w_hh[pk::kMaxLayers], b_ih[pk::kMaxLayers],
         b_hh[pk::kMaxLayers], enc_w, enc_b, pred_w, pred_b, out_w, out_b, durations, special;
+    // bulk loop (tcgen05, many live utterances): weights, threshold, per-call buffers
+    pk::BulkWeights bulk{};
+    int bulk_ok = 0;
+    int bulk_min_live = 256;
+    DevBuf h16, x16, dcount;
     // per-call workspace
     DevBuf prof;
     DevBuf livef, hst, xnew, hidc;
     DevBuf enc, encp, h, c, predp, hid, ust, keys, live, emit, ctl, bar, tstart, finish, tok,
         tokregion, bnd, bndregion, frameoff, offsets, boffsets, compact, bcompact;
     DevBuf tr_logits, tr_h, tr_c, tr_tok, tr_dur, tr_ftok, tr_fdur;
-    cudaEvent_t ev[6] = {};
+    cudaEvent_t ev[7] = {};
     // prefetched host encoder outputs: a queue of up to two staged copies made on a
     // copy stream (pk_prefetch_batch); copy n records cev[n & 1]
     cudaStream_t cstream = nullptr;
@@ -117,7 +122,7 @@ struct pk_ctx {
                                    &keys, &live, &emit, &ctl, &bar, &tstart, &finish, &tok,
                                    &tokregion, &bnd, &bndregion, &frameoff, &offsets, &boffsets,
                                    &compact, &bcompact, &tr_logits, &tr_h, &tr_c, &tr_tok, &tr_dur,
-                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &hst, &xnew, &hidc, &ep_w16, &ep_err,
+                                   &tr_ftok, &tr_fdur, &g0, &prof, &livef, &hst, &xnew, &hidc, &ep_w16, &ep_err, &h16, &x16, &dcount,
                                    &stg[0], &stg[1]};
         for (int i = 0; i < 2 + pk::kMaxLayers; ++i) { v.push_back(&tc_frag[i]); v.push_back(&tc_scale[i]); }
         for (int l = 0; l < pk::kMaxLayers; ++l) {
@@ -484,7 +489,7 @@ struct Run {
     std::vector<int32_t> ust;
     std::vector<int32_t> ctl;
     unsigned long long prof[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    float ms_encproj = 0.f, ms_loop = 0.f;
+    float ms_encproj = 0.f, ms_loop = 0.f, ms_bulk = 0.f;
     int launches = 0;          // kernels launched by this call
 };
 
@@ -690,7 +695,34 @@ pk_status run_loop(pk_ctx * x, Run & r) {
             P.forced_dur = x->tr_fdur.as<int32_t>();
         }
     }
+    // Fresh batches that start with many live utterances run their first iterations on
+    // the tcgen05 bulk loop; the persistent loop continues where it stops.
+    bool all_fresh = B > 0;
+    for (int b = 0; b < B && all_fresh; ++b) all_fresh = r.fresh[b] != 0;
+    const bool use_bulk = use_tc && x->bulk_ok && x->bulk_min_live > 0 && all_fresh &&
+                          (int) live.size() >= x->bulk_min_live && B <= x->grid * bulk_threads();
+    BulkParams q{};
+    if (use_bulk) {
+        PK_CK(x->h16.ensure(2 * (size_t) L * Bs * H * 4));
+        PK_CK(x->x16.ensure((size_t) L * Bs * H * 4));
+        PK_CK(x->dcount.ensure((size_t) x->grid * 8));
+        q.P = P;
+        q.min_live = x->bulk_min_live;
+        for (int l = 0; l < L; ++l) q.gl[l] = x->bulk.gl[l];
+        q.gp = x->bulk.gp;
+        q.gj = x->bulk.gj;
+        q.lbias = x->bulk.lbias;
+        q.h16 = x->h16.as<unsigned char>();
+        q.x16 = x->x16.as<unsigned char>();
+        q.dcount = x->dcount.as<int2>();
+        P.resume = 1;
+    }
     PK_CK(cudaEventRecord(x->ev[3], s));
+    if (use_bulk) {
+        PK_CK(launch_bulk(q, x->grid, s));
+        ++r.launches;
+    }
+    PK_CK(cudaEventRecord(x->ev[6], s));
     if (B > 0) {
         PK_CK(launch_step_loop(P, x->grid, use_tc ? x->tc_smem : x->smem, s));
         ++r.launches;
@@ -704,6 +736,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(cudaStreamSynchronize(s));
     PK_CK(cudaEventElapsedTime(&r.ms_encproj, x->ev[1], x->ev[2]));
     PK_CK(cudaEventElapsedTime(&r.ms_loop, x->ev[3], x->ev[4]));
+    PK_CK(cudaEventElapsedTime(&r.ms_bulk, x->ev[3], x->ev[6]));
     if (ep_tc && frames > 0) {
         int ep_err = 0;
         PK_CK(copy_sync(x, &ep_err, x->ep_err.p, sizeof(int), cudaMemcpyDeviceToHost));
@@ -752,6 +785,8 @@ pk_status emit_results(pk_ctx * x, Run & r, pk_result * res) {
     for (int i = 0; i < 8; ++i) res->phase_ms[i] = (double) r.prof[i] * 1e-6;
     res->encproj_ms = r.ms_encproj;
     res->loop_ms = r.ms_loop;
+    res->bulk_ms = r.ms_bulk;
+    res->bulk_iterations = r.ctl[C_BULKITERS];
     if (ntok > res->tokens_cap || (ntok > 0 && !res->tokens))
         return fail(PK_ERR_CAPACITY, "token buffer holds %lld, %lld needed", (long long) res->tokens_cap,
                     (long long) ntok);
@@ -957,6 +992,24 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
     if (st != PK_OK) return cleanup(st);
     setup_encproj(x, (size_t) prop.sharedMemPerBlockOptin);
     x->math = x->tc_ok ? PK_MATH_TC : PK_MATH_F32;
+    // the tcgen05 loop for iterations with many live utterances (tensor-core models only)
+    if (x->tc_ok && bulk_supported(x->H, x->J, x->L) && bulk_smem_bytes() <= (size_t) prop.sharedMemPerBlockOptin) {
+        int bps = 0;
+        if (bulk_configure() == cudaSuccess && bulk_occupancy(&bps) == cudaSuccess && bps >= 1) {
+            const float * wih[kMaxLayers], * whh[kMaxLayers], * bih[kMaxLayers], * bhh[kMaxLayers];
+            for (int l = 0; l < x->L; ++l) {
+                wih[l] = x->w_ih[l].as<float>(); whh[l] = x->w_hh[l].as<float>();
+                bih[l] = x->b_ih[l].as<float>(); bhh[l] = x->b_hh[l].as<float>();
+            }
+            if (bulk_prepare(x->bulk, x->H, x->J, x->L, x->Vo, wih, whh, bih, bhh, x->pred_w.as<float>(),
+                             x->out_w.as<float>(), x->stream) != cudaSuccess) {
+                bulk_release(x->bulk);
+                return cleanup(fail(PK_ERR_CUDA, "bulk-loop weight preparation failed"));
+            }
+            x->bulk_ok = 1;
+            x->weight_bytes += x->bulk.bytes;
+        }
+    }
     *out = x;
     return PK_OK;
 }
@@ -967,6 +1020,7 @@ void pk_destroy(pk_ctx * x) {
     if (x->stream) cudaStreamSynchronize(x->stream);
     if (x->cstream) cudaStreamSynchronize(x->cstream);
     for (DevBuf * b : x->all_bufs()) b->release();
+    bulk_release(x->bulk);
     for (auto & e : x->ev)
         if (e) cudaEventDestroy(e);
     for (auto & e : x->cev)
@@ -1005,6 +1059,10 @@ pk_status pk_set_option(pk_ctx * x, int32_t opt, int64_t v) {
             return PK_OK;
         case PK_OPT_TEST_STALL:
             x->test_stall = v != 0 ? 1 : 0;
+            return PK_OK;
+        case PK_OPT_BULK_MIN_LIVE:
+            if (v < 0) return fail(PK_ERR_INVALID, "bulk threshold must be >= 0");
+            x->bulk_min_live = (int) std::min<int64_t>(v, 1 << 30);
             return PK_OK;
         default:
             return fail(PK_ERR_INVALID, "unknown option %d", opt);

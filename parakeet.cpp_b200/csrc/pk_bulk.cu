@@ -1,0 +1,876 @@
+// pk_bulk.cu -- the greedy step loop for iterations with many live utterances,
+// on the 5th-generation tensor cores (tcgen05.mma, accumulators in tensor memory).
+//
+// The persistent loop (pk_loop.cu) keeps every weight slice stationary in one
+// CTA's shared memory, so each CTA reads every live utterance's activation row
+// once per phase: with thousands of live utterances that is 148 reads of each
+// row per iteration, and the loop is bound by L2 ingress rather than by the
+// tensor cores. This loop instead tiles every step-loop GEMM in two dimensions,
+//
+//   tile = 128 utterances (UMMA M) x up to 256 weight rows (UMMA N), K in steps of 64,
+//
+// streaming both operands from L2 (the weights, ~42 MB as f16 halves, stay
+// L2-resident), so an activation row is read once per weight tile and a weight
+// tile once per utterance tile. It runs while at least `min_live` utterances are
+// live and then exits; the persistent loop continues the same batch from the
+// state, lists and control words left here (LoopParams::resume).
+//
+// Per iteration (same order and semantics as the persistent loop):
+//   LSTM layer l   gates[e] = W_hh h_prev (+ W_ih x) for the emit list, then the
+//                  cell update in the epilogue (host_lstm_step,
+//                  src/parakeet_tdt.cpp:106-142; layer 0's b_ih + W_ih x comes from the
+//                  per-token table g0 exactly as in the persistent loop)
+//   pred           predp[utt] = b_pred + W_pred h[L-1] for the emit list
+//   hidden         hidc[i] = relu(encp[t_i] + predp[utt_i]) for the live list
+//                  (host_joint_step, :154-177)
+//   joint          logits = b_out + W_out hid, folded into 64-bit argmax keys
+//                  (argmax_f32, :25-32: first index of the maximum)
+//   decision       the greedy control (tdt_decode_window :938-968, eou_decode_window
+//                  src/parakeet_eou.cpp:271-333) for a slice of the live list per
+//                  CTA, then the next emit and live lists compacted over all CTAs
+// separated by grid barriers (bounded waits, like every wait here).
+//
+// Arithmetic: both operands as exact-or-22-bit f16 halves, three products
+// (A_hi W_hi + A_lo W_hi + A_hi W_lo) accumulated in f32 in tensor memory: the
+// weights' halves are exact for q8_0 (d * q has at most 18 significant bits) and
+// f16; h and the joint hidden layer carry 22 significant bits; the dropped
+// A_lo W_lo term is ~2^-22 relative.
+//
+// Warp roles in a GEMM phase (12 warps): 0-3 stage A (one utterance row per
+// thread, 16-byte cp.async gathers into the 128-byte-swizzled K-major tile), 4
+// issues the weight tiles' TMA loads, 5 owns tensor memory and issues the MMAs
+// (two 256-column accumulators: the epilogue of one tile overlaps the next tile's
+// main loop), 8-11 run the epilogue (TMEM lane quarter = warp % 4). All warps
+// run the element-wise and decision phases.
+
+#include "pk_device.cuh"
+#include "pk_umma.cuh"
+
+#include <vector>
+
+namespace pk {
+namespace {
+
+constexpr int kBThreads = 384;
+constexpr int kBWarps = kBThreads / 32;
+constexpr int kBM = 128;                              // utterances per tile (UMMA M)
+constexpr int kBK = 64;                               // K per stage: one 128-byte f16 row
+constexpr int kBNmax = 256;                           // weight rows per tile (UMMA N)
+constexpr int kBStages = 2;
+constexpr unsigned kATile = kBM * kBK * 2;            // one f16 plane of an A stage (16 KB)
+constexpr unsigned kBBox = 64 * kBK * 2;              // one 64-row box of one B plane (8 KB)
+constexpr unsigned kBTile = kBNmax * kBK * 2;         // one B plane of a stage (32 KB)
+constexpr unsigned kStage = 2 * kATile + 2 * kBTile;  // 96 KB
+constexpr unsigned kTmemCols = 2 * kBNmax;            // two accumulators
+
+struct BulkSmem {
+    unsigned long long full_a[kBStages];
+    unsigned long long full_b[kBStages];
+    unsigned long long empty[kBStages];
+    unsigned long long acc_full[2];
+    unsigned long long acc_empty[2];
+    unsigned tmem_base;
+    int err;                       // a wait of this CTA gave up (shared by every role)
+    int scan[kBWarps + 2];
+    int flag[4];
+};
+
+enum { G_LSTM = 0, G_PRED = 1, G_JOINT = 2 };
+
+// Stage and accumulator counters: each role advances its own, in the same order.
+struct Pipe {
+    unsigned a = 0, b = 0, m = 0;   // K stages filled (A, B) / consumed (MMA)
+    unsigned acc_m = 0, acc_e = 0;  // tiles accumulated (MMA) / drained (epilogue)
+};
+
+struct Job {
+    int kind, l, M, N, nK, bn, nM, nN, tiles, split, sel;
+    const BulkGemm * g;
+};
+
+__device__ __forceinline__ Job make_job(const BulkParams & Q, int kind, int l, int M, int sel) {
+    Job j{};
+    j.kind = kind;
+    j.l = l;
+    j.M = M;
+    j.sel = sel;
+    j.g = kind == G_LSTM ? &Q.gl[l] : kind == G_PRED ? &Q.gp : &Q.gj;
+    j.N = j.g->N;
+    j.nK = j.g->K / kBK;
+    j.nM = (M + kBM - 1) / kBM;
+    j.split = (kind == G_LSTM && l > 0) ? Q.P.H / kBK : 0;
+    // tile width: fewest rounds of tiles over the CTAs, counting ~32 columns of
+    // fixed cost per tile (pipeline fill and drain)
+    const int G = (int) gridDim.x;
+    int best = kBNmax;
+    long long best_cost = -1;
+    for (int bn = kBNmax; bn >= 64; bn >>= 1) {
+        const long long tiles = (long long) j.nM * ((j.N + bn - 1) / bn);
+        const long long cost = ((tiles + G - 1) / G) * (bn + 32);
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
+    }
+    j.bn = best;
+    j.nN = (j.N + j.bn - 1) / j.bn;
+    j.tiles = j.nM * j.nN;
+    return j;
+}
+
+__device__ __forceinline__ void cp_async16(unsigned dst, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ bool err_set(const BulkParams & Q, BulkSmem & S) {
+    return *reinterpret_cast<volatile int *>(&S.err) != 0;
+}
+
+// Bounded wait on an mbarrier phase; on timeout flags the CTA and the call.
+__device__ __forceinline__ bool wait_bar(const BulkParams & Q, BulkSmem & S, unsigned long long * b, unsigned parity) {
+    if (mbar_wait(b, parity, Q.P.timeout_ns, &S.err)) return true;
+    atomicCAS(&Q.P.ctl[C_ERR], 0, (int) PK_ERR_TIMEOUT);
+    return false;
+}
+
+// ---- one GEMM phase ------------------------------------------------------------
+
+// A producer: thread r (warps 0-3) stages row r of every tile: 8 chunks of 16 bytes
+// per plane and K stage, at chunk c ^ (r & 7) of the row (128-byte swizzle).
+__device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, const Job & J, Pipe & pp) {
+    const LoopParams & P = Q.P;
+    const int r = threadIdx.x;
+    const int H = P.H, L = P.L, B = P.B;
+    const unsigned rb16 = 4u * (unsigned) H;
+    for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
+        const int row = (t % J.nM) * kBM + r;
+        const bool valid = row < J.M;
+        // per-row sources: segment 0 for K stages [0, split), segment 1 for the rest;
+        // plane offset = bytes from the hi part to the lo part of a source row
+        const unsigned char * src0 = nullptr;
+        const unsigned char * src1 = nullptr;
+        unsigned plane = 0;
+        bool zero1 = false;
+        if (valid) {
+            if (J.kind == G_JOINT) {
+                src1 = P.hidc + (size_t) row * P.rbj;
+                plane = 2u * (unsigned) P.J;
+            } else {
+                const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + row);
+                plane = 2u * (unsigned) H;
+                if (J.kind == G_PRED) {
+                    src1 = Q.x16 + ((size_t) (L - 1) * B + row) * rb16;
+                } else {
+                    const int hb = (e.y >> 30) & 1;
+                    zero1 = e.y < 0;                    // reset: h_prev = 0
+                    src1 = Q.h16 + (((size_t) (hb ^ 1) * L + J.l) * B + e.x) * rb16;
+                    if (J.l > 0) src0 = Q.x16 + ((size_t) (J.l - 1) * B + row) * rb16;
+                }
+            }
+        }
+        for (int kc = 0; kc < J.nK; ++kc) {
+            const unsigned s = pp.a % kBStages, ph = (pp.a / kBStages) & 1u;
+            ++pp.a;
+            if (!wait_bar(Q, S, &S.empty[s], ph ^ 1u)) return;
+            unsigned char * ahi = tiles + s * kStage;
+            const unsigned dhi = smem_u32(ahi) + (unsigned) r * 128u;
+            const unsigned dlo = dhi + kATile;
+            if (valid) {
+                const bool seg1 = kc >= J.split;
+                if (seg1 && zero1) {
+                    for (unsigned c = 0; c < 8; ++c) {
+                        const unsigned o = (c ^ ((unsigned) r & 7u)) << 4;
+                        *reinterpret_cast<uint4 *>(ahi + r * 128 + o) = make_uint4(0u, 0u, 0u, 0u);
+                        *reinterpret_cast<uint4 *>(ahi + kATile + r * 128 + o) = make_uint4(0u, 0u, 0u, 0u);
+                    }
+                } else {
+                    const unsigned char * src = seg1 ? src1 + (size_t) (kc - J.split) * 128 : src0 + (size_t) kc * 128;
+#pragma unroll
+                    for (unsigned c = 0; c < 8; ++c) {
+                        const unsigned o = (c ^ ((unsigned) r & 7u)) << 4;
+                        cp_async16(dhi + o, src + c * 16);
+                        cp_async16(dlo + o, src + plane + c * 16);
+                    }
+                }
+            }
+            cp_async_wait_all();
+            // this thread's generic-proxy writes (copies, zeros) before the MMAs read them
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&S.full_a[s]);
+        }
+    }
+}
+
+// B producer (warp 4, one lane): the tile's weight rows, hi and lo planes, as
+// 64-row TMA boxes (rows past N arrive as zeros).
+__device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, const Job & J, Pipe & pp) {
+    const CUtensorMap * mhi = reinterpret_cast<const CUtensorMap *>(J.g->map_hi);
+    const CUtensorMap * mlo = reinterpret_cast<const CUtensorMap *>(J.g->map_lo);
+    for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
+        const int n0 = (t / J.nM) * J.bn;
+        const int rows = min(J.bn, J.N - n0);
+        const int nb = (rows + 63) / 64;
+        for (int kc = 0; kc < J.nK; ++kc) {
+            const unsigned s = pp.b % kBStages, ph = (pp.b / kBStages) & 1u;
+            ++pp.b;
+            if (!wait_bar(Q, S, &S.empty[s], ph ^ 1u)) return;
+            unsigned char * bhi = tiles + s * kStage + 2 * kATile;
+            unsigned char * blo = bhi + kBTile;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                         :: "r"(smem_u32(&S.full_b[s])), "r"((unsigned) nb * 2u * kBBox) : "memory");
+            for (int b = 0; b < nb; ++b) {
+                tma_load_2d(bhi + b * kBBox, mhi, kc * kBK, n0 + 64 * b, &S.full_b[s]);
+                tma_load_2d(blo + b * kBBox, mlo, kc * kBK, n0 + 64 * b, &S.full_b[s]);
+            }
+        }
+    }
+}
+
+// MMA issuer (warp 5, one lane): per K stage and 16-wide K step, three products
+// into the tile's accumulator (columns acc * 256).
+__device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, unsigned tmem, const Job & J,
+                         Pipe & pp) {
+    for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
+        const int n0 = (t / J.nM) * J.bn;
+        const int rows = min(J.bn, J.N - n0);
+        const int nmma = (rows + 15) & ~15;
+        const unsigned idesc = umma_idesc_f16(kBM, nmma);
+        const unsigned a = pp.acc_m & 1u, aph = (pp.acc_m >> 1) & 1u;
+        ++pp.acc_m;
+        if (!wait_bar(Q, S, &S.acc_empty[a], aph ^ 1u)) return;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const unsigned d = tmem + a * (unsigned) kBNmax;
+        for (int kc = 0; kc < J.nK; ++kc) {
+            const unsigned s = pp.m % kBStages, ph = (pp.m / kBStages) & 1u;
+            ++pp.m;
+            if (!wait_bar(Q, S, &S.full_a[s], ph)) return;
+            if (!wait_bar(Q, S, &S.full_b[s], ph)) return;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const unsigned base = smem_u32(tiles + s * kStage);
+            const unsigned ahi = base, alo = base + kATile, bhi = base + 2 * kATile, blo = bhi + kBTile;
+#pragma unroll
+            for (int k16 = 0; k16 < kBK / 16; ++k16) {
+                const unsigned ko = (unsigned) k16 * 32u;
+                umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(bhi + ko), idesc, (kc | k16) ? 1u : 0u);
+                umma_f16(d, umma_desc_sw128(alo + ko), umma_desc_sw128(bhi + ko), idesc, 1u);
+                umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
+            }
+            umma_commit(&S.empty[s]);      // the stage is free once these MMAs have read it
+        }
+        umma_commit(&S.acc_full[a]);       // the tile's accumulator is complete
+    }
+}
+
+__device__ __forceinline__ void tmem_ld32(unsigned taddr, float (&v)[32]) {
+    unsigned u[32];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                   "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+                   "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+                   "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+                   "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]);
+}
+
+// f16 hi / lo halves of 8 values, as two 16-byte vectors.
+__device__ __forceinline__ void split8(const float (&x)[8], uint4 & hi, uint4 & lo) {
+    unsigned h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half a = __float2half_rn(x[2 * i]), b = __float2half_rn(x[2 * i + 1]);
+        const __half la = __float2half_rn(x[2 * i] - __half2float(a));
+        const __half lb = __float2half_rn(x[2 * i + 1] - __half2float(b));
+        __half2 hh = __halves2half2(a, b), ll = __halves2half2(la, lb);
+        h[i] = *reinterpret_cast<unsigned *>(&hh);
+        l[i] = *reinterpret_cast<unsigned *>(&ll);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Epilogue of the LSTM layer: the tile's columns are gates (i, f, g, o) of units
+// [n0 / 4, (n0 + rows) / 4); row = emit-list index.
+__device__ __forceinline__ void epi_lstm(const BulkParams & Q, const Job & J, unsigned tacc, int row, int n0, int rows) {
+    const LoopParams & P = Q.P;
+    const int H = P.H, L = P.L, B = P.B, l = J.l;
+    const bool valid = row < J.M;
+    int utt = 0, tok = 0, hb = 0, reset = 0;
+    if (valid) {
+        const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + row);
+        utt = e.x;
+        tok = e.y & 0x3FFFFFFF;
+        hb = (e.y >> 30) & 1;
+        reset = e.y < 0 ? 1 : 0;
+    }
+    const unsigned rb16 = 4u * (unsigned) H;
+    for (int c0 = 0; c0 < rows; c0 += 32) {
+        float v[32];
+        tmem_ld32(tacc + (unsigned) c0, v);            // warp-wide: every lane takes part
+        if (!valid) continue;
+        const int j0 = (n0 + c0) >> 2;                  // first of the 8 units in these columns
+        if (j0 >= H) continue;
+        float hn[8], cn[8];
+        const float * bias = Q.lbias + (size_t) l * 4 * H + 4 * j0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + u;
+            float g[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float pre = __ldg(bias + 4 * u + q);
+                if (l == 0) pre += __ldg(P.g0 + (size_t) tok * 4 * H + q * H + j);
+                g[q] = pre + v[4 * u + q];
+            }
+            const float i_g = sigmoid_ref(g[0]);
+            const float f_g = sigmoid_ref(g[1]);
+            const float g_g = tanhf(g[2]);
+            const float o_g = sigmoid_ref(g[3]);
+            const float c_old = reset ? 0.0f : __ldcg(P.c + ((size_t) l * B + utt) * H + j);
+            cn[u] = f_g * c_old + i_g * g_g;
+            hn[u] = o_g * tanhf(cn[u]);
+        }
+        float * cp = P.c + ((size_t) l * B + utt) * H + j0;
+        float * hp = P.h + (((size_t) hb * L + l) * B + utt) * H + j0;
+        reinterpret_cast<float4 *>(cp)[0] = make_float4(cn[0], cn[1], cn[2], cn[3]);
+        reinterpret_cast<float4 *>(cp)[1] = make_float4(cn[4], cn[5], cn[6], cn[7]);
+        reinterpret_cast<float4 *>(hp)[0] = make_float4(hn[0], hn[1], hn[2], hn[3]);
+        reinterpret_cast<float4 *>(hp)[1] = make_float4(hn[4], hn[5], hn[6], hn[7]);
+        uint4 hi, lo;
+        split8(hn, hi, lo);
+        unsigned char * st = Q.h16 + (((size_t) hb * L + l) * B + utt) * rb16;
+        unsigned char * xn = Q.x16 + ((size_t) l * B + row) * rb16;
+        *reinterpret_cast<uint4 *>(st + 2 * j0) = hi;
+        *reinterpret_cast<uint4 *>(st + 2 * H + 2 * j0) = lo;
+        *reinterpret_cast<uint4 *>(xn + 2 * j0) = hi;
+        *reinterpret_cast<uint4 *>(xn + 2 * H + 2 * j0) = lo;
+        // the persistent loop's staged state row (it continues the batch)
+        unsigned char * hrow = P.hst + ((((size_t) hb * L + l) * B + utt) * P.rbh);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) put_h(P, hrow, j0 + u, hn[u]);
+    }
+}
+
+__device__ __forceinline__ void epi_pred(const BulkParams & Q, const Job & J, unsigned tacc, int row, int n0, int rows) {
+    const LoopParams & P = Q.P;
+    const bool valid = row < J.M;
+    const int utt = valid ? __ldcg(&P.emit[2 * row]) : 0;
+    for (int c0 = 0; c0 < rows; c0 += 32) {
+        float v[32];
+        tmem_ld32(tacc + (unsigned) c0, v);
+        if (!valid) continue;
+        float * o = P.predp + (size_t) utt * P.J + n0 + c0;
+        const float * b = P.pred_b + n0 + c0;
+#pragma unroll
+        for (int q = 0; q < 32; q += 4) {
+            if (n0 + c0 + q < P.J)
+                *reinterpret_cast<float4 *>(o + q) = make_float4(v[q] + __ldg(b + q), v[q + 1] + __ldg(b + q + 1),
+                                                                 v[q + 2] + __ldg(b + q + 2), v[q + 3] + __ldg(b + q + 3));
+        }
+    }
+}
+
+__device__ __forceinline__ void epi_joint(const BulkParams & Q, const Job & J, unsigned tacc, int row, int n0,
+                                          int rows, unsigned long long * keys) {
+    const LoopParams & P = Q.P;
+    const bool valid = row < J.M;
+    int utt = 0, step = 0;
+    if (valid) {
+        utt = __ldcg(P.live + (size_t) J.sel * P.B + row);
+        if (P.trace_steps > 0) step = __ldcg(&P.ust[utt * kUst + U_STEPS]);
+    }
+    unsigned long long bt = 0ull, bd = 0ull;
+    for (int c0 = 0; c0 < rows; c0 += 32) {
+        float v[32];
+        tmem_ld32(tacc + (unsigned) c0, v);
+        if (!valid) continue;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+            const int r = n0 + c0 + q;
+            if (r >= P.Vo) break;
+            const float logit = __ldg(P.out_b + r) + v[q];
+            if (P.trace_steps > 0 && step < P.trace_steps)
+                P.tr_logits[((size_t) utt * P.trace_steps + step) * P.Vo + r] = logit;
+            if (r < P.V1) {
+                const unsigned long long k = make_key(logit, r);
+                bt = k > bt ? k : bt;
+            } else {
+                const unsigned long long k = make_key(logit, r - P.V1);
+                bd = k > bd ? k : bd;
+            }
+        }
+    }
+    if (valid) {
+        if (bt) atomicMax(&keys[2 * utt + 0], bt);
+        if (bd) atomicMax(&keys[2 * utt + 1], bd);
+    }
+}
+
+// Epilogue warps 8-11: warp % 4 selects the TMEM lane quarter = rows 32 (warp % 4) .. + 31.
+__device__ void gemm_epilogue(const BulkParams & Q, BulkSmem & S, unsigned tmem, const Job & J, Pipe & pp,
+                              unsigned long long * keys) {
+    const int quarter = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
+    for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
+        const int row = (t % J.nM) * kBM + quarter * 32 + lane;
+        const int n0 = (t / J.nM) * J.bn;
+        const int rows = min(J.bn, J.N - n0);
+        const unsigned a = pp.acc_e & 1u, aph = (pp.acc_e >> 1) & 1u;
+        ++pp.acc_e;
+        if (!wait_bar(Q, S, &S.acc_full[a], aph)) return;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const unsigned tacc = tmem + ((unsigned) (quarter * 32) << 16) + a * (unsigned) kBNmax;
+        if (J.kind == G_LSTM) epi_lstm(Q, J, tacc, row, n0, rows);
+        else if (J.kind == G_PRED) epi_pred(Q, J, tacc, row, n0, rows);
+        else epi_joint(Q, J, tacc, row, n0, rows, keys);
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&S.acc_empty[a]);
+    }
+}
+
+// Every thread of the CTA: its role's share of the phase. False if a wait gave up.
+__device__ bool gemm_phase(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, unsigned tmem, const Job & J,
+                           Pipe & pp, unsigned long long * keys) {
+    const int warp = threadIdx.x >> 5;
+    if (J.tiles > 0) {
+        if (warp < 4) gemm_produce_a(Q, S, tiles, J, pp);
+        else if (warp == 4) {
+            if ((threadIdx.x & 31) == 0) gemm_produce_b(Q, S, tiles, J, pp);
+            __syncwarp();
+        } else if (warp == 5) {
+            if ((threadIdx.x & 31) == 0) gemm_mma(Q, S, tiles, tmem, J, pp);
+            __syncwarp();
+        }
+        else if (warp >= 8) gemm_epilogue(Q, S, tmem, J, pp, keys);
+    }
+    return __syncthreads_or(err_set(Q, S) ? 1 : 0) == 0;
+}
+
+// ---- grid barrier and block scan -------------------------------------------------
+
+// k-th barrier of this launch on the counter P.bar[6] (zeroed by the host).
+__device__ bool bulk_barrier(const BulkParams & Q, BulkSmem & S, unsigned & k) {
+    const LoopParams & P = Q.P;
+    __syncthreads();
+    const unsigned target = (k + 1u) * gridDim.x;
+    ++k;
+    if (threadIdx.x == 0) {
+        red_add_release(&P.bar[6], 1u);
+        int ok = 1;
+        const unsigned long long t0 = gtimer();
+        for (unsigned it = 1;; ++it) {
+            if ((int) (ld_acquire(&P.bar[6]) - target) >= 0) break;
+            if ((it & 63u) == 0u) {
+                if (__ldcg(&P.ctl[C_ERR]) != 0) { ok = 0; break; }
+                if ((long long) (gtimer() - t0) > P.timeout_ns) {
+                    atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        S.flag[0] = ok;
+    }
+    __syncthreads();
+    return S.flag[0] != 0;
+}
+
+__device__ int bulk_scan(BulkSmem & S, int v, int & total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) S.scan[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = lane < kBWarps ? S.scan[lane] : 0;
+        int y = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int z = __shfl_up_sync(0xFFFFFFFFu, y, o);
+            if (lane >= o) y += z;
+        }
+        if (lane < kBWarps) S.scan[lane] = y - w;
+        if (lane == kBWarps - 1) S.scan[kBWarps] = y;
+    }
+    __syncthreads();
+    total = S.scan[kBWarps];
+    const int r = x - v + S.scan[warp];
+    __syncthreads();
+    return r;
+}
+
+// ---- element-wise phase: joint hidden layer (and the trace's state dump) ------------
+
+__device__ void hidden_phase(const BulkParams & Q, int sel, int n_live, int n_prev) {
+    const LoopParams & P = Q.P;
+    const int J = P.J, B = P.B;
+    const int q4 = J / 4;
+    const long long total = (long long) n_live * q4;
+    const long long stride = (long long) gridDim.x * blockDim.x;
+    const int * live = P.live + (size_t) sel * B;
+    const long long * lfr = reinterpret_cast<const long long *>(P.live_frame) + (size_t) sel * B;
+    for (long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+        const int i = (int) (idx / q4), q = (int) (idx - (long long) i * q4);
+        const int utt = __ldcg(live + i);
+        const long long fr = __ldcg(lfr + i);
+        const float4 e = __ldcg(reinterpret_cast<const float4 *>(P.encp + (size_t) fr * J) + q);
+        const float4 p = __ldcg(reinterpret_cast<const float4 *>(P.predp + (size_t) utt * J) + q);
+        // relu as the persistent loop writes it: (0 < v) ? v : 0
+        const float vv[4] = {e.x + p.x, e.y + p.y, e.z + p.z, e.w + p.w};
+        float x[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[k] = (0.0f < vv[k]) ? vv[k] : 0.0f;
+        unsigned char * rowp = P.hidc + (size_t) i * P.rbj;
+        __half hh[4], hl[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            hh[k] = __float2half_rn(x[k]);
+            hl[k] = __float2half_rn(x[k] - __half2float(hh[k]));
+        }
+        __half2 h01 = __halves2half2(hh[0], hh[1]), h23 = __halves2half2(hh[2], hh[3]);
+        __half2 l01 = __halves2half2(hl[0], hl[1]), l23 = __halves2half2(hl[2], hl[3]);
+        *reinterpret_cast<uint2 *>(rowp + 8 * q) =
+            make_uint2(*reinterpret_cast<unsigned *>(&h01), *reinterpret_cast<unsigned *>(&h23));
+        *reinterpret_cast<uint2 *>(rowp + 2 * J + 8 * q) =
+            make_uint2(*reinterpret_cast<unsigned *>(&l01), *reinterpret_cast<unsigned *>(&l23));
+    }
+    // teacher-forced trace: state after each step decided by the previous iteration
+    if (P.trace_steps > 0 && n_prev > 0) {
+        const int H = P.H, L = P.L, LH = L * H;
+        const int * prev = P.live + (size_t) (sel ^ 1) * B;
+        const long long tot2 = (long long) n_prev * LH;
+        for (long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x; idx < tot2; idx += stride) {
+            const int i = (int) (idx / LH), k = (int) (idx - (long long) i * LH);
+            const int utt = __ldcg(prev + i);
+            const int step = __ldcg(&P.ust[utt * kUst + U_STEPS]) - 1;
+            if (step < 0 || step >= P.trace_steps) continue;
+            const int hb = __ldcg(&P.ust[utt * kUst + U_HBUF]);
+            const int l = k / H, j = k - (k / H) * H;
+            const size_t dst = ((size_t) utt * P.trace_steps + step) * LH + k;
+            if (P.tr_h) P.tr_h[dst] = __ldcg(P.h + (((size_t) hb * L + l) * B + utt) * H + j);
+            if (P.tr_c) P.tr_c[dst] = __ldcg(P.c + ((size_t) l * B + utt) * H + j);
+        }
+    }
+}
+
+// ---- the kernel -------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_constant__ BulkParams Q) {
+    const LoopParams & P = Q.P;
+    extern __shared__ __align__(1024) unsigned char bk_raw[];
+    unsigned char * tiles = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(bk_raw) + 1023) & ~(uintptr_t) 1023);
+    BulkSmem & S = *reinterpret_cast<BulkSmem *>(tiles + kBStages * kStage);
+    const int warp = threadIdx.x >> 5;
+    const int G = (int) gridDim.x;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kBStages; ++s) {
+            mbar_init(&S.full_a[s], 128);
+            mbar_init(&S.full_b[s], 1);
+            mbar_init(&S.empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&S.acc_full[a], 1);
+            mbar_init(&S.acc_empty[a], 128);
+        }
+        S.err = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(&S.tmem_base)), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tmem = S.tmem_base;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *P.t_start = gtimer();
+
+    Pipe pp;
+    unsigned nbar = 0;
+    int sel = __ldcg(&P.ctl[C_SEL]);
+    int n_emit = __ldcg(&P.ctl[C_NEMIT]);
+    int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
+    int n_prev = 0, iter = 0, emit_iters = 0;
+    unsigned long long * keys = P.keys;                 // one key buffer: cleared by the decision that reads it
+    bool ok = __ldcg(&P.ctl[C_ERR]) == 0;
+    while (ok && n_live >= Q.min_live && n_live > 0) {
+        if (iter > P.max_iters) {
+            if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+            break;
+        }
+        if (n_emit > 0) {
+            ++emit_iters;
+            for (int l = 0; l < P.L && ok; ++l) {
+                ok = gemm_phase(Q, S, tiles, tmem, make_job(Q, G_LSTM, l, n_emit, sel), pp, keys);
+                ok = ok && bulk_barrier(Q, S, nbar);
+            }
+            if (ok) ok = gemm_phase(Q, S, tiles, tmem, make_job(Q, G_PRED, 0, n_emit, sel), pp, keys);
+            ok = ok && bulk_barrier(Q, S, nbar);
+        }
+        if (!ok) break;
+        hidden_phase(Q, sel, n_live, n_prev);
+        if (!bulk_barrier(Q, S, nbar)) break;
+        if (!gemm_phase(Q, S, tiles, tmem, make_job(Q, G_JOINT, 0, n_live, sel), pp, keys)) break;
+        if (!bulk_barrier(Q, S, nbar)) break;
+
+        // ---- decision, part 1: this CTA's slice of the live list ----
+        const int ch = (n_live + G - 1) / G;
+        const int g = (int) blockIdx.x * ch + (int) threadIdx.x;
+        const bool mine = (int) threadIdx.x < ch && g < n_live;
+        int e = 0, lv = 0, utt = -1, etok = 0, ereset = 0, ehb = 0, bad = 0;
+        long long lframe = 0;
+        if (mine) {
+            utt = __ldcg(P.live + (size_t) sel * P.B + g);
+            int * u = P.ust + utt * kUst;
+            const unsigned long long kt = __ldcg(&keys[2 * utt + 0]);
+            const unsigned long long kd = P.is_tdt ? __ldcg(&keys[2 * utt + 1]) : 0ull;
+            const int4 u0 = __ldcg(reinterpret_cast<const int4 *>(u));
+            const int4 u1 = __ldcg(reinterpret_cast<const int4 *>(u) + 1);
+            const int4 u2 = __ldcg(reinterpret_cast<const int4 *>(u) + 2);
+            const long long foff = __ldg(P.frame_off + utt);
+            const int uf[12] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w, u2.x, u2.y, u2.z, u2.w};
+            keys[2 * utt + 0] = 0ull;
+            if (P.is_tdt) keys[2 * utt + 1] = 0ull;
+            int tok = key_index(kt);
+            int di = P.is_tdt ? key_index(kd) : 0;
+            if (keys_bad(P, kt, kd, tok, di)) {
+                atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
+                P.ctl[C_ERRINFO] = utt;
+                bad = 1;
+                tok = P.blank;
+                di = 0;
+            }
+            const int step = uf[U_STEPS];
+            if (P.trace_steps > 0 && step < P.trace_steps) {
+                const size_t ti = (size_t) utt * P.trace_steps + step;
+                if (P.tr_tok) P.tr_tok[ti] = tok;
+                if (P.tr_dur) P.tr_dur[ti] = di;
+                if (P.forced_tok) {
+                    const int ft = __ldg(P.forced_tok + ti);
+                    if (ft >= 0 && ft < P.V1) {
+                        tok = ft;
+                        const int fd = P.forced_dur ? __ldg(P.forced_dur + ti) : 0;
+                        di = (P.is_tdt && fd >= 0 && fd < P.Nd) ? fd : 0;
+                    }
+                }
+            }
+            u[U_STEPS] = step + 1;
+            const int s0 = uf[U_SYM];
+            const int T = uf[U_NFRAMES];
+            const Decision d = decide_core(P, tok, di, s0);
+            const int t = uf[U_T] + d.adv;
+            e = d.e; etok = d.etok; ereset = d.ereset;
+            int ntok = uf[U_NTOK];
+            if (!P.is_tdt) eou_effects(P, u, uf, utt, d, s0, ntok, tok, T);
+            if (d.emit_tok && !put_token(P, utt, tok, ntok, T)) bad = 1;
+            if (e) {
+                ehb = uf[U_HBUF] ^ 1;
+                u[U_HBUF] = ehb;
+            }
+            u[U_T] = t;
+            u[U_SYM] = d.sym;
+            u[U_NTOK] = ntok;
+            lv = t < T ? 1 : 0;
+            if (lv) lframe = foff + t;
+            if (!lv) P.finish_ns[utt] = gtimer();
+        }
+        int tot = 0;
+        const int pf = bulk_scan(S, e | (lv << 16), tot);
+        if (threadIdx.x == 0) Q.dcount[blockIdx.x] = make_int2(tot & 0xFFFF, tot >> 16);
+        if (__syncthreads_or(bad)) { ok = false; break; }
+        if (!bulk_barrier(Q, S, nbar)) break;
+
+        // ---- decision, part 2: list positions from every CTA's counts ----
+        int be = 0, bl = 0, te = 0, tl = 0;
+        for (int k = threadIdx.x; k < G; k += blockDim.x) {
+            const int2 c = __ldcg(Q.dcount + k);
+            if (k < (int) blockIdx.x) { be += c.x; bl += c.y; }
+            te += c.x;
+            tl += c.y;
+        }
+        int sbe = 0, sbl = 0, ste = 0, stl = 0;
+        bulk_scan(S, be, sbe);
+        bulk_scan(S, bl, sbl);
+        bulk_scan(S, te, ste);
+        bulk_scan(S, tl, stl);
+        const int nsel = sel ^ 1;
+        if (e) {
+            reinterpret_cast<int2 *>(P.emit)[sbe + (pf & 0xFFFF)] =
+                make_int2(utt, etok | (ehb << 30) | (ereset << 31));
+        }
+        if (lv) {
+            const int pos = sbl + (pf >> 16);
+            P.live[(size_t) nsel * P.B + pos] = utt;
+            P.live_frame[(size_t) nsel * P.B + pos] = lframe;
+            prefetch_l2(P.encp + (size_t) lframe * P.J, (unsigned) P.J * 4u);
+        }
+        if (blockIdx.x == 0 && threadIdx.x == 0) {
+            P.ctl[C_NEMIT] = ste;
+            P.ctl[C_NLIVE0 + nsel] = stl;
+            P.ctl[C_NDECIDED] = n_live;
+            P.ctl[C_SEL] = nsel;
+            P.ctl[C_ITERS] = iter + 1;
+            P.ctl[C_EMITITERS] = emit_iters;
+            P.ctl[C_BULKITERS] = iter + 1;
+        }
+        n_prev = n_live;
+        sel = nsel;
+        n_emit = ste;
+        n_live = stl;
+        ++iter;
+        if (!bulk_barrier(Q, S, nbar)) break;
+    }
+
+    // ---- teardown: every role is done with tensor memory ----
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 5) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ---- bulk weights ------------------------------------------------------------------------
+
+// dst [rows][K] hi / lo halves of row-gathered f32 weights: LSTM layer l uses
+// rows 4j + q <- gate row q * H + j and K = [W_ih (kin) | W_hh (H)] (layer 0: W_hh only).
+__global__ void bulk_split_lstm(const float * __restrict__ w_ih, const float * __restrict__ w_hh, int H, int kin,
+                                __half * __restrict__ hi, __half * __restrict__ lo) {
+    const int K = kin + H;
+    const long long n = (long long) 4 * H * K;
+    for (long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x) {
+        const int r = (int) (i / K), k = (int) (i - (long long) r * K);
+        const int j = r >> 2, q = r & 3;
+        const int src = q * H + j;
+        const float x = k < kin ? w_ih[(size_t) src * kin + k] : w_hh[(size_t) src * H + (k - kin)];
+        const __half h = __float2half_rn(x);
+        hi[i] = h;
+        lo[i] = __float2half_rn(x - __half2float(h));
+    }
+}
+
+__global__ void bulk_split_rows(const float * __restrict__ w, long long n, __half * __restrict__ hi,
+                                __half * __restrict__ lo) {
+    for (long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x) {
+        const float x = w[i];
+        const __half h = __float2half_rn(x);
+        hi[i] = h;
+        lo[i] = __float2half_rn(x - __half2float(h));
+    }
+}
+
+__global__ void bulk_lstm_bias(const float * __restrict__ b_ih, const float * __restrict__ b_hh, int H, int first,
+                               float * __restrict__ out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= 4 * H) return;
+    const int src = (r & 3) * H + (r >> 2);
+    out[r] = first ? b_hh[src] : b_ih[src] + b_hh[src];
+}
+
+}  // namespace
+
+cudaError_t encode_2d(void * map, CUtensorMapDataType type, size_t esize, const void * base, long long rows,
+                      long long cols, int box_rows, int box_cols, CUtensorMapSwizzle swz);
+
+bool bulk_supported(int H, int J, int L) {
+    return H > 0 && J > 0 && H % kBK == 0 && J % kBK == 0 && L >= 1 && L <= kMaxLayers;
+}
+
+size_t bulk_smem_bytes() { return 1024 + (size_t) kBStages * kStage + sizeof(BulkSmem); }
+
+int bulk_threads() { return kBThreads; }
+
+cudaError_t bulk_configure() {
+    return cudaFuncSetAttribute(bulk_loop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) bulk_smem_bytes());
+}
+
+cudaError_t bulk_occupancy(int * blocks_per_sm) {
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, bulk_loop_kernel, kBThreads, bulk_smem_bytes());
+}
+
+void bulk_release(BulkWeights & w) {
+    if (w.mem) cudaFree(w.mem);
+    w = BulkWeights{};
+}
+
+cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, const float * const * w_ih,
+                         const float * const * w_hh, const float * const * b_ih, const float * const * b_hh,
+                         const float * pred_w, const float * out_w, cudaStream_t s) {
+    bulk_release(w);
+    // layout: [maps: (L + 2) x 2 x 128 B][lbias L x 4H f32][halves]
+    const int nmat = L + 2;
+    size_t off = 0;
+    const size_t maps = off;
+    off += (size_t) nmat * 2 * 128;
+    const size_t bias = off;
+    off += (size_t) L * 4 * H * 4;
+    off = (off + 255) & ~(size_t) 255;
+    size_t mat_off[kMaxLayers + 2];
+    long long mat_rows[kMaxLayers + 2], mat_k[kMaxLayers + 2];
+    for (int l = 0; l < L; ++l) { mat_rows[l] = 4LL * H; mat_k[l] = l == 0 ? H : 2LL * H; }
+    mat_rows[L] = J; mat_k[L] = H;            // pred
+    mat_rows[L + 1] = Vo; mat_k[L + 1] = J;   // joint
+    for (int m = 0; m < nmat; ++m) {
+        mat_off[m] = off;
+        off += (size_t) 2 * mat_rows[m] * mat_k[m] * 2;
+        off = (off + 255) & ~(size_t) 255;
+    }
+    cudaError_t e = cudaMalloc(&w.mem, off);
+    if (e != cudaSuccess) { w.mem = nullptr; return e; }
+    w.bytes = off;
+    unsigned char * base = static_cast<unsigned char *>(w.mem);
+    std::vector<CUtensorMap> host_maps((size_t) nmat * 2);   // 64-byte aligned, as the encoder requires
+    for (int m = 0; m < nmat; ++m) {
+        __half * hi = reinterpret_cast<__half *>(base + mat_off[m]);
+        __half * lo = hi + mat_rows[m] * mat_k[m];
+        if (m < L) {
+            bulk_split_lstm<<<1184, 256, 0, s>>>(m == 0 ? nullptr : w_ih[m], w_hh[m], H, m == 0 ? 0 : H, hi, lo);
+        } else {
+            bulk_split_rows<<<1184, 256, 0, s>>>(m == L ? pred_w : out_w, mat_rows[m] * mat_k[m], hi, lo);
+        }
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        e = encode_2d(&host_maps[(size_t) (2 * m)], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, hi, mat_rows[m],
+                      mat_k[m], 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (e != cudaSuccess) return e;
+        e = encode_2d(&host_maps[(size_t) (2 * m + 1)], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, lo, mat_rows[m],
+                      mat_k[m], 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (e != cudaSuccess) return e;
+        BulkGemm g;
+        g.map_hi = base + maps + (size_t) (2 * m) * 128;
+        g.map_lo = base + maps + (size_t) (2 * m + 1) * 128;
+        g.N = (int) mat_rows[m];
+        g.K = (int) mat_k[m];
+        if (m < L) w.gl[m] = g;
+        else if (m == L) w.gp = g;
+        else w.gj = g;
+    }
+    for (int l = 0; l < L; ++l) {
+        bulk_lstm_bias<<<(4 * H + 255) / 256, 256, 0, s>>>(b_ih[l], b_hh[l], H, l == 0 ? 1 : 0,
+                                                           reinterpret_cast<float *>(base + bias) + (size_t) l * 4 * H);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    w.lbias = reinterpret_cast<const float *>(base + bias);
+    e = cudaMemcpyAsync(base + maps, host_maps.data(), host_maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return e;
+    return cudaStreamSynchronize(s);
+}
+
+cudaError_t launch_bulk(const BulkParams & q, int grid, cudaStream_t s) {
+    void * args[] = {const_cast<BulkParams *>(&q)};
+    return cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(bulk_loop_kernel), dim3(grid), dim3(kBThreads),
+                                       args, bulk_smem_bytes(), s);
+}
+
+}  // namespace pk

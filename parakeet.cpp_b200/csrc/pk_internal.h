@@ -40,6 +40,7 @@ enum CtlField : int {
     C_ITERS,          // batched loop iterations completed
     C_ERRINFO,        // first failing utterance / index (diagnostics)
     C_EMITITERS,      // iterations whose leader produced a non-empty emit list
+    C_BULKITERS,      // iterations run by the bulk loop (pk_bulk.cu) before the persistent loop
     kCtl = 16
 };
 
@@ -74,6 +75,8 @@ struct LoopParams {
     long long timeout_ns;      // bound on every grid-barrier wait
     int max_iters;             // bound on batched loop iterations (max_b T_b * (max_sym + 1) + 2)
     int test_stall;            // test hook: CTA 0 returns before its first barrier
+    int resume;                // the loop continues a batch that the bulk loop (pk_bulk.cu) started:
+                               // control words, lists and state come from it, iteration counts add on
     // tensor-core phases (tc = 1)
     int tc;
     int stationary;            // copy TC weights into shared memory at kernel start
@@ -135,6 +138,47 @@ struct LoopParams {
     int32_t * tr_tok;
     int32_t * tr_dur;
 };
+
+// ---- bulk loop (pk_bulk.cu): iterations with many live utterances on tcgen05 ----
+//
+// One weight matrix of a step-loop GEMM, split into exact f16 halves (w = hi + lo)
+// for the tensor-memory loop: [N][K] f16 each, TMA descriptors (128 bytes each,
+// 64-byte aligned, in device memory) with a 64 x 64 box and 128-byte swizzle.
+struct BulkGemm {
+    const void * map_hi;
+    const void * map_lo;
+    int N, K;
+};
+
+struct BulkParams {
+    LoopParams P;              // lists, state, outputs and control words shared with the persistent loop
+    int min_live;              // iterate while at least this many utterances are live
+    BulkGemm gl[kMaxLayers];   // LSTM layer l: rows 4j + q = gate q of unit j; K = [W_ih | W_hh] (layer 0: W_hh)
+    BulkGemm gp;               // joint.pred [J][H]
+    BulkGemm gj;               // joint.out [Vo][J]
+    const float * lbias;       // [L][4H] gate biases in the same row order: layer 0 b_hh, above b_ih + b_hh
+    unsigned char * h16;       // [2][L][B] rows of 4H bytes: f16 hi[H] | lo[H] of h, by utterance
+    unsigned char * x16;       // [L][B] rows, same layout: layer l's new h by emit-list index
+    int2 * dcount;             // [grid] each CTA's (emit, live) counts from the decision
+};
+
+// Device-side bulk weights of a context (built once at pk_create).
+struct BulkWeights {
+    void * mem = nullptr;      // one allocation: f16 halves, biases, TMA descriptors
+    BulkGemm gl[kMaxLayers]{}, gp{}, gj{};
+    const float * lbias = nullptr;
+    size_t bytes = 0;
+};
+bool        bulk_supported(int H, int J, int L);
+cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, const float * const * w_ih,
+                         const float * const * w_hh, const float * const * b_ih, const float * const * b_hh,
+                         const float * pred_w, const float * out_w, cudaStream_t s);
+void        bulk_release(BulkWeights & w);
+size_t      bulk_smem_bytes();
+cudaError_t bulk_configure();
+cudaError_t bulk_occupancy(int * blocks_per_sm);
+int         bulk_threads();
+cudaError_t launch_bulk(const BulkParams & q, int grid, cudaStream_t s);
 
 // Launch wrappers (defined in the .cu files).
 cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s);
