@@ -324,14 +324,20 @@ PK_API pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_sha
  * tokens_cap must be >= n_frames * max(1, max_symbols_per_step). On success
  * *n_tokens and *steps (device int32) hold the token count and joint
  * evaluations (tdt_greedy_decode / eou_greedy_decode semantics for one
- * utterance).
+ * utterance). The input must be written and the outputs free before the call:
+ * the decode runs on the context's own stream, which does not wait for work
+ * the caller queued on other streams.
  *
- * The first call on a device looks up the array's device address on that
- * device (cudaGetSymbolAddress); make that first call before any stream
- * capture. All calls share the one array, which keeps the last call's
- * contents: calls that overlap on the GPU (from several threads or contexts
- * on the same device) race with each other and must be serialised by the
- * caller. The call blocks until its decode has finished. */
+ * It always runs the f32 CUDA-core enc-proj and step loop (PK_MATH_F32),
+ * whatever the context's math mode, so its tokens equal pk_decode_batch's
+ * with math = PK_MATH_F32. pk_create has already looked up the array's device
+ * address (cudaGetSymbolAddress), which loads the array with the library's
+ * module when CUDA loads modules lazily, and has run one decode on that loop,
+ * so a call made right after pk_create allocates nothing. All calls share the
+ * one array, which keeps the last call's contents: calls that overlap on the
+ * GPU (from several threads or contexts on the same device) race with each
+ * other and must be serialised by the caller. The call blocks until its
+ * decode has finished and leaves the caller's current device as it was. */
 #define PK_NOALLOC_MAX_FRAMES 4096
 #define PK_NOALLOC_SCRATCH_BYTES (17u * 1024u * 1024u)
 PK_API pk_status pk_decode_noalloc(pk_ctx * ctx, const float * enc, int32_t n_frames, int32_t d_enc,

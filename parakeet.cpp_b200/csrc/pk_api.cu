@@ -1010,6 +1010,32 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
             x->weight_bytes += x->bulk.bytes;
         }
     }
+    // pk_decode_noalloc allocates nothing: its module (and static scratch array) is
+    // loaded now, and one 1-frame decode on the f32 loop it runs sizes the context's
+    // local memory for that kernel here rather than at its first call
+    if (noalloc_prepare(device) != PK_OK) return cleanup(fail(PK_ERR_CUDA, "no-allocation path set-up failed"));
+    {
+        const int math = x->math;
+        x->math = PK_MATH_F32;
+        std::vector<float> frame((size_t) x->De, 0.0f);
+        const int64_t off0 = 0;
+        const int32_t one = 1;
+        pk_batch wb{};
+        wb.enc = frame.data();
+        wb.B = 1;
+        wb.d_enc = x->De;
+        wb.frame_offsets = &off0;
+        wb.n_frames = &one;
+        int32_t tok[64];
+        int64_t toff[2];
+        pk_result wr{};
+        wr.tokens = tok;
+        wr.tokens_cap = 64;
+        wr.token_offsets = toff;
+        const pk_status ws = batch_run(x, &wb, nullptr, &wr);
+        x->math = math;
+        if (ws != PK_OK) return cleanup(ws);
+    }
     *out = x;
     return PK_OK;
 }

@@ -244,6 +244,8 @@ struct CtxView {
     const uint8_t * special;
 };
 void ctx_view(const pk_ctx * ctx, CtxView * v);
+// pk_noalloc.cu: loads the no-allocation path's module on `device` (current).
+pk_status noalloc_prepare(int device);
 // Records `msg` as this thread's pk_last_error() text and returns s.
 pk_status set_error(pk_status s, const char * msg);
 

@@ -13,11 +13,15 @@
 // In host code `g_scratch` is only a host-side stand-in for the array: giving
 // it to a kernel would fault (or, where the GPU can reach host memory, use the
 // wrong memory). Host code therefore passes the array's device address, looked
-// up once per device with cudaGetSymbolAddress while that device is current
-// (the first call on a device does it; make that call before any stream
-// capture). All calls share the array and it keeps the last call's contents:
-// the init kernel below clears everything that must start at zero, and calls
-// that overlap on the GPU race with each other.
+// up once per device with cudaGetSymbolAddress while that device is current.
+// pk_create does that look-up (noalloc_prepare below), so this file's module --
+// and with it the array -- is loaded when the context is made, not lazily at the
+// first call, and it runs one 1-frame decode on the CUDA-core loop this entry
+// point uses, so that kernel's local memory is sized then too. The call itself
+// runs the f32 CUDA-core enc-proj and step loop whatever the context's math
+// mode. All calls share the array and it keeps the last call's contents: the
+// init kernel below clears everything that must start at zero, and calls that
+// overlap on the GPU race with each other.
 
 #include "pk_internal.h"
 
@@ -122,6 +126,21 @@ pk_status scratch_address(int device, unsigned char ** out) {
 }
 
 }  // namespace
+
+// Called by pk_create with the context's device current: looks up the scratch
+// array's device address, which loads this file's module (and with it the
+// array's device memory) now instead of at the first pk_decode_noalloc call, when
+// CUDA loads modules lazily (its default since 12.2).
+pk_status noalloc_prepare(int device) {
+    unsigned char * base = nullptr;
+    if (scratch_address(device, &base) != PK_OK) return PK_ERR_CUDA;
+    cudaFuncAttributes a{};
+    if (cudaFuncGetAttributes(&a, noalloc_init_kernel) != cudaSuccess ||
+        cudaFuncGetAttributes(&a, noalloc_finish_kernel) != cudaSuccess)
+        return PK_ERR_CUDA;
+    return PK_OK;
+}
+
 }  // namespace pk
 
 extern "C" PK_API pk_status pk_decode_noalloc(pk_ctx * ctx, const float * enc, int32_t n_frames,
@@ -146,7 +165,14 @@ extern "C" PK_API pk_status pk_decode_noalloc(pk_ctx * ctx, const float * enc, i
     const Layout o = layout(v.J, v.H, v.L);
     if (o.total > PK_NOALLOC_SCRATCH_BYTES)
         return na_fail(PK_ERR_INVALID, "pk_decode_noalloc: model too large for the static scratch array");
+    int prev_device = -1;
+    if (cudaGetDevice(&prev_device) != cudaSuccess) prev_device = -1;
     if (cudaSetDevice(v.device) != cudaSuccess) return na_fail(PK_ERR_CUDA, "pk_decode_noalloc: cudaSetDevice failed");
+    // the caller's current device comes back on every return from here on
+    struct Restore {
+        int d;
+        ~Restore() { if (d >= 0) cudaSetDevice(d); }
+    } restore{prev_device};
     unsigned char * base = nullptr;
     if (scratch_address(v.device, &base) != PK_OK)
         return na_fail(PK_ERR_CUDA, "pk_decode_noalloc: cudaGetSymbolAddress of the scratch array failed");
