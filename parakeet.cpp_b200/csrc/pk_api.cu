@@ -697,8 +697,11 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     }
     // Fresh batches that start with many live utterances run their first iterations on
     // the tcgen05 bulk loop; the persistent loop continues where it stops.
+    // (every live utterance must start from its init step: the bulk loop's first
+    // iteration computes pred-proj for the emit list only)
     bool all_fresh = B > 0;
-    for (int b = 0; b < B && all_fresh; ++b) all_fresh = r.fresh[b] != 0;
+    for (int b = 0; b < B && all_fresh; ++b)
+        all_fresh = r.fresh[b] != 0 || !(r.n_frames[b] > 0 && r.t0[b] < r.n_frames[b]);
     const bool use_bulk = use_tc && x->bulk_ok && x->bulk_min_live > 0 && all_fresh &&
                           (int) live.size() >= x->bulk_min_live && B <= x->grid * bulk_threads();
     BulkParams q{};
