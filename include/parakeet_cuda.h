@@ -200,6 +200,9 @@ typedef struct pk_result {
     double    total_ms;           /* device time of the whole call incl. copies */
     double    bulk_ms;            /* device time of the tcgen05 bulk loop (PK_OPT_BULK_MIN_LIVE), 0 if it did not run */
     int64_t   bulk_iterations;    /* loop iterations that ran on the bulk loop (included in loop_iterations) */
+    double    bulk_phase_ms[12];  /* bulk loop breakdown seen by CTA 0 (%globaltimer): for the LSTM layers,
+                                     pred-proj, joint hidden, joint, decision and list compaction,
+                                     [2i] = CTA 0's own share, [2i+1] = the grid barrier after it */
 } pk_result;
 
 /* Greedy decode of B fresh utterances (each starts from tdt_init_state /

@@ -178,7 +178,8 @@ class Decoder:
                "steps": steps[:B].copy(), "total_steps": int(r.total_steps),
                "loop_iterations": int(r.loop_iterations), "encproj_ms": r.encproj_ms,
                "loop_ms": r.loop_ms, "total_ms": r.total_ms, "tokens_needed": int(r.tokens_needed),
-               "bulk_ms": r.bulk_ms, "bulk_iterations": int(r.bulk_iterations)}
+               "bulk_ms": r.bulk_ms, "bulk_iterations": int(r.bulk_iterations),
+               "bulk_phase_ms": list(r.bulk_phase_ms)}
         if bounds is not None:
             out["bounds"] = [bounds[boffs[i]:boffs[i + 1]].copy() for i in range(B)]
         if want_finish:

@@ -63,7 +63,8 @@ class pk_result(C.Structure):
                 ("emit_iterations", C.c_int64), ("kernel_launches", C.c_int64),
                 ("phase_ms", C.c_double * 8),
                 ("encproj_ms", C.c_double), ("loop_ms", C.c_double), ("total_ms", C.c_double),
-                ("bulk_ms", C.c_double), ("bulk_iterations", C.c_int64)]
+                ("bulk_ms", C.c_double), ("bulk_iterations", C.c_int64),
+                ("bulk_phase_ms", C.c_double * 12)]
 
 
 class pk_trace(C.Structure):

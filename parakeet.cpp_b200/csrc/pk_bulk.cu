@@ -597,6 +597,19 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
 
     Pipe pp;
     unsigned nbar = 0;
+    // CTA 0's thread 0 times every phase: [2k] its own share, [2k + 1] the grid barrier
+    // after it (k: 0 LSTM layers, 1 pred-proj, 2 joint hidden, 3 joint, 4 decision,
+    // 5 list compaction)
+    const bool prof = blockIdx.x == 0 && threadIdx.x == 0 && Q.prof != nullptr;
+    unsigned long long pacc[12] = {0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
+    unsigned long long plast = prof ? gtimer() : 0ull;
+    auto mark = [&](int slot) {
+        if (prof) {
+            const unsigned long long now = gtimer();
+            pacc[slot] += now - plast;
+            plast = now;
+        }
+    };
     int sel = __ldcg(&P.ctl[C_SEL]);
     int n_emit = __ldcg(&P.ctl[C_NEMIT]);
     int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
@@ -612,16 +625,24 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
             ++emit_iters;
             for (int l = 0; l < P.L && ok; ++l) {
                 ok = gemm_phase(Q, S, tiles, tmem, make_job(Q, G_LSTM, l, n_emit, sel), pp, keys);
+                mark(0);
                 ok = ok && bulk_barrier(Q, S, nbar);
+                mark(1);
             }
             if (ok) ok = gemm_phase(Q, S, tiles, tmem, make_job(Q, G_PRED, 0, n_emit, sel), pp, keys);
+            mark(2);
             ok = ok && bulk_barrier(Q, S, nbar);
+            mark(3);
         }
         if (!ok) break;
         hidden_phase(Q, sel, n_live, n_prev);
+        mark(4);
         if (!bulk_barrier(Q, S, nbar)) break;
+        mark(5);
         if (!gemm_phase(Q, S, tiles, tmem, make_job(Q, G_JOINT, 0, n_live, sel), pp, keys)) break;
+        mark(6);
         if (!bulk_barrier(Q, S, nbar)) break;
+        mark(7);
 
         // ---- decision, part 1: this CTA's slice of the live list ----
         const int ch = (n_live + G - 1) / G;
@@ -688,7 +709,9 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
         const int pf = bulk_scan(S, e | (lv << 16), tot);
         if (threadIdx.x == 0) Q.dcount[blockIdx.x] = make_int2(tot & 0xFFFF, tot >> 16);
         if (__syncthreads_or(bad)) { ok = false; break; }
+        mark(8);
         if (!bulk_barrier(Q, S, nbar)) break;
+        mark(9);
 
         // ---- decision, part 2: list positions from every CTA's counts ----
         int be = 0, bl = 0, te = 0, tl = 0;
@@ -728,8 +751,12 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
         n_emit = ste;
         n_live = stl;
         ++iter;
+        mark(10);
         if (!bulk_barrier(Q, S, nbar)) break;
+        mark(11);
     }
+    if (prof)
+        for (int i = 0; i < 12; ++i) Q.prof[i] = pacc[i];
 
     // ---- teardown: every role is done with tensor memory ----
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
