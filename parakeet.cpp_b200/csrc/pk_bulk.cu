@@ -56,17 +56,16 @@ constexpr int kBWarps = kBThreads / 32;
 constexpr int kBM = 128;                              // utterances per tile (UMMA M)
 constexpr int kBK = 64;                               // K per stage: one 128-byte f16 row
 constexpr int kBNmax = 256;                           // weight rows per tile (UMMA N)
-constexpr int kBStages = 2;
+constexpr int kMaxStages = 4;
 constexpr unsigned kATile = kBM * kBK * 2;            // one f16 plane of an A stage (16 KB)
 constexpr unsigned kBBox = 64 * kBK * 2;              // one 64-row box of one B plane (8 KB)
-constexpr unsigned kBTile = kBNmax * kBK * 2;         // one B plane of a stage (32 KB)
-constexpr unsigned kStage = 2 * kATile + 2 * kBTile;  // 96 KB
+constexpr unsigned kRing = 192 * 1024;                // operand ring: 2 stages at N = 256, 3 at 128, 4 at 64
 constexpr unsigned kTmemCols = 2 * kBNmax;            // two accumulators
 
 struct BulkSmem {
-    unsigned long long full_a[kBStages];
-    unsigned long long full_b[kBStages];
-    unsigned long long empty[kBStages];
+    unsigned long long full_a[kMaxStages];
+    unsigned long long full_b[kMaxStages];
+    unsigned long long empty[kMaxStages];
     unsigned long long acc_full[2];
     unsigned long long acc_empty[2];
     unsigned tmem_base;
@@ -77,11 +76,30 @@ struct BulkSmem {
 
 enum { G_LSTM = 0, G_PRED = 1, G_JOINT = 2 };
 
-// Stage and accumulator counters: each role advances its own, in the same order.
+// Uses of every ring slot and accumulator so far: each role advances its own, in the
+// same order, so the mbarrier phase of a slot is its use count's parity. (The number
+// of slots changes with the tile width from phase to phase; every slot is drained at
+// the end of a phase.)
 struct Pipe {
-    unsigned a = 0, b = 0, m = 0;   // K stages filled (A, B) / consumed (MMA)
-    unsigned acc_m = 0, acc_e = 0;  // tiles accumulated (MMA) / drained (epilogue)
+    unsigned ua[kMaxStages] = {0u, 0u, 0u, 0u};   // A stages filled
+    unsigned ub[kMaxStages] = {0u, 0u, 0u, 0u};   // B stages filled
+    unsigned um[kMaxStages] = {0u, 0u, 0u, 0u};   // stages consumed by the MMAs
+    unsigned acc_m = 0, acc_e = 0;                // tiles accumulated (MMA) / drained (epilogue)
 };
+
+// Ring geometry of a phase: a stage is the A tile (hi, lo) then the B tile (hi, lo)
+// of bn rows; every part starts on a 1024-byte boundary (the swizzle atom).
+struct Ring {
+    unsigned stage, b_plane;
+    int n;
+};
+__device__ __forceinline__ Ring ring(int bn) {
+    Ring r;
+    r.b_plane = (unsigned) bn * kBK * 2u;
+    r.stage = 2u * kATile + 2u * r.b_plane;
+    r.n = min(kMaxStages, (int) (kRing / r.stage));
+    return r;
+}
 
 struct Job {
     int kind, l, M, N, nK, bn, nM, nN, tiles, split, sel;
@@ -118,8 +136,13 @@ __device__ __forceinline__ Job make_job(const BulkParams & Q, int kind, int l, i
 __device__ __forceinline__ void cp_async16(unsigned dst, const void * src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+// 128 zero bytes: the source of A rows that are zero (an EOU reset's h_prev).
+__device__ __align__(128) unsigned char g_zero128[128];
+
+// Arrives on the mbarrier once this thread's earlier cp.async copies have landed
+// (the barrier's expected count includes the arrival).
+__device__ __forceinline__ void cp_async_arrive(unsigned long long * b) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_u32(b)) : "memory");
 }
 
 __device__ __forceinline__ bool err_set(const BulkParams & Q, BulkSmem & S) {
@@ -140,6 +163,8 @@ __device__ __forceinline__ bool wait_bar(const BulkParams & Q, BulkSmem & S, uns
 __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, const Job & J, Pipe & pp) {
     const LoopParams & P = Q.P;
     const int r = threadIdx.x;
+    const Ring R = ring(J.bn);
+    int kk = 0;                                   // K stages of this phase so far
     const int H = P.H, L = P.L, B = P.B;
     const unsigned rb16 = 4u * (unsigned) H;
     for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
@@ -168,35 +193,29 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
                 }
             }
         }
-        for (int kc = 0; kc < J.nK; ++kc) {
-            const unsigned s = pp.a % kBStages, ph = (pp.a / kBStages) & 1u;
-            ++pp.a;
-            if (!wait_bar(Q, S, &S.empty[s], ph ^ 1u)) return;
-            unsigned char * ahi = tiles + s * kStage;
-            const unsigned dhi = smem_u32(ahi) + (unsigned) r * 128u;
+        for (int kc = 0; kc < J.nK; ++kc, ++kk) {
+            const int s = kk % R.n;
+            const unsigned u = pp.ua[s]++;
+            if (!wait_bar(Q, S, &S.empty[s], (u & 1u) ^ 1u)) return;
+            const unsigned dhi = smem_u32(tiles + (unsigned) s * R.stage) + (unsigned) r * 128u;
             const unsigned dlo = dhi + kATile;
             if (valid) {
                 const bool seg1 = kc >= J.split;
-                if (seg1 && zero1) {
-                    for (unsigned c = 0; c < 8; ++c) {
-                        const unsigned o = (c ^ ((unsigned) r & 7u)) << 4;
-                        *reinterpret_cast<uint4 *>(ahi + r * 128 + o) = make_uint4(0u, 0u, 0u, 0u);
-                        *reinterpret_cast<uint4 *>(ahi + kATile + r * 128 + o) = make_uint4(0u, 0u, 0u, 0u);
-                    }
-                } else {
-                    const unsigned char * src = seg1 ? src1 + (size_t) (kc - J.split) * 128 : src0 + (size_t) kc * 128;
+                // a reset row reads zeros (from a zero block, so that every write of
+                // the stage is a cp.async the arrival below tracks)
+                const unsigned char * shi = (seg1 && zero1) ? g_zero128
+                                          : seg1 ? src1 + (size_t) (kc - J.split) * 128 : src0 + (size_t) kc * 128;
+                const unsigned char * slo = (seg1 && zero1) ? g_zero128 : shi + plane;
 #pragma unroll
-                    for (unsigned c = 0; c < 8; ++c) {
-                        const unsigned o = (c ^ ((unsigned) r & 7u)) << 4;
-                        cp_async16(dhi + o, src + c * 16);
-                        cp_async16(dlo + o, src + plane + c * 16);
-                    }
+                for (unsigned c = 0; c < 8; ++c) {
+                    const unsigned o = (c ^ ((unsigned) r & 7u)) << 4;
+                    cp_async16(dhi + o, shi + c * 16);
+                    cp_async16(dlo + o, slo + c * 16);
                 }
             }
-            cp_async_wait_all();
-            // this thread's generic-proxy writes (copies, zeros) before the MMAs read them
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&S.full_a[s]);
+            // no wait here: the arrival fires when the copies land (the MMA thread
+            // orders them for the tensor cores with a proxy fence after its wait)
+            cp_async_arrive(&S.full_a[s]);
         }
     }
 }
@@ -206,16 +225,18 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
 __device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, const Job & J, Pipe & pp) {
     const CUtensorMap * mhi = reinterpret_cast<const CUtensorMap *>(J.g->map_hi);
     const CUtensorMap * mlo = reinterpret_cast<const CUtensorMap *>(J.g->map_lo);
+    const Ring R = ring(J.bn);
+    int kk = 0;
     for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
         const int n0 = (t / J.nM) * J.bn;
         const int rows = min(J.bn, J.N - n0);
         const int nb = (rows + 63) / 64;
-        for (int kc = 0; kc < J.nK; ++kc) {
-            const unsigned s = pp.b % kBStages, ph = (pp.b / kBStages) & 1u;
-            ++pp.b;
-            if (!wait_bar(Q, S, &S.empty[s], ph ^ 1u)) return;
-            unsigned char * bhi = tiles + s * kStage + 2 * kATile;
-            unsigned char * blo = bhi + kBTile;
+        for (int kc = 0; kc < J.nK; ++kc, ++kk) {
+            const int s = kk % R.n;
+            const unsigned u = pp.ub[s]++;
+            if (!wait_bar(Q, S, &S.empty[s], (u & 1u) ^ 1u)) return;
+            unsigned char * bhi = tiles + (unsigned) s * R.stage + 2 * kATile;
+            unsigned char * blo = bhi + R.b_plane;
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
                          :: "r"(smem_u32(&S.full_b[s])), "r"((unsigned) nb * 2u * kBBox) : "memory");
             for (int b = 0; b < nb; ++b) {
@@ -230,6 +251,8 @@ __device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char
 // into the tile's accumulator (columns acc * 256).
 __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, unsigned tmem, const Job & J,
                          Pipe & pp) {
+    const Ring R = ring(J.bn);
+    int kk = 0;
     for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
         const int n0 = (t / J.nM) * J.bn;
         const int rows = min(J.bn, J.N - n0);
@@ -240,14 +263,17 @@ __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * til
         if (!wait_bar(Q, S, &S.acc_empty[a], aph ^ 1u)) return;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const unsigned d = tmem + a * (unsigned) kBNmax;
-        for (int kc = 0; kc < J.nK; ++kc) {
-            const unsigned s = pp.m % kBStages, ph = (pp.m / kBStages) & 1u;
-            ++pp.m;
+        for (int kc = 0; kc < J.nK; ++kc, ++kk) {
+            const int s = kk % R.n;
+            const unsigned ph = pp.um[s]++ & 1u;
             if (!wait_bar(Q, S, &S.full_a[s], ph)) return;
             if (!wait_bar(Q, S, &S.full_b[s], ph)) return;
+            // the A stage was written by cp.async in the generic proxy: make it visible
+            // to the tensor cores' (async proxy) reads
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const unsigned base = smem_u32(tiles + s * kStage);
-            const unsigned ahi = base, alo = base + kATile, bhi = base + 2 * kATile, blo = bhi + kBTile;
+            const unsigned base = smem_u32(tiles + (unsigned) s * R.stage);
+            const unsigned ahi = base, alo = base + kATile, bhi = base + 2 * kATile, blo = bhi + R.b_plane;
 #pragma unroll
             for (int k16 = 0; k16 < kBK / 16; ++k16) {
                 const unsigned ko = (unsigned) k16 * 32u;
@@ -567,12 +593,12 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
     extern __shared__ __align__(1024) unsigned char bk_raw[];
     unsigned char * tiles = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(bk_raw) + 1023) & ~(uintptr_t) 1023);
-    BulkSmem & S = *reinterpret_cast<BulkSmem *>(tiles + kBStages * kStage);
+    BulkSmem & S = *reinterpret_cast<BulkSmem *>(tiles + kRing);
     const int warp = threadIdx.x >> 5;
     const int G = (int) gridDim.x;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kBStages; ++s) {
+        for (int s = 0; s < kMaxStages; ++s) {
             mbar_init(&S.full_a[s], 128);
             mbar_init(&S.full_b[s], 1);
             mbar_init(&S.empty[s], 1);
@@ -813,7 +839,7 @@ bool bulk_supported(int H, int J, int L) {
     return H > 0 && J > 0 && H % kBK == 0 && J % kBK == 0 && L >= 1 && L <= kMaxLayers;
 }
 
-size_t bulk_smem_bytes() { return 1024 + (size_t) kBStages * kStage + sizeof(BulkSmem); }
+size_t bulk_smem_bytes() { return 1024 + (size_t) kRing + sizeof(BulkSmem); }
 
 int bulk_threads() { return kBThreads; }
 
