@@ -240,6 +240,9 @@ def main():
     ap.add_argument("--blank-bias", type=float, default=None)
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (global for configuration 5, per GPU otherwise)")
+    ap.add_argument("--bulk-min-live", type=int, default=None,
+                    help="PK_OPT_BULK_MIN_LIVE: live utterances from which iterations run on the tcgen05 "
+                         "bulk loop (library default when absent; 0 = never)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--path", default="tdt", choices=["tdt", "ctc"],
@@ -436,7 +439,7 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     torch.cuda.set_device(local_rank)
-    dec = pk.Decoder(model, device=local_rank)
+    dec = pk.Decoder(model, device=local_rank, bulk_min_live=args.bulk_min_live)
     msym = dec.info.max_symbols_per_step
     Bn = len(T)
     cap = int(pk.lib().pk_tokens_capacity(T.ctypes.data, Bn, msym))

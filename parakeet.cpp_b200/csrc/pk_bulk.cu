@@ -68,6 +68,9 @@ struct BulkSmem {
     unsigned long long empty[kMaxStages];
     unsigned long long acc_full[2];
     unsigned long long acc_empty[2];
+    const unsigned char * a_s0[kBM];   // A rows of the current tile: segment-0 source
+    const unsigned char * a_s1[kBM];   // segment-1 source
+    unsigned char a_fl[kBM];           // bit 0: row in the batch, bit 1: segment 1 is zero
     unsigned tmem_base;
     int err;                       // a wait of this CTA gave up (shared by every role)
     int scan[kBWarps + 2];
@@ -158,65 +161,77 @@ __device__ __forceinline__ bool wait_bar(const BulkParams & Q, BulkSmem & S, uns
 
 // ---- one GEMM phase ------------------------------------------------------------
 
-// A producer: thread r (warps 0-3) stages row r of every tile: 8 chunks of 16 bytes
-// per plane and K stage, at chunk c ^ (r & 7) of the row (128-byte swizzle).
+// A producer (warps 0-3): warp w stages rows 32w .. 32w + 31 of every tile. Its
+// lanes first write those rows' sources to a per-warp table in shared memory;
+// then each K stage takes 8 rounds of 4 rows x 8 lanes, each lane one 16-byte
+// chunk per plane, so that a round reads 4 whole 128-byte row segments
+// (coalesced) and writes chunk c of row r at chunk c ^ (r & 7) (128-byte swizzle).
 __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, const Job & J, Pipe & pp) {
     const LoopParams & P = Q.P;
-    const int r = threadIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const Ring R = ring(J.bn);
     int kk = 0;                                   // K stages of this phase so far
     const int H = P.H, L = P.L, B = P.B;
     const unsigned rb16 = 4u * (unsigned) H;
+    const unsigned plane = J.kind == G_JOINT ? 2u * (unsigned) P.J : 2u * (unsigned) H;
     for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
-        const int row = (t % J.nM) * kBM + r;
-        const bool valid = row < J.M;
-        // per-row sources: segment 0 for K stages [0, split), segment 1 for the rest;
-        // plane offset = bytes from the hi part to the lo part of a source row
-        const unsigned char * src0 = nullptr;
-        const unsigned char * src1 = nullptr;
-        unsigned plane = 0;
-        bool zero1 = false;
-        if (valid) {
-            if (J.kind == G_JOINT) {
-                src1 = P.hidc + (size_t) row * P.rbj;
-                plane = 2u * (unsigned) P.J;
-            } else {
-                const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + row);
-                plane = 2u * (unsigned) H;
-                if (J.kind == G_PRED) {
-                    src1 = Q.x16 + ((size_t) (L - 1) * B + row) * rb16;
+        {   // this warp's rows: segment 0 for K stages [0, split), segment 1 for the rest
+            const int lr = warp * 32 + lane;
+            const int row = (t % J.nM) * kBM + lr;
+            const unsigned char * src0 = nullptr;
+            const unsigned char * src1 = nullptr;
+            unsigned char fl = 0;                 // bit 0: row in the batch, bit 1: segment 1 is zero
+            if (row < J.M) {
+                fl = 1;
+                if (J.kind == G_JOINT) {
+                    src1 = P.hidc + (size_t) row * P.rbj;
                 } else {
-                    const int hb = (e.y >> 30) & 1;
-                    zero1 = e.y < 0;                    // reset: h_prev = 0
-                    src1 = Q.h16 + (((size_t) (hb ^ 1) * L + J.l) * B + e.x) * rb16;
-                    if (J.l > 0) src0 = Q.x16 + ((size_t) (J.l - 1) * B + row) * rb16;
+                    const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + row);
+                    if (J.kind == G_PRED) {
+                        src1 = Q.x16 + ((size_t) (L - 1) * B + row) * rb16;
+                    } else {
+                        const int hb = (e.y >> 30) & 1;
+                        if (e.y < 0) fl |= 2;             // reset: h_prev = 0
+                        src1 = Q.h16 + (((size_t) (hb ^ 1) * L + J.l) * B + e.x) * rb16;
+                        if (J.l > 0) src0 = Q.x16 + ((size_t) (J.l - 1) * B + row) * rb16;
+                    }
                 }
             }
+            S.a_s0[lr] = src0;
+            S.a_s1[lr] = src1;
+            S.a_fl[lr] = fl;
+            __syncwarp();
         }
         for (int kc = 0; kc < J.nK; ++kc, ++kk) {
             const int s = kk % R.n;
             const unsigned u = pp.ua[s]++;
-            if (!wait_bar(Q, S, &S.empty[s], (u & 1u) ^ 1u)) return;
-            const unsigned dhi = smem_u32(tiles + (unsigned) s * R.stage) + (unsigned) r * 128u;
-            const unsigned dlo = dhi + kATile;
-            if (valid) {
-                const bool seg1 = kc >= J.split;
-                // a reset row reads zeros (from a zero block, so that every write of
-                // the stage is a cp.async the arrival below tracks)
-                const unsigned char * shi = (seg1 && zero1) ? g_zero128
-                                          : seg1 ? src1 + (size_t) (kc - J.split) * 128 : src0 + (size_t) kc * 128;
-                const unsigned char * slo = (seg1 && zero1) ? g_zero128 : shi + plane;
+            const bool ok = wait_bar(Q, S, &S.empty[s], (u & 1u) ^ 1u);
+            if (!__all_sync(0xFFFFFFFFu, ok)) return;
+            const bool seg1 = kc >= J.split;
+            const unsigned dst = smem_u32(tiles + (unsigned) s * R.stage);
+            const unsigned sub = (unsigned) lane & 7u;
 #pragma unroll
-                for (unsigned c = 0; c < 8; ++c) {
-                    const unsigned o = (c ^ ((unsigned) r & 7u)) << 4;
-                    cp_async16(dhi + o, shi + c * 16);
-                    cp_async16(dlo + o, slo + c * 16);
+            for (int k = 0; k < 8; ++k) {
+                const int lr = warp * 32 + k * 4 + (lane >> 3);
+                const unsigned char fl = S.a_fl[lr];
+                if (fl & 1) {
+                    // a reset row reads zeros (from a zero block, so that every write of
+                    // the stage is a cp.async the arrival below tracks)
+                    const bool zero = seg1 && (fl & 2);
+                    const unsigned char * shi = zero ? g_zero128
+                                              : seg1 ? S.a_s1[lr] + (size_t) (kc - J.split) * 128
+                                                     : S.a_s0[lr] + (size_t) kc * 128;
+                    const unsigned char * slo = zero ? g_zero128 : shi + plane;
+                    const unsigned o = (unsigned) lr * 128u + ((sub ^ ((unsigned) lr & 7u)) << 4);
+                    cp_async16(dst + o, shi + sub * 16);
+                    cp_async16(dst + kATile + o, slo + sub * 16);
                 }
             }
             // no wait here: the arrival fires when the copies land (the MMA thread
             // orders them for the tensor cores with a proxy fence after its wait)
             cp_async_arrive(&S.full_a[s]);
         }
+        __syncwarp();                             // every lane is done with the table
     }
 }
 
