@@ -200,9 +200,13 @@ typedef struct pk_result {
     double    total_ms;           /* device time of the whole call incl. copies */
     double    bulk_ms;            /* device time of the tcgen05 bulk loop (PK_OPT_BULK_MIN_LIVE), 0 if it did not run */
     int64_t   bulk_iterations;    /* loop iterations that ran on the bulk loop (included in loop_iterations) */
-    double    bulk_phase_ms[12];  /* bulk loop breakdown seen by CTA 0 (%globaltimer): for the LSTM layers,
-                                     pred-proj, joint hidden, joint, decision and list compaction,
-                                     [2i] = CTA 0's own share, [2i+1] = the grid barrier after it */
+    double    bulk_phase_ms[20];  /* bulk loop breakdown seen by CTA 0 (%globaltimer): [0..11] for the LSTM
+                                     layers, pred-proj, joint hidden, joint, decision and list
+                                     compaction, [2i] = CTA 0's own share, [2i+1] = the grid barrier
+                                     after it; [12..19] inside its GEMM phases: A staging waiting for a
+                                     free stage, weight loads waiting, MMA issue waiting for A, for the
+                                     weights, for a free accumulator, epilogue waiting for an
+                                     accumulator, epilogue work, MMA issue */
 } pk_result;
 
 /* Greedy decode of B fresh utterances (each starts from tdt_init_state /

@@ -489,7 +489,7 @@ struct Run {
     std::vector<int32_t> ust;
     std::vector<int32_t> ctl;
     unsigned long long prof[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    unsigned long long bprof[12] = {};
+    unsigned long long bprof[20] = {};
     float ms_encproj = 0.f, ms_loop = 0.f, ms_bulk = 0.f;
     int launches = 0;          // kernels launched by this call
 };
@@ -719,8 +719,8 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         q.h16 = x->h16.as<unsigned char>();
         q.x16 = x->x16.as<unsigned char>();
         q.dcount = x->dcount.as<int2>();
-        PK_CK(x->bprof.ensure(12 * 8));
-        PK_CK(cudaMemsetAsync(x->bprof.p, 0, 12 * 8, s));
+        PK_CK(x->bprof.ensure(20 * 8));
+        PK_CK(cudaMemsetAsync(x->bprof.p, 0, 20 * 8, s));
         q.prof = x->bprof.as<unsigned long long>();
         P.resume = 1;
     }
@@ -740,7 +740,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     if (B > 0) PK_CK(cudaMemcpyAsync(r.ust.data(), x->ust.p, (size_t) B * kUst * 4, cudaMemcpyDeviceToHost, s));
     PK_CK(cudaMemcpyAsync(r.ctl.data(), x->ctl.p, kCtl * 4, cudaMemcpyDeviceToHost, s));
     PK_CK(cudaMemcpyAsync(r.prof, x->prof.p, 8 * 8, cudaMemcpyDeviceToHost, s));
-    if (use_bulk) PK_CK(cudaMemcpyAsync(r.bprof, x->bprof.p, 12 * 8, cudaMemcpyDeviceToHost, s));
+    if (use_bulk) PK_CK(cudaMemcpyAsync(r.bprof, x->bprof.p, 20 * 8, cudaMemcpyDeviceToHost, s));
     PK_CK(cudaStreamSynchronize(s));
     PK_CK(cudaEventElapsedTime(&r.ms_encproj, x->ev[1], x->ev[2]));
     PK_CK(cudaEventElapsedTime(&r.ms_loop, x->ev[3], x->ev[4]));
@@ -795,7 +795,7 @@ pk_status emit_results(pk_ctx * x, Run & r, pk_result * res) {
     res->loop_ms = r.ms_loop;
     res->bulk_ms = r.ms_bulk;
     res->bulk_iterations = r.ctl[C_BULKITERS];
-    for (int i = 0; i < 12; ++i) res->bulk_phase_ms[i] = (double) r.bprof[i] * 1e-6;
+    for (int i = 0; i < 20; ++i) res->bulk_phase_ms[i] = (double) r.bprof[i] * 1e-6;
     if (ntok > res->tokens_cap || (ntok > 0 && !res->tokens))
         return fail(PK_ERR_CAPACITY, "token buffer holds %lld, %lld needed", (long long) res->tokens_cap,
                     (long long) ntok);

@@ -71,6 +71,7 @@ struct BulkSmem {
     const unsigned char * a_s0[kBM];   // A rows of the current tile: segment-0 source
     const unsigned char * a_s1[kBM];   // segment-1 source
     unsigned char a_fl[kBM];           // bit 0: row in the batch, bit 1: segment 1 is zero
+    unsigned long long rprof[8];       // CTA 0, per role: waits and work inside the GEMM phases (ns)
     unsigned tmem_base;
     int err;                       // a wait of this CTA gave up (shared by every role)
     int scan[kBWarps + 2];
@@ -161,6 +162,26 @@ __device__ __forceinline__ bool wait_bar(const BulkParams & Q, BulkSmem & S, uns
 
 // ---- one GEMM phase ------------------------------------------------------------
 
+// Role timing of CTA 0 (one thread per role adds to S.rprof[slot]): 0 A producer
+// waiting for a free stage, 1 B producer waiting, 2 MMA waiting for A, 3 MMA waiting
+// for B, 4 MMA waiting for a free accumulator, 5 epilogue waiting for an
+// accumulator, 6 epilogue work, 7 MMA issue.
+struct RoleClock {
+    bool on;
+    unsigned long long t;
+    __device__ __forceinline__ explicit RoleClock(bool enable) : on(enable), t(enable ? gtimer() : 0ull) {}
+    __device__ __forceinline__ void add(BulkSmem & S, int slot) {
+        if (on) {
+            const unsigned long long n = gtimer();
+            S.rprof[slot] += n - t;
+            t = n;
+        }
+    }
+    __device__ __forceinline__ void skip() {
+        if (on) t = gtimer();
+    }
+};
+
 // A producer (warps 0-3): warp w stages rows 32w .. 32w + 31 of every tile. Its
 // lanes first write those rows' sources to a per-warp table in shared memory;
 // then each K stage takes 8 rounds of 4 rows x 8 lanes, each lane one 16-byte
@@ -205,7 +226,9 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
         for (int kc = 0; kc < J.nK; ++kc, ++kk) {
             const int s = kk % R.n;
             const unsigned u = pp.ua[s]++;
+            RoleClock rc(Q.prof != nullptr && blockIdx.x == 0 && threadIdx.x == 0);
             const bool ok = wait_bar(Q, S, &S.empty[s], (u & 1u) ^ 1u);
+            rc.add(S, 0);
             if (!__all_sync(0xFFFFFFFFu, ok)) return;
             const bool seg1 = kc >= J.split;
             const unsigned dst = smem_u32(tiles + (unsigned) s * R.stage);
@@ -249,7 +272,9 @@ __device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char
         for (int kc = 0; kc < J.nK; ++kc, ++kk) {
             const int s = kk % R.n;
             const unsigned u = pp.ub[s]++;
+            RoleClock rc(Q.prof != nullptr && blockIdx.x == 0);
             if (!wait_bar(Q, S, &S.empty[s], (u & 1u) ^ 1u)) return;
+            rc.add(S, 1);
             unsigned char * bhi = tiles + (unsigned) s * R.stage + 2 * kATile;
             unsigned char * blo = bhi + R.b_plane;
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
@@ -275,14 +300,19 @@ __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * til
         const unsigned idesc = umma_idesc_f16(kBM, nmma);
         const unsigned a = pp.acc_m & 1u, aph = (pp.acc_m >> 1) & 1u;
         ++pp.acc_m;
+        RoleClock rc(Q.prof != nullptr && blockIdx.x == 0);
         if (!wait_bar(Q, S, &S.acc_empty[a], aph ^ 1u)) return;
+        rc.add(S, 4);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const unsigned d = tmem + a * (unsigned) kBNmax;
         for (int kc = 0; kc < J.nK; ++kc, ++kk) {
             const int s = kk % R.n;
             const unsigned ph = pp.um[s]++ & 1u;
+            rc.skip();
             if (!wait_bar(Q, S, &S.full_a[s], ph)) return;
+            rc.add(S, 2);
             if (!wait_bar(Q, S, &S.full_b[s], ph)) return;
+            rc.add(S, 3);
             // the A stage was written by cp.async in the generic proxy: make it visible
             // to the tensor cores' (async proxy) reads
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -297,6 +327,7 @@ __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * til
                 umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
             }
             umma_commit(&S.empty[s]);      // the stage is free once these MMAs have read it
+            rc.add(S, 7);
         }
         umma_commit(&S.acc_full[a]);       // the tile's accumulator is complete
     }
@@ -461,13 +492,16 @@ __device__ void gemm_epilogue(const BulkParams & Q, BulkSmem & S, unsigned tmem,
         const int rows = min(J.bn, J.N - n0);
         const unsigned a = pp.acc_e & 1u, aph = (pp.acc_e >> 1) & 1u;
         ++pp.acc_e;
+        RoleClock rc(Q.prof != nullptr && blockIdx.x == 0 && threadIdx.x == 256);
         if (!wait_bar(Q, S, &S.acc_full[a], aph)) return;
+        rc.add(S, 5);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const unsigned tacc = tmem + ((unsigned) (quarter * 32) << 16) + a * (unsigned) kBNmax;
         if (J.kind == G_LSTM) epi_lstm(Q, J, tacc, row, n0, rows);
         else if (J.kind == G_PRED) epi_pred(Q, J, tacc, row, n0, rows);
         else epi_joint(Q, J, tacc, row, n0, rows, keys);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        rc.add(S, 6);
         mbar_arrive(&S.acc_empty[a]);
     }
 }
@@ -623,6 +657,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
             mbar_init(&S.acc_empty[a], 128);
         }
         S.err = 0;
+        for (int i = 0; i < 8; ++i) S.rprof[i] = 0ull;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 5) {
@@ -796,8 +831,12 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
         if (!bulk_barrier(Q, S, nbar)) break;
         mark(11);
     }
-    if (prof)
+    if (prof) {
         for (int i = 0; i < 12; ++i) Q.prof[i] = pacc[i];
+    }
+    __syncthreads();
+    if (prof)
+        for (int i = 0; i < 8; ++i) Q.prof[12 + i] = S.rprof[i];
 
     // ---- teardown: every role is done with tensor memory ----
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

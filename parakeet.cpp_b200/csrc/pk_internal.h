@@ -160,7 +160,7 @@ struct BulkParams {
     unsigned char * h16;       // [2][L][B] rows of 4H bytes: f16 hi[H] | lo[H] of h, by utterance
     unsigned char * x16;       // [L][B] rows, same layout: layer l's new h by emit-list index
     int2 * dcount;             // [grid] each CTA's (emit, live) counts from the decision
-    unsigned long long * prof; // [12] CTA 0's time per phase (ns), see pk_result::bulk_phase_ms
+    unsigned long long * prof; // [20] CTA 0: time per phase and per GEMM role (ns), see pk_result::bulk_phase_ms
 };
 
 // Device-side bulk weights of a context (built once at pk_create).
