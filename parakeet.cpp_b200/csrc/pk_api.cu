@@ -716,6 +716,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         q.gp = x->bulk.gp;
         q.gj = x->bulk.gj;
         q.lbias = x->bulk.lbias;
+        q.e16 = x->bulk.e16;
         q.h16 = x->h16.as<unsigned char>();
         q.x16 = x->x16.as<unsigned char>();
         q.dcount = x->dcount.as<int2>();
@@ -1010,8 +1011,8 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
                 wih[l] = x->w_ih[l].as<float>(); whh[l] = x->w_hh[l].as<float>();
                 bih[l] = x->b_ih[l].as<float>(); bhh[l] = x->b_hh[l].as<float>();
             }
-            if (bulk_prepare(x->bulk, x->H, x->J, x->L, x->Vo, wih, whh, bih, bhh, x->pred_w.as<float>(),
-                             x->out_w.as<float>(), x->stream) != cudaSuccess) {
+            if (bulk_prepare(x->bulk, x->H, x->J, x->L, x->Vo, x->V1, x->embed.as<float>(), wih, whh, bih, bhh,
+                             x->pred_w.as<float>(), x->out_w.as<float>(), x->stream) != cudaSuccess) {
                 bulk_release(x->bulk);
                 return cleanup(fail(PK_ERR_CUDA, "bulk-loop weight preparation failed"));
             }

@@ -16,10 +16,10 @@
 // state, lists and control words left here (LoopParams::resume).
 //
 // Per iteration (same order and semantics as the persistent loop):
-//   LSTM layer l   gates[e] = W_hh h_prev (+ W_ih x) for the emit list, then the
-//                  cell update in the epilogue (host_lstm_step,
-//                  src/parakeet_tdt.cpp:106-142; layer 0's b_ih + W_ih x comes from the
-//                  per-token table g0 exactly as in the persistent loop)
+//   LSTM layer l   gates[e] = W_ih x + W_hh h_prev for the emit list (x = the token's
+//                  embedding row for layer 0, the new h of layer l-1 above), then the
+//                  cell update with b_ih + b_hh in the epilogue (host_lstm_step,
+//                  src/parakeet_tdt.cpp:106-142)
 //   pred           predp[utt] = b_pred + W_pred h[L-1] for the emit list
 //   hidden         hidc[i] = relu(encp[t_i] + predp[utt_i]) for the live list
 //                  (host_joint_step, :154-177)
@@ -120,7 +120,7 @@ __device__ __forceinline__ Job make_job(const BulkParams & Q, int kind, int l, i
     j.N = j.g->N;
     j.nK = j.g->K / kBK;
     j.nM = (M + kBM - 1) / kBM;
-    j.split = (kind == G_LSTM && l > 0) ? Q.P.H / kBK : 0;
+    j.split = kind == G_LSTM ? Q.P.H / kBK : 0;   // LSTM: K = [x | h_prev]
     // tile width: fewest rounds of tiles over the CTAs, counting ~32 columns of
     // fixed cost per tile (pipeline fill and drain)
     const int G = (int) gridDim.x;
@@ -214,7 +214,8 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
                         const int hb = (e.y >> 30) & 1;
                         if (e.y < 0) fl |= 2;             // reset: h_prev = 0
                         src1 = Q.h16 + (((size_t) (hb ^ 1) * L + J.l) * B + e.x) * rb16;
-                        if (J.l > 0) src0 = Q.x16 + ((size_t) (J.l - 1) * B + row) * rb16;
+                        src0 = J.l > 0 ? Q.x16 + ((size_t) (J.l - 1) * B + row) * rb16
+                                       : Q.e16 + (size_t) (e.y & 0x3FFFFFFF) * rb16;
                     }
                 }
             }
@@ -365,65 +366,94 @@ __device__ __forceinline__ void split8(const float (&x)[8], uint4 & hi, uint4 & 
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// Epilogue of the LSTM layer: the tile's columns are gates (i, f, g, o) of units
-// [n0 / 4, (n0 + rows) / 4); row = emit-list index.
+// Logistic and tanh from the hardware exponential (relative error ~1e-6, against
+// a tolerance of 2e-3 on the state; both saturate correctly for large |x|).
+__device__ __forceinline__ float sig_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, 1.0f + __expf(2.0f * x)); }
+
+// The persistent loop's staged row of 8 new h values at unit j0 (it continues the
+// batch): int16 fixed point as two int8 digit planes, or the f16 hi / lo halves.
+__device__ __forceinline__ void put_h8(const LoopParams & P, unsigned char * row, int j0, const float (&hn)[8],
+                                       const uint4 & hi, const uint4 & lo) {
+    if (P.h_int) {
+        unsigned dh[2] = {0u, 0u}, dl[2] = {0u, 0u};
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int q16 = max(-32767, min(32767, __float2int_rn(hn[u] * 32768.0f)));
+            dh[u >> 2] |= ((unsigned) (q16 >> 8) & 255u) << (8 * (u & 3));
+            dl[u >> 2] |= ((unsigned) q16 & 255u) << (8 * (u & 3));
+        }
+        *reinterpret_cast<uint2 *>(row + j0) = make_uint2(dh[0], dh[1]);
+        *reinterpret_cast<uint2 *>(row + P.H + j0) = make_uint2(dl[0], dl[1]);
+    } else {
+        *reinterpret_cast<uint4 *>(row + 2 * j0) = hi;
+        *reinterpret_cast<uint4 *>(row + 2 * P.H + 2 * j0) = lo;
+    }
+}
+
+// Epilogue of an LSTM layer: the tile's columns are gates (i, f, g, o) of units
+// [n0 / 4, (n0 + rows) / 4); row = emit-list index. Every 8 units take one
+// tensor-memory load of their 32 gate sums; their old cell state was requested
+// one group earlier.
 __device__ __forceinline__ void epi_lstm(const BulkParams & Q, const Job & J, unsigned tacc, int row, int n0, int rows) {
     const LoopParams & P = Q.P;
     const int H = P.H, L = P.L, B = P.B, l = J.l;
     const bool valid = row < J.M;
-    int utt = 0, tok = 0, hb = 0, reset = 0;
+    int utt = 0, hb = 0, reset = 1;
     if (valid) {
         const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + row);
         utt = e.x;
-        tok = e.y & 0x3FFFFFFF;
         hb = (e.y >> 30) & 1;
         reset = e.y < 0 ? 1 : 0;
     }
     const unsigned rb16 = 4u * (unsigned) H;
+    const float * crow = P.c + ((size_t) l * B + utt) * H;
+    float * cw = P.c + ((size_t) l * B + utt) * H;
+    float * hw = P.h + (((size_t) hb * L + l) * B + utt) * H;
+    unsigned char * st = Q.h16 + (((size_t) hb * L + l) * B + utt) * rb16;
+    unsigned char * xn = Q.x16 + ((size_t) l * B + row) * rb16;
+    unsigned char * hrow = P.hst + ((((size_t) hb * L + l) * B + utt) * P.rbh);
+    const float * bias = Q.lbias + (size_t) l * 4 * H;
+    // next group's old cell state is requested before this group's tensor-memory load
+    float4 cn0 = make_float4(0.f, 0.f, 0.f, 0.f), cn1 = cn0;
+    if (valid && !reset && rows > 0) {
+        cn0 = __ldcg(reinterpret_cast<const float4 *>(crow + (n0 >> 2)));
+        cn1 = __ldcg(reinterpret_cast<const float4 *>(crow + (n0 >> 2)) + 1);
+    }
     for (int c0 = 0; c0 < rows; c0 += 32) {
+        const float4 co0 = cn0, co1 = cn1;
+        if (valid && !reset && c0 + 32 < rows) {
+            cn0 = __ldcg(reinterpret_cast<const float4 *>(crow + ((n0 + c0 + 32) >> 2)));
+            cn1 = __ldcg(reinterpret_cast<const float4 *>(crow + ((n0 + c0 + 32) >> 2)) + 1);
+        }
         float v[32];
-        tmem_ld32(tacc + (unsigned) c0, v);            // warp-wide: every lane takes part
+        tmem_ld32(tacc + (unsigned) c0, v);                 // warp-wide: every lane takes part
         if (!valid) continue;
-        const int j0 = (n0 + c0) >> 2;                  // first of the 8 units in these columns
-        if (j0 >= H) continue;
+        const int j0 = (n0 + c0) >> 2;                      // first of the 8 units in these columns
+        const float4 * b4 = reinterpret_cast<const float4 *>(bias + 4 * j0);
+        const float cold[8] = {co0.x, co0.y, co0.z, co0.w, co1.x, co1.y, co1.z, co1.w};
         float hn[8], cn[8];
-        const float * bias = Q.lbias + (size_t) l * 4 * H + 4 * j0;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-            const int j = j0 + u;
-            float g[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                float pre = __ldg(bias + 4 * u + q);
-                if (l == 0) pre += __ldg(P.g0 + (size_t) tok * 4 * H + q * H + j);
-                g[q] = pre + v[4 * u + q];
-            }
-            const float i_g = sigmoid_ref(g[0]);
-            const float f_g = sigmoid_ref(g[1]);
-            const float g_g = tanhf(g[2]);
-            const float o_g = sigmoid_ref(g[3]);
-            const float c_old = reset ? 0.0f : __ldcg(P.c + ((size_t) l * B + utt) * H + j);
-            cn[u] = f_g * c_old + i_g * g_g;
-            hn[u] = o_g * tanhf(cn[u]);
+            const float4 bb = __ldg(b4 + u);
+            const float i_g = sig_fast(bb.x + v[4 * u + 0]);
+            const float f_g = sig_fast(bb.y + v[4 * u + 1]);
+            const float g_g = tanh_fast(bb.z + v[4 * u + 2]);
+            const float o_g = sig_fast(bb.w + v[4 * u + 3]);
+            cn[u] = f_g * cold[u] + i_g * g_g;
+            hn[u] = o_g * tanh_fast(cn[u]);
         }
-        float * cp = P.c + ((size_t) l * B + utt) * H + j0;
-        float * hp = P.h + (((size_t) hb * L + l) * B + utt) * H + j0;
-        reinterpret_cast<float4 *>(cp)[0] = make_float4(cn[0], cn[1], cn[2], cn[3]);
-        reinterpret_cast<float4 *>(cp)[1] = make_float4(cn[4], cn[5], cn[6], cn[7]);
-        reinterpret_cast<float4 *>(hp)[0] = make_float4(hn[0], hn[1], hn[2], hn[3]);
-        reinterpret_cast<float4 *>(hp)[1] = make_float4(hn[4], hn[5], hn[6], hn[7]);
+        reinterpret_cast<float4 *>(cw + j0)[0] = make_float4(cn[0], cn[1], cn[2], cn[3]);
+        reinterpret_cast<float4 *>(cw + j0)[1] = make_float4(cn[4], cn[5], cn[6], cn[7]);
+        reinterpret_cast<float4 *>(hw + j0)[0] = make_float4(hn[0], hn[1], hn[2], hn[3]);
+        reinterpret_cast<float4 *>(hw + j0)[1] = make_float4(hn[4], hn[5], hn[6], hn[7]);
         uint4 hi, lo;
         split8(hn, hi, lo);
-        unsigned char * st = Q.h16 + (((size_t) hb * L + l) * B + utt) * rb16;
-        unsigned char * xn = Q.x16 + ((size_t) l * B + row) * rb16;
         *reinterpret_cast<uint4 *>(st + 2 * j0) = hi;
         *reinterpret_cast<uint4 *>(st + 2 * H + 2 * j0) = lo;
         *reinterpret_cast<uint4 *>(xn + 2 * j0) = hi;
         *reinterpret_cast<uint4 *>(xn + 2 * H + 2 * j0) = lo;
-        // the persistent loop's staged state row (it continues the batch)
-        unsigned char * hrow = P.hst + ((((size_t) hb * L + l) * B + utt) * P.rbh);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) put_h(P, hrow, j0 + u, hn[u]);
+        put_h8(P, hrow, j0, hn, hi, lo);
     }
 }
 
@@ -446,6 +476,10 @@ __device__ __forceinline__ void epi_pred(const BulkParams & Q, const Job & J, un
     }
 }
 
+// Joint epilogue: logits = bias + acc over the tile's rows of joint.out; the first
+// index of the largest token logit and of the largest duration logit of the tile
+// (strict >, in index order, as argmax_f32 scans) become one 64-bit key each,
+// max-reduced over the tiles of the row.
 __device__ __forceinline__ void epi_joint(const BulkParams & Q, const Job & J, unsigned tacc, int row, int n0,
                                           int rows, unsigned long long * keys) {
     const LoopParams & P = Q.P;
@@ -455,30 +489,45 @@ __device__ __forceinline__ void epi_joint(const BulkParams & Q, const Job & J, u
         utt = __ldcg(P.live + (size_t) J.sel * P.B + row);
         if (P.trace_steps > 0) step = __ldcg(&P.ust[utt * kUst + U_STEPS]);
     }
-    unsigned long long bt = 0ull, bd = 0ull;
+    const bool tr = valid && P.trace_steps > 0 && step < P.trace_steps;
+    float bt = 0.0f, bd = 0.0f;
+    int it = -1, id = -1;
     for (int c0 = 0; c0 < rows; c0 += 32) {
         float v[32];
         tmem_ld32(tacc + (unsigned) c0, v);
         if (!valid) continue;
+        const int r0 = n0 + c0;
+        const bool full = r0 + 32 <= P.Vo;
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-            const int r = n0 + c0 + q;
-            if (r >= P.Vo) break;
-            const float logit = __ldg(P.out_b + r) + v[q];
-            if (P.trace_steps > 0 && step < P.trace_steps)
-                P.tr_logits[((size_t) utt * P.trace_steps + step) * P.Vo + r] = logit;
-            if (r < P.V1) {
-                const unsigned long long k = make_key(logit, r);
-                bt = k > bt ? k : bt;
+        for (int k = 0; k < 8; ++k) {
+            float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (full) {
+                bb = __ldg(reinterpret_cast<const float4 *>(P.out_b + r0) + k);
             } else {
-                const unsigned long long k = make_key(logit, r - P.V1);
-                bd = k > bd ? k : bd;
+                const int r = r0 + 4 * k;
+                bb.x = r < P.Vo ? __ldg(P.out_b + r) : 0.f;
+                bb.y = r + 1 < P.Vo ? __ldg(P.out_b + r + 1) : 0.f;
+                bb.z = r + 2 < P.Vo ? __ldg(P.out_b + r + 2) : 0.f;
+                bb.w = r + 3 < P.Vo ? __ldg(P.out_b + r + 3) : 0.f;
+            }
+            const float lg[4] = {bb.x + v[4 * k], bb.y + v[4 * k + 1], bb.z + v[4 * k + 2], bb.w + v[4 * k + 3]};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int r = r0 + 4 * k + q;
+                if (r < P.Vo) {
+                    if (tr) P.tr_logits[((size_t) utt * P.trace_steps + step) * P.Vo + r] = lg[q];
+                    if (r < P.V1) {
+                        if (it < 0 || lg[q] > bt) { bt = lg[q]; it = r; }
+                    } else {
+                        if (id < 0 || lg[q] > bd) { bd = lg[q]; id = r - P.V1; }
+                    }
+                }
             }
         }
     }
     if (valid) {
-        if (bt) atomicMax(&keys[2 * utt + 0], bt);
-        if (bd) atomicMax(&keys[2 * utt + 1], bd);
+        if (it >= 0) atomicMax(&keys[2 * utt + 0], make_key(bt, it));
+        if (id >= 0) atomicMax(&keys[2 * utt + 1], make_key(bd, id));
     }
 }
 
@@ -876,12 +925,25 @@ __global__ void bulk_split_rows(const float * __restrict__ w, long long n, __hal
     }
 }
 
-__global__ void bulk_lstm_bias(const float * __restrict__ b_ih, const float * __restrict__ b_hh, int H, int first,
+__global__ void bulk_lstm_bias(const float * __restrict__ b_ih, const float * __restrict__ b_hh, int H,
                                float * __restrict__ out) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= 4 * H) return;
     const int src = (r & 3) * H + (r >> 2);
-    out[r] = first ? b_hh[src] : b_ih[src] + b_hh[src];
+    out[r] = b_ih[src] + b_hh[src];
+}
+
+// Embedding rows [V1][H] f32 -> rows of 4H bytes: f16 hi[H] | lo[H].
+__global__ void bulk_split_embed(const float * __restrict__ e, long long n, int H, unsigned char * __restrict__ out) {
+    for (long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x) {
+        const long long v = i / H;
+        const int j = (int) (i - v * H);
+        const float x = e[i];
+        const __half h = __float2half_rn(x);
+        __half * row = reinterpret_cast<__half *>(out + v * 4LL * H);
+        row[j] = h;
+        row[H + j] = __float2half_rn(x - __half2float(h));
+    }
 }
 
 }  // namespace
@@ -910,11 +972,11 @@ void bulk_release(BulkWeights & w) {
     w = BulkWeights{};
 }
 
-cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, const float * const * w_ih,
-                         const float * const * w_hh, const float * const * b_ih, const float * const * b_hh,
-                         const float * pred_w, const float * out_w, cudaStream_t s) {
+cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
+                         const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
+                         const float * const * b_hh, const float * pred_w, const float * out_w, cudaStream_t s) {
     bulk_release(w);
-    // layout: [maps: (L + 2) x 2 x 128 B][lbias L x 4H f32][halves]
+    // layout: [maps: (L + 2) x 2 x 128 B][lbias L x 4H f32][embedding halves][weight halves]
     const int nmat = L + 2;
     size_t off = 0;
     const size_t maps = off;
@@ -922,9 +984,12 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, const flo
     const size_t bias = off;
     off += (size_t) L * 4 * H * 4;
     off = (off + 255) & ~(size_t) 255;
+    const size_t emb = off;
+    off += (size_t) V1 * 4 * H;
+    off = (off + 255) & ~(size_t) 255;
     size_t mat_off[kMaxLayers + 2];
     long long mat_rows[kMaxLayers + 2], mat_k[kMaxLayers + 2];
-    for (int l = 0; l < L; ++l) { mat_rows[l] = 4LL * H; mat_k[l] = l == 0 ? H : 2LL * H; }
+    for (int l = 0; l < L; ++l) { mat_rows[l] = 4LL * H; mat_k[l] = 2LL * H; }   // K = [W_ih | W_hh]
     mat_rows[L] = J; mat_k[L] = H;            // pred
     mat_rows[L + 1] = Vo; mat_k[L + 1] = J;   // joint
     for (int m = 0; m < nmat; ++m) {
@@ -941,7 +1006,7 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, const flo
         __half * hi = reinterpret_cast<__half *>(base + mat_off[m]);
         __half * lo = hi + mat_rows[m] * mat_k[m];
         if (m < L) {
-            bulk_split_lstm<<<1184, 256, 0, s>>>(m == 0 ? nullptr : w_ih[m], w_hh[m], H, m == 0 ? 0 : H, hi, lo);
+            bulk_split_lstm<<<1184, 256, 0, s>>>(w_ih[m], w_hh[m], H, H, hi, lo);
         } else {
             bulk_split_rows<<<1184, 256, 0, s>>>(m == L ? pred_w : out_w, mat_rows[m] * mat_k[m], hi, lo);
         }
@@ -963,11 +1028,15 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, const flo
         else w.gj = g;
     }
     for (int l = 0; l < L; ++l) {
-        bulk_lstm_bias<<<(4 * H + 255) / 256, 256, 0, s>>>(b_ih[l], b_hh[l], H, l == 0 ? 1 : 0,
+        bulk_lstm_bias<<<(4 * H + 255) / 256, 256, 0, s>>>(b_ih[l], b_hh[l], H,
                                                            reinterpret_cast<float *>(base + bias) + (size_t) l * 4 * H);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
+    bulk_split_embed<<<1184, 256, 0, s>>>(embed, (long long) V1 * H, H, base + emb);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    w.e16 = base + emb;
     w.lbias = reinterpret_cast<const float *>(base + bias);
     e = cudaMemcpyAsync(base + maps, host_maps.data(), host_maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return e;

@@ -153,10 +153,11 @@ struct BulkGemm {
 struct BulkParams {
     LoopParams P;              // lists, state, outputs and control words shared with the persistent loop
     int min_live;              // iterate while at least this many utterances are live
-    BulkGemm gl[kMaxLayers];   // LSTM layer l: rows 4j + q = gate q of unit j; K = [W_ih | W_hh] (layer 0: W_hh)
+    BulkGemm gl[kMaxLayers];   // LSTM layer l: rows 4j + q = gate q of unit j; K = [W_ih | W_hh]
     BulkGemm gp;               // joint.pred [J][H]
     BulkGemm gj;               // joint.out [Vo][J]
-    const float * lbias;       // [L][4H] gate biases in the same row order: layer 0 b_hh, above b_ih + b_hh
+    const float * lbias;       // [L][4H] gate biases b_ih + b_hh in the same row order
+    const unsigned char * e16; // [V+1] rows of 4H bytes: f16 hi | lo of the embedding (layer 0's x)
     unsigned char * h16;       // [2][L][B] rows of 4H bytes: f16 hi[H] | lo[H] of h, by utterance
     unsigned char * x16;       // [L][B] rows, same layout: layer l's new h by emit-list index
     int2 * dcount;             // [grid] each CTA's (emit, live) counts from the decision
@@ -168,12 +169,13 @@ struct BulkWeights {
     void * mem = nullptr;      // one allocation: f16 halves, biases, TMA descriptors
     BulkGemm gl[kMaxLayers]{}, gp{}, gj{};
     const float * lbias = nullptr;
+    const unsigned char * e16 = nullptr;
     size_t bytes = 0;
 };
 bool        bulk_supported(int H, int J, int L);
-cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, const float * const * w_ih,
-                         const float * const * w_hh, const float * const * b_ih, const float * const * b_hh,
-                         const float * pred_w, const float * out_w, cudaStream_t s);
+cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
+                         const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
+                         const float * const * b_hh, const float * pred_w, const float * out_w, cudaStream_t s);
 void        bulk_release(BulkWeights & w);
 size_t      bulk_smem_bytes();
 cudaError_t bulk_configure();
