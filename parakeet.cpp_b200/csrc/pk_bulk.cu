@@ -7,7 +7,7 @@
 // row per iteration, and the loop is bound by L2 ingress rather than by the
 // tensor cores. This loop instead tiles every step-loop GEMM in two dimensions,
 //
-//   tile = 128 utterances (UMMA M) x up to 256 weight rows (UMMA N), K in steps of 32,
+//   tile = 128 utterances (UMMA M) x up to 256 weight rows (UMMA N), K in steps of 64,
 //
 // streaming both operands from L2 (the weights, ~42 MB as f16 halves, stay
 // L2-resident), so an activation row is read once per weight tile and a weight
@@ -36,8 +36,8 @@
 // f16; h and the joint hidden layer carry 22 significant bits; the dropped
 // A_lo W_lo term is ~2^-22 relative.
 //
-// Warp roles in a GEMM phase (12 warps): 0-3 stage A (utterance rows gathered with
-// 16-byte cp.async into the 64-byte-swizzled K-major tile, 4-8 stages deep), 4
+// Warp roles in a GEMM phase (12 warps): 0-3 stage A (one utterance row per
+// thread, 16-byte cp.async gathers into the 128-byte-swizzled K-major tile), 4
 // issues the weight tiles' TMA loads, 5 owns tensor memory and issues the MMAs
 // (two 256-column accumulators: the epilogue of one tile overlaps the next tile's
 // main loop), 8-11 run the epilogue (TMEM lane quarter = warp % 4). All warps
@@ -54,13 +54,12 @@ namespace {
 constexpr int kBThreads = 384;
 constexpr int kBWarps = kBThreads / 32;
 constexpr int kBM = 128;                              // utterances per tile (UMMA M)
-constexpr int kBK = 32;                               // K per stage: one 64-byte f16 row (64-byte swizzle)
-constexpr unsigned kRowB = kBK * 2;                   // bytes of one operand row per stage
+constexpr int kBK = 64;                               // K per stage: one 128-byte f16 row
 constexpr int kBNmax = 256;                           // weight rows per tile (UMMA N)
-constexpr int kMaxStages = 8;
-constexpr unsigned kATile = kBM * kBK * 2;            // one f16 plane of an A stage (8 KB)
-constexpr unsigned kBBox = 64 * kBK * 2;              // one 64-row box of one B plane (4 KB)
-constexpr unsigned kRing = 192 * 1024;                // operand ring: 4 stages at N = 256, 6 at 128, 8 at 64
+constexpr int kMaxStages = 4;
+constexpr unsigned kATile = kBM * kBK * 2;            // one f16 plane of an A stage (16 KB)
+constexpr unsigned kBBox = 64 * kBK * 2;              // one 64-row box of one B plane (8 KB)
+constexpr unsigned kRing = 192 * 1024;                // operand ring: 2 stages at N = 256, 3 at 128, 4 at 64
 constexpr unsigned kTmemCols = 2 * kBNmax;            // two accumulators
 
 struct BulkSmem {
@@ -86,14 +85,14 @@ enum { G_LSTM = 0, G_PRED = 1, G_JOINT = 2 };
 // of slots changes with the tile width from phase to phase; every slot is drained at
 // the end of a phase.)
 struct Pipe {
-    unsigned ua[kMaxStages] = {};   // A stages filled
-    unsigned ub[kMaxStages] = {};   // B stages filled
-    unsigned um[kMaxStages] = {};   // stages consumed by the MMAs
+    unsigned ua[kMaxStages] = {0u, 0u, 0u, 0u};   // A stages filled
+    unsigned ub[kMaxStages] = {0u, 0u, 0u, 0u};   // B stages filled
+    unsigned um[kMaxStages] = {0u, 0u, 0u, 0u};   // stages consumed by the MMAs
     unsigned acc_m = 0, acc_e = 0;                // tiles accumulated (MMA) / drained (epilogue)
 };
 
 // Ring geometry of a phase: a stage is the A tile (hi, lo) then the B tile (hi, lo)
-// of bn rows; every part starts on a 512-byte boundary (the swizzle atom).
+// of bn rows; every part starts on a 1024-byte boundary (the swizzle atom).
 struct Ring {
     unsigned stage, b_plane;
     int n;
@@ -185,10 +184,9 @@ struct RoleClock {
 
 // A producer (warps 0-3): warp w stages rows 32w .. 32w + 31 of every tile. Its
 // lanes first write those rows' sources to a per-warp table in shared memory;
-// then each K stage takes 4 rounds of 8 rows x 4 lanes, each lane one 16-byte
-// chunk per plane, so that a round reads 8 whole 64-byte row segments
-// (coalesced) and writes chunk c of row r at chunk c ^ ((r >> 1) & 3) (64-byte
-// swizzle).
+// then each K stage takes 8 rounds of 4 rows x 8 lanes, each lane one 16-byte
+// chunk per plane, so that a round reads 4 whole 128-byte row segments
+// (coalesced) and writes chunk c of row r at chunk c ^ (r & 7) (128-byte swizzle).
 __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, const Job & J, Pipe & pp) {
     const LoopParams & P = Q.P;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -235,20 +233,20 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
             if (!__all_sync(0xFFFFFFFFu, ok)) return;
             const bool seg1 = kc >= J.split;
             const unsigned dst = smem_u32(tiles + (unsigned) s * R.stage);
-            const unsigned sub = (unsigned) lane & 3u;
+            const unsigned sub = (unsigned) lane & 7u;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int lr = warp * 32 + k * 8 + (lane >> 2);
+            for (int k = 0; k < 8; ++k) {
+                const int lr = warp * 32 + k * 4 + (lane >> 3);
                 const unsigned char fl = S.a_fl[lr];
                 if (fl & 1) {
                     // a reset row reads zeros (from a zero block, so that every write of
                     // the stage is a cp.async the arrival below tracks)
                     const bool zero = seg1 && (fl & 2);
                     const unsigned char * shi = zero ? g_zero128
-                                              : seg1 ? S.a_s1[lr] + (size_t) (kc - J.split) * kRowB
-                                                     : S.a_s0[lr] + (size_t) kc * kRowB;
+                                              : seg1 ? S.a_s1[lr] + (size_t) (kc - J.split) * 128
+                                                     : S.a_s0[lr] + (size_t) kc * 128;
                     const unsigned char * slo = zero ? g_zero128 : shi + plane;
-                    const unsigned o = (unsigned) lr * kRowB + ((sub ^ (((unsigned) lr >> 1) & 3u)) << 4);
+                    const unsigned o = (unsigned) lr * 128u + ((sub ^ ((unsigned) lr & 7u)) << 4);
                     cp_async16(dst + o, shi + sub * 16);
                     cp_async16(dst + kATile + o, slo + sub * 16);
                 }
@@ -325,9 +323,9 @@ __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * til
 #pragma unroll
             for (int k16 = 0; k16 < kBK / 16; ++k16) {
                 const unsigned ko = (unsigned) k16 * 32u;
-                umma_f16(d, umma_desc_sw64(ahi + ko), umma_desc_sw64(bhi + ko), idesc, (kc | k16) ? 1u : 0u);
-                umma_f16(d, umma_desc_sw64(alo + ko), umma_desc_sw64(bhi + ko), idesc, 1u);
-                umma_f16(d, umma_desc_sw64(ahi + ko), umma_desc_sw64(blo + ko), idesc, 1u);
+                umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(bhi + ko), idesc, (kc | k16) ? 1u : 0u);
+                umma_f16(d, umma_desc_sw128(alo + ko), umma_desc_sw128(bhi + ko), idesc, 1u);
+                umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
             }
             umma_commit(&S.empty[s]);      // the stage is free once these MMAs have read it
             rc.add(S, 7);
@@ -954,7 +952,7 @@ cudaError_t encode_2d(void * map, CUtensorMapDataType type, size_t esize, const 
                       long long cols, int box_rows, int box_cols, CUtensorMapSwizzle swz);
 
 bool bulk_supported(int H, int J, int L) {
-    return H > 0 && J > 0 && H % 64 == 0 && J % 64 == 0 && L >= 1 && L <= kMaxLayers;
+    return H > 0 && J > 0 && H % kBK == 0 && J % kBK == 0 && L >= 1 && L <= kMaxLayers;
 }
 
 size_t bulk_smem_bytes() { return 1024 + (size_t) kRing + sizeof(BulkSmem); }
@@ -1015,10 +1013,10 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, c
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         e = encode_2d(&host_maps[(size_t) (2 * m)], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, hi, mat_rows[m],
-                      mat_k[m], 64, kBK, CU_TENSOR_MAP_SWIZZLE_64B);
+                      mat_k[m], 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
         if (e != cudaSuccess) return e;
         e = encode_2d(&host_maps[(size_t) (2 * m + 1)], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, lo, mat_rows[m],
-                      mat_k[m], 64, kBK, CU_TENSOR_MAP_SWIZZLE_64B);
+                      mat_k[m], 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
         if (e != cudaSuccess) return e;
         BulkGemm g;
         g.map_hi = base + maps + (size_t) (2 * m) * 128;

@@ -57,19 +57,6 @@ __device__ __forceinline__ unsigned long long umma_desc_sw128(unsigned saddr) {
     return d;
 }
 
-// K-major operand tile of `rows` x 32 f16 in the 64-byte swizzle layout: 8-row
-// atoms of 512 bytes, row r at byte r * 64, 16-byte chunk c stored at chunk
-// c ^ ((r >> 1) & 3).
-__device__ __forceinline__ unsigned long long umma_desc_sw64(unsigned saddr) {
-    unsigned long long d = 0;
-    d |= (unsigned long long) ((saddr >> 4) & 0x3FFFu);          // start address
-    d |= (unsigned long long) 1u << 16;                           // leading byte offset (unused for swizzled K-major)
-    d |= (unsigned long long) (512u >> 4) << 32;                  // stride byte offset: next 8-row atom
-    d |= (unsigned long long) 1u << 46;                           // descriptor version (tcgen05)
-    d |= (unsigned long long) 4u << 61;                           // layout: 64-byte swizzle
-    return d;
-}
-
 // kind::f16 instruction descriptor: f32 accumulator, f16 A and B, both K-major.
 __host__ __device__ constexpr unsigned umma_idesc_f16(int m, int n) {
     return (1u << 4)                          // D format f32
