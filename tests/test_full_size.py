@@ -8,10 +8,11 @@ tests/golden/full/<config>.npz: the output of src/parakeet_tdt.cpp /
 src/parakeet_eou.cpp themselves, built unchanged (oracle/_ref/libref_decoder.so),
 on the same inputs (tests/golden/make_full_golden.py). The bar (the reference's
 own gate is exact token equality, test/test_tdt_decoder_parity.cpp:210-221): an
-utterance differs only where the CPU oracle -- bit-identical to that build --
-shows under teacher forcing a near-tie (top-2 margin < 1e-3) at which the device's
-argmax differs, with logits and LSTM state within 2e-3 on the way. The number of
-such utterances is counted.
+utterance may differ only when its first differing decision falls on a step where
+the CPU oracle -- bit-identical to that build -- has a top-2 margin below 1e-3 (a
+near-tie), and teacher forced on each step loop its logits and LSTM state stay
+within 2e-3 with no argmax mismatch away from near-ties. Such utterances are
+counted (at most 1% of a batch).
 
 Large batches start on the tcgen05 bulk loop and finish on the persistent loop;
 the same batches are also checked reversed and as one rank's LPT shard (other
@@ -75,10 +76,26 @@ def check_reference(orc, m, enc, offs, T, r, fx, idx, dec, max_excused_frac=0.01
         gb = ob = None
         if "bnd_hash" in fx:
             gb, ob = [r["bounds"][i] for i in d], ro["bounds"]
+        # replay on both step loops: the batch ran its first iterations on the bulk loop
+        decs = [dec, pk_decoder(m, 1), pk_decoder(m, 0)]
         excused = parity.compare_free_running(dec, o, enc, so, sT, [r["tokens"][i] for i in d], ro["tokens"],
-                                              gpu_bounds=gb, oracle_bounds=ob)
+                                              gpu_bounds=gb, oracle_bounds=ob, tf_decoders=decs,
+                                              gpu_steps=[r["steps"][i] for i in d], oracle_steps=ro["steps"])
     assert excused <= max(2, int(max_excused_frac * len(idx))), f"{excused} of {len(idx)} utterances differ"
     return len(idx) - len(diff), excused
+
+
+_DECODERS = {}
+
+
+def pk_decoder(m, bulk_min_live):
+    """A decoder of model m on one step loop (bulk 1: the bulk loop for every
+    iteration; 0: the persistent loop alone), kept for the module."""
+    import sys
+    key = (id(m), bulk_min_live)
+    if key not in _DECODERS:
+        _DECODERS[key] = sys.modules["parakeet_b200"].Decoder(m, math="tc", bulk_min_live=bulk_min_live)
+    return _DECODERS[key]
 
 
 def check_reordered(orc, m, dec, enc, offs, T, fx, shard):
