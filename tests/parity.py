@@ -14,10 +14,18 @@ STATE_TOL = 2e-3
 TIE_MARGIN = 1e-3
 
 
-def teacher_forced(dec, o, enc_utt, max_symbols=None):
-    """Compare one utterance step by step. Returns a dict of error statistics."""
+def oracle_trace(o, enc_utt, max_symbols=None):
+    """The oracle's free-running decode of one utterance with every step traced."""
     T = int(enc_utt.shape[0])
-    r = o.decode_window(enc_utt, max_symbols=max_symbols, trace_steps=max(1, T * 12 + 8))
+    msym = o.model.max_symbols_per_step if max_symbols is None else max_symbols
+    return o.decode_window(enc_utt, max_symbols=max_symbols, trace_steps=max(1, T * (msym + 1) + 8))
+
+
+def teacher_forced(dec, o, enc_utt, max_symbols=None, trace=None):
+    """Compare one utterance step by step (trace: its oracle_trace, if already made).
+    Returns a dict of error statistics."""
+    T = int(enc_utt.shape[0])
+    r = trace if trace is not None else oracle_trace(o, enc_utt, max_symbols)
     S = r["steps"]
     if S == 0:
         return {"steps": 0, "logit_err": 0.0, "h_err": 0.0, "c_err": 0.0, "near_ties": 0,
@@ -70,15 +78,13 @@ def emitted_steps(o, tokens):
     return (tok != m.blank_id) & (tok != m.eob_id) & (tok != m.eou_id) & ~sp
 
 
-def divergence_at_near_tie(o, enc_utt, gpu_tokens, max_symbols=None):
+def divergence_at_near_tie(o, enc_utt, gpu_tokens, max_symbols=None, trace=None):
     """Where a free-running device decode first parts from the oracle's: the
     oracle steps between its last common emitted token and the next one (the
     whole trace when the token lists are equal). Returns (near_tie_in_window,
     (first_step, last_step)): whether one of those steps has an oracle token or
     duration margin below 1e-3, i.e. the first differing decision is a near-tie."""
-    T = int(enc_utt.shape[0])
-    msym = o.model.max_symbols_per_step if max_symbols is None else max_symbols
-    r = o.decode_window(enc_utt, max_symbols=max_symbols, trace_steps=T * (msym + 1) + 8)
+    r = trace if trace is not None else oracle_trace(o, enc_utt, max_symbols)
     S = r["steps"]
     em = np.nonzero(emitted_steps(o, r["token"][:S]))[0]
     ot, gt = r["tokens"], np.asarray(gpu_tokens)
@@ -116,10 +122,11 @@ def compare_free_running(dec, o, enc, offs, n_frames, gpu_tokens, oracle_tokens,
         if same:
             continue
         e = enc[int(offs[b]):int(offs[b]) + int(n_frames[b])]
-        near, win = divergence_at_near_tie(o, e, gpu_tokens[b], max_symbols)
+        tr = oracle_trace(o, e, max_symbols)
+        near, win = divergence_at_near_tie(o, e, gpu_tokens[b], max_symbols, trace=tr)
         assert near, f"utterance {b}: first differing decision (oracle steps {win}) is not at a near-tie"
         for d in decs:
-            st = teacher_forced(d, o, e, max_symbols)
+            st = teacher_forced(d, o, e, max_symbols, trace=tr)
             assert_tf_ok(st, f"utterance {b}")
         excused += 1
     return excused
