@@ -174,17 +174,20 @@ class ClockSampler:
 # ------------------------------------------------------------ CPU legs ----
 
 def cpu_sample_run(orc_o, enc, offs, T, threads, budget_s, msym=None):
-    """Oracle decode of a bounded sample: the first utterances of the batch,
-    each truncated to a frame cap chosen so the run takes about budget_s."""
+    """The reference CPU decoder on a bounded sample: the batch's first utterances,
+    whole, as many as about budget_s of work on `threads` threads takes (each
+    utterance truncated only if one alone would exceed that)."""
     # calibrate: one utterance of up to 40 frames
     t40 = int(min(40, max(1, T[0])))
     t0 = time.perf_counter()
     orc_o.decode_window(enc[int(offs[0]):int(offs[0]) + t40], max_symbols=msym)
     per_frame = max((time.perf_counter() - t0) / t40, 1e-5)
-    n_utt = int(min(len(T), max(1, threads)))
-    cap = int(max(10, min(int(np.max(T)), budget_s * threads / (n_utt * per_frame))))
-    Ts = np.minimum(T[:n_utt], cap).astype(np.int32)
-    Ts = np.maximum(Ts, 1)
+    frames_budget = budget_s * threads / per_frame
+    cap = int(max(10, min(int(np.max(T)), frames_budget / max(1, threads))))
+    Ts = np.maximum(np.minimum(T, cap), 1).astype(np.int32)
+    n_utt = int(np.searchsorted(np.cumsum(Ts.astype(np.int64)), frames_budget)) + 1
+    n_utt = int(min(len(T), max(threads, n_utt)))
+    Ts = Ts[:n_utt]
     t0 = time.perf_counter()
     r = orc_o.decode_batch(enc, offs[:n_utt], Ts, n_threads=threads, max_symbols=msym)
     wall = time.perf_counter() - t0
@@ -268,8 +271,8 @@ def main():
     T_all = global_lengths(pk, cfg, B_total)
     idx = pk.multi.shard_indices(T_all, world)[rank] if world > 1 else np.arange(B_total)
     if args.impl == "reference":
-        # the CPU arm decodes a bounded sample: the rank's first utterances, one per host thread
-        idx = idx[:host_cores()]
+        # the CPU arm decodes a bounded sample of the rank's first utterances
+        idx = idx[:64 * host_cores()]
     T = T_all[idx].astype(np.int32)
     if strong:
         # every utterance has the same frames whichever rank decodes it
