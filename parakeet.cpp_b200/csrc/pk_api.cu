@@ -94,6 +94,8 @@ struct pk_ctx {
     int bulk_ok = 0;
     int bulk_min_live = 256;
     DevBuf h16, x16, dcount, bprof;
+    void * pin = nullptr;          // pinned staging of a call's small inputs (copy_segments)
+    size_t pin_cap = 0;
     // per-call workspace
     DevBuf prof;
     DevBuf livef, hst, xnew, hidc;
@@ -599,21 +601,48 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     ctl[C_SEL] = 0;
     ctl[C_NLIVE0] = (int32_t) live.size();
     ctl[C_NEMIT] = (int32_t) (emit.size() / 2);
-    if (B > 0) {
-        PK_CK(cudaMemcpyAsync(x->ust.p, ust.data(), ust.size() * 4, cudaMemcpyHostToDevice, s));
-        PK_CK(cudaMemcpyAsync(x->frameoff.p, r.frame_off, (size_t) B * 8, cudaMemcpyHostToDevice, s));
-        PK_CK(cudaMemcpyAsync(x->tokregion.p, tokregion.data(), (size_t) B * 8, cudaMemcpyHostToDevice, s));
-        PK_CK(cudaMemcpyAsync(x->bndregion.p, bndregion.data(), (size_t) B * 8, cudaMemcpyHostToDevice, s));
-        if (!live.empty()) {
-            PK_CK(cudaMemcpyAsync(x->live.p, live.data(), live.size() * 4, cudaMemcpyHostToDevice, s));
-            PK_CK(cudaMemcpyAsync(x->livef.p, live_frame.data(), live_frame.size() * 8, cudaMemcpyHostToDevice, s));
+    {   // the call's small inputs go through pinned host memory and one copy kernel, not the
+        // copy engines, which a prefetched encoder copy may keep busy meanwhile
+        HostSegments g{};
+        size_t need = 0;
+        auto plan = [&](void * dst, const void * src, size_t bytes) {
+            if (bytes == 0) return;
+            g.seg[g.n].src = src;   // host address for now; rebased below
+            g.seg[g.n].dst = dst;
+            g.seg[g.n].bytes = bytes;
+            ++g.n;
+            need += (bytes + 15) & ~(size_t) 15;
+        };
+        if (B > 0) {
+            plan(x->ust.p, ust.data(), ust.size() * 4);
+            plan(x->frameoff.p, r.frame_off, (size_t) B * 8);
+            plan(x->tokregion.p, tokregion.data(), (size_t) B * 8);
+            plan(x->bndregion.p, bndregion.data(), (size_t) B * 8);
+            plan(x->live.p, live.data(), live.size() * 4);
+            plan(x->livef.p, live_frame.data(), live_frame.size() * 8);
+            plan(x->emit.p, emit.data(), emit.size() * 4);
+            PK_CK(cudaMemsetAsync(x->keys.p, 0, (size_t) B * 32, s));
+            PK_CK(cudaMemsetAsync(x->finish.p, 0, (size_t) B * 8, s));
         }
-        if (!emit.empty())
-            PK_CK(cudaMemcpyAsync(x->emit.p, emit.data(), emit.size() * 4, cudaMemcpyHostToDevice, s));
-        PK_CK(cudaMemsetAsync(x->keys.p, 0, (size_t) B * 32, s));
-        PK_CK(cudaMemsetAsync(x->finish.p, 0, (size_t) B * 8, s));
+        plan(x->ctl.p, ctl.data(), kCtl * 4);
+        if (need > x->pin_cap) {
+            if (x->pin) cudaFreeHost(x->pin);
+            x->pin = nullptr;
+            x->pin_cap = 0;
+            PK_CK(cudaHostAlloc(&x->pin, need + need / 4 + 4096, cudaHostAllocMapped));
+            x->pin_cap = need + need / 4 + 4096;
+        }
+        void * pin_dev = nullptr;
+        PK_CK(cudaHostGetDevicePointer(&pin_dev, x->pin, 0));
+        size_t off = 0;
+        for (int i = 0; i < g.n; ++i) {
+            std::memcpy(static_cast<unsigned char *>(x->pin) + off, g.seg[i].src, g.seg[i].bytes);
+            g.seg[i].src = static_cast<unsigned char *>(pin_dev) + off;
+            off += (g.seg[i].bytes + 15) & ~(size_t) 15;
+        }
+        PK_CK(launch_copy_segments(g, s));
+        ++r.launches;
     }
-    PK_CK(cudaMemcpyAsync(x->ctl.p, ctl.data(), kCtl * 4, cudaMemcpyHostToDevice, s));
     PK_CK(cudaMemsetAsync(x->bar.p, 0, 32, s));
     if (r.h_in) {
         PK_CK(cudaMemcpyAsync(x->h.p, r.h_in, (size_t) L * H * 4, cudaMemcpyDeviceToDevice, s));
@@ -1014,6 +1043,7 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
             if (bulk_prepare(x->bulk, x->H, x->J, x->L, x->Vo, x->V1, x->embed.as<float>(), wih, whh, bih, bhh,
                              x->pred_w.as<float>(), x->out_w.as<float>(), x->stream) != cudaSuccess) {
                 bulk_release(x->bulk);
+    if (x->pin) cudaFreeHost(x->pin);
                 return cleanup(fail(PK_ERR_CUDA, "bulk-loop weight preparation failed"));
             }
             x->bulk_ok = 1;

@@ -222,6 +222,18 @@ cudaError_t encproj_tc_prepare(const float * w, int J, int K, unsigned short * w
                                cudaStream_t s);
 cudaError_t launch_encproj_tc(const float * enc, long long frames, int K, const void * tmap, int J,
                               const float * bias, float * out, long long timeout_ns, int * err, cudaStream_t s);
+// Up to 12 copies from pinned host memory (device-readable) to device memory, in one
+// kernel; sizes are multiples of 4 bytes, addresses 4-byte aligned.
+struct HostSegment {
+    const void * src;
+    void * dst;
+    unsigned long long bytes;
+};
+struct HostSegments {
+    HostSegment seg[12];
+    int n;
+};
+cudaError_t launch_copy_segments(const HostSegments & g, cudaStream_t s);
 cudaError_t launch_extract_field(const int32_t * ust, int B, int field, int32_t * dst,
                                  cudaStream_t s);
 

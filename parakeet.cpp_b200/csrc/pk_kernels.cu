@@ -3,6 +3,8 @@
 
 #include "pk_internal.h"
 
+#include <algorithm>
+
 #include <cuda_fp16.h>
 
 namespace pk {
@@ -268,6 +270,28 @@ cudaError_t launch_stage_rows(const float * src, int n_rows, int H, int es, int 
     const int n = n_rows * H;
     if (n <= 0) return cudaSuccess;
     stage_rows_kernel<<<(n + 255) / 256, 256, 0, s>>>(src, n_rows, H, es, rb, dst);
+    return cudaGetLastError();
+}
+
+// Copies of small host arrays staged in pinned host memory, read by the SMs over
+// the bus (so they do not queue behind a large host-to-device copy in flight on
+// the copy engines, as a prefetched batch's encoder copy is).
+__global__ void copy_segments_kernel(HostSegments g) {
+    const long long stride = (long long) gridDim.x * blockDim.x;
+    for (int i = 0; i < g.n; ++i) {
+        const unsigned * src = static_cast<const unsigned *>(g.seg[i].src);
+        unsigned * dst = static_cast<unsigned *>(g.seg[i].dst);
+        const long long words = (long long) (g.seg[i].bytes / 4);
+        for (long long k = (long long) blockIdx.x * blockDim.x + threadIdx.x; k < words; k += stride) dst[k] = src[k];
+    }
+}
+
+cudaError_t launch_copy_segments(const HostSegments & g, cudaStream_t s) {
+    if (g.n <= 0) return cudaSuccess;
+    unsigned long long words = 0;
+    for (int i = 0; i < g.n; ++i) words += g.seg[i].bytes / 4;
+    const unsigned blocks = (unsigned) std::min<unsigned long long>(64, (words + 255) / 256 + 1);
+    copy_segments_kernel<<<blocks, 256, 0, s>>>(g);
     return cudaGetLastError();
 }
 
