@@ -1040,8 +1040,14 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
                 wih[l] = x->w_ih[l].as<float>(); whh[l] = x->w_hh[l].as<float>();
                 bih[l] = x->b_ih[l].as<float>(); bhh[l] = x->b_hh[l].as<float>();
             }
+            // matrices whose source tensors are all f16 have zero lo halves
+            int f16w[kMaxLayers + 2] = {};
+            for (int l = 0; l < x->L; ++l)
+                f16w[l] = d->lstm[l].w_ih.type == PK_GGML_F16 && d->lstm[l].w_hh.type == PK_GGML_F16;
+            f16w[x->L] = d->joint_pred_w.type == PK_GGML_F16;
+            f16w[x->L + 1] = d->joint_out_w.type == PK_GGML_F16;
             if (bulk_prepare(x->bulk, x->H, x->J, x->L, x->Vo, x->V1, x->embed.as<float>(), wih, whh, bih, bhh,
-                             x->pred_w.as<float>(), x->out_w.as<float>(), x->stream) != cudaSuccess) {
+                             x->pred_w.as<float>(), x->out_w.as<float>(), f16w, x->stream) != cudaSuccess) {
                 bulk_release(x->bulk);
     if (x->pin) cudaFreeHost(x->pin);
                 return cleanup(fail(PK_ERR_CUDA, "bulk-loop weight preparation failed"));

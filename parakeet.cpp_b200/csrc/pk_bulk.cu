@@ -278,11 +278,12 @@ __device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char
             rc.add(S, 1);
             unsigned char * bhi = tiles + (unsigned) s * R.stage + 2 * kATile;
             unsigned char * blo = bhi + R.b_plane;
+            const unsigned planes = J.g->lo_zero ? 1u : 2u;
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
-                         :: "r"(smem_u32(&S.full_b[s])), "r"((unsigned) nb * 2u * kBBox) : "memory");
+                         :: "r"(smem_u32(&S.full_b[s])), "r"((unsigned) nb * planes * kBBox) : "memory");
             for (int b = 0; b < nb; ++b) {
                 tma_load_2d(bhi + b * kBBox, mhi, kc * kBK, n0 + 64 * b, &S.full_b[s]);
-                tma_load_2d(blo + b * kBBox, mlo, kc * kBK, n0 + 64 * b, &S.full_b[s]);
+                if (planes == 2u) tma_load_2d(blo + b * kBBox, mlo, kc * kBK, n0 + 64 * b, &S.full_b[s]);
             }
         }
     }
@@ -325,7 +326,7 @@ __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * til
                 const unsigned ko = (unsigned) k16 * 32u;
                 umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(bhi + ko), idesc, (kc | k16) ? 1u : 0u);
                 umma_f16(d, umma_desc_sw128(alo + ko), umma_desc_sw128(bhi + ko), idesc, 1u);
-                umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
+                if (!J.g->lo_zero) umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
             }
             umma_commit(&S.empty[s]);      // the stage is free once these MMAs have read it
             rc.add(S, 7);
@@ -412,7 +413,6 @@ __device__ __forceinline__ void epi_lstm(const BulkParams & Q, const Job & J, un
     float * hw = P.h + (((size_t) hb * L + l) * B + utt) * H;
     unsigned char * st = Q.h16 + (((size_t) hb * L + l) * B + utt) * rb16;
     unsigned char * xn = Q.x16 + ((size_t) l * B + row) * rb16;
-    unsigned char * hrow = P.hst + ((((size_t) hb * L + l) * B + utt) * P.rbh);
     const float * bias = Q.lbias + (size_t) l * 4 * H;
     // next group's old cell state is requested before this group's tensor-memory load
     float4 cn0 = make_float4(0.f, 0.f, 0.f, 0.f), cn1 = cn0;
@@ -445,15 +445,16 @@ __device__ __forceinline__ void epi_lstm(const BulkParams & Q, const Job & J, un
         }
         reinterpret_cast<float4 *>(cw + j0)[0] = make_float4(cn[0], cn[1], cn[2], cn[3]);
         reinterpret_cast<float4 *>(cw + j0)[1] = make_float4(cn[4], cn[5], cn[6], cn[7]);
-        reinterpret_cast<float4 *>(hw + j0)[0] = make_float4(hn[0], hn[1], hn[2], hn[3]);
-        reinterpret_cast<float4 *>(hw + j0)[1] = make_float4(hn[4], hn[5], hn[6], hn[7]);
+        if (P.trace_steps > 0) {   // f32 h: only the trace's state dump reads it
+            reinterpret_cast<float4 *>(hw + j0)[0] = make_float4(hn[0], hn[1], hn[2], hn[3]);
+            reinterpret_cast<float4 *>(hw + j0)[1] = make_float4(hn[4], hn[5], hn[6], hn[7]);
+        }
         uint4 hi, lo;
         split8(hn, hi, lo);
         *reinterpret_cast<uint4 *>(st + 2 * j0) = hi;
         *reinterpret_cast<uint4 *>(st + 2 * H + 2 * j0) = lo;
         *reinterpret_cast<uint4 *>(xn + 2 * j0) = hi;
         *reinterpret_cast<uint4 *>(xn + 2 * H + 2 * j0) = lo;
-        put_h8(P, hrow, j0, hn, hi, lo);
     }
 }
 
@@ -684,6 +685,37 @@ __device__ void hidden_phase(const BulkParams & Q, int sel, int n_live, int n_pr
     }
 }
 
+// ---- hand-over to the persistent loop ------------------------------------------------
+
+// The persistent loop keeps h in its own staged layout (pk_loop.cu): write both h
+// buffers of every layer of every utterance still live into it, from the f16
+// halves kept here (h = hi + lo, the value this loop computed). Only the last
+// buffer written is ever read; the other is written too so that nothing needs to
+// know which one that is.
+__device__ void handoff_phase(const BulkParams & Q, int sel, int n_live) {
+    const LoopParams & P = Q.P;
+    const int H = P.H, L = P.L, B = P.B;
+    const int groups = H / 8;
+    const long long total = (long long) n_live * 2 * L * groups;
+    const long long stride = (long long) gridDim.x * blockDim.x;
+    const unsigned rb16 = 4u * (unsigned) H;
+    for (long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+        const int g = (int) (idx % groups);
+        const long long r = idx / groups;                 // (live entry, buffer, layer)
+        const int l = (int) (r % L), hb = (int) ((r / L) % 2), i = (int) (r / (2 * L));
+        const int utt = __ldcg(P.live + (size_t) sel * B + i);
+        const unsigned char * src = Q.h16 + (((size_t) hb * L + l) * B + utt) * rb16;
+        const uint4 hi = __ldcg(reinterpret_cast<const uint4 *>(src + 16 * g));
+        const uint4 lo = __ldcg(reinterpret_cast<const uint4 *>(src + 2 * H + 16 * g));
+        const __half * hh = reinterpret_cast<const __half *>(&hi);
+        const __half * hl = reinterpret_cast<const __half *>(&lo);
+        float hn[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) hn[u] = __half2float(hh[u]) + __half2float(hl[u]);
+        put_h8(P, P.hst + ((((size_t) hb * L + l) * B + utt) * P.rbh), 8 * g, hn, hi, lo);
+    }
+}
+
 // ---- the kernel -------------------------------------------------------------------
 
 __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_constant__ BulkParams Q) {
@@ -880,6 +912,8 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
         if (!bulk_barrier(Q, S, nbar)) break;
         mark(11);
     }
+    // hand the live utterances' state to the persistent loop (it reads its own layout)
+    if (n_live > 0 && __ldcg(&P.ctl[C_ERR]) == 0) handoff_phase(Q, sel, n_live);
     if (prof) {
         for (int i = 0; i < 12; ++i) Q.prof[i] = pacc[i];
     }
@@ -974,7 +1008,8 @@ void bulk_release(BulkWeights & w) {
 
 cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
                          const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
-                         const float * const * b_hh, const float * pred_w, const float * out_w, cudaStream_t s) {
+                         const float * const * b_hh, const float * pred_w, const float * out_w,
+                         const int * f16_weights, cudaStream_t s) {
     bulk_release(w);
     // layout: [maps: (L + 2) x 2 x 128 B][lbias L x 4H f32][embedding halves][weight halves]
     const int nmat = L + 2;
@@ -1023,6 +1058,7 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, c
         g.map_lo = base + maps + (size_t) (2 * m + 1) * 128;
         g.N = (int) mat_rows[m];
         g.K = (int) mat_k[m];
+        g.lo_zero = f16_weights[m];   // f16 weights are exact in the hi half
         if (m < L) w.gl[m] = g;
         else if (m == L) w.gp = g;
         else w.gj = g;

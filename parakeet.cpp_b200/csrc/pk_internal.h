@@ -148,6 +148,7 @@ struct BulkGemm {
     const void * map_hi;
     const void * map_lo;
     int N, K;
+    int lo_zero;               // every lo half is zero (f16 weights): two products, no lo tiles
 };
 
 struct BulkParams {
@@ -175,7 +176,8 @@ struct BulkWeights {
 bool        bulk_supported(int H, int J, int L);
 cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
                          const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
-                         const float * const * b_hh, const float * pred_w, const float * out_w, cudaStream_t s);
+                         const float * const * b_hh, const float * pred_w, const float * out_w,
+                         const int * f16_weights, cudaStream_t s);
 void        bulk_release(BulkWeights & w);
 size_t      bulk_smem_bytes();
 cudaError_t bulk_configure();
