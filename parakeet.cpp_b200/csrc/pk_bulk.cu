@@ -688,22 +688,23 @@ __device__ void hidden_phase(const BulkParams & Q, int sel, int n_live, int n_pr
 // ---- hand-over to the persistent loop ------------------------------------------------
 
 // The persistent loop keeps h in its own staged layout (pk_loop.cu): write both h
-// buffers of every layer of every utterance still live into it, from the f16
-// halves kept here (h = hi + lo, the value this loop computed). Only the last
-// buffer written is ever read; the other is written too so that nothing needs to
-// know which one that is.
-__device__ void handoff_phase(const BulkParams & Q, int sel, int n_live) {
+// buffers of every layer of every utterance still live or about to take its LSTM
+// step into it, from the f16 halves kept here (h = hi + lo, the value this loop
+// computed). Only the last buffer written is ever read; the other is written too
+// so that nothing needs to know which one that is.
+__device__ void handoff_phase(const BulkParams & Q, int sel, int n_live, int n_emit) {
     const LoopParams & P = Q.P;
     const int H = P.H, L = P.L, B = P.B;
     const int groups = H / 8;
-    const long long total = (long long) n_live * 2 * L * groups;
+    // the live list, then the emit list (its last LSTM step runs on the persistent loop)
+    const long long total = (long long) (n_live + n_emit) * 2 * L * groups;
     const long long stride = (long long) gridDim.x * blockDim.x;
     const unsigned rb16 = 4u * (unsigned) H;
     for (long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
         const int g = (int) (idx % groups);
         const long long r = idx / groups;                 // (live entry, buffer, layer)
         const int l = (int) (r % L), hb = (int) ((r / L) % 2), i = (int) (r / (2 * L));
-        const int utt = __ldcg(P.live + (size_t) sel * B + i);
+        const int utt = i < n_live ? __ldcg(P.live + (size_t) sel * B + i) : __ldcg(P.emit + 2 * (i - n_live));
         const unsigned char * src = Q.h16 + (((size_t) hb * L + l) * B + utt) * rb16;
         const uint4 hi = __ldcg(reinterpret_cast<const uint4 *>(src + 16 * g));
         const uint4 lo = __ldcg(reinterpret_cast<const uint4 *>(src + 2 * H + 16 * g));
@@ -913,7 +914,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
         mark(11);
     }
     // hand the live utterances' state to the persistent loop (it reads its own layout)
-    if (n_live > 0 && __ldcg(&P.ctl[C_ERR]) == 0) handoff_phase(Q, sel, n_live);
+    if (n_live + n_emit > 0 && __ldcg(&P.ctl[C_ERR]) == 0) handoff_phase(Q, sel, n_live, n_emit);
     if (prof) {
         for (int i = 0; i < 12; ++i) Q.prof[i] = pacc[i];
     }
