@@ -199,35 +199,37 @@ def cpu_sample_run(orc_o, enc, offs, T, threads, budget_s, msym=None):
 
 # ------------------------------------------------------------ helpers ----
 
-def per_iter_bytes(model):
-    """Algorithmic weight bytes of one batched loop iteration, as stored (q8_0 34 B
-    per 32 weights, f16 2 B, f32 4 B): the joint output layer every iteration;
-    LSTM + pred-proj (+ biases) in iterations with an emission."""
-    p = model.prefix
-    T = model.tensors
-    joint = T[f"{p}.joint.out.weight"].nbytes + T[f"{p}.joint.out.bias"].nbytes
-    lstm = sum(T[f"{p}.predict.lstm.{l}.{k}"].nbytes for l in range(model.n_layers)
-               for k in ("w_ih", "w_hh", "b_ih", "b_hh"))
-    pred = T[f"{p}.joint.pred.weight"].nbytes + T[f"{p}.joint.pred.bias"].nbytes
-    return joint, lstm + pred
+def bulk_flops(model):
+    """Algorithmic FLOPs of the tcgen05 bulk loop's matrix products: per joint
+    evaluation (one live utterance in one iteration) the joint.out product
+    2 * joint_hidden * v_out; per LSTM step (an emission or an utterance's first step)
+    the gate products of every layer, 2 * 4H * (in + H) with in = H (the embedding
+    and the lower layer's h are H wide), and the pred projection 2 * joint_hidden * H.
+    Returns (per joint evaluation, per LSTM step)."""
+    H, J = model.pred_hidden, model.joint_hidden
+    joint = 2 * J * model.v_out
+    lstm = model.n_layers * 2 * 4 * H * (H + H) + 2 * J * H
+    return joint, lstm
 
 
 def profiled_traffic(config_key):
-    """dram bytes per loop iteration of the step-loop kernel from the committed ncu
-    summary (profiles/step_loop_kernel_config<k>.md), or None."""
-    path = os.path.join(ROOT, "profiles", f"step_loop_kernel_config{config_key}.md")
+    """dram bytes per joint evaluation of the bulk-loop kernel from the committed ncu
+    summary (profiles/bulk_loop_kernel_config<k>.md), or None."""
+    path = os.path.join(ROOT, "profiles", f"bulk_loop_kernel_config{config_key}.md")
     if not os.path.exists(path):
         return None
-    m = re.search(r"dram_bytes_per_iteration:\s*([0-9.eE+]+)", open(path).read())
+    m = re.search(r"dram_bytes_per_joint_evaluation:\s*([0-9.eE+]+)", open(path).read())
     return float(m.group(1)) if m else None
 
 
-def read_peaks():
+def read_peaks(kind="hbm"):
+    """(peak, "measured" | "fallback"): HBM copy GB/s, or the sustained cuBLAS bf16
+    TFLOP/s (the bulk loop runs for a large part of every step, back to back)."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         d = json.load(open(path))
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return (float(d["hbm_gbs"]) if kind == "hbm" else float(d["bf16_tflops_sustained"])), "measured"
+    return (6650.0 if kind == "hbm" else 1400.0), "fallback"
 
 
 # ------------------------------------------------------------------ main ----
@@ -520,6 +522,8 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
     t_wall = time.perf_counter()
     tot_ms = loop_ms = enc_ms = 0.0
     tokens = steps = iters = emit_iters = launches = 0
+    bulk_ms = 0.0
+    bulk_steps = bulk_lstm = bulk_iters = 0
     phase = np.zeros(8)
     lat = None
     for _ in range(args.steps):
@@ -533,6 +537,10 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
         emit_iters += r.emit_iterations
         launches += r.kernel_launches
         phase += np.array(r.phase_ms[:], np.float64)
+        bulk_ms += r.bulk_ms
+        bulk_steps += r.bulk_steps
+        bulk_lstm += r.bulk_lstm_steps
+        bulk_iters += r.bulk_iterations
         lat = r.encproj_ms + fin[:Bn].astype(np.float64)
     barrier()
     wall_s = time.perf_counter() - t_wall
@@ -592,11 +600,14 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
     result = None
     if rank == 0:
         value = tokens_all / (tot_ms / 1e3) if tot_ms > 0 else 0.0
-        joint_b, lstm_b = per_iter_bytes(model)
-        alg_bytes = joint_b * iters + lstm_b * emit_iters
-        achieved = alg_bytes / (loop_ms / 1e3) / 1e9 if loop_ms > 0 else 0.0
-        peak, peak_kind = read_peaks()
+        fj, fl = bulk_flops(model)
+        alg_flops = fj * bulk_steps + fl * bulk_lstm
+        achieved = alg_flops / (bulk_ms / 1e3) / 1e12 if bulk_ms > 0 else 0.0
+        peak, peak_kind = read_peaks("tensor")
         tr = profiled_traffic(args.config)
+        # products issued per algorithmic product: activations split into f16 hi + lo;
+        # q8_0 weights (scaled) split into hi + lo too, f16 weights are exact
+        products = 3 if wtype == "q8_0" else 2
         h2d = int(enc.nbytes)
         d2h = int(tokens / max(1, args.steps)) * 4 + (Bn + 1) * 8 + Bn * 4
         parity = None
@@ -637,14 +648,20 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
                                "timing": "one pk_decode_batch call at a time, copies inside the call, "
                                          "the library's CUDA events; max over ranks"},
                     "tokens_match_device_run": same},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak if peak else None,
-                         "traffic": (tr * iters / args.steps) if tr else None,
-                         "kernel": "step_loop_kernel",
-                         "note": f"algorithmic bytes = joint.out weights ({joint_b} B) per loop "
-                                 f"iteration + LSTM/pred-proj weights ({lstm_b} B) per iteration with "
-                                 f"an emission, as stored ({wtype}); time = step-loop kernel CUDA events; "
-                                 f"peak {peak_kind}"},
+                         "traffic": (tr * bulk_steps / args.steps) if tr else None,
+                         "kernel": "bulk_loop_kernel",
+                         "issued_tflops": achieved * products,
+                         "note": f"algorithmic FLOPs = {fj} per joint evaluation ({bulk_steps // args.steps} "
+                                 f"per launch) + {fl} per LSTM step ({bulk_lstm // args.steps} per launch), "
+                                 f"one product each; the kernel issues {products} f16 tcgen05 products per "
+                                 f"algorithmic product (issued_tflops); time = the bulk kernel's CUDA events "
+                                 f"({bulk_ms / args.steps:.2f} ms per launch, {bulk_iters // args.steps} iterations); "
+                                 f"peak = cuBLAS bf16 sustained, {peak_kind}; traffic = dram bytes per joint "
+                                 f"evaluation from the committed ncu summary x evaluations per launch"},
+            "persistent_loop": {"kernel": "step_loop_kernel", "ms_per_step": (loop_ms - bulk_ms) / args.steps,
+                                "iterations_per_step": (iters - bulk_iters) / args.steps},
         }
     if world == 1 and not args.no_cpu_baseline and rank == 0:
         o, kind = reference_decoder(model)

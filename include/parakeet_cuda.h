@@ -207,6 +207,8 @@ typedef struct pk_result {
                                      free stage, weight loads waiting, MMA issue waiting for A, for the
                                      weights, for a free accumulator, epilogue waiting for an
                                      accumulator, epilogue work, MMA issue */
+    int64_t   bulk_steps;         /* joint evaluations made on the bulk loop (of total_steps) */
+    int64_t   bulk_lstm_steps;    /* LSTM steps (emissions and initial steps) made on the bulk loop */
 } pk_result;
 
 /* Greedy decode of B fresh utterances (each starts from tdt_init_state /

@@ -179,7 +179,8 @@ class Decoder:
                "loop_iterations": int(r.loop_iterations), "encproj_ms": r.encproj_ms,
                "loop_ms": r.loop_ms, "total_ms": r.total_ms, "tokens_needed": int(r.tokens_needed),
                "bulk_ms": r.bulk_ms, "bulk_iterations": int(r.bulk_iterations),
-               "bulk_phase_ms": list(r.bulk_phase_ms)}
+               "bulk_phase_ms": list(r.bulk_phase_ms), "bulk_steps": int(r.bulk_steps),
+               "bulk_lstm_steps": int(r.bulk_lstm_steps)}
         if bounds is not None:
             out["bounds"] = [bounds[boffs[i]:boffs[i + 1]].copy() for i in range(B)]
         if want_finish:

@@ -64,7 +64,8 @@ class pk_result(C.Structure):
                 ("phase_ms", C.c_double * 8),
                 ("encproj_ms", C.c_double), ("loop_ms", C.c_double), ("total_ms", C.c_double),
                 ("bulk_ms", C.c_double), ("bulk_iterations", C.c_int64),
-                ("bulk_phase_ms", C.c_double * 20)]
+                ("bulk_phase_ms", C.c_double * 20),
+                ("bulk_steps", C.c_int64), ("bulk_lstm_steps", C.c_int64)]
 
 
 class pk_trace(C.Structure):

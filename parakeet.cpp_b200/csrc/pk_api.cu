@@ -826,6 +826,8 @@ pk_status emit_results(pk_ctx * x, Run & r, pk_result * res) {
     res->bulk_ms = r.ms_bulk;
     res->bulk_iterations = r.ctl[C_BULKITERS];
     for (int i = 0; i < 20; ++i) res->bulk_phase_ms[i] = (double) r.bprof[i] * 1e-6;
+    res->bulk_steps = r.ctl[C_BULKSTEPS];
+    res->bulk_lstm_steps = r.ctl[C_BULKEMITS];
     if (ntok > res->tokens_cap || (ntok > 0 && !res->tokens))
         return fail(PK_ERR_CAPACITY, "token buffer holds %lld, %lld needed", (long long) res->tokens_cap,
                     (long long) ntok);

@@ -772,6 +772,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
     int n_emit = __ldcg(&P.ctl[C_NEMIT]);
     int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
     int n_prev = 0, iter = 0, emit_iters = 0;
+    long long sum_live = 0, sum_emit = 0;    // this loop's joint evaluations and LSTM steps
     unsigned long long * keys = P.keys;                 // one key buffer: cleared by the decision that reads it
     bool ok = __ldcg(&P.ctl[C_ERR]) == 0;
     while (ok && n_live >= Q.min_live && n_live > 0) {
@@ -903,7 +904,11 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
             P.ctl[C_ITERS] = iter + 1;
             P.ctl[C_EMITITERS] = emit_iters;
             P.ctl[C_BULKITERS] = iter + 1;
+            P.ctl[C_BULKSTEPS] = (int) (sum_live + n_live);
+            P.ctl[C_BULKEMITS] = (int) (sum_emit + n_emit);
         }
+        sum_live += n_live;
+        sum_emit += n_emit;
         n_prev = n_live;
         sel = nsel;
         n_emit = ste;

@@ -41,6 +41,8 @@ enum CtlField : int {
     C_ERRINFO,        // first failing utterance / index (diagnostics)
     C_EMITITERS,      // iterations whose leader produced a non-empty emit list
     C_BULKITERS,      // iterations run by the bulk loop (pk_bulk.cu) before the persistent loop
+    C_BULKSTEPS,      // joint evaluations (live utterance-iterations) on the bulk loop
+    C_BULKEMITS,      // LSTM steps (emit-list entries) on the bulk loop
     kCtl = 16
 };
 
