@@ -550,25 +550,32 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
     # step's decode. Time = host wall clock around the K synchronous decode calls
     # (every copy in and out inside it), max over ranks. ----
     def prefetch(batch):
-        rc = dec.prefetch_raw(batch)
+        rc, ticket = dec.prefetch_raw(batch)
         if rc != 0:
             raise pk.PkError(rc, "pk_prefetch_batch", pk.last_error())
+        return ticket
+
+    def call_staged(ticket):
+        batch_host.prefetch_ticket = ticket
+        try:
+            return call(batch_host, res_host())
+        finally:
+            batch_host.prefetch_ticket = 0
 
     # untimed: the host-input paths once each, so that their device buffers (two
     # prefetch slots, the in-call copy's buffer) exist before timing, as in a server
-    prefetch(batch_host)
-    prefetch(batch_host)
-    call(batch_host, res_host())
-    call(batch_host, res_host())
+    staged = [prefetch(batch_host), prefetch(batch_host)]
+    call_staged(staged[0])
+    call_staged(staged[1])
     call(batch_host, res_host())
     barrier()
     e2e_tokens = 0
     t_e2e = time.perf_counter()
-    prefetch(batch_host)
+    staged = [prefetch(batch_host)]
     for k in range(args.steps):
         if k + 1 < args.steps:
-            prefetch(batch_host)
-        r = call(batch_host, res_host())
+            staged.append(prefetch(batch_host))
+        r = call_staged(staged.pop(0))
         e2e_tokens += r.tokens_needed
     e2e_ms = (time.perf_counter() - t_e2e) * 1e3
     barrier()

@@ -169,6 +169,9 @@ typedef struct pk_batch {
     int32_t         max_symbols_per_step; /* <= 0: model default */
     const int64_t * frame_offsets;     /* host, B entries */
     const int32_t * n_frames;          /* host, B entries (>= 0) */
+    uint64_t        prefetch_ticket;   /* 0: host input is copied by the call; else a ticket of
+                                          pk_prefetch_batch: the call reads that staged copy
+                                          (and not `enc`) */
 } pk_batch;
 
 /* Results. Pointers are host memory unless results_on_device = 1. Token ids of
@@ -225,28 +228,34 @@ PK_API int64_t   pk_tokens_capacity(const int32_t * n_frames, int32_t B, int32_t
  * has no device copy to overlap (include/parakeet/engine.h:35-55).
  *
  * Starts copying a batch's HOST encoder outputs (frames 0 .. max_b
- * frame_offsets[b] + n_frames[b]) to the device on a copy stream of the context
- * and returns without waiting for the copy. Prefetched copies form a queue of at
- * most two; a third prefetch replaces the oldest. The next decode call with host
- * input (pk_decode_batch, pk_decode_trace, pk_stream_window) whose `enc` pointer
- * is the queue head's and whose frames the head covers uses that copy (the
- * device waits for it) instead of copying itself; a call with any other host
- * input empties the queue and copies as usual. Calls with device input leave
- * the queue alone. So the copy of batch k+1 overlaps the decode of batch k:
+ * frame_offsets[b] + n_frames[b]) to the device on a copy stream of the context,
+ * returns without waiting for the copy, and writes a ticket (nonzero) naming the
+ * staged copy to *ticket. A decode call (pk_decode_batch, pk_decode_trace) whose
+ * pk_batch carries that ticket in prefetch_ticket reads the staged copy -- the
+ * device waits for it -- instead of copying `enc`; the batch must not read more
+ * frames than the prefetch covered. A ticket is used once. At most two copies are
+ * staged: a prefetch made while two are staged replaces the older one, and its
+ * ticket is no longer valid. A decode given a ticket that is not staged (used
+ * already, replaced) or that covers too few frames fails with PK_ERR_INVALID and
+ * copies nothing. Calls without a ticket (prefetch_ticket = 0, device input,
+ * pk_stream_window) leave the staged copies alone. So the copy of batch k+1
+ * overlaps the decode of batch k:
  *
- *     pk_prefetch_batch(ctx, &b[0]);
+ *     pk_prefetch_batch(ctx, &b[0], &b[0].prefetch_ticket);
  *     for (k = 0; k < n; ++k) {
- *         if (k + 1 < n) pk_prefetch_batch(ctx, &b[k + 1]);
+ *         if (k + 1 < n) pk_prefetch_batch(ctx, &b[k + 1], &b[k + 1].prefetch_ticket);
  *         pk_decode_batch(ctx, &b[k], &res[k]);
  *     }
  *
- * The host buffer must stay valid and unchanged until the decode that uses its
- * copy returns. Pinned host memory makes the copy asynchronous; pageable memory
- * is copied before this call returns. When it returns, the copy of the prefetch
- * two calls earlier has completed. A batch with enc_on_device = 1 is rejected
- * (PK_ERR_INVALID). The decode's total_ms does not include a prefetched copy
- * except for any wait for it to finish. */
-PK_API pk_status pk_prefetch_batch(pk_ctx * ctx, const pk_batch * batch);
+ * The staged copy is the host buffer as it was when the copy ran: the buffer
+ * must stay valid and unchanged until the copy has completed, which is when the
+ * decode that uses the ticket returns, or the second later pk_prefetch_batch call
+ * returns, whichever comes first; after that the caller may refill it. Pinned
+ * host memory makes the copy asynchronous; pageable memory is copied before this
+ * call returns. A batch with enc_on_device = 1 is rejected (PK_ERR_INVALID); a
+ * batch that reads no frames stages nothing and gets ticket 0. The decode's
+ * total_ms does not include a prefetched copy except for any wait for it. */
+PK_API pk_status pk_prefetch_batch(pk_ctx * ctx, const pk_batch * batch, uint64_t * ticket);
 
 /* --- teacher-forced trace (parity harness) -------------------------------- */
 

@@ -53,7 +53,7 @@ def lib():
             "pk_get_info": ([P, P], I32), "pk_set_option": ([P, I32, I64], I32),
             "pk_last_error": ([], C.c_char_p), "pk_abi_version": ([], I32),
             "pk_decode_batch": ([P, P, P], I32), "pk_tokens_capacity": ([P, I32, I32], I64),
-            "pk_prefetch_batch": ([P, P], I32),
+            "pk_prefetch_batch": ([P, P, P], I32),
             "pk_decode_trace": ([P, P, P, P], I32), "pk_stream_create": ([P, P], I32),
             "pk_stream_destroy": ([P], None), "pk_stream_reset": ([P], I32),
             "pk_stream_window": ([P, P, I32, I32, I32, I32, I32, P, I32, P, P, P, I32, P], I32),
@@ -129,8 +129,10 @@ class Decoder:
     def set_option(self, opt: int, value: int):
         _check(lib().pk_set_option(self.h, opt, value), "pk_set_option")
 
-    def make_batch(self, enc, offs, n_frames, max_symbols=None, enc_on_device=False, d_enc=None):
-        """A pk_batch plus the arrays it points to (keep both alive)."""
+    def make_batch(self, enc, offs, n_frames, max_symbols=None, enc_on_device=False, d_enc=None,
+                   ticket: int = 0):
+        """A pk_batch plus the arrays it points to (keep both alive). ticket: a
+        prefetch ticket whose staged copy the decode reads instead of enc."""
         n_frames = np.ascontiguousarray(n_frames, np.int32)
         offs = np.ascontiguousarray(offs, np.int64)
         b = abi.pk_batch()
@@ -145,6 +147,7 @@ class Decoder:
         b.max_symbols_per_step = 0 if max_symbols is None else max_symbols
         b.frame_offsets = offs.ctypes.data_as(C.POINTER(C.c_int64))
         b.n_frames = n_frames.ctypes.data_as(C.POINTER(C.c_int32))
+        b.prefetch_ticket = int(ticket)
         return b, (enc, offs, n_frames)
 
     def _msym(self, max_symbols):
@@ -152,9 +155,10 @@ class Decoder:
 
     def decode_batch(self, enc, offs, n_frames, max_symbols: Optional[int] = None,
                      enc_on_device: bool = False, d_enc: Optional[int] = None,
-                     want_finish: bool = False):
-        """Greedy decode of a ragged batch. Returns dict(tokens=[...], steps, ...)."""
-        b, keep = self.make_batch(enc, offs, n_frames, max_symbols, enc_on_device, d_enc)
+                     want_finish: bool = False, ticket: int = 0):
+        """Greedy decode of a ragged batch. Returns dict(tokens=[...], steps, ...).
+        ticket: a prefetch() ticket; the decode then reads that staged copy."""
+        b, keep = self.make_batch(enc, offs, n_frames, max_symbols, enc_on_device, d_enc, ticket)
         n_frames = keep[2]
         B = len(n_frames)
         cap = int(lib().pk_tokens_capacity(_p(n_frames), B, self._msym(max_symbols)))
@@ -187,19 +191,23 @@ class Decoder:
             out["finish_ms"] = fin[:B].copy()
         return out
 
-    def prefetch(self, enc, offs, n_frames, d_enc: Optional[int] = None):
-        """pk_prefetch_batch: start copying host encoder outputs for the next
-        decode_batch call with the same array (see the header for the queue rules).
-        The arrays are kept alive here until two later prefetches have been made,
-        by which time their copy has completed."""
+    def prefetch(self, enc, offs, n_frames, d_enc: Optional[int] = None) -> int:
+        """pk_prefetch_batch: start copying host encoder outputs; returns the ticket
+        to pass to decode_batch (see the header for the staging rules). The arrays
+        are kept alive here until two later prefetches have been made, by which time
+        their copy has completed."""
         b, keep = self.make_batch(enc, offs, n_frames, d_enc=d_enc)
-        _check(lib().pk_prefetch_batch(self.h, C.byref(b)), "pk_prefetch_batch")
+        t = C.c_uint64(0)
+        _check(lib().pk_prefetch_batch(self.h, C.byref(b), C.byref(t)), "pk_prefetch_batch")
         self._prefetched = (getattr(self, "_prefetched", ()) + (keep,))[-2:]
-        return keep[0]
+        return int(t.value)
 
-    def prefetch_raw(self, batch: abi.pk_batch) -> int:
-        """Direct pk_prefetch_batch call on a prepared struct (benchmarks)."""
-        return int(lib().pk_prefetch_batch(self.h, C.byref(batch)))
+    def prefetch_raw(self, batch: abi.pk_batch):
+        """Direct pk_prefetch_batch call on a prepared struct (benchmarks).
+        Returns (status, ticket)."""
+        t = C.c_uint64(0)
+        rc = int(lib().pk_prefetch_batch(self.h, C.byref(batch), C.byref(t)))
+        return rc, int(t.value)
 
     def decode_batch_raw(self, batch: abi.pk_batch, result: abi.pk_result) -> int:
         """Direct pk_decode_batch call on prepared structs (benchmarks)."""

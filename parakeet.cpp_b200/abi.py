@@ -50,7 +50,8 @@ class pk_info(C.Structure):
 class pk_batch(C.Structure):
     _fields_ = [("enc", C.c_void_p), ("enc_on_device", C.c_int32), ("B", C.c_int32),
                 ("d_enc", C.c_int32), ("max_symbols_per_step", C.c_int32),
-                ("frame_offsets", C.POINTER(C.c_int64)), ("n_frames", C.POINTER(C.c_int32))]
+                ("frame_offsets", C.POINTER(C.c_int64)), ("n_frames", C.POINTER(C.c_int32)),
+                ("prefetch_ticket", C.c_uint64)]
 
 
 class pk_result(C.Structure):

@@ -103,21 +103,14 @@ struct pk_ctx {
         tokregion, bnd, bndregion, frameoff, offsets, boffsets, compact, bcompact;
     DevBuf tr_logits, tr_h, tr_c, tr_tok, tr_dur, tr_ftok, tr_fdur;
     cudaEvent_t ev[7] = {};
-    // prefetched host encoder outputs: a queue of up to two staged copies made on a
-    // copy stream (pk_prefetch_batch); copy n records cev[n & 1]
+    // prefetched host encoder outputs: up to two staged copies made on a copy stream
+    // (pk_prefetch_batch), each named by its ticket n + 1; copy n records cev[n & 1]
     cudaStream_t cstream = nullptr;
     cudaEvent_t cev[2] = {};
     uint64_t n_copies = 0;
     DevBuf stg[2];
-    const float * stg_src[2] = {nullptr, nullptr};
     int64_t stg_frames[2] = {0, 0};
-    uint64_t stg_seq[2] = {0, 0};   // 0: empty; else 1 + the copy's number (queue order)
-    int stg_head() const {          // oldest staged copy, or -1
-        if (!stg_seq[0] && !stg_seq[1]) return -1;
-        if (!stg_seq[0]) return 1;
-        if (!stg_seq[1]) return 0;
-        return stg_seq[0] < stg_seq[1] ? 0 : 1;
-    }
+    uint64_t stg_seq[2] = {0, 0};   // 0: empty; else 1 + the copy's number = its ticket
     std::vector<DevBuf *> all_bufs() {
         std::vector<DevBuf *> v = {&embed, &enc_w, &enc_b, &pred_w, &pred_b, &out_w, &out_b,
                                    &durations, &special, &enc, &encp, &h, &c, &predp, &hid, &ust,
@@ -483,6 +476,7 @@ struct Run {
     const int64_t * frame_off = nullptr;
     const int32_t * n_frames = nullptr;
     int msym = 1;
+    uint64_t ticket = 0;             // staged prefetch copy to read (pk_batch::prefetch_ticket)
     std::vector<int32_t> t0, sym0, nbefore, segstart, last, symx, fresh;
     const float * h_in = nullptr;    // device [L][H] state to resume (B == 1)
     const float * c_in = nullptr;
@@ -509,7 +503,19 @@ pk_status run_loop(pk_ctx * x, Run & r) {
             frames = std::max<int64_t>(frames, r.frame_off[b] + r.n_frames[b]);
         }
     }
-    if (frames > 0 && !r.enc) return fail(PK_ERR_INVALID, "null encoder output");
+    int stage = -1;                  // the staged prefetch copy this call reads
+    if (r.ticket) {
+        if (r.enc_dev) return fail(PK_ERR_INVALID, "prefetch_ticket given with device input");
+        for (int i = 0; i < 2; ++i)
+            if (x->stg_seq[i] == r.ticket) stage = i;
+        if (stage < 0)
+            return fail(PK_ERR_INVALID, "prefetch ticket %llu is not staged (already used, or replaced "
+                        "by two later prefetches)", (unsigned long long) r.ticket);
+        if (x->stg_frames[stage] < frames)
+            return fail(PK_ERR_INVALID, "prefetch ticket %llu holds %lld frames, the batch reads %lld",
+                        (unsigned long long) r.ticket, (long long) x->stg_frames[stage], (long long) frames);
+    }
+    if (frames > 0 && !r.enc && stage < 0) return fail(PK_ERR_INVALID, "null encoder output");
     const int msym1 = std::max(1, r.msym);
     std::vector<int64_t> tokregion(B), bndregion(B);
     int64_t tok_total = 0, bnd_total = 0;
@@ -550,20 +556,16 @@ pk_status run_loop(pk_ctx * x, Run & r) {
 
     PK_CK(cudaEventRecord(x->ev[0], s));
     const float * encsrc = r.enc;
-    if (frames > 0 && !r.enc_dev) {
-        const int q = x->stg_head();
-        if (q >= 0 && x->stg_src[q] == r.enc && x->stg_frames[q] >= frames) {
-            // the queue head is this input, prefetched: wait for its copy on the device
-            PK_CK(cudaStreamWaitEvent(s, x->cev[(x->stg_seq[q] - 1) & 1], 0));
-            encsrc = x->stg[q].as<float>();
-            x->stg_seq[q] = 0;
-        } else {
-            // other host input: prefetched copies are out of order with the calls, drop them
-            x->stg_seq[0] = x->stg_seq[1] = 0;
-            PK_CK(x->enc.ensure((size_t) frames * x->De * 4));
-            PK_CK(cudaMemcpyAsync(x->enc.p, r.enc, (size_t) frames * x->De * 4, cudaMemcpyHostToDevice, s));
-            encsrc = x->enc.as<float>();
-        }
+    if (stage >= 0) {
+        // the prefetched copy: the device waits for it (copy n recorded cev[n & 1]; a
+        // later copy that re-recorded that event was queued after it on the copy stream)
+        PK_CK(cudaStreamWaitEvent(s, x->cev[(x->stg_seq[stage] - 1) & 1], 0));
+        encsrc = x->stg[stage].as<float>();
+        x->stg_seq[stage] = 0;       // a ticket is used once
+    } else if (frames > 0 && !r.enc_dev) {
+        PK_CK(x->enc.ensure((size_t) frames * x->De * 4));
+        PK_CK(cudaMemcpyAsync(x->enc.p, r.enc, (size_t) frames * x->De * 4, cudaMemcpyHostToDevice, s));
+        encsrc = x->enc.as<float>();
     }
     PK_CK(cudaEventRecord(x->ev[1], s));
     const bool ep_tc = use_tc && x->ep_ok && (reinterpret_cast<uintptr_t>(encsrc) & 15u) == 0;
@@ -913,6 +915,7 @@ pk_status batch_run(pk_ctx * x, const pk_batch * b, const pk_trace * trace, pk_r
     r.frame_off = b->frame_offsets;
     r.n_frames = b->n_frames;
     r.msym = b->max_symbols_per_step > 0 ? b->max_symbols_per_step : x->max_sym;
+    r.ticket = b->prefetch_ticket;
     r.trace = trace;
     const size_t n = (size_t) std::max(b->B, 0);
     r.t0.assign(n, 0); r.sym0.assign(n, 0); r.nbefore.assign(n, 0); r.segstart.assign(n, 0);
@@ -1154,8 +1157,9 @@ pk_status pk_decode_batch(pk_ctx * x, const pk_batch * b, pk_result * res) {
     return batch_run(x, b, nullptr, res);
 }
 
-pk_status pk_prefetch_batch(pk_ctx * x, const pk_batch * b) {
-    if (!x || !b) return fail(PK_ERR_INVALID, "null argument");
+pk_status pk_prefetch_batch(pk_ctx * x, const pk_batch * b, uint64_t * ticket) {
+    if (ticket) *ticket = 0;
+    if (!x || !b || !ticket) return fail(PK_ERR_INVALID, "null argument");
     if (b->enc_on_device) return fail(PK_ERR_INVALID, "prefetch takes host encoder outputs");
     if (b->d_enc != x->De)
         return fail(PK_ERR_DMODEL, "encoder d_model mismatch (%d vs %d)", b->d_enc, x->De);
@@ -1169,7 +1173,7 @@ pk_status pk_prefetch_batch(pk_ctx * x, const pk_batch * b) {
             frames = std::max<int64_t>(frames, b->frame_offsets[i] + b->n_frames[i]);
         }
     }
-    if (frames == 0) return PK_OK;            // nothing the decode would copy
+    if (frames == 0) return PK_OK;            // nothing to copy: ticket 0, the decode copies nothing
     if (!b->enc) return fail(PK_ERR_INVALID, "null encoder output");
     PK_CK(cudaSetDevice(x->device));
     // copy n reuses copy n-2's event: wait for that copy (so its host buffer and,
@@ -1189,9 +1193,9 @@ pk_status pk_prefetch_batch(pk_ctx * x, const pk_batch * b) {
     PK_CK(cudaMemcpyAsync(x->stg[q].p, b->enc, bytes, cudaMemcpyHostToDevice, x->cstream));
     PK_CK(cudaEventRecord(x->cev[n & 1], x->cstream));
     x->n_copies = n + 1;
-    x->stg_src[q] = b->enc;
     x->stg_frames[q] = frames;
     x->stg_seq[q] = n + 1;
+    *ticket = n + 1;
     return PK_OK;
 }
 

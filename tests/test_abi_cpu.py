@@ -69,7 +69,7 @@ def test_invalid_arguments_report_status(pk):
     assert L.pk_shard_lpt(None, 3, 0, None) == pk.abi.PK_ERR_INVALID
     assert "sharding" in pk.last_error()
     assert L.pk_create(None, 0, None) == pk.abi.PK_ERR_INVALID
-    assert L.pk_prefetch_batch(None, None) == pk.abi.PK_ERR_INVALID
+    assert L.pk_prefetch_batch(None, None, None) == pk.abi.PK_ERR_INVALID
 
 
 def test_create_without_device_fails_cleanly(pk):

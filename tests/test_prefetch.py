@@ -1,6 +1,7 @@
 """pk_prefetch_batch: host encoder outputs copied ahead on the context's copy
-stream and used by the next decode call with the same input; any other host
-input empties the queue. Every decode must return what a plain decode returns."""
+stream; the ticket it returns names the staged copy, and a decode whose batch
+carries the ticket reads that copy. Every decode must return what a plain decode
+of the same frames returns; misuse of a ticket fails loudly."""
 import numpy as np
 import pytest
 
@@ -32,95 +33,122 @@ def _same(a, b):
     assert np.array_equal(a["steps"], b["steps"])
 
 
+def _differs(a, b):
+    return any(not np.array_equal(x, y) for x, y in zip(a["tokens"], b["tokens"]))
+
+
 def test_pipeline_matches_plain_decode(built, model):
-    """prefetch(b0); for k: prefetch(b[k+1]); decode(b[k]) over distinct batches."""
+    """t0 = prefetch(b0); for k: t[k+1] = prefetch(b[k+1]); decode(b[k], t[k])."""
     pk = built
     dec = pk.Decoder(model)
     bs = [_batch(pk, model, s) for s in (1, 2, 3, 4)]
     plain = [dec.decode_batch(*b) for b in bs]
-    dec.prefetch(*bs[0])
+    tickets = [dec.prefetch(*bs[0])]
     for k in range(len(bs)):
         if k + 1 < len(bs):
-            dec.prefetch(*bs[k + 1])
-        _same(dec.decode_batch(*bs[k]), plain[k])
+            tickets.append(dec.prefetch(*bs[k + 1]))
+        _same(dec.decode_batch(*bs[k], ticket=tickets[k]), plain[k])
+    assert len(set(tickets)) == len(tickets) and 0 not in tickets
 
 
-def test_decode_uses_the_prefetched_copy(built, model):
-    """Pageable input is copied before prefetch returns, so changing the host array
-    afterwards shows which copy the decode used: the staged one (the contract says
-    the array must not change; the test breaks it on purpose, on the host)."""
+def test_refilled_buffer_reads_the_staged_copy(built, model):
+    """A server refills its (pageable) buffer with the next request right after the
+    prefetch: the decode with the ticket still reads the frames as they were; a
+    decode without a ticket reads the buffer as it is now."""
     pk = built
     dec = pk.Decoder(model)
     enc, offs, T = _batch(pk, model, 5)
     enc2 = np.ascontiguousarray(enc[::-1])
     want_old = dec.decode_batch(enc, offs, T)
     want_new = dec.decode_batch(enc2.copy(), offs, T)
-    assert any(not np.array_equal(x, y) for x, y in zip(want_old["tokens"], want_new["tokens"]))
+    assert _differs(want_old, want_new)
     buf = enc.copy()
-    dec.prefetch(buf, offs, T)
-    buf[:] = enc2                       # after the copy has been made
-    _same(dec.decode_batch(buf, offs, T), want_old)
-    # the queue is empty now: the next decode copies the array as it is
-    _same(dec.decode_batch(buf, offs, T), want_new)
+    t = dec.prefetch(buf, offs, T)
+    buf[:] = enc2                       # pageable: the copy was made before prefetch returned
+    _same(dec.decode_batch(buf, offs, T), want_new)          # no ticket: the buffer as it is
+    _same(dec.decode_batch(buf, offs, T, ticket=t), want_old)
 
 
-def test_same_array_queued_twice(built, model):
+def test_ticket_is_used_once(built, model):
     pk = built
     dec = pk.Decoder(model)
     enc, offs, T = _batch(pk, model, 6)
     want = dec.decode_batch(enc, offs, T)
-    dec.prefetch(enc, offs, T)
-    dec.prefetch(enc, offs, T)
-    _same(dec.decode_batch(enc, offs, T), want)
-    _same(dec.decode_batch(enc, offs, T), want)
+    t = dec.prefetch(enc, offs, T)
+    _same(dec.decode_batch(enc, offs, T, ticket=t), want)
+    with pytest.raises(pk.PkError) as e:
+        dec.decode_batch(enc, offs, T, ticket=t)
+    assert e.value.status == pk.abi.PK_ERR_INVALID and "not staged" in str(e.value)
+    with pytest.raises(pk.PkError):
+        dec.decode_batch(enc, offs, T, ticket=12345)             # never issued
 
 
 def test_out_of_order_and_replaced_copies(built, model):
-    """A decode whose input is not the queue head drops the queue and copies its own
-    input; a third prefetch replaces the oldest; a prefetch covering fewer frames
-    than the decode needs is not used."""
+    """Staged copies are used in any order; a third prefetch replaces the oldest
+    staged copy, whose ticket then fails; a ticket covering fewer frames than the
+    batch reads fails; a failed decode leaves the other staged copy usable."""
     pk = built
     dec = pk.Decoder(model)
     A, Bb, Cc = (_batch(pk, model, s) for s in (7, 8, 9))
     want = [dec.decode_batch(*x) for x in (A, Bb, Cc)]
-    dec.prefetch(*A)
-    dec.prefetch(*Bb)
-    _same(dec.decode_batch(*Bb), want[1])          # head is A: dropped, direct copy
-    _same(dec.decode_batch(*A), want[0])
-    for x in (A, Bb, Cc):
-        dec.prefetch(*x)                            # C replaces A
-    for x, w in zip((A, Bb, Cc), want):
-        _same(dec.decode_batch(*x), w)
+    ta, tb = dec.prefetch(*A), dec.prefetch(*Bb)
+    _same(dec.decode_batch(*Bb, ticket=tb), want[1])
+    _same(dec.decode_batch(*A, ticket=ta), want[0])
+    ta, tb, tc = (dec.prefetch(*x) for x in (A, Bb, Cc))          # C replaces A
+    with pytest.raises(pk.PkError):
+        dec.decode_batch(*A, ticket=ta)
+    _same(dec.decode_batch(*Cc, ticket=tc), want[2])
+    _same(dec.decode_batch(*Bb, ticket=tb), want[1])
     enc, offs, T = A
-    dec.prefetch(enc, offs[:2], T[:2])             # fewer frames than the whole batch
-    _same(dec.decode_batch(*A), want[0])
+    tshort = dec.prefetch(enc, offs[:2], T[:2])                   # fewer frames than the whole batch
+    with pytest.raises(pk.PkError) as e:
+        dec.decode_batch(*A, ticket=tshort)
+    assert "frames" in str(e.value)
+    _same(dec.decode_batch(enc, offs[:2], T[:2], ticket=tshort), {"tokens": want[0]["tokens"][:2],
+                                                                   "steps": want[0]["steps"][:2]})
 
 
-def test_device_input_leaves_the_queue(built, model):
+def test_calls_without_ticket_leave_staged_copies(built, model):
+    """Device input, host input without a ticket and stream windows neither use nor
+    drop a staged copy; a device batch with a ticket and a device prefetch are
+    rejected."""
     import torch
     pk = built
     dec = pk.Decoder(model)
     A, Bb = _batch(pk, model, 10), _batch(pk, model, 11)
     want_a, want_b = dec.decode_batch(*A), dec.decode_batch(*Bb)
-    dec.prefetch(*A)
+    ta = dec.prefetch(*A)
     ed = torch.from_numpy(Bb[0]).cuda()
     torch.cuda.synchronize()
     _same(dec.decode_batch(ed.data_ptr(), Bb[1], Bb[2], enc_on_device=True), want_b)
-    _same(dec.decode_batch(*A), want_a)
+    _same(dec.decode_batch(*Bb), want_b)
+    dec.stream().window(np.ascontiguousarray(Bb[0][:20]))
+    with pytest.raises(pk.PkError):
+        dec.decode_batch(ed.data_ptr(), Bb[1], Bb[2], enc_on_device=True, ticket=ta)
+    _same(dec.decode_batch(*A, ticket=ta), want_a)
     b, _ = dec.make_batch(ed.data_ptr(), Bb[1], Bb[2], enc_on_device=True)
-    assert dec.prefetch_raw(b) == pk.abi.PK_ERR_INVALID
+    rc, t = dec.prefetch_raw(b)
+    assert rc == pk.abi.PK_ERR_INVALID and t == 0
 
 
-def test_stream_window_uses_prefetch(built, model):
+def test_pinned_pipeline_overlaps_refill(built, model):
+    """Pinned input (asynchronous copy): a two-buffer ring where each buffer is
+    refilled once the second later prefetch has returned, as the header allows;
+    every decode matches the plain decode of its request."""
+    import torch
     pk = built
     dec = pk.Decoder(model)
-    enc, _, T = _batch(pk, model, 12, B=1)
-    s0 = dec.stream()
-    want = s0.window(enc)
-    assert not np.array_equal(dec.stream().window(np.ascontiguousarray(enc[::-1]))["tokens"], want["tokens"])
-    s1 = dec.stream()
-    buf = enc.copy()
-    dec.prefetch(buf, np.zeros(1, np.int64), T)
-    buf[:] = enc[::-1]                  # after the copy: the window must see the staged copy
-    got = s1.window(buf)
-    assert np.array_equal(got["tokens"], want["tokens"]) and got["steps"] == want["steps"]
+    reqs = [_batch(pk, model, 20 + s, B=4) for s in range(6)]
+    rows = max(int(max(o + t for o, t in zip(r[1], r[2]))) for r in reqs)
+    ring = [torch.zeros((rows, model.d_enc), dtype=torch.float32).pin_memory() for _ in range(2)]
+    plain = [dec.decode_batch(*r) for r in reqs]
+    tickets = []
+    for k, (enc, offs, T) in enumerate(reqs):
+        buf = ring[k % 2].numpy()
+        buf[:enc.shape[0]] = enc
+        tickets.append(dec.prefetch(buf, offs, T))
+        if k >= 1:
+            _same(dec.decode_batch(ring[(k - 1) % 2].numpy(), reqs[k - 1][1], reqs[k - 1][2],
+                                   ticket=tickets[k - 1]), plain[k - 1])
+    _same(dec.decode_batch(ring[(len(reqs) - 1) % 2].numpy(), reqs[-1][1], reqs[-1][2],
+                           ticket=tickets[-1]), plain[-1])
