@@ -32,6 +32,12 @@ def tok_hash(a) -> np.uint64:
     return np.frombuffer(hashlib.blake2b(b, digest_size=8).digest(), dtype="<u8")[0]
 
 
+def config5_lengths(S):
+    """Configuration 5's utterance lengths: log-normal, median 250 frames, sigma 0.8,
+    clipped to [25, 3750], 4096 utterances."""
+    return S.lengths_lognormal(4096, 250.0, 0.8, 25, 3750, seed=7)
+
+
 def cases(pk):
     """name -> (model factory, (enc, offs, T) factory, keep full token arrays)."""
     S = pk.synth
@@ -52,10 +58,13 @@ def cases(pk):
         offs = (np.arange(B, dtype=np.int64) * 613) % (pool - TT + 1)
         return enc, offs, np.full(B, TT, np.int32)
 
-    def c5():
-        T = S.lengths_lognormal(4096, 250.0, 0.8, 25, 3750, seed=7)
-        enc, offs = S.encoder_pooled(T, np.arange(len(T)), 1024, seed=99)
-        return enc, offs, T
+    def c5(ids=None):
+        """ids: only these utterances' frames (each utterance's frames depend on its id
+        alone); offsets then index the returned rows, in the order of ids."""
+        T = config5_lengths(S)
+        ids = np.arange(len(T)) if ids is None else np.asarray(ids)
+        enc, offs = S.encoder_pooled(T[ids], ids, 1024, seed=99)
+        return enc, offs, T[ids]
 
     return {
         "config2": (lambda: S.tdt_0_6b(seed=1234), c2, True),

@@ -1,9 +1,10 @@
 """CPU tests of the oracle (the CPU restatement of the reference decoder).
 
-The oracle is pinned against (1) gguf-py's dequantization of the same q8_0/f16
-bytes and (2) golden vectors from an independent float64 numpy restatement
-(tests/golden/make_golden.py). The reference's own fixtures need real GGUF
-models and cannot run here.
+Checked here against (1) gguf-py's dequantization of the same q8_0/f16 bytes and
+(2) golden vectors from an independent float64 numpy restatement
+(tests/golden/make_golden.py). The pin against the reference's own decoder, built
+unchanged from its sources, is tests/test_ref_pin.py. The reference's own test
+fixtures need real GGUF models and NeMo dumps that are not available here.
 """
 import os
 
