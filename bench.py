@@ -57,13 +57,19 @@ CONFIGS = {
 }
 DEFAULT_CONFIG = "5"
 METRIC = "tdt_greedy_decode_tokens_per_sec"
-# What the default (tensor-core) step loop computes in, by weight type: exact weights,
-# h as int16 fixed point in two int8 digits for the q8_0 LSTM / pred-proj (int8 MMA,
-# int32 per 32-wide block, f32 block scale), the joint hidden layer as f16 hi + lo
-# (22 significant bits) against exact f16 weights, f32 accumulation and state.
-DTYPE = {"q8_0": "q8_0 weights; int16 fixed-point h (int8 MMA) in LSTM/pred-proj; f16 hi+lo joint; f32 accumulate",
+# What the default (tensor-core) step loops compute in, by weight type: exact weights;
+# in the persistent loop h as int16 fixed point in two int8 digits for the q8_0 LSTM /
+# pred-proj (int8 MMA, int32 per 32-wide block, f32 block scale) and the joint hidden
+# layer as f16 hi + lo (22 significant bits); in the bulk loop activations and q8_0
+# weights as f16 hi + lo (three tcgen05 products), the joint of large iterations
+# screened by one f16 product with the candidates recomputed in f32; f32 accumulation
+# and state.
+DTYPE = {"q8_0": "q8_0 weights; activations as int16 fixed point (int8 MMA) or f16 hi+lo (f16 MMA, 22 bits); "
+                 "screened joint: 1 f16 product + f32 recomputation of candidates; f32 accumulate",
          "f16": "f16 weights; f16 hi+lo activations; f32 accumulate",
-         "f32": "f32"}
+         "f32": "f32",
+         "q8": "q8_0 weights x q8_0-quantised activations (int8 MMA per 32-block, both scales; ggml "
+               "vec_dot_q8_0_q8_0); f32 accumulate"}
 
 
 def load(name, path, pkg_dir=None):
@@ -248,6 +254,12 @@ def main():
     ap.add_argument("--bulk-min-live", type=int, default=None,
                     help="PK_OPT_BULK_MIN_LIVE: live utterances from which iterations run on the tcgen05 "
                          "bulk loop (library default when absent; 0 = never)")
+    ap.add_argument("--no-screen", action="store_true",
+                    help="PK_OPT_BULK_SCREEN = 0: the bulk loop's joint always takes three f16 products per "
+                         "logit, never one screening product and the f32 recomputation of the candidates")
+    ap.add_argument("--math", default=None, choices=["tc", "q8", "f32"],
+                    help="PK_OPT_MATH (library default when absent: tc); q8 = the optional q8_0-activation "
+                         "mode (ggml's vec_dot_q8_0_q8_0 arithmetic, persistent loop only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--path", default="tdt", choices=["tdt", "ctc"],
@@ -467,7 +479,9 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     torch.cuda.set_device(local_rank)
-    dec = pk.Decoder(model, device=local_rank, bulk_min_live=args.bulk_min_live)
+    dec = pk.Decoder(model, device=local_rank, bulk_min_live=args.bulk_min_live, math=args.math)
+    if args.no_screen:
+        dec.set_option(pk.abi.PK_OPT_BULK_SCREEN, 0)
     msym = dec.info.max_symbols_per_step
     Bn = len(T)
     cap = int(pk.lib().pk_tokens_capacity(T.ctypes.data, Bn, msym))
@@ -523,7 +537,7 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
     tot_ms = loop_ms = enc_ms = 0.0
     tokens = steps = iters = emit_iters = launches = 0
     bulk_ms = 0.0
-    bulk_steps = bulk_lstm = bulk_iters = 0
+    bulk_steps = bulk_lstm = bulk_iters = bulk_scr = 0
     phase = np.zeros(8)
     lat = None
     for _ in range(args.steps):
@@ -540,6 +554,7 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
         bulk_ms += r.bulk_ms
         bulk_steps += r.bulk_steps
         bulk_lstm += r.bulk_lstm_steps
+        bulk_scr += r.bulk_screened_steps
         bulk_iters += r.bulk_iterations
         lat = r.encproj_ms + fin[:Bn].astype(np.float64)
     barrier()
@@ -612,9 +627,12 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
         achieved = alg_flops / (bulk_ms / 1e3) / 1e12 if bulk_ms > 0 else 0.0
         peak, peak_kind = read_peaks("tensor")
         tr = profiled_traffic(args.config)
-        # products issued per algorithmic product: activations split into f16 hi + lo;
-        # q8_0 weights (scaled) split into hi + lo too, f16 weights are exact
+        # f16 tcgen05 products issued per algorithmic product: the LSTM and pred-proj
+        # split activations into f16 hi + lo, q8_0 weights (scaled) into hi + lo too (f16
+        # weights are exact); the screened joint issues one (--no-screen: as the LSTM)
         products = 3 if wtype == "q8_0" else 2
+        issued = ((products * fl * bulk_lstm + fj * (products * (bulk_steps - bulk_scr) + bulk_scr))
+                  / (bulk_ms / 1e3) / 1e12 if bulk_ms > 0 else 0.0)
         h2d = int(enc.nbytes)
         d2h = int(tokens / max(1, args.steps)) * 4 + (Bn + 1) * 8 + Bn * 4
         parity = None
@@ -628,7 +646,8 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
-            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": DTYPE[wtype],
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": DTYPE["q8" if args.math == "q8" else "f32" if args.math == "f32" else wtype],
             "data": "synthetic (seeded random-init weights of the named geometry, N(0,1) encoder outputs)",
             "config": config,
             "steps_per_sec": steps_all / (tot_ms / 1e3) if tot_ms > 0 else 0.0,
@@ -659,11 +678,14 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
                          "frac": achieved / peak if peak else None,
                          "traffic": (tr * bulk_steps / args.steps) if tr else None,
                          "kernel": "bulk_loop_kernel",
-                         "issued_tflops": achieved * products,
+                         "issued_tflops": issued,
                          "note": f"algorithmic FLOPs = {fj} per joint evaluation ({bulk_steps // args.steps} "
                                  f"per launch) + {fl} per LSTM step ({bulk_lstm // args.steps} per launch), "
                                  f"one product each; the kernel issues {products} f16 tcgen05 products per "
-                                 f"algorithmic product (issued_tflops); time = the bulk kernel's CUDA events "
+                                 f"algorithmic LSTM / pred-proj product and per unscreened joint product, "
+                                 f"one per screened joint product ({bulk_scr // args.steps} screened "
+                                 f"evaluations per launch) "
+                                 f"(issued_tflops); time = the bulk kernel's CUDA events "
                                  f"({bulk_ms / args.steps:.2f} ms per launch, {bulk_iters // args.steps} iterations); "
                                  f"peak = cuBLAS bf16 sustained, {peak_kind}; traffic = dram bytes per joint "
                                  f"evaluation from the committed ncu summary x evaluations per launch"},

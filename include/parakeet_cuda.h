@@ -115,9 +115,16 @@ typedef struct pk_ctx pk_ctx;
 /* Math modes for the step loop (pk_set_option(PK_OPT_MATH, ...)). */
 enum {
     PK_MATH_F32 = 0,  /* exact dequantized weights, f32 activations, f32 FMA on CUDA cores */
-    PK_MATH_TC  = 1   /* tensor cores (mma.sync f16, f32 accumulate): exact q8_0/f16 weights,
+    PK_MATH_TC  = 1,  /* tensor cores (mma.sync f16, f32 accumulate): exact q8_0/f16 weights,
                          activations as f16 hi+lo (22 significant bits); the default when every
                          step-loop weight is q8_0 or f16 and H, J are multiples of 32 */
+    PK_MATH_Q8  = 2   /* optional, never the default: the arithmetic of ggml's q8_0 matrix
+                         products (vec_dot_q8_0_q8_0), as the reference's graph path runs them:
+                         the LSTM, pred-proj and joint-output activations quantised to q8_0 blocks
+                         (d = max|x| / 127 per 32 values, q = round(x / d)), one int8 tensor-core
+                         product per block scaled by both blocks' d. Persistent loop only (no bulk
+                         loop); needs every step-loop weight in q8_0. Logits move by ~1e-2, so
+                         tokens differ from the f32 reference at more than its near-ties. */
 };
 
 /* Options. */
@@ -128,10 +135,17 @@ enum {
     PK_OPT_TEST_STALL  = 4,  /* test hook: 1 = CTA 0 of the next step loop never arrives at its first
                                 grid barrier, so the other CTAs' bounded waits run out and the call
                                 returns PK_ERR_TIMEOUT (exercises failure detection without a fault) */
-    PK_OPT_BULK_MIN_LIVE = 5 /* tensor-core math: iterations with at least this many live utterances run
+    PK_OPT_BULK_MIN_LIVE = 5, /* tensor-core math: iterations with at least this many live utterances run
                                 on the tcgen05 bulk loop (two-dimensional tiles, accumulators in tensor
                                 memory), the rest on the persistent loop; default 256, 0 = never,
                                 1 = every iteration of a fresh batch (trace runs too) */
+    PK_OPT_BULK_SCREEN = 6   /* bulk-loop iterations with at least this many live utterances (default
+                                1024; 0 = never) compute the joint output screened: one f16 product
+                                per logit screens the tokens against a proven error bound, and the
+                                candidates and the duration logits are recomputed in f32, so the
+                                argmax is that of f32 logits; other iterations take three f16
+                                products per logit (22-bit activations) and the argmax of those.
+                                Trace runs never screen. */
 };
 
 /* Static information about a context. */
@@ -212,6 +226,7 @@ typedef struct pk_result {
                                      accumulator, epilogue work, MMA issue */
     int64_t   bulk_steps;         /* joint evaluations made on the bulk loop (of total_steps) */
     int64_t   bulk_lstm_steps;    /* LSTM steps (emissions and initial steps) made on the bulk loop */
+    int64_t   bulk_screened_steps;/* of bulk_steps, joint evaluations made screened (PK_OPT_BULK_SCREEN) */
 } pk_result;
 
 /* Greedy decode of B fresh utterances (each starts from tdt_init_state /

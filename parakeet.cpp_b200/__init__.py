@@ -99,7 +99,8 @@ class Decoder:
 
     def __init__(self, model, device: int = 0, desc: Optional[abi.ModelDesc] = None,
                  math: Optional[str] = None, bulk_min_live: Optional[int] = None):
-        """math: None (library default: tensor cores when the weights allow), "tc" or "f32".
+        """math: None (library default: tensor cores when the weights allow), "tc", "f32" or
+        "q8" (PK_MATH_Q8: q8_0-quantised activations, ggml's vec_dot_q8_0_q8_0 arithmetic).
         bulk_min_live: PK_OPT_BULK_MIN_LIVE (None: the library default; 0 never runs the
         tcgen05 bulk loop, 1 runs it for every iteration of a fresh batch)."""
         self.model = model
@@ -111,7 +112,8 @@ class Decoder:
         _check(lib().pk_get_info(self.h, C.byref(info)), "pk_get_info")
         self.info = info
         if math is not None:
-            self.set_option(abi.PK_OPT_MATH, {"tc": abi.PK_MATH_TC, "f32": abi.PK_MATH_F32}[math])
+            self.set_option(abi.PK_OPT_MATH, {"tc": abi.PK_MATH_TC, "f32": abi.PK_MATH_F32,
+                                              "q8": abi.PK_MATH_Q8}[math])
         if bulk_min_live is not None:
             self.set_option(abi.PK_OPT_BULK_MIN_LIVE, int(bulk_min_live))
 
@@ -184,7 +186,7 @@ class Decoder:
                "loop_ms": r.loop_ms, "total_ms": r.total_ms, "tokens_needed": int(r.tokens_needed),
                "bulk_ms": r.bulk_ms, "bulk_iterations": int(r.bulk_iterations),
                "bulk_phase_ms": list(r.bulk_phase_ms), "bulk_steps": int(r.bulk_steps),
-               "bulk_lstm_steps": int(r.bulk_lstm_steps)}
+               "bulk_lstm_steps": int(r.bulk_lstm_steps), "bulk_screened_steps": int(r.bulk_screened_steps)}
         if bounds is not None:
             out["bounds"] = [bounds[boffs[i]:boffs[i + 1]].copy() for i in range(B)]
         if want_finish:

@@ -93,7 +93,8 @@ struct pk_ctx {
     pk::BulkWeights bulk{};
     int bulk_ok = 0;
     int bulk_min_live = 256;
-    DevBuf h16, x16, dcount, bprof;
+    int bulk_screen_min = 1024;    // PK_OPT_BULK_SCREEN
+    DevBuf h16, x16, dcount, bprof, norm2, jsum;
     void * pin = nullptr;          // pinned staging of a call's small inputs (copy_segments)
     size_t pin_cap = 0;
     // per-call workspace
@@ -118,7 +119,7 @@ struct pk_ctx {
                                    &tokregion, &bnd, &bndregion, &frameoff, &offsets, &boffsets,
                                    &compact, &bcompact, &tr_logits, &tr_h, &tr_c, &tr_tok, &tr_dur,
                                    &tr_ftok, &tr_fdur, &g0, &prof, &livef, &hst, &xnew, &hidc, &ep_w16, &ep_err, &h16, &x16, &dcount, &bprof,
-                                   &stg[0], &stg[1]};
+                                   &norm2, &jsum, &stg[0], &stg[1]};
         for (int i = 0; i < 2 + pk::kMaxLayers; ++i) { v.push_back(&tc_frag[i]); v.push_back(&tc_scale[i]); }
         for (int l = 0; l < pk::kMaxLayers; ++l) {
             v.push_back(&w_ih[l]); v.push_back(&w_hh[l]); v.push_back(&b_ih[l]); v.push_back(&b_hh[l]);
@@ -529,7 +530,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     PK_CK(x->encp.ensure((size_t) frames * J * 4));
     PK_CK(x->h.ensure(2 * (size_t) L * Bs * H * 4));
     PK_CK(x->c.ensure((size_t) L * Bs * H * 4));
-    const bool use_tc = x->math == PK_MATH_TC && x->tc_ok;
+    const bool use_tc = (x->math == PK_MATH_TC || x->math == PK_MATH_Q8) && x->tc_ok;
     if (use_tc) {
         PK_CK(x->hst.ensure(2 * (size_t) L * Bs * x->tc_rbh));
         PK_CK(x->xnew.ensure((size_t) L * Bs * x->tc_rbh));
@@ -671,6 +672,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         P.sm_weights = x->tc_sm_weights;
         P.rbh = x->tc_rbh; P.rbj = x->tc_rbj; P.area = x->tc_area; P.mb = x->tc_mb;
         P.rpc_j = x->rpc_j; P.rpc_p = x->rpc_p; P.upc = x->upc; P.h_int = x->tc_hint;
+        P.q8 = x->math == PK_MATH_Q8 ? 1 : 0;
         P.tcj = x->tcj; P.tcp = x->tcp;
         for (int l = 0; l < L; ++l) P.tcl[l] = x->tcl[l];
         P.g0 = x->g0.as<float>();
@@ -734,7 +736,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
     bool all_fresh = B > 0;
     for (int b = 0; b < B && all_fresh; ++b)
         all_fresh = r.fresh[b] != 0 || !(r.n_frames[b] > 0 && r.t0[b] < r.n_frames[b]);
-    const bool use_bulk = use_tc && x->bulk_ok && x->bulk_min_live > 0 && all_fresh &&
+    const bool use_bulk = use_tc && x->math == PK_MATH_TC && x->bulk_ok && x->bulk_min_live > 0 && all_fresh &&
                           (int) live.size() >= x->bulk_min_live && B <= x->grid * bulk_threads();
     BulkParams q{};
     if (use_bulk) {
@@ -751,6 +753,19 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         q.h16 = x->h16.as<unsigned char>();
         q.x16 = x->x16.as<unsigned char>();
         q.dcount = x->dcount.as<int2>();
+        // screened joint (not for trace runs, which report the GEMM's own logits)
+        const bool scr = x->bulk_screen_min > 0 && P.trace_steps == 0 && bulk_screen_supported(x->J) &&
+                         x->Vo < 0xFFFF && x->bulk.wnorm != nullptr;
+        q.screen_min = scr ? x->bulk_screen_min : 0;
+        if (scr) {
+            q.jsum_stride = (x->Vo + 63) / 64;
+            PK_CK(x->norm2.ensure(Bs * 4));
+            PK_CK(x->jsum.ensure(Bs * (size_t) q.jsum_stride * 32));
+            PK_CK(cudaMemsetAsync(x->norm2.p, 0, Bs * 4, s));
+            q.norm2 = x->norm2.as<float>();
+            q.jsum = x->jsum.as<uint4>();
+            q.wnorm = x->bulk.wnorm;
+        }
         PK_CK(x->bprof.ensure(20 * 8));
         PK_CK(cudaMemsetAsync(x->bprof.p, 0, 20 * 8, s));
         q.prof = x->bprof.as<unsigned long long>();
@@ -830,6 +845,7 @@ pk_status emit_results(pk_ctx * x, Run & r, pk_result * res) {
     for (int i = 0; i < 20; ++i) res->bulk_phase_ms[i] = (double) r.bprof[i] * 1e-6;
     res->bulk_steps = r.ctl[C_BULKSTEPS];
     res->bulk_lstm_steps = r.ctl[C_BULKEMITS];
+    res->bulk_screened_steps = r.ctl[C_BULKSCREENED];
     if (ntok > res->tokens_cap || (ntok > 0 && !res->tokens))
         return fail(PK_ERR_CAPACITY, "token buffer holds %lld, %lld needed", (long long) res->tokens_cap,
                     (long long) ntok);
@@ -1054,7 +1070,6 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
             if (bulk_prepare(x->bulk, x->H, x->J, x->L, x->Vo, x->V1, x->embed.as<float>(), wih, whh, bih, bhh,
                              x->pred_w.as<float>(), x->out_w.as<float>(), f16w, x->stream) != cudaSuccess) {
                 bulk_release(x->bulk);
-    if (x->pin) cudaFreeHost(x->pin);
                 return cleanup(fail(PK_ERR_CUDA, "bulk-loop weight preparation failed"));
             }
             x->bulk_ok = 1;
@@ -1098,6 +1113,7 @@ void pk_destroy(pk_ctx * x) {
     if (x->cstream) cudaStreamSynchronize(x->cstream);
     for (DevBuf * b : x->all_bufs()) b->release();
     bulk_release(x->bulk);
+    if (x->pin) cudaFreeHost(x->pin);
     for (auto & e : x->ev)
         if (e) cudaEventDestroy(e);
     for (auto & e : x->cev)
@@ -1127,7 +1143,10 @@ pk_status pk_set_option(pk_ctx * x, int32_t opt, int64_t v) {
         case PK_OPT_MATH:
             if (v == PK_MATH_TC && !x->tc_ok)
                 return fail(PK_ERR_INVALID, "tensor-core math needs q8_0/f16 step-loop weights and H, J multiples of 32");
-            if (v != PK_MATH_F32 && v != PK_MATH_TC) return fail(PK_ERR_INVALID, "unsupported math mode %lld", (long long) v);
+            if (v == PK_MATH_Q8 && !(x->tc_ok && x->tc_hint && x->tcj.is_i8))
+                return fail(PK_ERR_INVALID, "q8_0-activation math needs q8_0 weights in every step-loop matrix");
+            if (v != PK_MATH_F32 && v != PK_MATH_TC && v != PK_MATH_Q8)
+                return fail(PK_ERR_INVALID, "unsupported math mode %lld", (long long) v);
             x->math = (int) v;
             return PK_OK;
         case PK_OPT_MAX_SYMBOLS:
@@ -1140,6 +1159,10 @@ pk_status pk_set_option(pk_ctx * x, int32_t opt, int64_t v) {
         case PK_OPT_BULK_MIN_LIVE:
             if (v < 0) return fail(PK_ERR_INVALID, "bulk threshold must be >= 0");
             x->bulk_min_live = (int) std::min<int64_t>(v, 1 << 30);
+            return PK_OK;
+        case PK_OPT_BULK_SCREEN:
+            if (v < 0) return fail(PK_ERR_INVALID, "screening threshold must be >= 0");
+            x->bulk_screen_min = (int) std::min<int64_t>(v, 1 << 30);
             return PK_OK;
         default:
             return fail(PK_ERR_INVALID, "unknown option %d", opt);

@@ -72,6 +72,8 @@ struct BulkSmem {
     const unsigned char * a_s1[kBM];   // segment-1 source
     unsigned char a_fl[kBM];           // bit 0: row in the batch, bit 1: segment 1 is zero
     unsigned long long rprof[8];       // CTA 0, per role: waits and work inside the GEMM phases (ns)
+    int tok_s[kBThreads];              // screened joint: this CTA's slice of the live list, exact argmax
+    int dur_s[kBThreads];
     unsigned tmem_base;
     int err;                       // a wait of this CTA gave up (shared by every role)
     int scan[kBWarps + 2];
@@ -91,24 +93,31 @@ struct Pipe {
     unsigned acc_m = 0, acc_e = 0;                // tiles accumulated (MMA) / drained (epilogue)
 };
 
-// Ring geometry of a phase: a stage is the A tile (hi, lo) then the B tile (hi, lo)
-// of bn rows; every part starts on a 1024-byte boundary (the swizzle atom).
+// Ring geometry of a phase: a stage is the A tile (hi[, lo]) then the B tile (hi[, lo])
+// of bn rows; every part starts on a 1024-byte boundary (the swizzle atom). The
+// screened joint keeps only the hi planes (planes = 1).
 struct Ring {
-    unsigned stage, b_plane;
+    unsigned stage, b_plane, b_off;
     int n;
 };
-__device__ __forceinline__ Ring ring(int bn) {
+__device__ __forceinline__ Ring ring(int bn, int planes) {
     Ring r;
     r.b_plane = (unsigned) bn * kBK * 2u;
-    r.stage = 2u * kATile + 2u * r.b_plane;
+    r.b_off = (unsigned) planes * kATile;
+    r.stage = r.b_off + (unsigned) planes * r.b_plane;
     r.n = min(kMaxStages, (int) (kRing / r.stage));
     return r;
 }
 
 struct Job {
-    int kind, l, M, N, nK, bn, nM, nN, tiles, split, sel;
+    int kind, l, M, N, nK, bn, nM, nN, tiles, split, sel, planes;
     const BulkGemm * g;
 };
+
+// Iterations whose joint runs screened (one product, exact recomputation of the candidates).
+__device__ __forceinline__ bool screened(const BulkParams & Q, int n_live) {
+    return Q.screen_min > 0 && n_live >= Q.screen_min;
+}
 
 __device__ __forceinline__ Job make_job(const BulkParams & Q, int kind, int l, int M, int sel) {
     Job j{};
@@ -121,6 +130,7 @@ __device__ __forceinline__ Job make_job(const BulkParams & Q, int kind, int l, i
     j.nK = j.g->K / kBK;
     j.nM = (M + kBM - 1) / kBM;
     j.split = kind == G_LSTM ? Q.P.H / kBK : 0;   // LSTM: K = [x | h_prev]
+    j.planes = (kind == G_JOINT && screened(Q, M)) ? 1 : 2;
     // tile width: fewest rounds of tiles over the CTAs, counting ~32 columns of
     // fixed cost per tile (pipeline fill and drain)
     const int G = (int) gridDim.x;
@@ -190,7 +200,8 @@ struct RoleClock {
 __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, const Job & J, Pipe & pp) {
     const LoopParams & P = Q.P;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const Ring R = ring(J.bn);
+    const Ring R = ring(J.bn, J.planes);
+    const bool lo = J.planes == 2;
     int kk = 0;                                   // K stages of this phase so far
     const int H = P.H, L = P.L, B = P.B;
     const unsigned rb16 = 4u * (unsigned) H;
@@ -248,7 +259,7 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
                     const unsigned char * slo = zero ? g_zero128 : shi + plane;
                     const unsigned o = (unsigned) lr * 128u + ((sub ^ ((unsigned) lr & 7u)) << 4);
                     cp_async16(dst + o, shi + sub * 16);
-                    cp_async16(dst + kATile + o, slo + sub * 16);
+                    if (lo) cp_async16(dst + kATile + o, slo + sub * 16);
                 }
             }
             // no wait here: the arrival fires when the copies land (the MMA thread
@@ -264,7 +275,7 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
 __device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, const Job & J, Pipe & pp) {
     const CUtensorMap * mhi = reinterpret_cast<const CUtensorMap *>(J.g->map_hi);
     const CUtensorMap * mlo = reinterpret_cast<const CUtensorMap *>(J.g->map_lo);
-    const Ring R = ring(J.bn);
+    const Ring R = ring(J.bn, J.planes);
     int kk = 0;
     for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
         const int n0 = (t / J.nM) * J.bn;
@@ -276,9 +287,9 @@ __device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char
             RoleClock rc(Q.prof != nullptr && blockIdx.x == 0);
             if (!wait_bar(Q, S, &S.empty[s], (u & 1u) ^ 1u)) return;
             rc.add(S, 1);
-            unsigned char * bhi = tiles + (unsigned) s * R.stage + 2 * kATile;
+            unsigned char * bhi = tiles + (unsigned) s * R.stage + R.b_off;
             unsigned char * blo = bhi + R.b_plane;
-            const unsigned planes = J.g->lo_zero ? 1u : 2u;
+            const unsigned planes = (J.g->lo_zero || J.planes == 1) ? 1u : 2u;
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
                          :: "r"(smem_u32(&S.full_b[s])), "r"((unsigned) nb * planes * kBBox) : "memory");
             for (int b = 0; b < nb; ++b) {
@@ -293,7 +304,8 @@ __device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char
 // into the tile's accumulator (columns acc * 256).
 __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * tiles, unsigned tmem, const Job & J,
                          Pipe & pp) {
-    const Ring R = ring(J.bn);
+    const Ring R = ring(J.bn, J.planes);
+    const bool three = J.planes == 2 && !J.g->lo_zero;
     int kk = 0;
     for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
         const int n0 = (t / J.nM) * J.bn;
@@ -320,13 +332,13 @@ __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * til
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const unsigned base = smem_u32(tiles + (unsigned) s * R.stage);
-            const unsigned ahi = base, alo = base + kATile, bhi = base + 2 * kATile, blo = bhi + R.b_plane;
+            const unsigned ahi = base, alo = base + kATile, bhi = base + R.b_off, blo = bhi + R.b_plane;
 #pragma unroll
             for (int k16 = 0; k16 < kBK / 16; ++k16) {
                 const unsigned ko = (unsigned) k16 * 32u;
                 umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(bhi + ko), idesc, (kc | k16) ? 1u : 0u);
-                umma_f16(d, umma_desc_sw128(alo + ko), umma_desc_sw128(bhi + ko), idesc, 1u);
-                if (!J.g->lo_zero) umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
+                if (J.planes == 2) umma_f16(d, umma_desc_sw128(alo + ko), umma_desc_sw128(bhi + ko), idesc, 1u);
+                if (three) umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
             }
             umma_commit(&S.empty[s]);      // the stage is free once these MMAs have read it
             rc.add(S, 7);
@@ -532,6 +544,63 @@ __device__ __forceinline__ void epi_joint(const BulkParams & Q, const Job & J, u
     }
 }
 
+// Screened joint epilogue: the tile's approximate token logits (bias + A_hi W_hi) are
+// reduced to their four largest values and the indices of the first three, written to
+// the row's summary slot for this N tile; duration columns are left to the decision,
+// which computes them in f32. A NaN among the tile's logits sets the slot's flag so
+// that the decision falls back to the full index-order scan.
+__device__ __forceinline__ void epi_joint_screen(const BulkParams & Q, const Job & J, unsigned tacc, int row, int n0,
+                                                 int rows, int nt) {
+    const LoopParams & P = Q.P;
+    const bool valid = row < J.M;
+    const int tok_end = min(rows, P.V1 - n0);          // token columns: [n0, n0 + tok_end)
+    float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY, m4 = -INFINITY;
+    unsigned j1 = 0xFFFFFFFFu, j2 = 0xFFFFFFFFu, j3 = 0xFFFFFFFFu;
+    bool nan = false;
+    for (int c0 = 0; c0 < rows; c0 += 32) {
+        float v[32];
+        tmem_ld32(tacc + (unsigned) c0, v);                 // warp-wide: every lane takes part
+        if (c0 >= tok_end) continue;                        // the same for the whole warp
+        const int r0 = n0 + c0;
+        const int cnt = min(32, tok_end - c0);
+        float lg[32];
+        if (cnt == 32) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float4 bb = __ldg(reinterpret_cast<const float4 *>(P.out_b + r0) + k);
+                lg[4 * k + 0] = bb.x + v[4 * k + 0];
+                lg[4 * k + 1] = bb.y + v[4 * k + 1];
+                lg[4 * k + 2] = bb.z + v[4 * k + 2];
+                lg[4 * k + 3] = bb.w + v[4 * k + 3];
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) lg[q] = q < cnt ? __ldg(P.out_b + r0 + q) + v[q] : -INFINITY;
+        }
+        // branch-free insertion into m1 >= m2 >= m3 >= m4 (strict > keeps the earlier
+        // index first among equal values)
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+            const float x = lg[q];
+            const unsigned jq = (unsigned) (r0 + q);
+            nan |= x != x;
+            const bool g1 = x > m1, g2 = x > m2, g3 = x > m3, g4 = x > m4;
+            m4 = g3 ? m3 : (g4 ? x : m4);
+            m3 = g2 ? m2 : (g3 ? x : m3);
+            j3 = g2 ? j2 : (g3 ? jq : j3);
+            m2 = g1 ? m1 : (g2 ? x : m2);
+            j2 = g1 ? j1 : (g2 ? jq : j2);
+            m1 = g1 ? x : m1;
+            j1 = g1 ? jq : j1;
+        }
+    }
+    if (valid) {
+        uint4 * d = Q.jsum + ((size_t) row * Q.jsum_stride + nt) * 2;
+        d[0] = make_uint4(__float_as_uint(m1), __float_as_uint(m2), __float_as_uint(m3), __float_as_uint(m4));
+        d[1] = make_uint4(j1, j2, j3, nan ? 1u : 0u);
+    }
+}
+
 // Epilogue warps 8-11: warp % 4 selects the TMEM lane quarter = rows 32 (warp % 4) .. + 31.
 __device__ void gemm_epilogue(const BulkParams & Q, BulkSmem & S, unsigned tmem, const Job & J, Pipe & pp,
                               unsigned long long * keys) {
@@ -549,6 +618,7 @@ __device__ void gemm_epilogue(const BulkParams & Q, BulkSmem & S, unsigned tmem,
         const unsigned tacc = tmem + ((unsigned) (quarter * 32) << 16) + a * (unsigned) kBNmax;
         if (J.kind == G_LSTM) epi_lstm(Q, J, tacc, row, n0, rows);
         else if (J.kind == G_PRED) epi_pred(Q, J, tacc, row, n0, rows);
+        else if (J.planes == 1) epi_joint_screen(Q, J, tacc, row, n0, rows, t / J.nM);
         else epi_joint(Q, J, tacc, row, n0, rows, keys);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         rc.add(S, 6);
@@ -665,6 +735,20 @@ __device__ void hidden_phase(const BulkParams & Q, int sel, int n_live, int n_pr
             make_uint2(*reinterpret_cast<unsigned *>(&h01), *reinterpret_cast<unsigned *>(&h23));
         *reinterpret_cast<uint2 *>(rowp + 2 * J + 8 * q) =
             make_uint2(*reinterpret_cast<unsigned *>(&l01), *reinterpret_cast<unsigned *>(&l23));
+        if (screened(Q, n_live)) {
+            // ||hid||^2 of the row as the decision's f32 recomputation sees it (hi + lo).
+            // J / 4 is a multiple of 32 (bulk_screen_supported) and a warp's 32 indices are
+            // consecutive from a multiple of 32, so the whole warp is in row i.
+            float ss = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float av = __half2float(hh[k]) + __half2float(hl[k]);
+                ss = fmaf(av, av, ss);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+            if ((threadIdx.x & 31) == 0) atomicAdd(Q.norm2 + i, ss);
+        }
     }
     // teacher-forced trace: state after each step decided by the previous iteration
     if (P.trace_steps > 0 && n_prev > 0) {
@@ -681,6 +765,216 @@ __device__ void hidden_phase(const BulkParams & Q, int sel, int n_live, int n_pr
             const size_t dst = ((size_t) utt * P.trace_steps + step) * LH + k;
             if (P.tr_h) P.tr_h[dst] = __ldcg(P.h + (((size_t) hb * L + l) * B + utt) * H + j);
             if (P.tr_c) P.tr_c[dst] = __ldcg(P.c + ((size_t) l * B + utt) * H + j);
+        }
+    }
+}
+
+// ---- screened joint: the exact argmax ---------------------------------------------
+
+constexpr int kScreenMaxJ = 1024;          // hidden rows held in registers: J / 32 <= 32 per lane
+
+// f32 logits of kCand joint.out rows (rows[c]; every entry a valid row) for the hidden
+// row the warp holds (lane l has a[m] = hid[64 m + 2 l .. + 1]). The weights are read
+// as their exact f16 halves (hi + lo, the arrays the joint GEMM streams); every lane
+// returns the same values (fixed summation order). N2 = J / 64 is a compile-time
+// trip count so that every load can be issued before the first product.
+constexpr int kCand = 8;
+template <int N2>
+__device__ __forceinline__ void exact_logits_n(const BulkParams & Q, const float2 (&a)[kScreenMaxJ / 64],
+                                               const int (&rows)[kCand], float (&out)[kCand]) {
+    const LoopParams & P = Q.P;
+    const int lane = threadIdx.x & 31;
+    const __half2 * whi = static_cast<const __half2 *>(Q.gj.hi);
+    const __half2 * wlo = static_cast<const __half2 *>(Q.gj.lo);
+    const int rs = P.J / 2;                            // half2 per weight row
+    float s[kCand];
+#pragma unroll
+    for (int c = 0; c < kCand; ++c) s[c] = 0.0f;
+#pragma unroll
+    for (int m = 0; m < N2; ++m) {
+#pragma unroll
+        for (int c = 0; c < kCand; ++c) {
+            const size_t o = (size_t) rows[c] * rs + lane + 32 * m;
+            const float2 h = __half22float2(__ldg(whi + o)), l = __half22float2(__ldg(wlo + o));
+            s[c] = fmaf(h.y + l.y, a[m].y, fmaf(h.x + l.x, a[m].x, s[c]));
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < kCand; ++c) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s[c] += __shfl_xor_sync(0xFFFFFFFFu, s[c], o);
+        out[c] = __ldg(P.out_b + rows[c]) + s[c];
+    }
+}
+
+// rows[0 .. n) with 1 <= n <= kCand; entries past n repeat the last row.
+__device__ __forceinline__ void exact_logits(const BulkParams & Q, const float2 (&a)[kScreenMaxJ / 64],
+                                             int (&rows)[kCand], int n, float (&out)[kCand]) {
+#pragma unroll
+    for (int c = 1; c < kCand; ++c)
+        if (c >= n) rows[c] = rows[c - 1];
+    switch (Q.P.J / 64) {
+        case 2: exact_logits_n<2>(Q, a, rows, out); break;
+        case 4: exact_logits_n<4>(Q, a, rows, out); break;
+        case 6: exact_logits_n<6>(Q, a, rows, out); break;
+        case 8: exact_logits_n<8>(Q, a, rows, out); break;
+        case 10: exact_logits_n<10>(Q, a, rows, out); break;
+        case 12: exact_logits_n<12>(Q, a, rows, out); break;
+        case 14: exact_logits_n<14>(Q, a, rows, out); break;
+        default: exact_logits_n<16>(Q, a, rows, out); break;
+    }
+}
+
+// One warp: the token and duration decisions of live row g from the screened joint.
+//
+// Bound: with w~ = f16(w), a~ = f16(a) (the hi halves the GEMM used) and a = hi + lo
+// (the row the f32 recomputation uses), |w a - w~ a~| <= 2^-10 (1 + 2^-11) |w||a| per
+// term; the tensor core's f32 accumulation and the recomputation's f32 sums add at most
+// (K + 37) 2^-23 sum |w||a| (< 1.3e-4 sum |w||a| for K <= 1024, counting one rounding
+// per addition), so the total stays below 2^-9 sum |w||a|; and sum |w||a| <=
+// max_j ||w_j|| ||a|| (Cauchy-Schwarz). So every token's approximate logit is within
+// E = 2^-9 ||w||max ||a|| (plus a slack for the bias additions) of its recomputed value,
+// and the recomputed argmax j* satisfies approx(j*) >= M - 2E, M the largest
+// approximate logit. The candidates -- every token with approx >= M - 2E, through each
+// N tile's top three, or the whole tile when its fourth value also qualifies -- are
+// recomputed in f32 and the largest wins, ties to the smallest index (argmax_f32's
+// first-index rule, src/parakeet_tdt.cpp:25-32). A NaN or infinity anywhere sends the
+// row to the full index-order scan. The duration logits (TDT) are recomputed with the
+// token candidates, and argmax_f32 runs over them.
+//
+// Memory round trips: (1) the hidden row, the row norm and every tile's top value;
+// (2) the full summaries of the tiles that reach the threshold (usually one or two);
+// (3) the candidate and duration rows.
+__device__ void screen_row(const BulkParams & Q, const Job & JJ, int g, int & tok, int & dur) {
+    const LoopParams & P = Q.P;
+    const int lane = threadIdx.x & 31;
+    const int npair = P.J / 64;                        // half2 pairs per lane
+    const __half2 * hi = reinterpret_cast<const __half2 *>(P.hidc + (size_t) g * P.rbj);
+    const __half2 * lo = hi + P.J / 2;
+    const uint4 * sm = Q.jsum + (size_t) g * Q.jsum_stride * 2;
+    float2 a[kScreenMaxJ / 64];
+#pragma unroll
+    for (int m = 0; m < kScreenMaxJ / 64; ++m) {
+        a[m] = make_float2(0.0f, 0.0f);
+        if (m < npair) {
+            const float2 h = __half22float2(__ldcg(hi + lane + 32 * m)), l = __half22float2(__ldcg(lo + lane + 32 * m));
+            a[m] = make_float2(h.x + l.x, h.y + l.y);
+        }
+    }
+    const float n2 = __ldcg(Q.norm2 + g);
+    constexpr int kTl = 8;                             // tiles per lane: nN <= 256
+    float t1[kTl];
+#pragma unroll
+    for (int k = 0; k < kTl; ++k) {
+        const int t = lane + 32 * k;
+        t1[k] = t < JJ.nN ? __ldcg(reinterpret_cast<const float *>(sm + 2 * t)) : -INFINITY;
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kTl; ++k) mx = fmaxf(mx, t1[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    const float E = 0x1p-9f * 1.01f * __ldg(Q.wnorm) * sqrtf(n2) + 1e-5f * (1.0f + fabsf(mx));
+    bool wild = !isfinite(mx) || !isfinite(E) || JJ.nN > 32 * kTl;
+    const float thr = mx - 2.0f * E;
+    // (2) tiles whose top value reaches the threshold: their summaries and NaN flags
+    int rows[kCand];
+    float v[kCand];
+#pragma unroll
+    for (int c = 0; c < kCand; ++c) rows[c] = 0;
+    int n = 0;
+    float best = 0.0f, bd = 0.0f;
+    int bj = -1;
+    dur = 0;
+    // fold the queued rows into (best, bj): largest value, then smallest index; queued
+    // duration rows (index >= V1) into (bd, dur) by argmax_f32 (first index of the largest)
+    auto flush = [&]() {
+        exact_logits(Q, a, rows, n, v);
+#pragma unroll
+        for (int c = 0; c < kCand; ++c) {
+            if (c < n) {
+                const int r = rows[c];
+                if (r >= P.V1) {
+                    const int d = r - P.V1;
+                    if (d == 0 || v[c] > bd) { bd = v[c]; dur = d; }
+                } else if (bj < 0 || v[c] > best || (v[c] == best && r < bj)) {
+                    best = v[c];
+                    bj = r;
+                }
+            }
+        }
+        n = 0;
+    };
+    auto push = [&](int j) {
+#pragma unroll
+        for (int c = 0; c < kCand; ++c)
+            if (c == n) rows[c] = j;
+        if (++n == kCand) flush();
+    };
+    if (!wild) {
+        // one pass over the lanes' tiles, in tile order (durations are queued first, in
+        // index order, so their argmax sees them in order even across flushes)
+        if (P.is_tdt)
+            for (int d = 0; d < P.Nd; ++d) push(P.V1 + d);
+#pragma unroll
+        for (int k = 0; k < kTl; ++k) {
+            unsigned hit = __ballot_sync(0xFFFFFFFFu, t1[k] >= thr);
+            uint4 e0 = make_uint4(0u, 0u, 0u, 0u), e1 = e0;
+            if (t1[k] >= thr) {
+                e0 = __ldcg(sm + 2 * (lane + 32 * k));
+                e1 = __ldcg(sm + 2 * (lane + 32 * k) + 1);
+            }
+            const bool flag = t1[k] >= thr && e1.w != 0u;
+            if (__any_sync(0xFFFFFFFFu, flag)) { wild = true; break; }
+            while (hit) {
+                const int src = __ffs(hit) - 1;
+                hit &= hit - 1;
+                const float m2 = __uint_as_float(__shfl_sync(0xFFFFFFFFu, e0.y, src));
+                const float m3 = __uint_as_float(__shfl_sync(0xFFFFFFFFu, e0.z, src));
+                const float m4 = __uint_as_float(__shfl_sync(0xFFFFFFFFu, e0.w, src));
+                const int j1 = (int) __shfl_sync(0xFFFFFFFFu, e1.x, src);
+                const int j2 = (int) __shfl_sync(0xFFFFFFFFu, e1.y, src);
+                const int j3 = (int) __shfl_sync(0xFFFFFFFFu, e1.z, src);
+                if (m4 >= thr) {                       // more than three candidates: the whole tile
+                    const int r0 = (32 * k + src) * JJ.bn, r1 = min(r0 + JJ.bn, P.V1);
+                    for (int j = r0; j < r1; ++j) push(j);
+                } else {
+                    push(j1);
+                    if (m2 >= thr) push(j2);
+                    if (m3 >= thr) push(j3);
+                }
+            }
+        }
+    }
+    if (!wild) {
+        if (n > 0) flush();
+        tok = bj;
+        return;
+    }
+    // argmax_f32 over every token, in index order (strict >: only index 0 can win as NaN),
+    // then over the durations
+    n = 0;
+    bj = -1;
+    for (int j0 = 0; j0 < P.V1; j0 += kCand) {
+        const int cnt = min(kCand, P.V1 - j0);
+#pragma unroll
+        for (int c = 0; c < kCand; ++c) rows[c] = j0 + min(c, cnt - 1);
+        exact_logits(Q, a, rows, cnt, v);
+#pragma unroll
+        for (int c = 0; c < kCand; ++c)
+            if (c < cnt && (j0 + c == 0 || v[c] > best)) { best = v[c]; bj = j0 + c; }
+    }
+    tok = bj;
+    dur = 0;
+    if (P.is_tdt) {
+        for (int d0 = 0; d0 < P.Nd; d0 += kCand) {
+            const int cnt = min(kCand, P.Nd - d0);
+#pragma unroll
+            for (int c = 0; c < kCand; ++c) rows[c] = P.V1 + d0 + min(c, cnt - 1);
+            exact_logits(Q, a, rows, cnt, v);
+#pragma unroll
+            for (int c = 0; c < kCand; ++c)
+                if (c < cnt && (d0 + c == 0 || v[c] > bd)) { bd = v[c]; dur = d0 + c; }
         }
     }
 }
@@ -773,6 +1067,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
     int n_live = __ldcg(&P.ctl[C_NLIVE0 + sel]);
     int n_prev = 0, iter = 0, emit_iters = 0;
     long long sum_live = 0, sum_emit = 0;    // this loop's joint evaluations and LSTM steps
+    long long sum_scr = 0;                   // of them, screened joint evaluations
     unsigned long long * keys = P.keys;                 // one key buffer: cleared by the decision that reads it
     bool ok = __ldcg(&P.ctl[C_ERR]) == 0;
     while (ok && n_live >= Q.min_live && n_live > 0) {
@@ -807,23 +1102,42 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
         const int ch = (n_live + G - 1) / G;
         const int g = (int) blockIdx.x * ch + (int) threadIdx.x;
         const bool mine = (int) threadIdx.x < ch && g < n_live;
+        const bool scr = screened(Q, n_live);
+        if (scr) {                                      // exact argmax of the screened joint, a warp per row
+            const Job JJ = make_job(Q, G_JOINT, 0, n_live, sel);
+            for (int i = warp; i < ch && (int) blockIdx.x * ch + i < n_live; i += kBWarps) {
+                int tk = 0, du = 0;
+                screen_row(Q, JJ, (int) blockIdx.x * ch + i, tk, du);
+                if ((threadIdx.x & 31) == 0) { S.tok_s[i] = tk; S.dur_s[i] = du; }
+            }
+            __syncthreads();
+        }
         int e = 0, lv = 0, utt = -1, etok = 0, ereset = 0, ehb = 0, bad = 0;
         long long lframe = 0;
         if (mine) {
             utt = __ldcg(P.live + (size_t) sel * P.B + g);
             int * u = P.ust + utt * kUst;
-            const unsigned long long kt = __ldcg(&keys[2 * utt + 0]);
-            const unsigned long long kd = P.is_tdt ? __ldcg(&keys[2 * utt + 1]) : 0ull;
+            const unsigned long long kt = scr ? 0ull : __ldcg(&keys[2 * utt + 0]);
+            const unsigned long long kd = (P.is_tdt && !scr) ? __ldcg(&keys[2 * utt + 1]) : 0ull;
             const int4 u0 = __ldcg(reinterpret_cast<const int4 *>(u));
             const int4 u1 = __ldcg(reinterpret_cast<const int4 *>(u) + 1);
             const int4 u2 = __ldcg(reinterpret_cast<const int4 *>(u) + 2);
             const long long foff = __ldg(P.frame_off + utt);
             const int uf[12] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w, u2.x, u2.y, u2.z, u2.w};
-            keys[2 * utt + 0] = 0ull;
-            if (P.is_tdt) keys[2 * utt + 1] = 0ull;
-            int tok = key_index(kt);
-            int di = P.is_tdt ? key_index(kd) : 0;
-            if (keys_bad(P, kt, kd, tok, di)) {
+            int tok, di;
+            bool kbad;
+            if (scr) {
+                tok = S.tok_s[threadIdx.x];
+                di = S.dur_s[threadIdx.x];
+                kbad = tok < 0 || tok >= P.V1 || (P.is_tdt && (di < 0 || di >= P.Nd));
+            } else {
+                keys[2 * utt + 0] = 0ull;
+                if (P.is_tdt) keys[2 * utt + 1] = 0ull;
+                tok = key_index(kt);
+                di = P.is_tdt ? key_index(kd) : 0;
+                kbad = keys_bad(P, kt, kd, tok, di);
+            }
+            if (kbad) {
                 atomicCAS(&P.ctl[C_ERR], 0, (int) PK_ERR_DEVICE);
                 P.ctl[C_ERRINFO] = utt;
                 bad = 1;
@@ -886,6 +1200,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
         bulk_scan(S, te, ste);
         bulk_scan(S, tl, stl);
         const int nsel = sel ^ 1;
+        if (scr && mine) Q.norm2[g] = 0.0f;        // read by part 1; the next hidden phase adds into it
         if (e) {
             reinterpret_cast<int2 *>(P.emit)[sbe + (pf & 0xFFFF)] =
                 make_int2(utt, etok | (ehb << 30) | (ereset << 31));
@@ -906,9 +1221,11 @@ __global__ void __launch_bounds__(kBThreads, 1) bulk_loop_kernel(const __grid_co
             P.ctl[C_BULKITERS] = iter + 1;
             P.ctl[C_BULKSTEPS] = (int) (sum_live + n_live);
             P.ctl[C_BULKEMITS] = (int) (sum_emit + n_emit);
+            P.ctl[C_BULKSCREENED] = (int) (sum_scr + (scr ? n_live : 0));
         }
         sum_live += n_live;
         sum_emit += n_emit;
+        if (scr) sum_scr += n_live;
         n_prev = n_live;
         sel = nsel;
         n_emit = ste;
@@ -986,6 +1303,23 @@ __global__ void bulk_split_embed(const float * __restrict__ e, long long n, int 
     }
 }
 
+// max over rows [0, rows) of ||w[r]||_2, rounded up (x 1.0001 covers the f32 sums for
+// K <= 1024), into *out as float bits (positive floats order as unsigned integers).
+__global__ void bulk_row_norm_max(const float * __restrict__ w, int rows, int K, unsigned * __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const long long nw = (long long) gridDim.x * blockDim.x / 32;
+    for (long long r = ((long long) blockIdx.x * blockDim.x + threadIdx.x) / 32; r < rows; r += nw) {
+        float ss = 0.0f;
+        for (int k = lane; k < K; k += 32) {
+            const float x = w[r * K + k];
+            ss = fmaf(x, x, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        if (lane == 0) atomicMax(out, __float_as_uint(sqrtf(ss) * 1.0001f));
+    }
+}
+
 }  // namespace
 
 cudaError_t encode_2d(void * map, CUtensorMapDataType type, size_t esize, const void * base, long long rows,
@@ -994,6 +1328,8 @@ cudaError_t encode_2d(void * map, CUtensorMapDataType type, size_t esize, const 
 bool bulk_supported(int H, int J, int L) {
     return H > 0 && J > 0 && H % kBK == 0 && J % kBK == 0 && L >= 1 && L <= kMaxLayers;
 }
+
+bool bulk_screen_supported(int J) { return J % 128 == 0 && J <= kScreenMaxJ; }
 
 size_t bulk_smem_bytes() { return 1024 + (size_t) kRing + sizeof(BulkSmem); }
 
@@ -1017,11 +1353,14 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, c
                          const float * const * b_hh, const float * pred_w, const float * out_w,
                          const int * f16_weights, cudaStream_t s) {
     bulk_release(w);
-    // layout: [maps: (L + 2) x 2 x 128 B][lbias L x 4H f32][embedding halves][weight halves]
+    // layout: [maps: (L + 2) x 2 x 128 B][row-norm bound, 256 B][lbias L x 4H f32][embedding halves]
+    //         [weight halves]
     const int nmat = L + 2;
     size_t off = 0;
     const size_t maps = off;
     off += (size_t) nmat * 2 * 128;
+    const size_t wn = off;
+    off += 256;
     const size_t bias = off;
     off += (size_t) L * 4 * H * 4;
     off = (off + 255) & ~(size_t) 255;
@@ -1062,6 +1401,8 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, c
         BulkGemm g;
         g.map_hi = base + maps + (size_t) (2 * m) * 128;
         g.map_lo = base + maps + (size_t) (2 * m + 1) * 128;
+        g.hi = hi;
+        g.lo = lo;
         g.N = (int) mat_rows[m];
         g.K = (int) mat_k[m];
         g.lo_zero = f16_weights[m];   // f16 weights are exact in the hi half
@@ -1078,6 +1419,12 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, c
     bulk_split_embed<<<1184, 256, 0, s>>>(embed, (long long) V1 * H, H, base + emb);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(base + wn, 0, 256, s);
+    if (e != cudaSuccess) return e;
+    bulk_row_norm_max<<<1184, 256, 0, s>>>(out_w, V1, J, reinterpret_cast<unsigned *>(base + wn));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    w.wnorm = reinterpret_cast<const float *>(base + wn);
     w.e16 = base + emb;
     w.lbias = reinterpret_cast<const float *>(base + bias);
     e = cudaMemcpyAsync(base + maps, host_maps.data(), host_maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s);

@@ -43,6 +43,7 @@ enum CtlField : int {
     C_BULKITERS,      // iterations run by the bulk loop (pk_bulk.cu) before the persistent loop
     C_BULKSTEPS,      // joint evaluations (live utterance-iterations) on the bulk loop
     C_BULKEMITS,      // LSTM steps (emit-list entries) on the bulk loop
+    C_BULKSCREENED,   // joint evaluations of the bulk loop made screened (one f16 product)
     kCtl = 16
 };
 
@@ -88,6 +89,7 @@ struct LoopParams {
     int mb;                    // m16 blocks per pass: passes of 16 * mb utterances
     int rpc_j, rpc_p, upc;     // joint rows, pred rows, LSTM units per CTA
     int h_int;                 // LSTM outputs staged as int16 fixed point (two int8 digit planes)
+    int q8;                    // PK_MATH_Q8: staged activations quantised to q8_0 blocks, int8 products
     TcBlock tcj, tcp, tcl[kMaxLayers];
     const float * g0;          // [V+1][4H]: b_ih0 + W_ih0 . embed[v] (layer-0 input projection)
     // weights (f32, row-major [out][in])
@@ -149,6 +151,8 @@ struct LoopParams {
 struct BulkGemm {
     const void * map_hi;
     const void * map_lo;
+    const void * hi;           // the f16 halves themselves, [N][K] each (hi + lo = the weight, exactly)
+    const void * lo;
     int N, K;
     int lo_zero;               // every lo half is zero (f16 weights): two products, no lo tiles
 };
@@ -165,6 +169,16 @@ struct BulkParams {
     unsigned char * x16;       // [L][B] rows, same layout: layer l's new h by emit-list index
     int2 * dcount;             // [grid] each CTA's (emit, live) counts from the decision
     unsigned long long * prof; // [20] CTA 0: time per phase and per GEMM role (ns), see pk_result::bulk_phase_ms
+    // Screened joint (iterations with at least screen_min live utterances; 0 = never):
+    // the joint GEMM takes one f16 product (A_hi W_hi) and keeps, per (live row, N
+    // tile), its four largest token logits; the decision recomputes in f32 every token
+    // whose approximate logit is within twice a proven error bound of the row's
+    // maximum, and every duration logit.
+    int screen_min;
+    float * norm2;             // [B] sum of squares of the joint hidden row, by live index
+    uint4 * jsum;              // [B][jsum_stride][2] per (live row, N tile): (m1..m4 bits), (j1, j2, j3, NaN flag)
+    int jsum_stride;           // N tiles of the narrowest joint tiling: ceil(Vo / 64)
+    const float * wnorm;       // device: max over token rows of joint.out of ||row||_2 (rounded up)
 };
 
 // Device-side bulk weights of a context (built once at pk_create).
@@ -173,9 +187,11 @@ struct BulkWeights {
     BulkGemm gl[kMaxLayers]{}, gp{}, gj{};
     const float * lbias = nullptr;
     const unsigned char * e16 = nullptr;
+    const float * wnorm = nullptr;   // max row norm of joint.out's token rows (screened joint)
     size_t bytes = 0;
 };
 bool        bulk_supported(int H, int J, int L);
+bool        bulk_screen_supported(int J);   // the screened joint's row norms need J % 128 == 0
 cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
                          const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
                          const float * const * b_hh, const float * pred_w, const float * out_w,

@@ -899,6 +899,49 @@ __device__ __forceinline__ bool tc_stage(const LoopParams & P, const TcSmem & S,
     return ok;
 }
 
+// PK_MATH_Q8: the staged activation rows [0, nc) at base (stride rb) become q8_0
+// blocks in place, as ggml's quantize_row_q8_0 makes them for vec_dot_q8_0_q8_0:
+// per 32 consecutive values d = max|x| / 127, q = roundf(x / d) (0 when d = 0), d
+// kept as binary16. K values per row, read as int16 fixed point (two int8 digit
+// planes, hi at +k, lo at +lo + k: x = (hi * 256 + lo) / 2^15) or as f16 halves
+// (hi at +2k, lo at +lo + 2k: x = hi + lo). Written: q at byte positions [0, K),
+// in the k order of the B fragments the GEMM pairs them with (identity for
+// mma.m16n8k32 fragments; the k16-fragment order of the joint's weights when
+// perm), and d (f32 of its binary16 value) at +lo + 4 * block. One warp per row,
+// lane l holding value 32 b + l of block b: every lane has read a block (before
+// the block's max reduction) before any lane writes it, and a block's writes only
+// touch bytes of values of that block or of earlier ones.
+__device__ void q8_rows(unsigned char * base, int nc, int rb, int K, int lo, bool src_i16, bool perm) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // position of value kk (< 16) of a k16 half within the fragment order: lane t of
+    // the k16 fragments holds kk = 2t, 2t + 1, 2t + 8, 2t + 9 at positions 4t .. 4t + 3
+    const int kk = lane & 15;
+    const int pos = perm ? ((lane & 16) + 4 * ((kk & 7) >> 1) + (kk & 1) + 2 * (kk >> 3)) : lane;
+    for (int c = warp; c < nc; c += kWarps) {
+        unsigned char * row = base + (size_t) c * rb;
+        for (int b = 0; b < (K >> 5); ++b) {
+            const int k = 32 * b + lane;
+            float x;
+            if (src_i16) {
+                x = (float) ((int) (signed char) row[k] * 256 + (int) row[lo + k]) * (1.0f / 32768.0f);
+            } else {
+                x = __half2float(reinterpret_cast<const __half *>(row)[k]) +
+                    __half2float(reinterpret_cast<const __half *>(row + lo)[k]);
+            }
+            float amax = fabsf(x);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            const float d = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            const int q = (int) roundf(x * id);
+            row[32 * b + pos] = (unsigned char) (signed char) q;
+            if (lane == 0) *reinterpret_cast<float *>(row + lo + 4 * b) = __half2float(__float2half_rn(d));
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+}
+
 __device__ __forceinline__ const uint8_t * tc_frag(const LoopParams & P, const TcSmem & S, const TcBlock & b) {
     return P.stationary ? S.w + b.sm_frag : b.frag + (size_t) blockIdx.x * b.cta_bytes;
 }
@@ -930,7 +973,7 @@ struct ATile {
 // partial sums fit after them they go to the end of the area, the rows survive
 // the call (a phase's next call on further tiles reads them again) and no CTA
 // barrier has to separate the warps' last row reads from the partial writes.
-template <int NT, int MB>
+template <int NT, int MB, bool Q8>
 __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, const ATile & A,
                            int kw, int keep) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -946,10 +989,43 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
         for (int m = 0; m < MB; ++m) acc[r][m][0] = acc[r][m][1] = acc[r][m][2] = acc[r][m][3] = 0.0f;
     const int mrow = ((lane >> 3) & 1) * 8 + (lane & 7);
     const int mb16 = (lane >> 4) * 16;                 // byte column of this lane's ldmatrix row
-    const int kbytes = b.imma ? 32 : 64;               // bytes of one 32-wide K block per part
+    const int kbytes = (b.imma || Q8) ? 32 : 64;       // bytes of one 32-wide K block per part
     const size_t mstep = (size_t) 16 * A.rb;           // bytes between m16 blocks
     const unsigned char * a0 = A.r0 + mrow * A.rb + mb16;
     const unsigned char * a1 = A.r1 + mrow * A.rb + mb16 - A.kb_split * kbytes;
+    if constexpr (Q8) {
+        // q8_0 activations (q8_rows) x q8_0 weights: one int8 product per block, scaled
+        // by the weight row's d and the activation row's d (vec_dot_q8_0_q8_0)
+        const uint32_t flip = b.imma ? 0u : 0x80808080u;   // biased bytes q + 128 -> int8 q
+        for (int kb = kb0; kb < kb1; ++kb) {
+            const bool first = kb < A.kb_split;
+            const unsigned char * hp = (first ? a0 : a1) + kb * 32;
+            const unsigned char * dp = (first ? A.r0 : A.r1) + g * A.rb + A.lo + 4 * (first ? kb : kb - A.kb_split);
+            uint32_t aq[MB][4];
+            float dx0[MB], dx1[MB];
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                ldsm_x4(aq[m], hp + m * mstep);
+                dx0[m] = *reinterpret_cast<const float *>(dp + m * mstep);
+                dx1[m] = *reinterpret_cast<const float *>(dp + m * mstep + 8 * A.rb);
+            }
+#pragma unroll
+            for (int r = 0; r < NT; ++r) {
+                const size_t u = (size_t) (t0 + r) * nkb + kb;
+                const uint2 w = *reinterpret_cast<const uint2 *>(frag + (u * 32 + lane) * 8);
+                const float2 sc = *reinterpret_cast<const float2 *>(scale + u * 8 + 2 * t);
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    int dq[4] = {0, 0, 0, 0};
+                    imma_s8s8(dq, aq[m], w.x ^ flip, w.y ^ flip);
+                    acc[r][m][0] = fmaf(sc.x * dx0[m], (float) dq[0], acc[r][m][0]);
+                    acc[r][m][1] = fmaf(sc.y * dx0[m], (float) dq[1], acc[r][m][1]);
+                    acc[r][m][2] = fmaf(sc.x * dx1[m], (float) dq[2], acc[r][m][2]);
+                    acc[r][m][3] = fmaf(sc.y * dx1[m], (float) dq[3], acc[r][m][3]);
+                }
+            }
+        }
+    } else {
     if (b.imma) {
         for (int kb = kb0; kb < kb1; ++kb) {
             const unsigned char * hp = (kb < A.kb_split ? a0 : a1) + kb * 32;
@@ -1042,6 +1118,7 @@ __device__ void tc_gemm_nt(const LoopParams & P, const TcSmem & S, const TcBlock
             }
         }
     }
+    }
     constexpr int W = 16 * MB;                         // utterance columns of a partial tile
     // rows padded to W + 4 floats: a store's 32 lanes (rows 2t / 2t + 1, columns g)
     // then fall on 32 distinct banks (2 (W + 4) = 8 mod 32)
@@ -1082,31 +1159,33 @@ __device__ __forceinline__ int c_index(int r, int c, int W) { return (r >> 3) * 
 // mbp: m16 blocks of this pass (2 only when the pass has more than 16
 // utterances and the loop was set up for 32-utterance passes). Two-block calls
 // take at most 7 tiles, one-block calls 8 (callers split larger groups).
-__device__ __forceinline__ void tc_gemm(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt,
+template <bool Q8>
+__device__ __forceinline__ void tc_gemm_q(const LoopParams & P, const TcSmem & S, const TcBlock & b, int t0, int nt,
                                         const ATile & A, int mbp, int kw, int keep = 0) {
     if (mbp == 2) {
         switch (nt) {
-            case 1: tc_gemm_nt<1, 2>(P, S, b, t0, A, kw, keep); break;
-            case 2: tc_gemm_nt<2, 2>(P, S, b, t0, A, kw, keep); break;
-            case 3: tc_gemm_nt<3, 2>(P, S, b, t0, A, kw, keep); break;
-            case 4: tc_gemm_nt<4, 2>(P, S, b, t0, A, kw, keep); break;
-            case 5: tc_gemm_nt<5, 2>(P, S, b, t0, A, kw, keep); break;
-            case 6: tc_gemm_nt<6, 2>(P, S, b, t0, A, kw, keep); break;
-            default: tc_gemm_nt<7, 2>(P, S, b, t0, A, kw, keep); break;
+            case 1: tc_gemm_nt<1, 2, Q8>(P, S, b, t0, A, kw, keep); break;
+            case 2: tc_gemm_nt<2, 2, Q8>(P, S, b, t0, A, kw, keep); break;
+            case 3: tc_gemm_nt<3, 2, Q8>(P, S, b, t0, A, kw, keep); break;
+            case 4: tc_gemm_nt<4, 2, Q8>(P, S, b, t0, A, kw, keep); break;
+            case 5: tc_gemm_nt<5, 2, Q8>(P, S, b, t0, A, kw, keep); break;
+            case 6: tc_gemm_nt<6, 2, Q8>(P, S, b, t0, A, kw, keep); break;
+            default: tc_gemm_nt<7, 2, Q8>(P, S, b, t0, A, kw, keep); break;
         }
         return;
     }
     switch (nt) {
-        case 1: tc_gemm_nt<1, 1>(P, S, b, t0, A, kw, keep); break;
-        case 2: tc_gemm_nt<2, 1>(P, S, b, t0, A, kw, keep); break;
-        case 3: tc_gemm_nt<3, 1>(P, S, b, t0, A, kw, keep); break;
-        case 4: tc_gemm_nt<4, 1>(P, S, b, t0, A, kw, keep); break;
-        case 5: tc_gemm_nt<5, 1>(P, S, b, t0, A, kw, keep); break;
-        case 6: tc_gemm_nt<6, 1>(P, S, b, t0, A, kw, keep); break;
-        case 7: tc_gemm_nt<7, 1>(P, S, b, t0, A, kw, keep); break;
-        default: tc_gemm_nt<8, 1>(P, S, b, t0, A, kw, keep); break;
+        case 1: tc_gemm_nt<1, 1, Q8>(P, S, b, t0, A, kw, keep); break;
+        case 2: tc_gemm_nt<2, 1, Q8>(P, S, b, t0, A, kw, keep); break;
+        case 3: tc_gemm_nt<3, 1, Q8>(P, S, b, t0, A, kw, keep); break;
+        case 4: tc_gemm_nt<4, 1, Q8>(P, S, b, t0, A, kw, keep); break;
+        case 5: tc_gemm_nt<5, 1, Q8>(P, S, b, t0, A, kw, keep); break;
+        case 6: tc_gemm_nt<6, 1, Q8>(P, S, b, t0, A, kw, keep); break;
+        case 7: tc_gemm_nt<7, 1, Q8>(P, S, b, t0, A, kw, keep); break;
+        default: tc_gemm_nt<8, 1, Q8>(P, S, b, t0, A, kw, keep); break;
     }
 }
+
 
 // Records of one emit-list block: utterance, token, reset | h buffer << 1.
 __device__ __forceinline__ void tc_emit_record(const LoopParams & P, const TcSmem & T, int i, int g) {
@@ -1250,6 +1329,7 @@ __device__ unsigned long long rep_decide(const LoopParams & P, const TcSmem & T,
     return pack_ctl(0u, any_err, sel ^ 1, n_emit, n_next);
 }
 
+template <bool Q8>
 __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcSmem & T) {
     const int H = P.H, L = P.L, B = P.B;
     const int upc = P.upc;
@@ -1314,7 +1394,11 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
         A.rb = P.rbh;
         A.lo = H * es;
         A.kb_split = l == 0 ? (bk.K >> 5) : (H >> 5);
-        tc_gemm(P, S, bk, 0, bk.tiles, A, mbp, 4,
+        if constexpr (Q8) {
+            q8_rows(S.area, nc, P.rbh, H, A.lo, true, false);
+            if (l > 0) q8_rows(reg1, nc, P.rbh, H, A.lo, true, false);
+        }
+        tc_gemm_q<Q8>(P, S, bk, 0, bk.tiles, A, mbp, 4,
                 l == 0 ? nc * P.rbh : PR * P.rbh + nc * P.rbh);
         SUBMARK(3);
         // cell update (parakeet_tdt.cpp:123-136); block row = unit * 4 + gate
@@ -1347,6 +1431,7 @@ __device__ void tc_phase_lstm(const LoopParams & P, int l, int n_emit, const TcS
     }
 }
 
+template <bool Q8>
 __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int sel, int n_live,
                               const TcSmem & T) {
     const int H = P.H, J = P.J, L = P.L, B = P.B;
@@ -1400,9 +1485,10 @@ __device__ void tc_phase_pred(const LoopParams & P, bool first, int n_emit, int 
             A.rb = P.rbh;
             A.lo = H * es;
             A.kb_split = P.tcp.K >> 5;
+            if constexpr (Q8) q8_rows(S.area, nc, P.rbh, H, A.lo, true, false);
             for (int t0 = 0; t0 < P.tcp.tiles; t0 += TG) {
                 const int nt = min(TG, P.tcp.tiles - t0);
-                tc_gemm(P, S, P.tcp, t0, nt, A, mbp, mbp == 2 ? kWarps : 4, nc * P.rbh);
+                tc_gemm_q<Q8>(P, S, P.tcp, t0, nt, A, mbp, mbp == 2 ? kWarps : 4, nc * P.rbh);
                 for (int idx = threadIdx.x; idx < nc * nt * 8; idx += blockDim.x) {
                     const int rr = idx / nc, cc = idx - rr * nc, row = t0 * 8 + rr;   // utterance fastest
                     if (row < nr) {
@@ -1483,6 +1569,7 @@ __device__ __forceinline__ void joint_keys(const LoopParams & P, const TcSmem & 
     SUBMARK(22);
 }
 
+template <bool Q8>
 __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const TcSmem & T, unsigned long long * keys) {
     const int J = P.J, B = P.B;
     const int rpc = P.rpc_j;
@@ -1519,9 +1606,10 @@ __device__ void tc_phase_joint(const LoopParams & P, int sel, int n_live, const 
         A.rb = P.rbj;
         A.lo = J * 2;
         A.kb_split = P.tcj.K >> 5;
+        if constexpr (Q8) q8_rows(S.area, nc, P.rbj, J, A.lo, false, true);
         for (int t0 = 0; t0 < P.tcj.tiles; t0 += TG) {
             const int nt = min(TG, P.tcj.tiles - t0);
-            tc_gemm(P, S, P.tcj, t0, nt, A, mbp, 4, nc * P.rbj);
+            tc_gemm_q<Q8>(P, S, P.tcj, t0, nt, A, mbp, 4, nc * P.rbj);
             SUBMARK(11);
             if (mbp == 2) joint_keys<2 * kTcM>(P, S, nc, nt, t0, nr, r0, keys);
             else joint_keys<kTcM>(P, S, nc, nt, t0, nr, r0, keys);
@@ -1549,7 +1637,9 @@ __device__ void tc_load_stationary(const LoopParams & P, const TcSmem & T) {
     __syncthreads();
 }
 
-template <bool TC>
+// Q8: PK_MATH_Q8 (its own instantiation, so that the default kernel's register
+// allocation does not carry the q8_0-activation code).
+template <bool TC, bool Q8>
 __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams P) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem S;
@@ -1656,21 +1746,21 @@ __global__ void __launch_bounds__(kThreads, 1) step_loop_kernel(const LoopParams
         }
         if (n_emit > 0) {
             for (int l = 0; l < P.L; ++l) {
-                if constexpr (TC) tc_phase_lstm(P, l, n_emit, T);
+                if constexpr (TC) tc_phase_lstm<Q8>(P, l, n_emit, T);
                 else phase_lstm(P, l, n_emit, S);
                 mark(0);
                 if (!grid_barrier(P, nbar, S)) return;
                 mark(1);
             }
         }
-        if constexpr (TC) tc_phase_pred(P, first, n_emit, sel, n_live, T);
+        if constexpr (TC) tc_phase_pred<Q8>(P, first, n_emit, sel, n_live, T);
         else phase_pred(P, first, n_emit, sel, n_live, S);
         mark(2);
         if (!grid_barrier(P, nbar, S)) return;
         mark(3);
         first = false;
         if (n_live == 0) break;
-        if constexpr (TC) tc_phase_joint(P, sel, n_live, T, keys);
+        if constexpr (TC) tc_phase_joint<Q8>(P, sel, n_live, T, keys);
         else phase_joint(P, sel, n_live, S, keys);
         mark(4);
         bool rep_now = false;
@@ -1727,26 +1817,38 @@ size_t step_loop_tc_smem_bytes(unsigned sm_weights, int area, int rpc_j, int rpc
 }
 
 cudaError_t step_loop_configure(size_t smem, int tc) {
-    return tc ? cudaFuncSetAttribute(step_loop_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem)
-              : cudaFuncSetAttribute(step_loop_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (!tc) return cudaFuncSetAttribute(step_loop_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    const cudaError_t e = cudaFuncSetAttribute(step_loop_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int) smem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(step_loop_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
 }
 
 size_t step_loop_static_smem(int tc) {
     cudaFuncAttributes a{};
-    const cudaError_t e = tc ? cudaFuncGetAttributes(&a, step_loop_kernel<true>)
-                             : cudaFuncGetAttributes(&a, step_loop_kernel<false>);
-    return e == cudaSuccess ? a.sharedSizeBytes : 0;
+    cudaFuncAttributes q{};
+    const cudaError_t e = tc ? cudaFuncGetAttributes(&a, step_loop_kernel<true, false>)
+                             : cudaFuncGetAttributes(&a, step_loop_kernel<false, false>);
+    if (e != cudaSuccess) return 0;
+    if (tc && cudaFuncGetAttributes(&q, step_loop_kernel<true, true>) == cudaSuccess)
+        return a.sharedSizeBytes > q.sharedSizeBytes ? a.sharedSizeBytes : q.sharedSizeBytes;
+    return a.sharedSizeBytes;
 }
 
 cudaError_t step_loop_occupancy(size_t smem, int tc, int * blocks_per_sm) {
-    return tc ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, step_loop_kernel<true>, kThreads, smem)
-              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, step_loop_kernel<false>, kThreads, smem);
+    if (!tc) return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, step_loop_kernel<false, false>, kThreads, smem);
+    int a = 0, q = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, step_loop_kernel<true, false>, kThreads, smem);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&q, step_loop_kernel<true, true>, kThreads, smem);
+    *blocks_per_sm = a < q ? a : q;
+    return e;
 }
 
 cudaError_t launch_step_loop(const LoopParams & p, int grid, size_t smem, cudaStream_t s) {
     void * args[] = {const_cast<LoopParams *>(&p)};
-    const void * fn = p.tc ? reinterpret_cast<const void *>(step_loop_kernel<true>)
-                           : reinterpret_cast<const void *>(step_loop_kernel<false>);
+    const void * fn = !p.tc ? reinterpret_cast<const void *>(step_loop_kernel<false, false>)
+                      : p.q8 ? reinterpret_cast<const void *>(step_loop_kernel<true, true>)
+                             : reinterpret_cast<const void *>(step_loop_kernel<true, false>);
     return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kThreads), args, smem, s);
 }
 
