@@ -137,15 +137,20 @@ enum {
                                 returns PK_ERR_TIMEOUT (exercises failure detection without a fault) */
     PK_OPT_BULK_MIN_LIVE = 5, /* tensor-core math: iterations with at least this many live utterances run
                                 on the tcgen05 bulk loop (two-dimensional tiles, accumulators in tensor
-                                memory), the rest on the persistent loop; default 256, 0 = never,
+                                memory), the rest on the persistent loop; default 128, 0 = never,
                                 1 = every iteration of a fresh batch (trace runs too) */
-    PK_OPT_BULK_SCREEN = 6   /* bulk-loop iterations with at least this many live utterances (default
+    PK_OPT_BULK_SCREEN = 6,  /* bulk-loop iterations with at least this many live utterances (default
                                 1024; 0 = never) compute the joint output screened: one f16 product
                                 per logit screens the tokens against a proven error bound, and the
                                 candidates and the duration logits are recomputed in f32, so the
                                 argmax is that of f32 logits; other iterations take three f16
                                 products per logit (22-bit activations) and the argmax of those.
                                 Trace runs never screen. */
+    PK_OPT_BULK_I8 = 7       /* bulk loop's LSTM and pred-proj GEMMs: 1 (default) = tcgen05 kind::i8 on
+                                int16 fixed-point activations and per-row int16-requantised weights, each
+                                as two signed int8 digits (three int8 products; the layer-0 input
+                                projection from a per-token table); 0 = kind::f16 on f16 hi/lo halves
+                                (three f16 products) */
 };
 
 /* Static information about a context. */

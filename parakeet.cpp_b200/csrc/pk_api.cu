@@ -92,8 +92,9 @@ struct pk_ctx {
     // bulk loop (tcgen05, many live utterances): weights, threshold, per-call buffers
     pk::BulkWeights bulk{};
     int bulk_ok = 0;
-    int bulk_min_live = 256;
+    int bulk_min_live = 128;
     int bulk_screen_min = 1024;    // PK_OPT_BULK_SCREEN
+    int bulk_i8 = 1;               // PK_OPT_BULK_I8
     DevBuf h16, x16, dcount, bprof, norm2, jsum;
     void * pin = nullptr;          // pinned staging of a call's small inputs (copy_segments)
     size_t pin_cap = 0;
@@ -745,8 +746,11 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         PK_CK(x->dcount.ensure((size_t) x->grid * 8));
         q.P = P;
         q.min_live = x->bulk_min_live;
-        for (int l = 0; l < L; ++l) q.gl[l] = x->bulk.gl[l];
-        q.gp = x->bulk.gp;
+        // LSTM and pred-proj as int8 digit planes (kind::i8) when prepared, else f16 halves
+        const bool bi8 = x->bulk_i8 && x->bulk.i8_ok;
+        for (int l = 0; l < L; ++l) q.gl[l] = bi8 ? x->bulk.gli[l] : x->bulk.gl[l];
+        q.gp = bi8 ? x->bulk.gpi : x->bulk.gp;
+        q.g0b = bi8 ? x->bulk.g0b : nullptr;
         q.gj = x->bulk.gj;
         q.lbias = x->bulk.lbias;
         q.e16 = x->bulk.e16;
@@ -1068,7 +1072,8 @@ pk_status pk_create(const pk_model_desc * d, int device, pk_ctx ** out) {
             f16w[x->L] = d->joint_pred_w.type == PK_GGML_F16;
             f16w[x->L + 1] = d->joint_out_w.type == PK_GGML_F16;
             if (bulk_prepare(x->bulk, x->H, x->J, x->L, x->Vo, x->V1, x->embed.as<float>(), wih, whh, bih, bhh,
-                             x->pred_w.as<float>(), x->out_w.as<float>(), f16w, x->stream) != cudaSuccess) {
+                             x->pred_w.as<float>(), x->out_w.as<float>(), f16w, x->g0.as<float>(),
+                             x->stream) != cudaSuccess) {
                 bulk_release(x->bulk);
                 return cleanup(fail(PK_ERR_CUDA, "bulk-loop weight preparation failed"));
             }
@@ -1159,6 +1164,9 @@ pk_status pk_set_option(pk_ctx * x, int32_t opt, int64_t v) {
         case PK_OPT_BULK_MIN_LIVE:
             if (v < 0) return fail(PK_ERR_INVALID, "bulk threshold must be >= 0");
             x->bulk_min_live = (int) std::min<int64_t>(v, 1 << 30);
+            return PK_OK;
+        case PK_OPT_BULK_I8:
+            x->bulk_i8 = v != 0 ? 1 : 0;
             return PK_OK;
         case PK_OPT_BULK_SCREEN:
             if (v < 0) return fail(PK_ERR_INVALID, "screening threshold must be >= 0");

