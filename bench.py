@@ -205,16 +205,19 @@ def cpu_sample_run(orc_o, enc, offs, T, threads, budget_s, msym=None):
 
 # ------------------------------------------------------------ helpers ----
 
-def bulk_flops(model):
-    """Algorithmic FLOPs of the tcgen05 bulk loop's matrix products: per joint
-    evaluation (one live utterance in one iteration) the joint.out product
-    2 * joint_hidden * v_out; per LSTM step (an emission or an utterance's first step)
-    the gate products of every layer, 2 * 4H * (in + H) with in = H (the embedding
-    and the lower layer's h are H wide), and the pred projection 2 * joint_hidden * H.
-    Returns (per joint evaluation, per LSTM step)."""
+def bulk_flops(model, layer0_table=True):
+    """FLOPs of the tcgen05 bulk loop's matrix products: per joint evaluation (one live
+    utterance in one iteration) the joint.out product 2 * joint_hidden * v_out; per
+    LSTM step (an emission or an utterance's first step) the gate products of every
+    layer, 2 * 4H * (in + H) with in = H (the lower layer's h), and the pred projection
+    2 * joint_hidden * H. Layer 0's input projection W_ih0 . embed is a per-token table
+    lookup on the int8 path (layer0_table: not counted, in = 0 for layer 0), a product
+    of the embedding on the f16 path. Returns (per joint evaluation, per LSTM step)."""
     H, J = model.pred_hidden, model.joint_hidden
     joint = 2 * J * model.v_out
     lstm = model.n_layers * 2 * 4 * H * (H + H) + 2 * J * H
+    if layer0_table:
+        lstm -= 2 * 4 * H * H
     return joint, lstm
 
 
@@ -257,6 +260,9 @@ def main():
     ap.add_argument("--no-screen", action="store_true",
                     help="PK_OPT_BULK_SCREEN = 0: the bulk loop's joint always takes three f16 products per "
                          "logit, never one screening product and the f32 recomputation of the candidates")
+    ap.add_argument("--no-i8", action="store_true",
+                    help="PK_OPT_BULK_I8 = 0: the bulk loop's LSTM and pred-proj on f16 hi/lo halves "
+                         "(kind::f16) instead of int8 digits (kind::i8)")
     ap.add_argument("--math", default=None, choices=["tc", "q8", "f32"],
                     help="PK_OPT_MATH (library default when absent: tc); q8 = the optional q8_0-activation "
                          "mode (ggml's vec_dot_q8_0_q8_0 arithmetic, persistent loop only)")
@@ -482,6 +488,8 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
     dec = pk.Decoder(model, device=local_rank, bulk_min_live=args.bulk_min_live, math=args.math)
     if args.no_screen:
         dec.set_option(pk.abi.PK_OPT_BULK_SCREEN, 0)
+    if args.no_i8:
+        dec.set_option(pk.abi.PK_OPT_BULK_I8, 0)
     msym = dec.info.max_symbols_per_step
     Bn = len(T)
     cap = int(pk.lib().pk_tokens_capacity(T.ctypes.data, Bn, msym))
@@ -622,16 +630,19 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
     result = None
     if rank == 0:
         value = tokens_all / (tot_ms / 1e3) if tot_ms > 0 else 0.0
-        fj, fl = bulk_flops(model)
+        fj, fl = bulk_flops(model, layer0_table=not args.no_i8)
         alg_flops = fj * bulk_steps + fl * bulk_lstm
         achieved = alg_flops / (bulk_ms / 1e3) / 1e12 if bulk_ms > 0 else 0.0
         peak, peak_kind = read_peaks("tensor")
         tr = profiled_traffic(args.config)
-        # f16 tcgen05 products issued per algorithmic product: the LSTM and pred-proj
-        # split activations into f16 hi + lo, q8_0 weights (scaled) into hi + lo too (f16
-        # weights are exact); the screened joint issues one (--no-screen: as the LSTM)
+        # tensor work issued per algorithmic product, in f16-product equivalents: the joint
+        # splits activations into f16 hi + lo and q8_0 weights (scaled) into hi + lo (three
+        # products; f16 weights are exact: two), its screened iterations issue one; the
+        # LSTM and pred-proj issue three int8 products (each half an f16 product's time;
+        # --no-i8: as the joint); the int8 layer 0 has K = H instead of 2H
         products = 3 if wtype == "q8_0" else 2
-        issued = ((products * fl * bulk_lstm + fj * (products * (bulk_steps - bulk_scr) + bulk_scr))
+        pl = products if args.no_i8 else 1.5
+        issued = ((pl * fl * bulk_lstm + fj * (products * (bulk_steps - bulk_scr) + bulk_scr))
                   / (bulk_ms / 1e3) / 1e12 if bulk_ms > 0 else 0.0)
         h2d = int(enc.nbytes)
         d2h = int(tokens / max(1, args.steps)) * 4 + (Bn + 1) * 8 + Bn * 4
@@ -679,10 +690,10 @@ def run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wty
                          "traffic": (tr * bulk_steps / args.steps) if tr else None,
                          "kernel": "bulk_loop_kernel",
                          "issued_tflops": issued,
-                         "note": f"algorithmic FLOPs = {fj} per joint evaluation ({bulk_steps // args.steps} "
+                         "note": f"FLOPs of the products computed = {fj} per joint evaluation ({bulk_steps // args.steps} "
                                  f"per launch) + {fl} per LSTM step ({bulk_lstm // args.steps} per launch), "
-                                 f"one product each; the kernel issues {products} f16 tcgen05 products per "
-                                 f"algorithmic LSTM / pred-proj product and per unscreened joint product, "
+                                 f"one product each; the kernel issues {pl} f16-product equivalents per "
+                                 f"algorithmic LSTM / pred-proj product, {products} per unscreened joint product, "
                                  f"one per screened joint product ({bulk_scr // args.steps} screened "
                                  f"evaluations per launch) "
                                  f"(issued_tflops); time = the bulk kernel's CUDA events "
