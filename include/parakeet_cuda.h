@@ -146,11 +146,14 @@ enum {
                                 argmax is that of f32 logits; other iterations take three f16
                                 products per logit (22-bit activations) and the argmax of those.
                                 Trace runs never screen. */
-    PK_OPT_BULK_I8 = 7       /* bulk loop's LSTM and pred-proj GEMMs: 1 (default) = tcgen05 kind::i8 on
+    PK_OPT_BULK_I8 = 7,      /* bulk loop's LSTM and pred-proj GEMMs: 1 (default) = tcgen05 kind::i8 on
                                 int16 fixed-point activations and per-row int16-requantised weights, each
                                 as two signed int8 digits (three int8 products; the layer-0 input
                                 projection from a per-token table); 0 = kind::f16 on f16 hi/lo halves
                                 (three f16 products) */
+    PK_OPT_BULK_TMA_A = 8    /* bulk loop: 1 (default) = activation rows stored in list order (the joint
+                                hidden layer, the pred-proj input, the lower layer's new h) reach shared
+                                memory as 2-D TMA boxes; 0 = every A row is gathered with cp.async */
 };
 
 /* Static information about a context. */

@@ -10,7 +10,7 @@ PK_OK, PK_ERR_DMODEL, PK_ERR_INVALID, PK_ERR_MODEL, PK_ERR_CUDA = 0, 1, 2, 3, 4
 PK_ERR_OOM, PK_ERR_TIMEOUT, PK_ERR_CAPACITY, PK_ERR_NO_DEVICE, PK_ERR_DEVICE = 5, 6, 7, 8, 9
 PK_MODEL_TDT, PK_MODEL_EOU = 1, 2
 PK_OPT_TIMEOUT_US, PK_OPT_MATH, PK_OPT_MAX_SYMBOLS, PK_OPT_TEST_STALL, PK_OPT_BULK_MIN_LIVE = 1, 2, 3, 4, 5
-PK_OPT_BULK_SCREEN, PK_OPT_BULK_I8 = 6, 7
+PK_OPT_BULK_SCREEN, PK_OPT_BULK_I8, PK_OPT_BULK_TMA_A = 6, 7, 8
 PK_MATH_F32, PK_MATH_TC, PK_MATH_Q8 = 0, 1, 2
 
 STATUS_NAMES = {0: "PK_OK", 1: "PK_ERR_DMODEL", 2: "PK_ERR_INVALID", 3: "PK_ERR_MODEL",

@@ -95,6 +95,7 @@ struct pk_ctx {
     int bulk_min_live = 128;
     int bulk_screen_min = 1024;    // PK_OPT_BULK_SCREEN
     int bulk_i8 = 1;               // PK_OPT_BULK_I8
+    int bulk_tma_a = 1;            // PK_OPT_BULK_TMA_A
     DevBuf h16, x16, dcount, bprof, norm2, jsum;
     void * pin = nullptr;          // pinned staging of a call's small inputs (copy_segments)
     size_t pin_cap = 0;
@@ -757,6 +758,12 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         q.h16 = x->h16.as<unsigned char>();
         q.x16 = x->x16.as<unsigned char>();
         q.dcount = x->dcount.as<int2>();
+        // the compact activation rows as TMA boxes (row strides are multiples of 16 bytes)
+        q.tma_a = x->bulk_tma_a;
+        if (q.tma_a) {
+            PK_CK(bulk_row_map(q.map_x16, x->x16.p, (long long) L * Bs, 4LL * H));
+            PK_CK(bulk_row_map(q.map_hid, x->hidc.p, (long long) Bs, (long long) x->tc_rbj));
+        }
         // screened joint (not for trace runs, which report the GEMM's own logits)
         const bool scr = x->bulk_screen_min > 0 && P.trace_steps == 0 && bulk_screen_supported(x->J) &&
                          x->Vo < 0xFFFF && x->bulk.wnorm != nullptr;
@@ -1164,6 +1171,9 @@ pk_status pk_set_option(pk_ctx * x, int32_t opt, int64_t v) {
         case PK_OPT_BULK_MIN_LIVE:
             if (v < 0) return fail(PK_ERR_INVALID, "bulk threshold must be >= 0");
             x->bulk_min_live = (int) std::min<int64_t>(v, 1 << 30);
+            return PK_OK;
+        case PK_OPT_BULK_TMA_A:
+            x->bulk_tma_a = v != 0 ? 1 : 0;
             return PK_OK;
         case PK_OPT_BULK_I8:
             x->bulk_i8 = v != 0 ? 1 : 0;

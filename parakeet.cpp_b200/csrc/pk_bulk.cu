@@ -250,6 +250,25 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
             if (!__all_sync(0xFFFFFFFFu, ok)) return;
             const bool seg1 = kc >= J.split;
             const unsigned dst = smem_u32(tiles + (unsigned) s * R.stage);
+            // compact rows (the joint's hidden rows, the pred-proj input and the lower layer's
+            // new h: consecutive list positions) arrive as TMA boxes; h_prev, by utterance,
+            // is gathered with cp.async
+            if (Q.tma_a && (seg1 ? J.kind != G_LSTM : J.l > 0)) {
+                if (threadIdx.x == 0) {
+                    const CUtensorMap * map = reinterpret_cast<const CUtensorMap *>(
+                        J.kind == G_JOINT ? Q.map_hid : Q.map_x16);
+                    const int m0 = (t % J.nM) * kBM;
+                    const int y = J.kind == G_JOINT ? m0 : (J.kind == G_PRED ? L - 1 : J.l - 1) * B + m0;
+                    const int x = (seg1 ? kc - J.split : kc) * 128;
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                                 :: "r"(smem_u32(&S.full_a[s])), "r"((lo ? 2u : 1u) * kATile) : "memory");
+                    tma_load_2d(tiles + (unsigned) s * R.stage, map, x, y, &S.full_a[s]);
+                    if (lo) tma_load_2d(tiles + (unsigned) s * R.stage + kATile, map, x + (int) plane, y, &S.full_a[s]);
+                } else {
+                    mbar_arrive(&S.full_a[s]);
+                }
+                continue;
+            }
             const unsigned sub = (unsigned) lane & 7u;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
@@ -1466,6 +1485,12 @@ cudaError_t encode_2d(void * map, CUtensorMapDataType type, size_t esize, const 
 
 bool bulk_supported(int H, int J, int L) {
     return H > 0 && J > 0 && H % kBK == 0 && J % kBK == 0 && L >= 1 && L <= kMaxLayers;
+}
+
+// TMA descriptor of `rows` activation rows of row_bytes bytes (a multiple of 16): bytes as
+// elements, 128-row x 128-byte boxes, 128-byte swizzle (the bulk loop's A stage layout).
+cudaError_t bulk_row_map(void * map, const void * base, long long rows, long long row_bytes) {
+    return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, row_bytes, kBM, 128, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool bulk_screen_supported(int J) { return J % 128 == 0 && J <= kScreenMaxJ; }

@@ -178,6 +178,12 @@ struct BulkParams {
     // tile), its four largest token logits; the decision recomputes in f32 every token
     // whose approximate logit is within twice a proven error bound of the row's
     // maximum, and every duration logit.
+    // 2-D TMA descriptors (CUtensorMap, 128 bytes) of the compact activation rows, bytes as
+    // elements, 128 x 128-byte boxes, 128-byte swizzle: x16 ([L][B] rows of 4H bytes) and hidc
+    // ([B] rows of rbj bytes); tma_a = 0 stages every A row with cp.async instead
+    alignas(64) unsigned char map_x16[128];
+    alignas(64) unsigned char map_hid[128];
+    int tma_a;
     int screen_min;
     float * norm2;             // [B] sum of squares of the joint hidden row, by live index
     uint4 * jsum;              // [B][jsum_stride][2] per (live row, N tile): (m1..m4 bits), (j1, j2, j3, NaN flag)
@@ -199,7 +205,8 @@ struct BulkWeights {
     size_t bytes = 0;
 };
 bool        bulk_supported(int H, int J, int L);
-bool        bulk_screen_supported(int J);   // the screened joint's row norms need J % 128 == 0
+bool        bulk_screen_supported(int J);
+cudaError_t bulk_row_map(void * map, const void * base, long long rows, long long row_bytes);   // the screened joint's row norms need J % 128 == 0
 cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
                          const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
                          const float * const * b_hh, const float * pred_w, const float * out_w,
