@@ -766,10 +766,11 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         }
         // screened joint (not for trace runs, which report the GEMM's own logits)
         const bool scr = x->bulk_screen_min > 0 && P.trace_steps == 0 && bulk_screen_supported(x->J) &&
-                         x->Vo < 0xFFFF && x->bulk.wnorm != nullptr;
+                         x->Vo < 0xFFFF && x->V1 >= 64 && x->bulk.wnorm != nullptr;
         q.screen_min = scr ? x->bulk_screen_min : 0;
         if (scr) {
             q.jsum_stride = (x->Vo + 63) / 64;
+            q.n_scr = (x->V1 / 64) * 64;
             PK_CK(x->norm2.ensure(Bs * 4));
             PK_CK(x->jsum.ensure(Bs * (size_t) q.jsum_stride * 32));
             PK_CK(cudaMemsetAsync(x->norm2.p, 0, Bs * 4, s));

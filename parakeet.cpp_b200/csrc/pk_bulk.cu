@@ -127,7 +127,9 @@ __device__ __forceinline__ Job make_job(const BulkParams & Q, int kind, int l, i
     j.M = M;
     j.sel = sel;
     j.g = kind == G_LSTM ? &Q.gl[l] : kind == G_PRED ? &Q.gp : &Q.gj;
-    j.N = j.g->N;
+    // the screened joint covers the token rows [0, n_scr) only (the last few token rows
+    // and the duration rows are recomputed exactly by the decision)
+    j.N = (kind == G_JOINT && screened(Q, M)) ? Q.n_scr : j.g->N;
     j.kel = j.g->i8 ? 2 * kBK : kBK;
     j.nK = j.g->K / j.kel;
     j.nM = (M + kBM - 1) / kBM;
@@ -933,7 +935,8 @@ __device__ __forceinline__ void exact_logits(const BulkParams & Q, const float2 
 // E = 2^-9 ||w||max ||a|| (plus a slack for the bias additions) of its recomputed value,
 // and the recomputed argmax j* satisfies approx(j*) >= M - 2E, M the largest
 // approximate logit. The candidates -- every token with approx >= M - 2E, through each
-// N tile's top three, or the whole tile when its fourth value also qualifies -- are
+// N tile's top three, or the whole tile when its fourth value also qualifies, and the
+// token rows past the last whole 64-row block, which are not screened -- are
 // recomputed in f32 and the largest wins, ties to the smallest index (argmax_f32's
 // first-index rule, src/parakeet_tdt.cpp:25-32). A NaN or infinity anywhere sends the
 // row to the full index-order scan. The duration logits (TDT) are recomputed with the
@@ -1010,9 +1013,11 @@ __device__ void screen_row(const BulkParams & Q, const Job & JJ, int g, int & to
     };
     if (!wild) {
         // one pass over the lanes' tiles, in tile order (durations are queued first, in
-        // index order, so their argmax sees them in order even across flushes)
+        // index order, so their argmax sees them in order even across flushes; then the
+        // unscreened token rows [n_scr, V1))
         if (P.is_tdt)
             for (int d = 0; d < P.Nd; ++d) push(P.V1 + d);
+        for (int j = Q.n_scr; j < P.V1; ++j) push(j);
 #pragma unroll
         for (int k = 0; k < kTl; ++k) {
             unsigned hit = __ballot_sync(0xFFFFFFFFu, t1[k] >= thr);

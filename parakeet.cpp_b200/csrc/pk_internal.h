@@ -188,6 +188,8 @@ struct BulkParams {
     float * norm2;             // [B] sum of squares of the joint hidden row, by live index
     uint4 * jsum;              // [B][jsum_stride][2] per (live row, N tile): (m1..m4 bits), (j1, j2, j3, NaN flag)
     int jsum_stride;           // N tiles of the narrowest joint tiling: ceil(Vo / 64)
+    int n_scr;                 // token rows [0, n_scr) screened (a multiple of 64); rows [n_scr, V1) and the
+                               // duration rows are always recomputed in f32
     const float * wnorm;       // device: max over token rows of joint.out of ||row||_2 (rounded up)
 };
 
