@@ -153,7 +153,8 @@ enum {
                                 (three f16 products) */
     PK_OPT_BULK_TMA_A = 8    /* bulk loop: 1 (default) = activation rows stored in list order (the joint
                                 hidden layer, the pred-proj input, the lower layer's new h) reach shared
-                                memory as 2-D TMA boxes; 0 = every A row is gathered with cp.async */
+                                memory as 2-D TMA boxes and h_prev rows as TMA gather4 loads; 0 = every
+                                A row is gathered with cp.async */
 };
 
 /* Static information about a context. */

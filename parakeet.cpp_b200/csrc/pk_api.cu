@@ -742,7 +742,7 @@ pk_status run_loop(pk_ctx * x, Run & r) {
                           (int) live.size() >= x->bulk_min_live && B <= x->grid * bulk_threads();
     BulkParams q{};
     if (use_bulk) {
-        PK_CK(x->h16.ensure(2 * (size_t) L * Bs * H * 4));
+        PK_CK(x->h16.ensure((2 * (size_t) L * Bs + 1) * H * 4));   // + one zero row (reset h_prev)
         PK_CK(x->x16.ensure((size_t) L * Bs * H * 4));
         PK_CK(x->dcount.ensure((size_t) x->grid * 8));
         q.P = P;
@@ -763,6 +763,9 @@ pk_status run_loop(pk_ctx * x, Run & r) {
         if (q.tma_a) {
             PK_CK(bulk_row_map(q.map_x16, x->x16.p, (long long) L * Bs, 4LL * H));
             PK_CK(bulk_row_map(q.map_hid, x->hidc.p, (long long) Bs, (long long) x->tc_rbj));
+            q.h16_zero_row = (int) (2 * (size_t) L * Bs);
+            PK_CK(cudaMemsetAsync(x->h16.as<unsigned char>() + (size_t) q.h16_zero_row * 4 * H, 0, (size_t) 4 * H, s));
+            PK_CK(bulk_row_map_gather(q.map_h16, x->h16.p, (long long) q.h16_zero_row + 1, 4LL * H));
         }
         // screened joint (not for trace runs, which report the GEMM's own logits)
         const bool scr = x->bulk_screen_min > 0 && P.trace_steps == 0 && bulk_screen_supported(x->J) &&

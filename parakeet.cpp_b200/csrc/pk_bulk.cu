@@ -70,6 +70,7 @@ struct BulkSmem {
     unsigned long long acc_empty[2];
     const unsigned char * a_s0[kBM];   // A rows of the current tile: segment-0 source
     const unsigned char * a_s1[kBM];   // segment-1 source
+    int a_r1[kBM];                     // segment-1 row of the h16 map (h_prev; the zero row for resets)
     unsigned char a_fl[kBM];           // bit 0: row in the batch, bit 1: segment 1 is zero
     unsigned long long rprof[8];       // CTA 0, per role: waits and work inside the GEMM phases (ns)
     int tok_s[kBThreads];              // screened joint: this CTA's slice of the live list, exact argmax
@@ -220,6 +221,7 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
             const int row = (t % J.nM) * kBM + lr;
             const unsigned char * src0 = nullptr;
             const unsigned char * src1 = nullptr;
+            int r1 = Q.h16_zero_row;
             unsigned char fl = 0;                 // bit 0: row in the batch, bit 1: segment 1 is zero
             if (row < J.M) {
                 fl = 1;
@@ -233,6 +235,7 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
                         const int hb = (e.y >> 30) & 1;
                         if (e.y < 0) fl |= 2;             // reset: h_prev = 0
                         src1 = Q.h16 + (((size_t) (hb ^ 1) * L + J.l) * B + e.x) * rb16;
+                        if (e.y >= 0) r1 = ((hb ^ 1) * L + J.l) * B + e.x;
                         src0 = J.l > 0 ? Q.x16 + ((size_t) (J.l - 1) * B + row) * rb16
                                        : Q.e16 + (size_t) (e.y & 0x3FFFFFFF) * rb16;
                     }
@@ -240,6 +243,7 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
             }
             S.a_s0[lr] = src0;
             S.a_s1[lr] = src1;
+            S.a_r1[lr] = r1;
             S.a_fl[lr] = fl;
             __syncwarp();
         }
@@ -269,6 +273,28 @@ __device__ void gemm_produce_a(const BulkParams & Q, BulkSmem & S, unsigned char
                 } else {
                     mbar_arrive(&S.full_a[s]);
                 }
+                continue;
+            }
+            if (Q.tma_a && seg1 && J.kind == G_LSTM) {
+                // h_prev rows by utterance: each warp's 32 rows as 8 gather4 loads per plane
+                // (lanes 0-7 the hi plane, 8-15 the lo plane); lane 0 posts the warp's bytes
+                if (lane == 0)
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                                 :: "r"(smem_u32(&S.full_a[s])), "r"((lo ? 2u : 1u) * 32u * 128u) : "memory");
+                __syncwarp();
+                if (lane < (lo ? 16 : 8)) {
+                    const int r0 = warp * 32 + 4 * (lane & 7);
+                    const int pl = lane >> 3;
+                    const unsigned d = dst + (unsigned) pl * kATile + (unsigned) r0 * 128u;
+                    const int x = (kc - J.split) * 128 + pl * (int) plane;
+                    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+                                 " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+                                 :: "r"(d), "l"(reinterpret_cast<const CUtensorMap *>(Q.map_h16)), "r"(x),
+                                    "r"(S.a_r1[r0]), "r"(S.a_r1[r0 + 1]), "r"(S.a_r1[r0 + 2]), "r"(S.a_r1[r0 + 3]),
+                                    "r"(smem_u32(&S.full_a[s]))
+                                 : "memory");
+                }
+                if (lane != 0) mbar_arrive(&S.full_a[s]);
                 continue;
             }
             const unsigned sub = (unsigned) lane & 7u;
@@ -1496,6 +1522,11 @@ bool bulk_supported(int H, int J, int L) {
 // elements, 128-row x 128-byte boxes, 128-byte swizzle (the bulk loop's A stage layout).
 cudaError_t bulk_row_map(void * map, const void * base, long long rows, long long row_bytes) {
     return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, row_bytes, kBM, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// The same rows with 1-row boxes (tile::gather4 loads four arbitrary rows each).
+cudaError_t bulk_row_map_gather(void * map, const void * base, long long rows, long long row_bytes) {
+    return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, row_bytes, 1, 128, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool bulk_screen_supported(int J) { return J % 128 == 0 && J <= kScreenMaxJ; }

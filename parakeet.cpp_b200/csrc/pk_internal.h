@@ -183,6 +183,10 @@ struct BulkParams {
     // ([B] rows of rbj bytes); tma_a = 0 stages every A row with cp.async instead
     alignas(64) unsigned char map_x16[128];
     alignas(64) unsigned char map_hid[128];
+    // the h state rows ([2][L][B] rows of 4H bytes, then one zero row) with 1-row boxes for
+    // tile::gather4: h_prev rows, indexed by utterance, four rows per TMA instruction
+    alignas(64) unsigned char map_h16[128];
+    int h16_zero_row;
     int tma_a;
     int screen_min;
     float * norm2;             // [B] sum of squares of the joint hidden row, by live index
@@ -208,7 +212,8 @@ struct BulkWeights {
 };
 bool        bulk_supported(int H, int J, int L);
 bool        bulk_screen_supported(int J);
-cudaError_t bulk_row_map(void * map, const void * base, long long rows, long long row_bytes);   // the screened joint's row norms need J % 128 == 0
+cudaError_t bulk_row_map(void * map, const void * base, long long rows, long long row_bytes);
+cudaError_t bulk_row_map_gather(void * map, const void * base, long long rows, long long row_bytes);   // the screened joint's row norms need J % 128 == 0
 cudaError_t bulk_prepare(BulkWeights & w, int H, int J, int L, int Vo, int V1, const float * embed,
                          const float * const * w_ih, const float * const * w_hh, const float * const * b_ih,
                          const float * const * b_hh, const float * pred_w, const float * out_w,
