@@ -17,8 +17,10 @@ enc-proj GEMM, the persistent step-loop kernel, token compaction.
 Default workload: benchmark configuration 5, TDT-0.6b-v3 q8_0, a global batch of
 4096 utterances with log-normal lengths (median 250 frames, sigma 0.8, clipped to
 [25, 3750]), blank bias +2. With N GPUs (torchrun, one rank per GPU) each rank
-decodes its LPT shard of the same 4096 utterances (strong scaling: N = 8 is the
-stated 4096-over-8 case; no collective on the decode path). Configurations 1-4
+decodes its shard of the same 4096 utterances (pk_shard_balanced: each shard's
+modelled decode time balanced; --shard lpt for the frame-count LPT partition;
+strong scaling: N = 8 is the stated 4096-over-8 case; no collective on the
+decode path). Configurations 1-4
 keep their per-GPU batch (weak scaling).
 
 --impl reference times the reference's own CPU decoder (src/parakeet_tdt.cpp /
@@ -266,6 +268,8 @@ def main():
     ap.add_argument("--math", default=None, choices=["tc", "q8", "f32"],
                     help="PK_OPT_MATH (library default when absent: tc); q8 = the optional q8_0-activation "
                          "mode (ggml's vec_dot_q8_0_q8_0 arithmetic, persistent loop only)")
+    ap.add_argument("--shard", default="balanced", choices=["balanced", "lpt"],
+                    help="partition of the utterances over ranks (N > 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--path", default="tdt", choices=["tdt", "ctc"],
@@ -289,7 +293,7 @@ def main():
     strong = bool(cfg.get("global_batch"))
     B_total = B if strong else B * world
     T_all = global_lengths(pk, cfg, B_total)
-    idx = pk.multi.shard_indices(T_all, world)[rank] if world > 1 else np.arange(B_total)
+    idx = pk.multi.shard_indices(T_all, world, args.shard)[rank] if world > 1 else np.arange(B_total)
     if args.impl == "reference":
         # the CPU arm decodes a bounded sample of the rank's first utterances
         idx = idx[:64 * host_cores()]
@@ -303,7 +307,7 @@ def main():
               "config": args.config, "utterances_per_gpu": int(len(T)), "global_batch": int(B_total),
               "frames_per_gpu": int(T.sum()), "frames_global": int(T_all.sum()), "blank_bias": blank_bias,
               "l2": f"inputs {enc.nbytes / 1e6:.0f} MB of encoder output per step (L2 is 126 MB)",
-              "parallelism": f"utterance shards x{world}" if world > 1 else "single GPU"}
+              "parallelism": f"utterance shards x{world} ({args.shard})" if world > 1 else "single GPU"}
     args.scaling = "strong" if strong else "weak"
 
     if args.impl == "reference":

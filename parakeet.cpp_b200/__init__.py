@@ -58,7 +58,7 @@ def lib():
             "pk_stream_destroy": ([P], None), "pk_stream_reset": ([P], I32),
             "pk_stream_window": ([P, P, I32, I32, I32, I32, I32, P, I32, P, P, P, I32, P], I32),
             "pk_stream_get_state": ([P, P], I32), "pk_stream_set_state": ([P, P], I32),
-            "pk_shard_lpt": ([P, I32, I32, P], I32),
+            "pk_shard_lpt": ([P, I32, I32, P], I32), "pk_shard_balanced": ([P, I32, I32, P], I32),
             "pk_ctc_create": ([I32, I32, I32, P], I32), "pk_ctc_destroy": ([P], None),
             "pk_ctc_greedy": ([P, P, I32, P, P, I32, P, P, I64, P, P, P], I32),
             "pk_vocab_create": ([I32, P, P, I32, I32, I32, I32, I32, P], I32), "pk_vocab_destroy": ([P], None),
@@ -91,6 +91,16 @@ def shard_lpt(n_frames: Sequence[int], n_shards: int) -> np.ndarray:
     n = np.ascontiguousarray(n_frames, np.int32)
     out = np.zeros(max(len(n), 1), np.int32)
     _check(lib().pk_shard_lpt(_p(n), len(n), n_shards, _p(out)), "pk_shard_lpt")
+    return out[:len(n)]
+
+
+def shard_balanced(n_frames: Sequence[int], n_shards: int) -> np.ndarray:
+    """pk_shard_balanced: partition of utterances over devices that balances each
+    shard's modelled decode time (its longest utterance's sequential decode and
+    the per-iteration cost of its live utterances), not its frames."""
+    n = np.ascontiguousarray(n_frames, np.int32)
+    out = np.zeros(max(len(n), 1), np.int32)
+    _check(lib().pk_shard_balanced(_p(n), len(n), n_shards, _p(out)), "pk_shard_balanced")
     return out[:len(n)]
 
 

@@ -91,7 +91,7 @@ EXPORTED_SYMBOLS = [
     "pk_stream_create", "pk_stream_destroy", "pk_stream_reset", "pk_stream_window",
     "pk_stream_get_state", "pk_stream_set_state", "pk_shard_lpt", "pk_decode_noalloc",
     "pk_ctc_create", "pk_ctc_destroy", "pk_ctc_greedy", "pk_vocab_create", "pk_vocab_destroy",
-    "pk_detokenize", "pk_prefetch_batch",
+    "pk_detokenize", "pk_prefetch_batch", "pk_shard_balanced",
 ]
 
 

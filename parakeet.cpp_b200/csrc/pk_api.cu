@@ -959,6 +959,27 @@ pk_status batch_run(pk_ctx * x, const pk_batch * b, const pk_trace * trace, pk_r
 
 }  // namespace
 
+namespace {
+
+// Modelled cost of one step-loop iteration with n live utterances (microseconds,
+// TDT-0.6b on one B200 at the default hand-over of 128 live): the persistent loop
+// below 128, the bulk loop from 128 up. Piecewise linear through measured points;
+// only its shape matters to the partition, which compares shards against each other.
+double iteration_cost(int64_t n) {
+    static const double px[] = {1, 16, 32, 64, 127}, py[] = {19.2, 20.7, 23.8, 34.5, 54.4};
+    static const double bx[] = {128, 256, 1024, 4096}, by[] = {80.8, 83.5, 118.9, 236.9};
+    auto interp = [](const double * x, const double * y, int m, double v) {
+        if (v <= x[0]) return y[0];
+        for (int i = 1; i < m; ++i)
+            if (v <= x[i]) return y[i - 1] + (y[i] - y[i - 1]) * (v - x[i - 1]) / (x[i] - x[i - 1]);
+        return y[m - 1] + (y[m - 1] - y[m - 2]) * (v - x[m - 1]) / (x[m - 1] - x[m - 2]);
+    };
+    if (n <= 0) return 0.0;
+    return n < 128 ? interp(px, py, 5, (double) n) : interp(bx, by, 4, (double) n);
+}
+
+}  // namespace
+
 extern "C" {
 
 const char * pk_last_error(void) { return g_err.c_str(); }
@@ -1404,6 +1425,36 @@ pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_shards, in
             if (load[(size_t) k] < load[(size_t) best]) best = k;
         shard_of[i] = best;
         load[(size_t) best] += std::max(n_frames[i], 0);
+    }
+    return PK_OK;
+}
+
+pk_status pk_shard_balanced(const int32_t * n_frames, int32_t B, int32_t n_shards, int32_t * shard_of) {
+    if (B < 0 || n_shards <= 0 || (B > 0 && (!n_frames || !shard_of)))
+        return fail(PK_ERR_INVALID, "bad sharding arguments");
+    // A shard's call lasts sum_i cost(live_i) over its loop iterations, live_i = its
+    // utterances with more than i decode steps; steps are taken proportional to
+    // frames. Utterances go in descending length, so every member already on a
+    // shard is at least as long as the next one: adding t frames to a shard of n
+    // adds t * (cost(n + 1) - cost(n)). Each goes where the shard's modelled time
+    // after adding it is smallest (ties to the lowest shard id).
+    std::vector<int> idx((size_t) B);
+    std::iota(idx.begin(), idx.end(), 0);
+    std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return n_frames[a] > n_frames[b]; });
+    std::vector<double> time((size_t) n_shards, 0.0);
+    std::vector<int64_t> count((size_t) n_shards, 0);
+    for (int i : idx) {
+        const double t = (double) std::max(n_frames[i], 0);
+        int best = 0;
+        double best_time = 0.0;
+        for (int k = 0; k < n_shards; ++k) {
+            const int64_t n = count[(size_t) k];
+            const double after = time[(size_t) k] + t * (iteration_cost(n + 1) - iteration_cost(n));
+            if (k == 0 || after < best_time) { best = k; best_time = after; }
+        }
+        shard_of[i] = best;
+        time[(size_t) best] = best_time;
+        ++count[(size_t) best];
     }
     return PK_OK;
 }

@@ -2,8 +2,10 @@
 
 Utterances are independent, so there is no collective on the decode path: each
 rank decodes a disjoint shard on its own device and the host gathers the token
-lists afterwards. The partition is pk_shard_lpt (longest-processing-time by
-frame count), computed identically on every rank.
+lists afterwards. The partition is computed identically on every rank: by default
+pk_shard_balanced (each shard's modelled decode time balanced: a shard holding a
+very long utterance, whose sequential decode sets the shard's call time, takes
+fewer others), or pk_shard_lpt (longest-processing-time by frame count).
 """
 from __future__ import annotations
 
@@ -12,10 +14,13 @@ from typing import Dict, List, Sequence
 import numpy as np
 
 
-def shard_indices(n_frames: Sequence[int], world: int) -> List[np.ndarray]:
-    """Utterance indices of each rank (ascending within a rank)."""
-    from . import shard_lpt
-    owner = shard_lpt(n_frames, world)
+def shard_indices(n_frames: Sequence[int], world: int, policy: str = "balanced") -> List[np.ndarray]:
+    """Utterance indices of each rank (ascending within a rank); policy "balanced"
+    (pk_shard_balanced) or "lpt" (pk_shard_lpt)."""
+    from . import shard_balanced, shard_lpt
+    if policy not in ("balanced", "lpt"):
+        raise ValueError(f"unknown sharding policy {policy!r}")
+    owner = (shard_balanced if policy == "balanced" else shard_lpt)(n_frames, world)
     return [np.nonzero(owner == r)[0].astype(np.int64) for r in range(world)]
 
 

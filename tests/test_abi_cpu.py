@@ -57,6 +57,63 @@ def test_shard_lpt_matches_python_lpt(pk):
     assert np.array_equal(pk.shard_lpt(T, 3), exp)
 
 
+def _iteration_cost(n):
+    """pk_shard_balanced's per-iteration cost model (microseconds vs live count)."""
+    if n <= 0:
+        return 0.0
+    if n < 128:
+        return float(np.interp(n, [1, 16, 32, 64, 127], [19.2, 20.7, 23.8, 34.5, 54.4]))
+    bx, by = [128, 256, 1024, 4096], [80.8, 83.5, 118.9, 236.9]
+    if n <= bx[-1]:
+        return float(np.interp(n, bx, by))
+    return by[-1] + (by[-1] - by[-2]) * (n - bx[-1]) / (bx[-1] - bx[-2])
+
+
+def _modelled_time(T):
+    """sum over loop iterations of the cost at that iteration's live count, steps = frames."""
+    T = np.sort(np.asarray(T, np.int64))[::-1]
+    if len(T) == 0 or T[0] <= 0:
+        return 0.0
+    cnt = np.bincount(T, minlength=int(T[0]) + 1)
+    live = len(T) - np.cumsum(cnt)[:-1]
+    return float(sum(_iteration_cost(int(n)) for n in live))
+
+
+def test_shard_balanced_matches_python_greedy(pk):
+    """The same greedy restated: descending frames, each to the shard whose modelled
+    time after adding it is smallest, ties to the lowest shard id."""
+    for T, world in ((np.array([5, 9, 9, 1, 0, 7, 3], np.int32), 3),
+                     (pk.synth.lengths_lognormal(300, seed=3), 4)):
+        order = sorted(range(len(T)), key=lambda i: (-int(T[i]), i))
+        tm, cnt = [0.0] * world, [0] * world
+        exp = np.zeros(len(T), np.int32)
+        for i in order:
+            after = [tm[k] + int(T[i]) * (_iteration_cost(cnt[k] + 1) - _iteration_cost(cnt[k]))
+                     for k in range(world)]
+            k = int(np.argmin(after))
+            exp[i] = k
+            tm[k] = after[k]
+            cnt[k] += 1
+        assert np.array_equal(pk.shard_balanced(T, world), exp)
+
+
+def test_shard_balanced_evens_modelled_time(pk):
+    """On configuration 5's lengths the balanced partition's slowest shard is modelled
+    no slower than LPT's, and the shard with the longest utterance holds fewer than
+    an equal share; every utterance is placed once, deterministically."""
+    T = pk.synth.lengths_lognormal(4096, 250.0, 0.8, 25, 3750, seed=7)
+    for world in (2, 4, 8):
+        bal, lpt = pk.shard_balanced(T, world), pk.shard_lpt(T, world)
+        assert bal.min() >= 0 and bal.max() < world and len(bal) == len(T)
+        assert np.array_equal(bal, pk.shard_balanced(T, world))
+        t_bal = max(_modelled_time(T[bal == k]) for k in range(world))
+        t_lpt = max(_modelled_time(T[lpt == k]) for k in range(world))
+        assert t_bal <= t_lpt * 1.0001
+        assert np.sum(bal == bal[int(np.argmax(T))]) < len(T) // world
+    assert np.array_equal(pk.shard_balanced(T, 1), np.zeros(len(T), np.int32))
+    assert len(pk.shard_balanced(np.zeros(0, np.int32), 3)) == 0
+
+
 def test_tokens_capacity(pk):
     T = np.array([3, 0, 10], np.int32)
     f = pk.lib().pk_tokens_capacity
@@ -68,6 +125,7 @@ def test_invalid_arguments_report_status(pk):
     L = pk.lib()
     assert L.pk_shard_lpt(None, 3, 0, None) == pk.abi.PK_ERR_INVALID
     assert "sharding" in pk.last_error()
+    assert L.pk_shard_balanced(None, 3, 0, None) == pk.abi.PK_ERR_INVALID
     assert L.pk_create(None, 0, None) == pk.abi.PK_ERR_INVALID
     assert L.pk_prefetch_batch(None, None, None) == pk.abi.PK_ERR_INVALID
 
