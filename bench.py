@@ -17,8 +17,9 @@ enc-proj GEMM, the persistent step-loop kernel, token compaction.
 Default workload: benchmark configuration 5, TDT-0.6b-v3 q8_0, a global batch of
 4096 utterances with log-normal lengths (median 250 frames, sigma 0.8, clipped to
 [25, 3750]), blank bias +2. With N GPUs (torchrun, one rank per GPU) each rank
-decodes its shard of the same 4096 utterances (pk_shard_balanced: each shard's
-modelled decode time balanced; --shard lpt for the frame-count LPT partition;
+decodes its shard of the same 4096 utterances (pk_shard_balanced: the longest
+utterances share shards and every shard's modelled decode time is bounded;
+--shard lpt for the frame-count LPT partition;
 strong scaling: N = 8 is the stated 4096-over-8 case; no collective on the
 decode path). Configurations 1-4
 keep their per-GPU batch (weak scaling).
@@ -294,9 +295,11 @@ def main():
     B_total = B if strong else B * world
     T_all = global_lengths(pk, cfg, B_total)
     idx = pk.multi.shard_indices(T_all, world, args.shard)[rank] if world > 1 else np.arange(B_total)
+    shard_sizes = [int(len(x)) for x in pk.multi.shard_indices(T_all, world, args.shard)] if world > 1 else [B_total]
     if args.impl == "reference":
-        # the CPU arm decodes a bounded sample of the rank's first utterances
-        idx = idx[:64 * host_cores()]
+        # the CPU arm (rank 0 alone) decodes a bounded sample of the batch's first
+        # utterances, whatever the rank count
+        idx = (np.arange(B_total) if strong else idx)[:64 * host_cores()]
     T = T_all[idx].astype(np.int32)
     if strong:
         # every utterance has the same frames whichever rank decodes it
@@ -304,7 +307,8 @@ def main():
     else:
         enc, offs = pk.synth.encoder_batch(T, model.d_enc, seed=99 + rank)
     config = {"workload": cfg["desc"] + (f" (wtype {wtype})" if wtype != cfg["wtype"] else ""),
-              "config": args.config, "utterances_per_gpu": int(len(T)), "global_batch": int(B_total),
+              "config": args.config, "utterances_per_gpu": shard_sizes if world > 1 else int(len(T)),
+              "global_batch": int(B_total),
               "frames_per_gpu": int(T.sum()), "frames_global": int(T_all.sum()), "blank_bias": blank_bias,
               "l2": f"inputs {enc.nbytes / 1e6:.0f} MB of encoder output per step (L2 is 126 MB)",
               "parallelism": f"utterance shards x{world} ({args.shard})" if world > 1 else "single GPU"}

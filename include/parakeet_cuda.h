@@ -348,14 +348,16 @@ PK_API pk_status pk_shard_lpt(const int32_t * n_frames, int32_t B, int32_t n_sha
 
 /* Partition that balances each shard's modelled decode time rather than its
  * frames (no counterpart in the reference, which decodes on one device). A call
- * lasts as long as its longest utterance's sequential decode, and each loop
- * iteration costs more with more utterances live, so a shard holding a very long
- * utterance should hold fewer others. Model: decode steps proportional to frames,
- * one iteration's cost a piecewise-linear function of the live count measured on
- * B200 (persistent loop below 128 live, bulk loop from 128). Greedy: descending
- * frame count, each utterance to the shard whose modelled time after adding it
- * is smallest (ties to the lowest shard id). Deterministic: every rank computes
- * the same partition. */
+ * lasts as long as its longest utterance's sequential decode, and one loop
+ * iteration costs little more with a few more utterances live, so long utterances
+ * are best decoded together on a shard rather than each setting its own shard's
+ * time. Model: decode steps proportional to frames, one iteration's cost a
+ * piecewise-linear function of the live count measured on B200 (persistent loop
+ * below 128 live, bulk loop from 128). First fit decreasing (descending frame
+ * count, each utterance to the lowest shard whose modelled time stays within a
+ * bound) with the bound bisected to the smallest that places every utterance.
+ * Shards may differ widely in size. Deterministic: every rank computes the same
+ * partition. */
 PK_API pk_status pk_shard_balanced(const int32_t * n_frames, int32_t B, int32_t n_shards, int32_t * shard_of);
 
 /* --- decode without device allocation ------------------------------------- */

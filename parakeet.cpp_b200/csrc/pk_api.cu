@@ -1434,27 +1434,54 @@ pk_status pk_shard_balanced(const int32_t * n_frames, int32_t B, int32_t n_shard
         return fail(PK_ERR_INVALID, "bad sharding arguments");
     // A shard's call lasts sum_i cost(live_i) over its loop iterations, live_i = its
     // utterances with more than i decode steps; steps are taken proportional to
-    // frames. Utterances go in descending length, so every member already on a
-    // shard is at least as long as the next one: adding t frames to a shard of n
-    // adds t * (cost(n + 1) - cost(n)). Each goes where the shard's modelled time
-    // after adding it is smallest (ties to the lowest shard id).
+    // frames. Utterances are placed in descending length, so every member already on
+    // a shard is at least as long as the next one: adding t frames to a shard of n
+    // adds t * (cost(n + 1) - cost(n)). First fit decreasing against a bound M on
+    // every shard's modelled time (each utterance to the lowest shard that stays
+    // within M), with M bisected down to the smallest bound that places every
+    // utterance: long utterances share shards, whose per-iteration cost barely
+    // grows with a few more live, instead of each setting its own shard's time.
     std::vector<int> idx((size_t) B);
     std::iota(idx.begin(), idx.end(), 0);
     std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return n_frames[a] > n_frames[b]; });
-    std::vector<double> time((size_t) n_shards, 0.0);
-    std::vector<int64_t> count((size_t) n_shards, 0);
-    for (int i : idx) {
-        const double t = (double) std::max(n_frames[i], 0);
-        int best = 0;
-        double best_time = 0.0;
-        for (int k = 0; k < n_shards; ++k) {
-            const int64_t n = count[(size_t) k];
-            const double after = time[(size_t) k] + t * (iteration_cost(n + 1) - iteration_cost(n));
-            if (k == 0 || after < best_time) { best = k; best_time = after; }
+    std::vector<double> time((size_t) n_shards);
+    std::vector<int64_t> count((size_t) n_shards);
+    std::vector<int32_t> trial((size_t) std::max(B, 1));
+    auto place = [&](double M) -> bool {
+        std::fill(time.begin(), time.end(), 0.0);
+        std::fill(count.begin(), count.end(), 0);
+        for (int i : idx) {
+            const double t = (double) std::max(n_frames[i], 0);
+            int k = 0;
+            for (; k < n_shards; ++k) {
+                const int64_t n = count[(size_t) k];
+                const double after = time[(size_t) k] + t * (iteration_cost(n + 1) - iteration_cost(n));
+                if (after <= M) {
+                    time[(size_t) k] = after;
+                    ++count[(size_t) k];
+                    trial[(size_t) i] = k;
+                    break;
+                }
+            }
+            if (k == n_shards) return false;
         }
-        shard_of[i] = best;
-        time[(size_t) best] = best_time;
-        ++count[(size_t) best];
+        return true;
+    };
+    if (B == 0) return PK_OK;
+    // bounds: the longest utterance alone; everything on one shard
+    double lo = (double) std::max(n_frames[idx[0]], 0) * iteration_cost(1), hi = 0.0;
+    for (size_t r = 0; r < idx.size(); ++r)
+        hi += (double) std::max(n_frames[idx[r]], 0) * (iteration_cost((int64_t) r + 1) - iteration_cost((int64_t) r));
+    place(hi);
+    std::copy(trial.begin(), trial.begin() + B, shard_of);
+    for (int it = 0; it < 64 && hi - lo > 1e-9 * hi; ++it) {
+        const double mid = 0.5 * (lo + hi);
+        if (place(mid)) {
+            hi = mid;
+            std::copy(trial.begin(), trial.begin() + B, shard_of);
+        } else {
+            lo = mid;
+        }
     }
     return PK_OK;
 }

@@ -3,9 +3,10 @@
 Utterances are independent, so there is no collective on the decode path: each
 rank decodes a disjoint shard on its own device and the host gathers the token
 lists afterwards. The partition is computed identically on every rank: by default
-pk_shard_balanced (each shard's modelled decode time balanced: a shard holding a
-very long utterance, whose sequential decode sets the shard's call time, takes
-fewer others), or pk_shard_lpt (longest-processing-time by frame count).
+pk_shard_balanced (each shard's modelled decode time bounded: the longest
+utterances, whose sequential decodes set a shard's call time, share shards, and
+the short ones fill the rest), or pk_shard_lpt (longest-processing-time by frame
+count).
 """
 from __future__ import annotations
 

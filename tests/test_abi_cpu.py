@@ -57,16 +57,24 @@ def test_shard_lpt_matches_python_lpt(pk):
     assert np.array_equal(pk.shard_lpt(T, 3), exp)
 
 
+def _interp(x, y, v):
+    """pk_shard_balanced's piecewise-linear interpolation, the same operations in the same order."""
+    if v <= x[0]:
+        return y[0]
+    for i in range(1, len(x)):
+        if v <= x[i]:
+            return y[i - 1] + (y[i] - y[i - 1]) * (v - x[i - 1]) / (x[i] - x[i - 1])
+    m = len(x)
+    return y[m - 1] + (y[m - 1] - y[m - 2]) * (v - x[m - 1]) / (x[m - 1] - x[m - 2])
+
+
 def _iteration_cost(n):
     """pk_shard_balanced's per-iteration cost model (microseconds vs live count)."""
     if n <= 0:
         return 0.0
     if n < 128:
-        return float(np.interp(n, [1, 16, 32, 64, 127], [19.2, 20.7, 23.8, 34.5, 54.4]))
-    bx, by = [128, 256, 1024, 4096], [80.8, 83.5, 118.9, 236.9]
-    if n <= bx[-1]:
-        return float(np.interp(n, bx, by))
-    return by[-1] + (by[-1] - by[-2]) * (n - bx[-1]) / (bx[-1] - bx[-2])
+        return _interp([1.0, 16.0, 32.0, 64.0, 127.0], [19.2, 20.7, 23.8, 34.5, 54.4], float(n))
+    return _interp([128.0, 256.0, 1024.0, 4096.0], [80.8, 83.5, 118.9, 236.9], float(n))
 
 
 def _modelled_time(T):
@@ -79,28 +87,53 @@ def _modelled_time(T):
     return float(sum(_iteration_cost(int(n)) for n in live))
 
 
-def test_shard_balanced_matches_python_greedy(pk):
-    """The same greedy restated: descending frames, each to the shard whose modelled
-    time after adding it is smallest, ties to the lowest shard id."""
-    for T, world in ((np.array([5, 9, 9, 1, 0, 7, 3], np.int32), 3),
-                     (pk.synth.lengths_lognormal(300, seed=3), 4)):
-        order = sorted(range(len(T)), key=lambda i: (-int(T[i]), i))
-        tm, cnt = [0.0] * world, [0] * world
-        exp = np.zeros(len(T), np.int32)
+def _ffd_bisect(T, world):
+    """The partition restated: first fit decreasing against a bound on every shard's
+    modelled time, the bound bisected to the smallest that places every utterance."""
+    order = sorted(range(len(T)), key=lambda i: (-int(T[i]), i))
+
+    def place(M):
+        tm, cnt, out = [0.0] * world, [0] * world, [0] * len(T)
         for i in order:
-            after = [tm[k] + int(T[i]) * (_iteration_cost(cnt[k] + 1) - _iteration_cost(cnt[k]))
-                     for k in range(world)]
-            k = int(np.argmin(after))
-            exp[i] = k
-            tm[k] = after[k]
-            cnt[k] += 1
-        assert np.array_equal(pk.shard_balanced(T, world), exp)
+            t = float(max(int(T[i]), 0))
+            for k in range(world):
+                after = tm[k] + t * (_iteration_cost(cnt[k] + 1) - _iteration_cost(cnt[k]))
+                if after <= M:
+                    tm[k], out[i] = after, k
+                    cnt[k] += 1
+                    break
+            else:
+                return None
+        return out
+
+    lo = float(max(int(T[order[0]]), 0)) * _iteration_cost(1)
+    hi = 0.0
+    for r, i in enumerate(order):
+        hi += float(max(int(T[i]), 0)) * (_iteration_cost(r + 1) - _iteration_cost(r))
+    best = place(hi)
+    it = 0
+    while it < 64 and hi - lo > 1e-9 * hi:
+        mid = 0.5 * (lo + hi)
+        p = place(mid)
+        if p is not None:
+            hi, best = mid, p
+        else:
+            lo = mid
+        it += 1
+    return np.array(best, np.int32)
+
+
+def test_shard_balanced_matches_python_restatement(pk):
+    for T, world in ((np.array([5, 9, 9, 1, 0, 7, 3], np.int32), 3),
+                     (pk.synth.lengths_lognormal(300, seed=3), 4),
+                     (np.array([40, 40, 40], np.int32), 8)):
+        assert np.array_equal(pk.shard_balanced(T, world), _ffd_bisect(T, world))
 
 
 def test_shard_balanced_evens_modelled_time(pk):
     """On configuration 5's lengths the balanced partition's slowest shard is modelled
-    no slower than LPT's, and the shard with the longest utterance holds fewer than
-    an equal share; every utterance is placed once, deterministically."""
+    well below LPT's, and the shard with the longest utterance holds fewer than an
+    equal share; every utterance is placed once, deterministically."""
     T = pk.synth.lengths_lognormal(4096, 250.0, 0.8, 25, 3750, seed=7)
     for world in (2, 4, 8):
         bal, lpt = pk.shard_balanced(T, world), pk.shard_lpt(T, world)
@@ -108,10 +141,12 @@ def test_shard_balanced_evens_modelled_time(pk):
         assert np.array_equal(bal, pk.shard_balanced(T, world))
         t_bal = max(_modelled_time(T[bal == k]) for k in range(world))
         t_lpt = max(_modelled_time(T[lpt == k]) for k in range(world))
-        assert t_bal <= t_lpt * 1.0001
+        assert t_bal < t_lpt
         assert np.sum(bal == bal[int(np.argmax(T))]) < len(T) // world
     assert np.array_equal(pk.shard_balanced(T, 1), np.zeros(len(T), np.int32))
     assert len(pk.shard_balanced(np.zeros(0, np.int32), 3)) == 0
+    # as many equal utterances as shards: one each
+    assert sorted(pk.shard_balanced(np.full(4, 100, np.int32), 4).tolist()) == [0, 1, 2, 3]
 
 
 def test_tokens_capacity(pk):

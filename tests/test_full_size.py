@@ -210,8 +210,9 @@ def config5_inputs(built):
 def test_config5_full(built, orc, config5_inputs, blank_bias):
     """TDT-0.6b q8_0, the whole 4096-utterance batch on one GPU (log-normal lengths,
     median 250, sigma 0.8, clipped to [25, 3750]), blank bias 0 / +2 / +4: every
-    utterance against the reference; reversed, and rank 0's shard of an 8-GPU LPT
-    partition decoded as its own batch."""
+    utterance against the reference; reversed, and two shards of 8-GPU partitions
+    decoded as their own batches (rank 0's LPT shard; the balanced partition's rank 6,
+    a thousand-odd shorter utterances)."""
     pk = built
     m = pk.synth.tdt_0_6b(seed=1234, blank_bias=blank_bias)
     fx = fixture(f"config5_bias{int(blank_bias)}")
@@ -223,9 +224,9 @@ def test_config5_full(built, orc, config5_inputs, blank_bias):
     rev = np.arange(len(T))[::-1]
     rr = dec.decode_batch(enc, np.ascontiguousarray(offs[rev]), np.ascontiguousarray(T[rev]))
     check_reference(orc, m, enc, offs[rev], T[rev], rr, fx, rev, dec)
-    sh = pk.multi.shard_indices(T, 8)[0]
-    rs = dec.decode_batch(enc, np.ascontiguousarray(offs[sh]), np.ascontiguousarray(T[sh]))
-    check_reference(orc, m, enc, offs[sh], T[sh], rs, fx, sh, dec)
+    for sh in (pk.multi.shard_indices(T, 8, "lpt")[0], pk.multi.shard_indices(T, 8, "balanced")[6]):
+        rs = dec.decode_batch(enc, np.ascontiguousarray(offs[sh]), np.ascontiguousarray(T[sh]))
+        check_reference(orc, m, enc, offs[sh], T[sh], rs, fx, sh, dec)
 
 
 @pytest.mark.parametrize("bulk", [0, 1])
