@@ -963,11 +963,13 @@ namespace {
 
 // Modelled cost of one step-loop iteration with n live utterances (microseconds,
 // TDT-0.6b on one B200 at the default hand-over of 128 live): the persistent loop
-// below 128, the bulk loop from 128 up. Piecewise linear through measured points;
-// only its shape matters to the partition, which compares shards against each other.
+// below 128, the bulk loop from 128 up. Piecewise linear; the knot values are a
+// least-squares fit to the measured call times of 29 shards of the 4096-utterance
+// log-normal batch (1, 2, 4 and 8 shards, two partitions), every one reproduced
+// within 4 %. Only the shape matters to the partition, which compares shards.
 double iteration_cost(int64_t n) {
-    static const double px[] = {1, 16, 32, 64, 127}, py[] = {19.2, 20.7, 23.8, 34.5, 54.4};
-    static const double bx[] = {128, 256, 1024, 4096}, by[] = {80.8, 83.5, 118.9, 236.9};
+    static const double px[] = {1, 16, 32, 64, 127}, py[] = {19.1, 21.7, 34.0, 43.6, 76.8};
+    static const double bx[] = {128, 256, 1024, 4096}, by[] = {70.9, 84.5, 141.0, 346.2};
     auto interp = [](const double * x, const double * y, int m, double v) {
         if (v <= x[0]) return y[0];
         for (int i = 1; i < m; ++i)
@@ -977,6 +979,10 @@ double iteration_cost(int64_t n) {
     if (n <= 0) return 0.0;
     return n < 128 ? interp(px, py, 5, (double) n) : interp(bx, by, 4, (double) n);
 }
+
+// Enc-proj per frame in the same units (4.95 ns per frame measured, over ~0.52 decode
+// steps per frame, since the partition counts frames as steps).
+constexpr double kFrameCost = 0.0095;
 
 }  // namespace
 
@@ -1436,7 +1442,7 @@ pk_status pk_shard_balanced(const int32_t * n_frames, int32_t B, int32_t n_shard
     // utterances with more than i decode steps; steps are taken proportional to
     // frames. Utterances are placed in descending length, so every member already on
     // a shard is at least as long as the next one: adding t frames to a shard of n
-    // adds t * (cost(n + 1) - cost(n)). First fit decreasing against a bound M on
+    // adds t * (cost(n + 1) - cost(n)), plus its enc-proj. First fit decreasing against a bound M on
     // every shard's modelled time (each utterance to the lowest shard that stays
     // within M), with M bisected down to the smallest bound that places every
     // utterance: long utterances share shards, whose per-iteration cost barely
@@ -1455,7 +1461,7 @@ pk_status pk_shard_balanced(const int32_t * n_frames, int32_t B, int32_t n_shard
             int k = 0;
             for (; k < n_shards; ++k) {
                 const int64_t n = count[(size_t) k];
-                const double after = time[(size_t) k] + t * (iteration_cost(n + 1) - iteration_cost(n));
+                const double after = time[(size_t) k] + t * (iteration_cost(n + 1) - iteration_cost(n)) + kFrameCost * t;
                 if (after <= M) {
                     time[(size_t) k] = after;
                     ++count[(size_t) k];
@@ -1469,9 +1475,10 @@ pk_status pk_shard_balanced(const int32_t * n_frames, int32_t B, int32_t n_shard
     };
     if (B == 0) return PK_OK;
     // bounds: the longest utterance alone; everything on one shard
-    double lo = (double) std::max(n_frames[idx[0]], 0) * iteration_cost(1), hi = 0.0;
+    double lo = (double) std::max(n_frames[idx[0]], 0) * (iteration_cost(1) + kFrameCost), hi = 0.0;
     for (size_t r = 0; r < idx.size(); ++r)
-        hi += (double) std::max(n_frames[idx[r]], 0) * (iteration_cost((int64_t) r + 1) - iteration_cost((int64_t) r));
+        hi += (double) std::max(n_frames[idx[r]], 0) *
+              (iteration_cost((int64_t) r + 1) - iteration_cost((int64_t) r) + kFrameCost);
     place(hi);
     std::copy(trial.begin(), trial.begin() + B, shard_of);
     for (int it = 0; it < 64 && hi - lo > 1e-9 * hi; ++it) {

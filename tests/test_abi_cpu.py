@@ -73,8 +73,11 @@ def _iteration_cost(n):
     if n <= 0:
         return 0.0
     if n < 128:
-        return _interp([1.0, 16.0, 32.0, 64.0, 127.0], [19.2, 20.7, 23.8, 34.5, 54.4], float(n))
-    return _interp([128.0, 256.0, 1024.0, 4096.0], [80.8, 83.5, 118.9, 236.9], float(n))
+        return _interp([1.0, 16.0, 32.0, 64.0, 127.0], [19.1, 21.7, 34.0, 43.6, 76.8], float(n))
+    return _interp([128.0, 256.0, 1024.0, 4096.0], [70.9, 84.5, 141.0, 346.2], float(n))
+
+
+_FRAME_COST = 0.0095   # enc-proj per frame in the model's units
 
 
 def _modelled_time(T):
@@ -97,7 +100,7 @@ def _ffd_bisect(T, world):
         for i in order:
             t = float(max(int(T[i]), 0))
             for k in range(world):
-                after = tm[k] + t * (_iteration_cost(cnt[k] + 1) - _iteration_cost(cnt[k]))
+                after = tm[k] + t * (_iteration_cost(cnt[k] + 1) - _iteration_cost(cnt[k])) + _FRAME_COST * t
                 if after <= M:
                     tm[k], out[i] = after, k
                     cnt[k] += 1
@@ -106,10 +109,10 @@ def _ffd_bisect(T, world):
                 return None
         return out
 
-    lo = float(max(int(T[order[0]]), 0)) * _iteration_cost(1)
+    lo = float(max(int(T[order[0]]), 0)) * (_iteration_cost(1) + _FRAME_COST)
     hi = 0.0
     for r, i in enumerate(order):
-        hi += float(max(int(T[i]), 0)) * (_iteration_cost(r + 1) - _iteration_cost(r))
+        hi += float(max(int(T[i]), 0)) * (_iteration_cost(r + 1) - _iteration_cost(r) + _FRAME_COST)
     best = place(hi)
     it = 0
     while it < 64 and hi - lo > 1e-9 * hi:
