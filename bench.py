@@ -271,6 +271,9 @@ def main():
                          "mode (ggml's vec_dot_q8_0_q8_0 arithmetic, persistent loop only)")
     ap.add_argument("--shard", default="balanced", choices=["balanced", "lpt"],
                     help="partition of the utterances over ranks (N > 1)")
+    ap.add_argument("--emulate-ranks", type=int, default=0,
+                    help="one GPU: decode each of the N shards of the global batch alone and report "
+                         "the slowest shard's call time (the N-GPU step time, since ranks share nothing)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--path", default="tdt", choices=["tdt", "ctc"],
@@ -279,6 +282,8 @@ def main():
     args.warmup = max(args.warmup, 0)
     if args.path == "ctc":
         return run_ctc(args)
+    if args.emulate_ranks > 0:
+        return run_emulated_ranks(args)
 
     cfg = dict(CONFIGS[args.config])
     wtype = args.wtype or cfg["wtype"]
@@ -317,6 +322,48 @@ def main():
     if args.impl == "reference":
         return run_reference(args, model, enc, offs, T, config, rank)
     return run_ours(args, pk, model, enc, offs, T, config, world, rank, local_rank, wtype, idx)
+
+
+def run_emulated_ranks(args):
+    """Strong scaling of a global batch over N ranks, emulated on one GPU: each rank's
+    shard (--shard) decoded alone with device-resident input, W warm-up and K timed calls
+    per shard (the library's CUDA events); the slowest shard's call time is the N-GPU
+    step time, since ranks share no data and no collective. Prints one JSON line
+    (not the bench contract's line: a measurement aid for the partition)."""
+    import torch
+    pk = pkg()
+    cfg = dict(CONFIGS[args.config])
+    if not cfg.get("global_batch"):
+        print(json.dumps({"emulate_ranks": args.emulate_ranks, "unavailable": "configuration has no global batch"}))
+        return 0
+    wtype = args.wtype or cfg["wtype"]
+    blank_bias = cfg["blank_bias"] if args.blank_bias is None else args.blank_bias
+    model = make_model(pk, cfg, wtype, blank_bias)
+    B_total = args.batch or cfg["B"]
+    T_all = global_lengths(pk, cfg, B_total)
+    shards = pk.multi.shard_indices(T_all, args.emulate_ranks, args.shard) if args.emulate_ranks > 1 \
+        else [np.arange(B_total)]
+    dec = pk.Decoder(model, bulk_min_live=args.bulk_min_live, math=args.math)
+    times, tokens = [], 0
+    for idx in shards:
+        T = T_all[idx].astype(np.int32)
+        enc, offs = pk.synth.encoder_pooled(T, idx, model.d_enc, seed=99)
+        ed = torch.from_numpy(enc).cuda()
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            dec.decode_batch(ed.data_ptr(), offs, T, enc_on_device=True)
+        rs = [dec.decode_batch(ed.data_ptr(), offs, T, enc_on_device=True) for _ in range(max(1, args.steps))]
+        times.append(float(np.median([r["total_ms"] for r in rs])))
+        tokens += sum(len(t) for t in rs[0]["tokens"])
+        del ed
+    dec.close()
+    slow = max(times)
+    print(json.dumps({"emulate_ranks": args.emulate_ranks, "shard": args.shard, "metric": METRIC,
+                      "value": tokens / (slow / 1e3), "unit": "tokens/s", "ms_per_step": slow,
+                      "shard_ms": [round(t, 3) for t in times], "shard_sizes": [int(len(i)) for i in shards],
+                      "config": {"workload": cfg["desc"], "global_batch": int(B_total)},
+                      "timing": "each shard alone on one GPU, median of K calls (CUDA events), slowest shard"}))
+    return 0
 
 
 def run_ctc(args):

@@ -212,7 +212,7 @@ def test_config5_full(built, orc, config5_inputs, blank_bias):
     median 250, sigma 0.8, clipped to [25, 3750]), blank bias 0 / +2 / +4: every
     utterance against the reference; reversed, and two shards of 8-GPU partitions
     decoded as their own batches (rank 0's LPT shard; the balanced partition's rank 6,
-    a thousand-odd shorter utterances)."""
+    several hundred shorter utterances)."""
     pk = built
     m = pk.synth.tdt_0_6b(seed=1234, blank_bias=blank_bias)
     fx = fixture(f"config5_bias{int(blank_bias)}")
