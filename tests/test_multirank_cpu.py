@@ -1,17 +1,19 @@
-"""world_size-2 gloo test of the multi-GPU host path: LPT sharding computed on
-every rank, per-rank decode of a disjoint shard, gather of token lists to rank 0.
+"""world_size-2 gloo test of the multi-GPU host path: the partition (balanced or
+LPT) computed on every rank, per-rank decode of a disjoint shard, gather of token
+lists to rank 0.
 The per-rank decode here is the CPU oracle (the sharding/gather logic is what is
 tested); on GPUs bench.py runs the same logic with libparakeet_cuda."""
 import os
 import sys
 
 import numpy as np
+import pytest
 import torch.multiprocessing as mp
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, policy):
     import torch.distributed as dist
     sys.path.insert(0, HERE)
     from conftest import load_oracle, load_pkg
@@ -25,7 +27,7 @@ def _worker(rank, world, port, q):
                                   n_layers=2, seed=21, blank_bias=1.5)
         T = pk.synth.lengths_uniform(9, 0, 30, seed=2)
         enc, offs = pk.synth.encoder_batch(T, 32, seed=4)
-        idx = pk.multi.shard_indices(T, world)[rank]
+        idx = pk.multi.shard_indices(T, world, policy)[rank]
         sub = pk.multi.sub_batch(enc, offs, T, idx)
         o = orc.Oracle(m)
         r = o.decode_batch(*sub, n_threads=1)
@@ -40,7 +42,8 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_two_rank_shard_and_gather():
+@pytest.mark.parametrize("policy", ["balanced", "lpt"])
+def test_two_rank_shard_and_gather(policy):
     import socket
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -48,7 +51,7 @@ def test_two_rank_shard_and_gather():
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, policy)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
